@@ -1,0 +1,515 @@
+// tcgen05 GEMM for sm_100a: bf16 operands, fp32 TMEM accumulators.
+//
+//   C[M,N] (+)= A[M,K] * B[K,N]
+//
+// Persistent kernel, one CTA per SM, 6 warps with fixed roles:
+//   warp 0      TMA producer (one elected lane) filling a STAGES-deep smem ring
+//   warp 1      TMEM allocator + MMA issuer (one elected lane, tcgen05.mma)
+//   warps 2..5  epilogue: tcgen05.ld of the 128xBN fp32 tile, convert, store
+// Two TMEM accumulators (2*BN columns) let the epilogue of tile i overlap the
+// main loop of tile i+1.
+//
+// Operand majorness is a template choice so that all three products of a
+// linear layer run without transposes:
+//   forward  y  = x  @ W     A K-major (x [M,K]),  B MN-major (W [K,N])
+//   grad-in  dx = dy @ W^T   A K-major (dy [M,N]), B K-major  (W read as [N,K])
+//   grad-W   dW = x^T @ dy   A MN-major (x [K,M]), B MN-major (dy [K,N])
+//
+// Modes
+//   DENSE      one problem
+//   GROUPED_M  MoE expert GEMMs: rows of A/C are partitioned into groups whose
+//              starts are multiples of 128 (the dispatch pads each expert's
+//              segment), each group multiplies its own B[g]; tile counts per
+//              group come from a device prefix array so no host sync is needed
+//   GROUPED_K  MoE expert weight gradients: the contraction runs over each
+//              group's (padded) row segment, C[g] = A_g^T B_g
+#include <torch/extension.h>
+
+#include "../common/host.h"
+#include "../common/sm100.cuh"
+
+namespace hb {
+
+constexpr int GEMM_BM = 128;
+constexpr int GEMM_BK = 64;
+constexpr int GEMM_THREADS = 192;
+
+enum GemmMode { DENSE = 0, GROUPED_M = 1, GROUPED_K = 2 };
+enum GemmEpi { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACC = 2 };
+
+struct GemmArgs {
+  int M, N, K;
+  int tiles_m, tiles_n;
+  int num_tiles;                // DENSE / GROUPED_K; GROUPED_M reads grp_tile_start[G]
+  int num_groups;
+  const int* grp_start;         // GROUPED_M: row start; GROUPED_K: k start
+  const int* grp_count;         // rows / k per group
+  const int* grp_tile_start;    // GROUPED_M: prefix of tiles per group [G+1]
+  void* C;
+  long long ldc;
+  long long c_group_stride;     // GROUPED_K: elements between C[g] and C[g+1]
+  float alpha;
+  int* status;
+  unsigned long long budget_ns;
+};
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
+  static constexpr int B_BYTES = BN * GEMM_BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : 2 * BN;  // power of two
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+struct TileInfo {
+  int m0, n0, k0, k_iters, group, m_limit;
+};
+
+template <int MODE, int BN>
+__device__ __forceinline__ bool get_tile(const GemmArgs& a, int t, TileInfo& ti) {
+  if (MODE == DENSE) {
+    if (t >= a.num_tiles) return false;
+    int mb = t / a.tiles_n, nb = t - mb * a.tiles_n;
+    ti.m0 = mb * GEMM_BM;
+    ti.n0 = nb * BN;
+    ti.k0 = 0;
+    ti.k_iters = (a.K + GEMM_BK - 1) / GEMM_BK;
+    ti.group = 0;
+    ti.m_limit = a.M;
+    return true;
+  } else if (MODE == GROUPED_M) {
+    const int total = __ldg(a.grp_tile_start + a.num_groups);
+    if (t >= total) return false;
+    int g = 0;
+    // groups are few (<= 256): linear scan over the prefix array
+    while (g + 1 < a.num_groups && __ldg(a.grp_tile_start + g + 1) <= t) ++g;
+    int local = t - __ldg(a.grp_tile_start + g);
+    int mb = local / a.tiles_n, nb = local - mb * a.tiles_n;
+    int start = __ldg(a.grp_start + g);
+    ti.m0 = start + mb * GEMM_BM;
+    ti.n0 = nb * BN;
+    ti.k0 = 0;
+    ti.k_iters = (a.K + GEMM_BK - 1) / GEMM_BK;
+    ti.group = g;
+    ti.m_limit = start + __ldg(a.grp_count + g);
+    return true;
+  } else {
+    if (t >= a.num_tiles) return false;
+    const int per = a.tiles_m * a.tiles_n;
+    int g = t / per;
+    int local = t - g * per;
+    int mb = local / a.tiles_n, nb = local - mb * a.tiles_n;
+    ti.m0 = mb * GEMM_BM;
+    ti.n0 = nb * BN;
+    ti.k0 = __ldg(a.grp_start + g);
+    ti.k_iters = (__ldg(a.grp_count + g) + GEMM_BK - 1) / GEMM_BK;
+    ti.group = g;
+    ti.m_limit = a.M;
+    return true;
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, int MODE, int EPI>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmArgs args) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* bar_area = smem + STAGES * Cfg::STAGE_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(bar_area);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&tfull_bar[i]), 1);
+      mbar_init(smem_u32(&tempty_bar[i]), 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok; t += gridDim.x) {
+        TileInfo ti;
+        if (!get_tile<MODE, BN>(args, t, ti)) break;
+        for (int kb = 0; kb < ti.k_iters; ++kb) {
+          if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, args.status, kErrTimeoutProducer,
+                         args.budget_ns)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&full_bar[stage]);
+          mbar_expect_tx(fb, Cfg::STAGE_BYTES);
+          const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t sb = sa + Cfg::A_BYTES;
+          const int kc = ti.k0 + kb * GEMM_BK;
+          if (!A_MN) {
+            tma_load_2d(sa, &tmA, fb, kc, ti.m0);
+          } else {
+#pragma unroll
+            for (int i = 0; i < GEMM_BM / 64; ++i) tma_load_2d(sa + i * 8192, &tmA, fb, ti.m0 + 64 * i, kc);
+          }
+          if (MODE == GROUPED_M) {
+            if (!B_MN) {
+              tma_load_3d(sb, &tmB, fb, kc, ti.n0, ti.group);
+            } else {
+#pragma unroll
+              for (int i = 0; i < BN / 64; ++i) tma_load_3d(sb + i * 8192, &tmB, fb, ti.n0 + 64 * i, kc, ti.group);
+            }
+          } else {
+            if (!B_MN) {
+              tma_load_2d(sb, &tmB, fb, kc, ti.n0);
+            } else {
+#pragma unroll
+              for (int i = 0; i < BN / 64; ++i) tma_load_2d(sb + i * 8192, &tmB, fb, ti.n0 + 64 * i, kc);
+            }
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idesc = make_idesc_bf16(GEMM_BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok; t += gridDim.x) {
+        TileInfo ti;
+        if (!get_tile<MODE, BN>(args, t, ti)) break;
+        if (!mbar_wait(smem_u32(&tempty_bar[acc]), acc_phase ^ 1, args.status, kErrTimeoutMma,
+                       args.budget_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < ti.k_iters; ++kb) {
+          if (!mbar_wait(smem_u32(&full_bar[stage]), phase, args.status, kErrTimeoutMma,
+                         args.budget_ns)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t sb = sa + Cfg::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
+            uint64_t ad, bd;
+            if (!A_MN)
+              ad = make_smem_desc(sa + kk * 32, 16, 1024);
+            else
+              ad = make_smem_desc(sa + kk * 2048, 8192, 1024);
+            if (!B_MN)
+              bd = make_smem_desc(sb + kk * 32, 16, 1024);
+            else
+              bd = make_smem_desc(sb + kk * 2048, 8192, 1024);
+            umma_f16(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(smem_u32(&empty_bar[stage]));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(smem_u32(&tfull_bar[acc]));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;  // TMEM lane quadrant accessible to this warp
+    const int row_in_tile = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x;; t += gridDim.x) {
+      TileInfo ti;
+      if (!get_tile<MODE, BN>(args, t, ti)) break;
+      if (!mbar_wait(smem_u32(&tfull_bar[acc]), acc_phase, args.status, kErrTimeoutEpilogue,
+                     args.budget_ns))
+        break;
+      tc_fence_after();
+      const int m = ti.m0 + row_in_tile;
+      const bool row_ok = m < ti.m_limit;
+      const bool has_k = ti.k_iters > 0;
+      char* cbase = reinterpret_cast<char*>(args.C);
+      if (MODE == GROUPED_K) cbase += (long long)ti.group * args.c_group_stride * (EPI == EPI_BF16 ? 2 : 4);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c * 32, r);
+        tmem_ld_wait();
+        const int n = ti.n0 + c * 32;
+        if (!row_ok || n >= args.N) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = has_k ? __uint_as_float(r[j]) * args.alpha : 0.f;
+        const bool full = (n + 32 <= args.N);
+        if (EPI == EPI_BF16) {
+          __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(cbase) + (long long)m * args.ldc + n;
+          if (full) {
+            uint4* o4 = reinterpret_cast<uint4*>(out);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 w;
+              w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+              w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+              w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+              w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+              o4[q] = w;
+            }
+          } else {
+            for (int j = 0; j < 32 && n + j < args.N; ++j) out[j] = __float2bfloat16_rn(v[j]);
+          }
+        } else {
+          float* out = reinterpret_cast<float*>(cbase) + (long long)m * args.ldc + n;
+          if (full) {
+            float4* o4 = reinterpret_cast<float4*>(out);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              float4 w = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+              if (EPI == EPI_F32_ACC) {
+                float4 o = o4[q];
+                w.x += o.x;
+                w.y += o.y;
+                w.z += o.z;
+                w.w += o.w;
+              }
+              o4[q] = w;
+            }
+          } else {
+            for (int j = 0; j < 32 && n + j < args.N; ++j) out[j] = (EPI == EPI_F32_ACC ? out[j] : 0.f) + v[j];
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&tempty_bar[acc]));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+}
+
+// ============================================================================
+// Host side
+// ============================================================================
+namespace {
+
+template <int BN, bool A_MN, bool B_MN, int MODE, int EPI>
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid) {
+  using Cfg = GemmCfg<BN>;
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, MODE, EPI>;
+  static bool configured = false;  // one static per instantiation
+  if (!configured) {
+    HB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    configured = true;
+  }
+  kern<<<grid, GEMM_THREADS, Cfg::SMEM, cur_stream()>>>(ta, tb, args);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+template <int BN, int MODE>
+void dispatch(bool a_mn, bool b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
+              const GemmArgs& args, int grid) {
+#define HB_G(AM, BM_, E)                                    \
+  if (a_mn == AM && b_mn == BM_ && epi == E) {              \
+    launch<BN, AM, BM_, MODE, E>(ta, tb, args, grid);       \
+    return;                                                 \
+  }
+  if (MODE == DENSE) {
+    HB_G(false, true, EPI_BF16) HB_G(false, true, EPI_F32) HB_G(false, true, EPI_F32_ACC)
+    HB_G(false, false, EPI_BF16) HB_G(false, false, EPI_F32) HB_G(false, false, EPI_F32_ACC)
+    HB_G(true, true, EPI_BF16) HB_G(true, true, EPI_F32) HB_G(true, true, EPI_F32_ACC)
+    HB_G(true, false, EPI_BF16) HB_G(true, false, EPI_F32) HB_G(true, false, EPI_F32_ACC)
+  } else if (MODE == GROUPED_M) {
+    HB_G(false, true, EPI_BF16) HB_G(false, true, EPI_F32)
+    HB_G(false, false, EPI_BF16) HB_G(false, false, EPI_F32)
+  } else {
+    HB_G(true, true, EPI_F32) HB_G(true, true, EPI_F32_ACC) HB_G(true, true, EPI_BF16)
+  }
+#undef HB_G
+  HB_CHECK(false, "unsupported gemm variant");
+}
+
+int pick_bn(int N) { return N >= 256 ? 256 : 128; }
+
+int epi_of(const torch::Tensor& c, bool accumulate) {
+  if (c.scalar_type() == at::kBFloat16) {
+    HB_CHECK(!accumulate, "accumulate requires an fp32 output");
+    return EPI_BF16;
+  }
+  HB_CHECK(c.scalar_type() == at::kFloat, "output must be bf16 or fp32");
+  return accumulate ? EPI_F32_ACC : EPI_F32;
+}
+
+GemmArgs base_args(const torch::Tensor& c, double alpha) {
+  GemmArgs a{};
+  a.C = c.data_ptr();
+  a.ldc = c.stride(-2);
+  a.alpha = (float)alpha;
+  a.status = status_ptr();
+  a.budget_ns = wait_budget_ns();
+  return a;
+}
+
+}  // namespace
+
+// c[M,N] (+)= op(a) @ op(b);  a is [M,K] (or [K,M] when trans_a); b is [K,N]
+// (or [N,K] when trans_b).  All operands row-major with unit column stride.
+void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool trans_a, bool trans_b,
+          bool accumulate, double alpha) {
+  check_bf16(a, "a");
+  check_bf16(b, "b");
+  HB_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2, "gemm expects 2-D tensors");
+  HB_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && c.stride(1) == 1, "unit column stride required");
+  const int M = trans_a ? a.size(1) : a.size(0);
+  const int K = trans_a ? a.size(0) : a.size(1);
+  const int N = trans_b ? b.size(0) : b.size(1);
+  HB_CHECK((trans_b ? b.size(1) : b.size(0)) == K, "gemm: inner dimensions differ");
+  HB_CHECK(c.size(0) == M && c.size(1) == N, "gemm: bad output shape");
+  if (M == 0 || N == 0) return;
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int BN = pick_bn(N);
+  // A operand
+  CUtensorMap ta = trans_a ? tmap_bf16_2d(a.data_ptr(), K, M, a.stride(0), 64, 64)
+                           : tmap_bf16_2d(a.data_ptr(), M, K, a.stride(0), 64, GEMM_BM);
+  CUtensorMap tb = trans_b ? tmap_bf16_2d(b.data_ptr(), N, K, b.stride(0), 64, BN)
+                           : tmap_bf16_2d(b.data_ptr(), K, N, b.stride(0), 64, 64);
+  GemmArgs args = base_args(c, alpha);
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.tiles_m = (M + GEMM_BM - 1) / GEMM_BM;
+  args.tiles_n = (N + BN - 1) / BN;
+  args.num_tiles = args.tiles_m * args.tiles_n;
+  if (K == 0) {
+    HB_CHECK(false, "gemm with K == 0 is not supported");
+  }
+  const int grid = std::min(args.num_tiles, num_sms());
+  const int epi = epi_of(c, accumulate);
+  if (BN == 256)
+    dispatch<256, DENSE>(trans_a, !trans_b, epi, ta, tb, args, grid);
+  else
+    dispatch<128, DENSE>(trans_a, !trans_b, epi, ta, tb, args, grid);
+}
+
+// Grouped over M (MoE forward / input-gradient):
+//   c[rows of g] = a[rows of g] @ op(b[g])
+// a: [R, K] bf16;  b: [G, K, N] (trans_b false) or [G, N, K] (trans_b true);
+// grp_start/grp_count: int32 [G] (starts multiples of 128);
+// grp_tile_start: int32 [G+1] prefix of ceil(count/128)*tiles_n (device).
+void grouped_gemm_m(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor grp_start,
+                    torch::Tensor grp_count, torch::Tensor grp_tile_start, bool trans_b) {
+  check_bf16(a, "a");
+  check_bf16(b, "b");
+  HB_CHECK(b.dim() == 3 && b.is_contiguous(), "b must be contiguous [G, *, *]");
+  const int G = b.size(0);
+  const int R = a.size(0), K = a.size(1);
+  const int N = trans_b ? b.size(1) : b.size(2);
+  HB_CHECK((trans_b ? b.size(2) : b.size(1)) == K, "grouped_gemm_m: inner dims differ");
+  HB_CHECK(c.size(0) == R && c.size(1) == N && c.stride(1) == 1, "grouped_gemm_m: bad output");
+  HB_CHECK(grp_start.numel() == G && grp_count.numel() == G && grp_tile_start.numel() == G + 1,
+           "grouped_gemm_m: bad group arrays");
+  if (R == 0) return;
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int BN = pick_bn(N);
+  CUtensorMap ta = tmap_bf16_2d(a.data_ptr(), R, K, a.stride(0), 64, GEMM_BM);
+  CUtensorMap tb = trans_b ? tmap_bf16_3d(b.data_ptr(), G, N, K, K, (uint64_t)N * K, 64, BN)
+                           : tmap_bf16_3d(b.data_ptr(), G, K, N, N, (uint64_t)K * N, 64, 64);
+  GemmArgs args = base_args(c, 1.0);
+  args.M = R;
+  args.N = N;
+  args.K = K;
+  args.tiles_n = (N + BN - 1) / BN;
+  args.num_groups = G;
+  args.grp_start = grp_start.data_ptr<int>();
+  args.grp_count = grp_count.data_ptr<int>();
+  args.grp_tile_start = grp_tile_start.data_ptr<int>();
+  const int max_tiles = ((R + GEMM_BM - 1) / GEMM_BM) * args.tiles_n;
+  const int grid = std::max(1, std::min(max_tiles, num_sms()));
+  const int epi = epi_of(c, false);
+  if (BN == 256)
+    dispatch<256, GROUPED_M>(false, !trans_b, epi, ta, tb, args, grid);
+  else
+    dispatch<128, GROUPED_M>(false, !trans_b, epi, ta, tb, args, grid);
+}
+
+// Grouped over K (MoE weight gradients):  c[g] (+)= a_g^T @ b_g
+// a: [R, M] bf16 rows of group g at [start, start+count);  b: [R, N] bf16;
+// c: [G, M, N] fp32 (or bf16 without accumulate); counts multiples of 64.
+void grouped_gemm_k(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor grp_start,
+                    torch::Tensor grp_count, bool accumulate) {
+  check_bf16(a, "a");
+  check_bf16(b, "b");
+  HB_CHECK(c.dim() == 3 && c.is_contiguous(), "c must be contiguous [G, M, N]");
+  const int G = c.size(0), M = c.size(1), N = c.size(2);
+  const int R = a.size(0);
+  HB_CHECK(a.size(1) == M && b.size(0) == R && b.size(1) == N, "grouped_gemm_k: bad shapes");
+  if (G == 0) return;
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int BN = pick_bn(N);
+  CUtensorMap ta = tmap_bf16_2d(a.data_ptr(), R, M, a.stride(0), 64, 64);
+  CUtensorMap tb = tmap_bf16_2d(b.data_ptr(), R, N, b.stride(0), 64, 64);
+  GemmArgs args = base_args(c, 1.0);
+  args.ldc = N;
+  args.c_group_stride = (long long)M * N;
+  args.M = M;
+  args.N = N;
+  args.K = R;
+  args.tiles_m = (M + GEMM_BM - 1) / GEMM_BM;
+  args.tiles_n = (N + BN - 1) / BN;
+  args.num_tiles = G * args.tiles_m * args.tiles_n;
+  args.num_groups = G;
+  args.grp_start = grp_start.data_ptr<int>();
+  args.grp_count = grp_count.data_ptr<int>();
+  const int grid = std::min(args.num_tiles, num_sms());
+  const int epi = epi_of(c, accumulate);
+  if (BN == 256)
+    dispatch<256, GROUPED_K>(true, true, epi, ta, tb, args, grid);
+  else
+    dispatch<128, GROUPED_K>(true, true, epi, ta, tb, args, grid);
+}
+
+}  // namespace hb

@@ -1,0 +1,103 @@
+"""tcgen05 GEMM numerics against an fp32 PyTorch matmul of the same bf16 inputs."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _ext():
+    from hanuman_b200.ops._ext import ext
+    return ext()
+
+
+def _rel_err(x, ref):
+    return ((x.float() - ref).norm() / ref.norm().clamp_min(1e-12)).item()
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 200, 136), (304, 200, 136), (1024, 1024, 1024),
+                                   (4096, 768, 1024), (77, 64, 520), (2048, 3072, 512)])
+@pytest.mark.parametrize("ta,tb", [(False, False), (False, True), (True, False), (True, True)])
+def test_dense_gemm(M, N, K, ta, tb):
+    # TMA needs 16-byte row strides: the contiguous dimension of each operand
+    # must be a multiple of 8 bf16 elements.
+    if (ta and M % 8) or (not ta and K % 8) or (tb and K % 8) or (not tb and N % 8):
+        pytest.skip("operand row stride not 16-byte aligned")
+    torch.manual_seed(0)
+    dev = "cuda"
+    a = torch.randn(K, M, device=dev) if ta else torch.randn(M, K, device=dev)
+    b = torch.randn(N, K, device=dev) if tb else torch.randn(K, N, device=dev)
+    a, b = a.bfloat16(), b.bfloat16()
+    A = a.float().t() if ta else a.float()
+    B = b.float().t() if tb else b.float()
+    ref = A @ B
+    c = torch.empty(M, N, device=dev, dtype=torch.float32)
+    _ext().gemm(a, b, c, ta, tb, False, 1.0)
+    torch.cuda.synchronize()
+    assert _rel_err(c, ref) < 1e-5
+    c16 = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    _ext().gemm(a, b, c16, ta, tb, False, 1.0)
+    assert _rel_err(c16, ref) < 1e-2
+    acc = torch.randn(M, N, device=dev)
+    ref2 = acc + 0.5 * ref
+    _ext().gemm(a, b, acc, ta, tb, True, 0.5)
+    assert _rel_err(acc, ref2) < 1e-5
+
+
+def _groups(counts, align=128):
+    starts, s = [], 0
+    for c in counts:
+        starts.append(s)
+        s += (c + align - 1) // align * align
+    return starts, s
+
+
+@pytest.mark.parametrize("trans_b", [False, True])
+def test_grouped_m(trans_b):
+    torch.manual_seed(1)
+    dev = "cuda"
+    G, K, N = 6, 512, 384
+    counts = [0, 130, 7, 256, 1000, 64]
+    starts, R = _groups(counts)
+    a = torch.randn(R, K, device=dev).bfloat16()
+    b = (torch.randn(G, N, K, device=dev) if trans_b else torch.randn(G, K, N, device=dev)).bfloat16()
+    c = torch.full((R, N), float("nan"), device=dev)
+    BN = 256 if N >= 256 else 128
+    tiles_n = (N + BN - 1) // BN
+    tstart = [0]
+    for cnt in counts:
+        tstart.append(tstart[-1] + (cnt + 127) // 128 * tiles_n)
+    gs = torch.tensor(starts, dtype=torch.int32, device=dev)
+    gc = torch.tensor(counts, dtype=torch.int32, device=dev)
+    gt = torch.tensor(tstart, dtype=torch.int32, device=dev)
+    _ext().grouped_gemm_m(a, b, c, gs, gc, gt, trans_b)
+    torch.cuda.synchronize()
+    for g in range(G):
+        if counts[g] == 0:
+            continue
+        s, n = starts[g], counts[g]
+        W = b[g].float().t() if trans_b else b[g].float()
+        ref = a[s:s + n].float() @ W
+        assert _rel_err(c[s:s + n], ref) < 1e-5
+
+
+@pytest.mark.parametrize("acc", [False, True])
+def test_grouped_k(acc):
+    torch.manual_seed(2)
+    dev = "cuda"
+    G, M, N = 5, 256, 384
+    counts = [128, 0, 384, 128, 1024]
+    starts, R = _groups(counts)
+    a = torch.randn(R, M, device=dev).bfloat16()
+    b = torch.randn(R, N, device=dev).bfloat16()
+    c = torch.randn(G, M, N, device=dev)
+    c0 = c.clone()
+    gs = torch.tensor(starts, dtype=torch.int32, device=dev)
+    gc = torch.tensor(counts, dtype=torch.int32, device=dev)
+    _ext().grouped_gemm_k(a, b, c, gs, gc, acc)
+    torch.cuda.synchronize()
+    for g in range(G):
+        s, n = starts[g], counts[g]
+        ref = a[s:s + n].float().t() @ b[s:s + n].float()
+        if acc:
+            ref = ref + c0[g]
+        assert _rel_err(c[g], ref) < 1e-5 or (n == 0 and torch.equal(c[g], ref))
