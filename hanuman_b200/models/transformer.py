@@ -1,0 +1,152 @@
+"""Pre-norm hybrid MoE transformer (model/transformer.py:27-417).
+
+Block: ``x += rs * attn(norm1(x)); x += rs * ffn(norm2(x))`` with ONE
+learnable residual scale per block shared by both adds (transformer.py:80-99),
+fp32 residual stream, per-layer attention type (full / swa / kda), dense FFN
+for the first ``dense_layers`` layers and MoE after, tied fp32-master
+embedding used as the output head.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from .. import ops
+from ..config import Config
+from ..ops import reference as ref
+from .layers import KDA, Attention, DenseFFN, MoE, RMSNorm
+
+
+class Block(nn.Module):
+    def __init__(self, cfg: Config, layer: int, gen: torch.Generator):
+        super().__init__()
+        self.layer = layer
+        self.attention_type = cfg.layer_types()[layer]
+        self.use_moe = layer >= cfg.dense_layers
+        self.norm1 = RMSNorm(cfg.d_model, cfg.norm_eps)
+        if self.attention_type == "kda":
+            self.attn = KDA(cfg.d_model, cfg.kda_heads, cfg.kda_head_dim, gen,
+                            chunk=cfg.kda_chunk_size, gate=cfg.kda_gate)
+        else:
+            self.attn = Attention(cfg.d_model, cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, gen,
+                                  window=cfg.layer_window(layer))
+        self.norm2 = RMSNorm(cfg.d_model, cfg.norm_eps)
+        if self.use_moe:
+            self.ffn = MoE(cfg.d_model, cfg.d_ff, cfg.n_experts, cfg.n_active,
+                           cfg.n_shared_experts, cfg.router_init_std, cfg.routed_scaling_factor,
+                           gen, d_ff_shared=cfg.d_ff_shared, router_type=cfg.router_type)
+        else:
+            self.ffn = DenseFFN(cfg.d_model, cfg.d_ff_shared, gen)
+        self.residual_scale = nn.Parameter(torch.tensor(float(cfg.residual_scale_init)))
+
+    def forward(self, x, cos, sin, dtype, positions=None, cache=None):
+        rs = self.residual_scale.float()
+        h = self.norm1(x, dtype)
+        if self.attention_type == "kda":
+            a = self.attn(h, dtype, state=None if cache is None else cache.kda_state(self.layer))
+        else:
+            a = self.attn(h, cos, sin, dtype, positions=positions,
+                          cache=None if cache is None else cache.kv(self.layer))
+        x = x + rs * a
+        h = self.norm2(x, dtype)
+        if self.use_moe:
+            f, aux = self.ffn(h, dtype)
+        else:
+            f, aux = self.ffn(h, dtype), {}
+        x = x + rs * f
+        return x, aux
+
+
+class Transformer(nn.Module):
+    """Full model.  ``forward(tokens)`` returns the final normed hidden state
+    (compute dtype) and the merged aux dict; :meth:`logits` applies the tied
+    head.  Training uses :meth:`loss`, which fuses the head with the CE."""
+
+    def __init__(self, cfg: Config, seed: int = 0):
+        super().__init__()
+        self.cfg = cfg
+        gen = torch.Generator().manual_seed(seed)
+        std = cfg.d_model ** -0.5
+        self.wte = nn.Parameter(torch.randn(cfg.vocab_size, cfg.d_model, generator=gen) * std)
+        self.blocks = nn.ModuleList([Block(cfg, i, gen) for i in range(cfg.layers)])
+        self.norm_f = RMSNorm(cfg.d_model, cfg.norm_eps)
+        max_len = max(cfg.seq_len, cfg.infer_seq_len)
+        cos, sin = ref.precompute_rope(cfg.head_dim, max_len, cfg.rope_base, cfg.yarn_factor,
+                                       cfg.yarn_beta_fast, cfg.yarn_beta_slow)
+        # RoPE tables are constants stored in the compute dtype (model/rope.py,
+        # model/transformer.py:197-206), not parameters.
+        dt = cfg.compute_dtype()
+        self.register_buffer("rope_cos", cos.to(dt), persistent=False)
+        self.register_buffer("rope_sin", sin.to(dt), persistent=False)
+        self.n_moe = sum(1 for b in self.blocks if b.use_moe)
+
+    @property
+    def dtype(self):
+        return self.cfg.compute_dtype()
+
+    def embed(self, tokens):
+        if tokens.is_cuda:
+            from ..ops.embed import embedding_cuda
+            return embedding_cuda(tokens, self.wte)
+        return self.wte[tokens].float()
+
+    def forward(self, tokens, positions=None, cache=None):
+        dtype = self.dtype
+        x = self.embed(tokens)
+        aux_list = []
+        for blk in self.blocks:
+            x, aux = blk(x, self.rope_cos, self.rope_sin, dtype, positions, cache)
+            if aux:
+                aux_list.append(aux)
+        h = self.norm_f(x, dtype)
+        return h, merge_aux(aux_list, self.cfg.n_experts, self.n_moe, x.device)
+
+    def logits(self, h):
+        return h.float() @ ops.working(self.wte, torch.float32).t() if not h.is_cuda else \
+            ops.linear(h, _Transposed(self.wte), out_dtype=torch.float32, compute_dtype=self.dtype)
+
+    def loss(self, tokens):
+        """Total loss and metrics (train.py:180-217): CE over the full-length
+        forward shifted by one, + z-loss + balance loss."""
+        cfg = self.cfg
+        h, aux = self(tokens)
+        B, S, D = h.shape
+        hs = h[:, :-1].reshape(B * (S - 1), D)
+        tgt = tokens[:, 1:].reshape(-1)
+        ce = ops.head_cross_entropy(hs, self.wte, tgt, compute_dtype=self.dtype)
+        z = cfg.z_loss_weight * aux["router_z_loss"]
+        bal = cfg.balance_loss_weight * aux["balance_loss"]
+        total = ce + z + bal
+        counts = aux["expert_counts"]
+        share = counts / (counts.sum(-1, keepdim=True) + 1e-9)
+        load_entropy = -(share * torch.log(share + 1e-9)).sum(-1)
+        eff = torch.exp(load_entropy).mean()
+        metrics = {"ce": ce.detach(), "z_loss": z.detach(), "bal_loss": bal.detach(),
+                   "mean_entropy": aux["mean_entropy"].detach(), "eff_experts": eff.detach(),
+                   "expert_counts": counts.detach()}
+        return total, metrics
+
+    def moe_layers(self):
+        return [b.ffn for b in self.blocks if b.use_moe]
+
+
+class _Transposed:
+    """Marker: use ``w`` (stored [V, D]) as the ``[D, V]`` right operand."""
+
+    def __init__(self, w):
+        self.w = w
+
+
+def merge_aux(aux_list, n_experts, n_moe, device):
+    """Average scalar aux over MoE layers, stack expert counts [n_moe, N]
+    (model/transformer.py:411-416)."""
+    if not aux_list:
+        z = torch.zeros((), device=device)
+        return {"router_z_loss": z, "balance_loss": z, "mean_entropy": z,
+                "expert_counts": torch.zeros(max(1, n_moe), n_experts, device=device)}
+    n = max(1, n_moe)
+    out = {}
+    for k in ("router_z_loss", "balance_loss", "mean_entropy"):
+        out[k] = torch.stack([a[k] for a in aux_list]).sum(0) / n
+    out["expert_counts"] = torch.stack([a["expert_counts"] for a in aux_list])
+    return out
