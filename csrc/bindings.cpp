@@ -7,11 +7,70 @@ namespace hb {
 void set_wait_budget_ns(uint64_t ns);
 // gemm
 void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool trans_a, bool trans_b,
-          bool accumulate, double alpha);
+          bool accumulate, double alpha, c10::optional<torch::Tensor> alpha_t);
 void grouped_gemm_m(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor grp_start,
-                    torch::Tensor grp_count, torch::Tensor grp_tile_start, bool trans_b);
+                    torch::Tensor grp_count, torch::Tensor grp_tile_start, bool trans_b,
+                    bool accumulate);
 void grouped_gemm_k(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor grp_start,
                     torch::Tensor grp_count, bool accumulate);
+// elementwise
+void rmsnorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor y, torch::Tensor rstd, double eps);
+void rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd,
+                 torch::Tensor dx, torch::Tensor dw, bool accumulate);
+void rope_apply(torch::Tensor q, torch::Tensor cos, torch::Tensor sin, int64_t seq_len,
+                c10::optional<torch::Tensor> positions, bool inverse);
+void swiglu_fwd(torch::Tensor gu, torch::Tensor h, c10::optional<torch::Tensor> row_src);
+void swiglu_bwd(torch::Tensor dh, torch::Tensor gu, torch::Tensor dgu, c10::optional<torch::Tensor> row_src);
+void embed_fwd(torch::Tensor tok, torch::Tensor wte, torch::Tensor x);
+void embed_bwd(torch::Tensor tok, torch::Tensor dx, torch::Tensor dwte);
+void ce_fwd_bwd(torch::Tensor logits, torch::Tensor tgt, c10::optional<torch::Tensor> valid,
+                torch::Tensor loss_sum, torch::Tensor dlogits, double scale);
+void sumsq(torch::Tensor a, torch::Tensor out);
+void fused_update(torch::Tensor p, torch::Tensor g, torch::Tensor m, c10::optional<torch::Tensor> v,
+                  torch::Tensor decay, torch::Tensor work, int64_t mode, double lr, double wd,
+                  double b1, double b2, double eps, int64_t step, torch::Tensor coef);
+// moe
+void router_fwd(torch::Tensor x, torch::Tensor W, torch::Tensor bias, int64_t S, int64_t K,
+                bool softmax_mode, double scaling, torch::Tensor logits, torch::Tensor topi,
+                torch::Tensor topw, torch::Tensor seq_counts, torch::Tensor seq_probs,
+                torch::Tensor sums);
+void router_bwd(torch::Tensor logits, torch::Tensor topi, torch::Tensor dtopw, torch::Tensor bal_coef,
+                int64_t S, bool softmax_mode, double scaling, torch::Tensor coef_z, torch::Tensor dlogits);
+void router_grads(torch::Tensor x, torch::Tensor W, torch::Tensor dl, torch::Tensor dx, torch::Tensor dW);
+void moe_plan(torch::Tensor topi, int64_t N, int64_t tiles_n, torch::Tensor counts,
+              torch::Tensor starts, torch::Tensor tile_prefix, torch::Tensor padded_counts,
+              torch::Tensor total_rows, torch::Tensor pos, torch::Tensor row_src);
+void moe_gather(torch::Tensor x, torch::Tensor row_src, torch::Tensor xp, int64_t K);
+void moe_scatter_add(torch::Tensor dxp, torch::Tensor pos, torch::Tensor dx);
+void moe_combine(torch::Tensor y, torch::Tensor pos, torch::Tensor w, torch::Tensor out);
+void moe_combine_bwd(torch::Tensor dout, torch::Tensor y, torch::Tensor pos, torch::Tensor w,
+                     torch::Tensor row_src, torch::Tensor dy, torch::Tensor dw);
+// attention
+void flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
+               int64_t window);
+void flash_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor dout,
+               torch::Tensor lse, torch::Tensor delta, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv,
+               int64_t window);
+// kda
+int64_t kda_chunk_size(int64_t dk);
+void kda_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
+             double scale, torch::Tensor o, torch::Tensor Wt, torch::Tensor Ut, torch::Tensor Kh,
+             torch::Tensor Qg, torch::Tensor Pm, torch::Tensor gC, torch::Tensor states,
+             c10::optional<torch::Tensor> init_state, c10::optional<torch::Tensor> final_state);
+void kda_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
+             double scale, torch::Tensor dout, torch::Tensor Wt, torch::Tensor Kh, torch::Tensor Qg,
+             torch::Tensor Pm, torch::Tensor gC, torch::Tensor states, torch::Tensor dstates,
+             torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor dg, torch::Tensor dbeta);
+void kda_prep_fwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::Tensor wv, torch::Tensor f,
+                  torch::Tensor a_log, torch::Tensor dt_bias, torch::Tensor braw, int64_t gate_mode,
+                  int64_t S, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
+                  torch::Tensor beta);
+void kda_prep_bwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::Tensor wv, torch::Tensor f,
+                  torch::Tensor a_log, torch::Tensor dt_bias, torch::Tensor beta, int64_t gate_mode,
+                  int64_t S, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor dg,
+                  torch::Tensor dbeta, torch::Tensor dconv, torch::Tensor df, torch::Tensor dbraw,
+                  torch::Tensor d_alog, torch::Tensor d_dtb, torch::Tensor draw, torch::Tensor dwq,
+                  torch::Tensor dwk, torch::Tensor dwv);
 }  // namespace hb
 
 static int64_t read_status() {
@@ -27,7 +86,37 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("read_status", &read_status, "read the device status word (0 = ok)");
   m.def("clear_status", &clear_status);
   m.def("set_wait_budget_ns", &hb::set_wait_budget_ns);
-  m.def("gemm", &hb::gemm, "c (+)= op(a) @ op(b) on tcgen05");
-  m.def("grouped_gemm_m", &hb::grouped_gemm_m);
+  m.def("gemm", &hb::gemm, "c (+)= op(a) @ op(b) on tcgen05", py::arg("a"), py::arg("b"),
+        py::arg("c"), py::arg("trans_a"), py::arg("trans_b"), py::arg("accumulate"),
+        py::arg("alpha") = 1.0, py::arg("alpha_t") = py::none());
+  m.def("grouped_gemm_m", &hb::grouped_gemm_m, py::arg("a"), py::arg("b"), py::arg("c"),
+        py::arg("grp_start"), py::arg("grp_count"), py::arg("grp_tile_start"), py::arg("trans_b"),
+        py::arg("accumulate") = false);
   m.def("grouped_gemm_k", &hb::grouped_gemm_k);
+  m.def("rmsnorm_fwd", &hb::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &hb::rmsnorm_bwd);
+  m.def("rope_apply", &hb::rope_apply);
+  m.def("swiglu_fwd", &hb::swiglu_fwd, py::arg("gu"), py::arg("h"), py::arg("row_src") = py::none());
+  m.def("swiglu_bwd", &hb::swiglu_bwd, py::arg("dh"), py::arg("gu"), py::arg("dgu"),
+        py::arg("row_src") = py::none());
+  m.def("embed_fwd", &hb::embed_fwd);
+  m.def("embed_bwd", &hb::embed_bwd);
+  m.def("ce_fwd_bwd", &hb::ce_fwd_bwd);
+  m.def("sumsq", &hb::sumsq);
+  m.def("fused_update", &hb::fused_update);
+  m.def("router_fwd", &hb::router_fwd);
+  m.def("router_bwd", &hb::router_bwd);
+  m.def("router_grads", &hb::router_grads);
+  m.def("moe_plan", &hb::moe_plan);
+  m.def("moe_gather", &hb::moe_gather);
+  m.def("moe_scatter_add", &hb::moe_scatter_add);
+  m.def("moe_combine", &hb::moe_combine);
+  m.def("moe_combine_bwd", &hb::moe_combine_bwd);
+  m.def("flash_fwd", &hb::flash_fwd);
+  m.def("flash_bwd", &hb::flash_bwd);
+  m.def("kda_chunk_size", &hb::kda_chunk_size);
+  m.def("kda_fwd", &hb::kda_fwd);
+  m.def("kda_bwd", &hb::kda_bwd);
+  m.def("kda_prep_fwd", &hb::kda_prep_fwd);
+  m.def("kda_prep_bwd", &hb::kda_prep_bwd);
 }

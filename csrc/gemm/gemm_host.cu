@@ -1,0 +1,149 @@
+// Host entry points of the tcgen05 GEMM: operand checks, TMA descriptors,
+// tile counts, and dispatch to the instantiation units.
+#include "gemm_kernel.cuh"
+
+namespace hb {
+
+namespace {
+
+int pick_bn(int N) { return N >= 256 ? 256 : 128; }
+
+int epi_of(const torch::Tensor& c, bool accumulate) {
+  if (c.scalar_type() == at::kBFloat16) {
+    HB_CHECK(!accumulate, "accumulate requires an fp32 output");
+    return EPI_BF16;
+  }
+  HB_CHECK(c.scalar_type() == at::kFloat, "output must be bf16 or fp32");
+  return accumulate ? EPI_F32_ACC : EPI_F32;
+}
+
+GemmArgs base_args(const torch::Tensor& c, double alpha,
+                   const c10::optional<torch::Tensor>& alpha_t = c10::nullopt) {
+  GemmArgs a{};
+  a.C = c.data_ptr();
+  a.ldc = c.stride(-2);
+  a.alpha = (float)alpha;
+  if (alpha_t.has_value()) {
+    HB_CHECK(alpha_t->scalar_type() == at::kFloat && alpha_t->numel() == 1 && alpha_t->is_cuda(),
+             "alpha tensor must be a CUDA fp32 scalar");
+    a.alpha_ptr = alpha_t->data_ptr<float>();
+  }
+  a.status = status_ptr();
+  a.budget_ns = wait_budget_ns();
+  return a;
+}
+
+}  // namespace
+
+// c[M,N] (+)= op(a) @ op(b);  a is [M,K] (or [K,M] when trans_a); b is [K,N]
+// (or [N,K] when trans_b).  All operands row-major with unit column stride.
+void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool trans_a, bool trans_b,
+          bool accumulate, double alpha, c10::optional<torch::Tensor> alpha_t) {
+  check_bf16(a, "a");
+  check_bf16(b, "b");
+  HB_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2, "gemm expects 2-D tensors");
+  HB_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && c.stride(1) == 1, "unit column stride required");
+  const int M = trans_a ? a.size(1) : a.size(0);
+  const int K = trans_a ? a.size(0) : a.size(1);
+  const int N = trans_b ? b.size(0) : b.size(1);
+  HB_CHECK((trans_b ? b.size(1) : b.size(0)) == K, "gemm: inner dimensions differ");
+  HB_CHECK(c.size(0) == M && c.size(1) == N, "gemm: bad output shape");
+  if (M == 0 || N == 0) return;
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int BN = pick_bn(N);
+  // A operand
+  CUtensorMap ta = trans_a ? tmap_bf16_2d(a.data_ptr(), K, M, a.stride(0), 64, 64)
+                           : tmap_bf16_2d(a.data_ptr(), M, K, a.stride(0), 64, GEMM_BM);
+  CUtensorMap tb = trans_b ? tmap_bf16_2d(b.data_ptr(), N, K, b.stride(0), 64, BN)
+                           : tmap_bf16_2d(b.data_ptr(), K, N, b.stride(0), 64, 64);
+  GemmArgs args = base_args(c, alpha, alpha_t);
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.tiles_m = (M + GEMM_BM - 1) / GEMM_BM;
+  args.tiles_n = (N + BN - 1) / BN;
+  args.num_tiles = args.tiles_m * args.tiles_n;
+  if (K == 0) {
+    HB_CHECK(false, "gemm with K == 0 is not supported");
+  }
+  const int grid = std::min(args.num_tiles, num_sms());
+  const int epi = epi_of(c, accumulate);
+  if (trans_a)
+    gemm_dispatch_dense_amn(BN, !trans_b, epi, ta, tb, args, grid);
+  else
+    gemm_dispatch_dense_ak(BN, !trans_b, epi, ta, tb, args, grid);
+}
+
+// Grouped over M (MoE forward / input-gradient):
+//   c[rows of g] = a[rows of g] @ op(b[g])
+// a: [R, K] bf16;  b: [G, K, N] (trans_b false) or [G, N, K] (trans_b true);
+// grp_start/grp_count: int32 [G] (starts multiples of 128);
+// grp_tile_start: int32 [G+1] prefix of ceil(count/128)*tiles_n (device).
+void grouped_gemm_m(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor grp_start,
+                    torch::Tensor grp_count, torch::Tensor grp_tile_start, bool trans_b,
+                    bool accumulate) {
+  check_bf16(a, "a");
+  check_bf16(b, "b");
+  HB_CHECK(b.dim() == 3 && b.is_contiguous(), "b must be contiguous [G, *, *]");
+  const int G = b.size(0);
+  const int R = a.size(0), K = a.size(1);
+  const int N = trans_b ? b.size(1) : b.size(2);
+  HB_CHECK((trans_b ? b.size(2) : b.size(1)) == K, "grouped_gemm_m: inner dims differ");
+  HB_CHECK(c.size(0) == R && c.size(1) == N && c.stride(1) == 1, "grouped_gemm_m: bad output");
+  HB_CHECK(grp_start.numel() == G && grp_count.numel() == G && grp_tile_start.numel() == G + 1,
+           "grouped_gemm_m: bad group arrays");
+  if (R == 0) return;
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int BN = pick_bn(N);
+  CUtensorMap ta = tmap_bf16_2d(a.data_ptr(), R, K, a.stride(0), 64, GEMM_BM);
+  CUtensorMap tb = trans_b ? tmap_bf16_3d(b.data_ptr(), G, N, K, K, (uint64_t)N * K, 64, BN)
+                           : tmap_bf16_3d(b.data_ptr(), G, K, N, N, (uint64_t)K * N, 64, 64);
+  GemmArgs args = base_args(c, 1.0);
+  args.M = R;
+  args.N = N;
+  args.K = K;
+  args.tiles_n = (N + BN - 1) / BN;
+  args.num_groups = G;
+  args.grp_start = grp_start.data_ptr<int>();
+  args.grp_count = grp_count.data_ptr<int>();
+  args.grp_tile_start = grp_tile_start.data_ptr<int>();
+  const int max_tiles = ((R + GEMM_BM - 1) / GEMM_BM) * args.tiles_n;
+  const int grid = std::max(1, std::min(max_tiles, num_sms()));
+  const int epi = epi_of(c, accumulate);
+  gemm_dispatch_grouped(GROUPED_M, BN, false, !trans_b, epi, ta, tb, args, grid);
+}
+
+// Grouped over K (MoE weight gradients):  c[g] (+)= a_g^T @ b_g
+// a: [R, M] bf16 rows of group g at [start, start+count);  b: [R, N] bf16;
+// c: [G, M, N] fp32 (or bf16 without accumulate); counts multiples of 64.
+void grouped_gemm_k(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor grp_start,
+                    torch::Tensor grp_count, bool accumulate) {
+  check_bf16(a, "a");
+  check_bf16(b, "b");
+  HB_CHECK(c.dim() == 3 && c.is_contiguous(), "c must be contiguous [G, M, N]");
+  const int G = c.size(0), M = c.size(1), N = c.size(2);
+  const int R = a.size(0);
+  HB_CHECK(a.size(1) == M && b.size(0) == R && b.size(1) == N, "grouped_gemm_k: bad shapes");
+  if (G == 0) return;
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int BN = pick_bn(N);
+  CUtensorMap ta = tmap_bf16_2d(a.data_ptr(), R, M, a.stride(0), 64, 64);
+  CUtensorMap tb = tmap_bf16_2d(b.data_ptr(), R, N, b.stride(0), 64, 64);
+  GemmArgs args = base_args(c, 1.0);
+  args.ldc = N;
+  args.c_group_stride = (long long)M * N;
+  args.M = M;
+  args.N = N;
+  args.K = R;
+  args.tiles_m = (M + GEMM_BM - 1) / GEMM_BM;
+  args.tiles_n = (N + BN - 1) / BN;
+  args.num_tiles = G * args.tiles_m * args.tiles_n;
+  args.num_groups = G;
+  args.grp_start = grp_start.data_ptr<int>();
+  args.grp_count = grp_count.data_ptr<int>();
+  const int grid = std::min(args.num_tiles, num_sms());
+  const int epi = epi_of(c, accumulate);
+  gemm_dispatch_grouped(GROUPED_K, BN, true, true, epi, ta, tb, args, grid);
+}
+
+}  // namespace hb

@@ -23,6 +23,7 @@
 //              group come from a device prefix array so no host sync is needed
 //   GROUPED_K  MoE expert weight gradients: the contraction runs over each
 //              group's (padded) row segment, C[g] = A_g^T B_g
+#pragma once
 #include <torch/extension.h>
 
 #include "../common/host.h"
@@ -49,6 +50,7 @@ struct GemmArgs {
   long long ldc;
   long long c_group_stride;     // GROUPED_K: elements between C[g] and C[g+1]
   float alpha;
+  const float* alpha_ptr;       // optional device scalar; overrides alpha
   int* status;
   unsigned long long budget_ns;
 };
@@ -257,6 +259,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;  // TMEM lane quadrant accessible to this warp
+    const float alpha = args.alpha_ptr ? *args.alpha_ptr : args.alpha;
     const int row_in_tile = quad * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -281,7 +284,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (!row_ok || n >= args.N) continue;
         float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = has_k ? __uint_as_float(r[j]) * args.alpha : 0.f;
+        for (int j = 0; j < 32; ++j) v[j] = has_k ? __uint_as_float(r[j]) * alpha : 0.f;
         const bool full = (n + 32 <= args.N);
         if (EPI == EPI_BF16) {
           __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(cbase) + (long long)m * args.ldc + n;
@@ -332,13 +335,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   if (warp == 1) tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
 }
 
-// ============================================================================
-// Host side
-// ============================================================================
-namespace {
 
 template <int BN, bool A_MN, bool B_MN, int MODE, int EPI>
-void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid) {
+void gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid) {
   using Cfg = GemmCfg<BN>;
   auto kern = gemm_tc_kernel<BN, A_MN, B_MN, MODE, EPI>;
   static bool configured = false;  // one static per instantiation
@@ -350,166 +349,12 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, 
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
-template <int BN, int MODE>
-void dispatch(bool a_mn, bool b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
-              const GemmArgs& args, int grid) {
-#define HB_G(AM, BM_, E)                                    \
-  if (a_mn == AM && b_mn == BM_ && epi == E) {              \
-    launch<BN, AM, BM_, MODE, E>(ta, tb, args, grid);       \
-    return;                                                 \
-  }
-  if (MODE == DENSE) {
-    HB_G(false, true, EPI_BF16) HB_G(false, true, EPI_F32) HB_G(false, true, EPI_F32_ACC)
-    HB_G(false, false, EPI_BF16) HB_G(false, false, EPI_F32) HB_G(false, false, EPI_F32_ACC)
-    HB_G(true, true, EPI_BF16) HB_G(true, true, EPI_F32) HB_G(true, true, EPI_F32_ACC)
-    HB_G(true, false, EPI_BF16) HB_G(true, false, EPI_F32) HB_G(true, false, EPI_F32_ACC)
-  } else if (MODE == GROUPED_M) {
-    HB_G(false, true, EPI_BF16) HB_G(false, true, EPI_F32)
-    HB_G(false, false, EPI_BF16) HB_G(false, false, EPI_F32)
-  } else {
-    HB_G(true, true, EPI_F32) HB_G(true, true, EPI_F32_ACC) HB_G(true, true, EPI_BF16)
-  }
-#undef HB_G
-  HB_CHECK(false, "unsupported gemm variant");
-}
-
-int pick_bn(int N) { return N >= 256 ? 256 : 128; }
-
-int epi_of(const torch::Tensor& c, bool accumulate) {
-  if (c.scalar_type() == at::kBFloat16) {
-    HB_CHECK(!accumulate, "accumulate requires an fp32 output");
-    return EPI_BF16;
-  }
-  HB_CHECK(c.scalar_type() == at::kFloat, "output must be bf16 or fp32");
-  return accumulate ? EPI_F32_ACC : EPI_F32;
-}
-
-GemmArgs base_args(const torch::Tensor& c, double alpha) {
-  GemmArgs a{};
-  a.C = c.data_ptr();
-  a.ldc = c.stride(-2);
-  a.alpha = (float)alpha;
-  a.status = status_ptr();
-  a.budget_ns = wait_budget_ns();
-  return a;
-}
-
-}  // namespace
-
-// c[M,N] (+)= op(a) @ op(b);  a is [M,K] (or [K,M] when trans_a); b is [K,N]
-// (or [N,K] when trans_b).  All operands row-major with unit column stride.
-void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool trans_a, bool trans_b,
-          bool accumulate, double alpha) {
-  check_bf16(a, "a");
-  check_bf16(b, "b");
-  HB_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2, "gemm expects 2-D tensors");
-  HB_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && c.stride(1) == 1, "unit column stride required");
-  const int M = trans_a ? a.size(1) : a.size(0);
-  const int K = trans_a ? a.size(0) : a.size(1);
-  const int N = trans_b ? b.size(0) : b.size(1);
-  HB_CHECK((trans_b ? b.size(1) : b.size(0)) == K, "gemm: inner dimensions differ");
-  HB_CHECK(c.size(0) == M && c.size(1) == N, "gemm: bad output shape");
-  if (M == 0 || N == 0) return;
-  const c10::cuda::CUDAGuard guard(a.device());
-  const int BN = pick_bn(N);
-  // A operand
-  CUtensorMap ta = trans_a ? tmap_bf16_2d(a.data_ptr(), K, M, a.stride(0), 64, 64)
-                           : tmap_bf16_2d(a.data_ptr(), M, K, a.stride(0), 64, GEMM_BM);
-  CUtensorMap tb = trans_b ? tmap_bf16_2d(b.data_ptr(), N, K, b.stride(0), 64, BN)
-                           : tmap_bf16_2d(b.data_ptr(), K, N, b.stride(0), 64, 64);
-  GemmArgs args = base_args(c, alpha);
-  args.M = M;
-  args.N = N;
-  args.K = K;
-  args.tiles_m = (M + GEMM_BM - 1) / GEMM_BM;
-  args.tiles_n = (N + BN - 1) / BN;
-  args.num_tiles = args.tiles_m * args.tiles_n;
-  if (K == 0) {
-    HB_CHECK(false, "gemm with K == 0 is not supported");
-  }
-  const int grid = std::min(args.num_tiles, num_sms());
-  const int epi = epi_of(c, accumulate);
-  if (BN == 256)
-    dispatch<256, DENSE>(trans_a, !trans_b, epi, ta, tb, args, grid);
-  else
-    dispatch<128, DENSE>(trans_a, !trans_b, epi, ta, tb, args, grid);
-}
-
-// Grouped over M (MoE forward / input-gradient):
-//   c[rows of g] = a[rows of g] @ op(b[g])
-// a: [R, K] bf16;  b: [G, K, N] (trans_b false) or [G, N, K] (trans_b true);
-// grp_start/grp_count: int32 [G] (starts multiples of 128);
-// grp_tile_start: int32 [G+1] prefix of ceil(count/128)*tiles_n (device).
-void grouped_gemm_m(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor grp_start,
-                    torch::Tensor grp_count, torch::Tensor grp_tile_start, bool trans_b) {
-  check_bf16(a, "a");
-  check_bf16(b, "b");
-  HB_CHECK(b.dim() == 3 && b.is_contiguous(), "b must be contiguous [G, *, *]");
-  const int G = b.size(0);
-  const int R = a.size(0), K = a.size(1);
-  const int N = trans_b ? b.size(1) : b.size(2);
-  HB_CHECK((trans_b ? b.size(2) : b.size(1)) == K, "grouped_gemm_m: inner dims differ");
-  HB_CHECK(c.size(0) == R && c.size(1) == N && c.stride(1) == 1, "grouped_gemm_m: bad output");
-  HB_CHECK(grp_start.numel() == G && grp_count.numel() == G && grp_tile_start.numel() == G + 1,
-           "grouped_gemm_m: bad group arrays");
-  if (R == 0) return;
-  const c10::cuda::CUDAGuard guard(a.device());
-  const int BN = pick_bn(N);
-  CUtensorMap ta = tmap_bf16_2d(a.data_ptr(), R, K, a.stride(0), 64, GEMM_BM);
-  CUtensorMap tb = trans_b ? tmap_bf16_3d(b.data_ptr(), G, N, K, K, (uint64_t)N * K, 64, BN)
-                           : tmap_bf16_3d(b.data_ptr(), G, K, N, N, (uint64_t)K * N, 64, 64);
-  GemmArgs args = base_args(c, 1.0);
-  args.M = R;
-  args.N = N;
-  args.K = K;
-  args.tiles_n = (N + BN - 1) / BN;
-  args.num_groups = G;
-  args.grp_start = grp_start.data_ptr<int>();
-  args.grp_count = grp_count.data_ptr<int>();
-  args.grp_tile_start = grp_tile_start.data_ptr<int>();
-  const int max_tiles = ((R + GEMM_BM - 1) / GEMM_BM) * args.tiles_n;
-  const int grid = std::max(1, std::min(max_tiles, num_sms()));
-  const int epi = epi_of(c, false);
-  if (BN == 256)
-    dispatch<256, GROUPED_M>(false, !trans_b, epi, ta, tb, args, grid);
-  else
-    dispatch<128, GROUPED_M>(false, !trans_b, epi, ta, tb, args, grid);
-}
-
-// Grouped over K (MoE weight gradients):  c[g] (+)= a_g^T @ b_g
-// a: [R, M] bf16 rows of group g at [start, start+count);  b: [R, N] bf16;
-// c: [G, M, N] fp32 (or bf16 without accumulate); counts multiples of 64.
-void grouped_gemm_k(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor grp_start,
-                    torch::Tensor grp_count, bool accumulate) {
-  check_bf16(a, "a");
-  check_bf16(b, "b");
-  HB_CHECK(c.dim() == 3 && c.is_contiguous(), "c must be contiguous [G, M, N]");
-  const int G = c.size(0), M = c.size(1), N = c.size(2);
-  const int R = a.size(0);
-  HB_CHECK(a.size(1) == M && b.size(0) == R && b.size(1) == N, "grouped_gemm_k: bad shapes");
-  if (G == 0) return;
-  const c10::cuda::CUDAGuard guard(a.device());
-  const int BN = pick_bn(N);
-  CUtensorMap ta = tmap_bf16_2d(a.data_ptr(), R, M, a.stride(0), 64, 64);
-  CUtensorMap tb = tmap_bf16_2d(b.data_ptr(), R, N, b.stride(0), 64, 64);
-  GemmArgs args = base_args(c, 1.0);
-  args.ldc = N;
-  args.c_group_stride = (long long)M * N;
-  args.M = M;
-  args.N = N;
-  args.K = R;
-  args.tiles_m = (M + GEMM_BM - 1) / GEMM_BM;
-  args.tiles_n = (N + BN - 1) / BN;
-  args.num_tiles = G * args.tiles_m * args.tiles_n;
-  args.num_groups = G;
-  args.grp_start = grp_start.data_ptr<int>();
-  args.grp_count = grp_count.data_ptr<int>();
-  const int grid = std::min(args.num_tiles, num_sms());
-  const int epi = epi_of(c, accumulate);
-  if (BN == 256)
-    dispatch<256, GROUPED_K>(true, true, epi, ta, tb, args, grid);
-  else
-    dispatch<128, GROUPED_K>(true, true, epi, ta, tb, args, grid);
-}
+// Dispatchers, each defined in its own translation unit.
+void gemm_dispatch_dense_ak(int bn, bool b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
+                            const GemmArgs& args, int grid);
+void gemm_dispatch_dense_amn(int bn, bool b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
+                             const GemmArgs& args, int grid);
+void gemm_dispatch_grouped(int mode, int bn, bool a_mn, bool b_mn, int epi, const CUtensorMap& ta,
+                           const CUtensorMap& tb, const GemmArgs& args, int grid);
 
 }  // namespace hb

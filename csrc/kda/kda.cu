@@ -1,0 +1,878 @@
+// Kimi Delta Attention: chunk-parallel gated delta rule, forward and backward,
+// plus the fused front-end (ShortConv4 + SiLU + L2 norm, decay gate, beta).
+//
+// Recurrence (model/kda.py:305-323), per token t with state S [K, V]:
+//   S <- diag(e^{g_t}) S;  v' = v_t - b_t S^T k_t;  S <- S + b_t k_t v'^T;
+//   o_t = scale * S^T q_t          (readout after the update)
+// Chunk form (chunk C, incoming state S0, G = cumsum(g) inside the chunk):
+//   A_ts = sum_c k_t k_s e^{G_t-G_s} (s<t),  P_ts = scale sum_c q_t k_s e^{G_t-G_s} (s<=t)
+//   L = I + diag(b^2) A;  Ut = L^{-1} diag(b) V;  Wt = L^{-1} diag(b^2) (K*e^G)
+//   U = Ut - Wt S0;  O = scale (Q*e^G) S0 + P U;  S_C = e^{G_C} S0 + (K*e^{G_C-G})^T U
+// Pairwise decays are evaluated as exp(G_t - G_s) of the difference, never as
+// exp(G_t) / exp(G_s), so strongly negative cumulative decays cannot underflow
+// into 0/0.  All arithmetic is fp32.
+//
+// Kernels
+//   kda_intra_fwd   grid (chunks, H, B): everything that does not depend on S0
+//   kda_state_fwd   grid (H, B): the sequential chunk recurrence; stores S0 of
+//                   every chunk for the backward
+//   kda_state_bwd   grid (H, B): reverse recurrence of dS (state gradient)
+//   kda_intra_bwd   grid (chunks, H, B): recomputes the chunk and emits dq, dk,
+//                   dv, dg, dbeta given S0, dS_C and dO
+#include <torch/extension.h>
+
+#include "../common/host.h"
+#include "../common/sm100.cuh"
+
+namespace hb {
+namespace kda {
+
+constexpr int NT = 256;
+
+// out[m][n] (+)= sum_k A(m,k) B(k,n); A(m,k) = a[m*lda + k] or a[k*lda + m] (TA)
+template <int M, int N, int KD, bool TA, bool TB>
+HB_DEVICE void mm(float* out, int ldo, const float* a, int lda, const float* b, int ldb, float alpha,
+                  bool acc) {
+  for (int e = threadIdx.x; e < M * N; e += NT) {
+    const int m = e / N, n = e % N;
+    float s = 0.f;
+#pragma unroll 8
+    for (int k = 0; k < KD; ++k) {
+      const float av = TA ? a[k * lda + m] : a[m * lda + k];
+      const float bv = TB ? b[n * ldb + k] : b[k * ldb + n];
+      s += av * bv;
+    }
+    out[m * ldo + n] = acc ? out[m * ldo + n] + alpha * s : alpha * s;
+  }
+}
+
+struct Ptrs {
+  const float *q, *k, *v, *g, *beta, *dout;
+  float *Wt, *Ut, *Kh, *Qg, *Pm, *gC, *o, *states, *dstates;
+  float *dq, *dk, *dv, *dg, *dbeta;
+  int B, S, H, NC;
+  float scale;
+  const float* init_state;  // optional [B, H, K, V]
+  float* final_state;       // optional
+};
+
+// global row pointer of token t in [B, S, H, DK]
+HB_DEVICE long long tok_off(const Ptrs& p, int b, int t, int h, int DK) {
+  return (((long long)b * p.S + t) * p.H + h) * DK;
+}
+// chunk-intermediate offset [B, H, NC, rows, cols]
+HB_DEVICE long long chunk_off(const Ptrs& p, int b, int h, int n, int sz) {
+  return ((((long long)b * p.H + h) * p.NC) + n) * sz;
+}
+
+// Shared prologue: load q, k, v, g, beta of one chunk (zeros past S) and
+// cumulate g -> G in place.
+template <int DK, int C>
+HB_DEVICE void load_chunk(const Ptrs& p, int b, int h, int n, float* q, float* k, float* v, float* G,
+                          float* bet) {
+  const int t0 = n * C;
+  for (int i = threadIdx.x; i < C * DK; i += NT) {
+    const int r = i / DK, c = i % DK;
+    const int t = t0 + r;
+    const bool ok = t < p.S;
+    const long long o = ok ? tok_off(p, b, t, h, DK) + c : 0;
+    q[i] = ok ? p.q[o] : 0.f;
+    k[i] = ok ? p.k[o] : 0.f;
+    v[i] = ok ? p.v[o] : 0.f;
+    G[i] = ok ? p.g[o] : 0.f;
+  }
+  for (int r = threadIdx.x; r < C; r += NT) {
+    const int t = t0 + r;
+    bet[r] = t < p.S ? p.beta[((long long)b * p.S + t) * p.H + h] : 0.f;
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < DK; c += NT) {
+    float s = 0.f;
+    for (int r = 0; r < C; ++r) {
+      s += G[r * DK + c];
+      G[r * DK + c] = s;
+    }
+  }
+  __syncthreads();
+}
+
+// A (strict lower) and P (lower incl., scaled) by pairwise log-space decay.
+template <int DK, int C>
+HB_DEVICE void pair_products(const float* q, const float* k, const float* G, float* A, float* P,
+                             float scale) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int t = warp; t < C; t += NT / 32) {
+    for (int s = 0; s < C; ++s) {
+      float a = 0.f, pp = 0.f;
+      if (s <= t) {
+        for (int c = lane; c < DK; c += 32) {
+          const float e = __expf(G[t * DK + c] - G[s * DK + c]);
+          const float ks = k[s * DK + c] * e;
+          a += k[t * DK + c] * ks;
+          pp += q[t * DK + c] * ks;
+        }
+      }
+      a = warp_sum(a);
+      pp = warp_sum(pp);
+      if (lane == 0) {
+        A[t * C + s] = (s < t) ? a : 0.f;
+        P[t * C + s] = (s <= t) ? pp * scale : 0.f;
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// In-place forward substitution X <- L^{-1} X for L = I + diag(b^2) A (unit lower):
+// X_t -= b_t^2 sum_{s<t} A_ts X_s ; columns independent (one thread per column).
+template <int C>
+HB_DEVICE void solve_lower(float* X, int ncol, int ldx, const float* A, const float* bet) {
+  for (int col = threadIdx.x; col < ncol; col += NT) {
+    for (int t = 1; t < C; ++t) {
+      float s = 0.f;
+      for (int j = 0; j < t; ++j) s += A[t * C + j] * X[j * ldx + col];
+      X[t * ldx + col] -= bet[t] * bet[t] * s;
+    }
+  }
+  __syncthreads();
+}
+// In-place backward substitution X <- L^{-T} X:  X_t -= sum_{s>t} A_st b_s^2 X_s
+template <int C>
+HB_DEVICE void solve_upper_t(float* X, int ncol, int ldx, const float* A, const float* bet) {
+  for (int col = threadIdx.x; col < ncol; col += NT) {
+    for (int t = C - 2; t >= 0; --t) {
+      float s = 0.f;
+      for (int j = t + 1; j < C; ++j) s += A[j * C + t] * bet[j] * bet[j] * X[j * ldx + col];
+      X[t * ldx + col] -= s;
+    }
+  }
+  __syncthreads();
+}
+
+// ------------------------------------------------------------------ intra fwd
+template <int DK, int C>
+__global__ void __launch_bounds__(NT) intra_fwd_kernel(Ptrs p) {
+  extern __shared__ float sm[];
+  float* q = sm;
+  float* k = q + C * DK;
+  float* v = k + C * DK;
+  float* G = v + C * DK;
+  float* Wt = G + C * DK;
+  float* A = Wt + C * DK;
+  float* P = A + C * C;
+  float* bet = P + C * C;
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  load_chunk<DK, C>(p, b, h, n, q, k, v, G, bet);
+  pair_products<DK, C>(q, k, G, A, P, p.scale);
+  // right-hand sides: Ut <- b v (in v), Wt <- b^2 k e^G
+  for (int i = threadIdx.x; i < C * DK; i += NT) {
+    const int r = i / DK;
+    v[i] *= bet[r];
+    Wt[i] = bet[r] * bet[r] * k[i] * __expf(G[i]);
+  }
+  __syncthreads();
+  solve_lower<C>(v, DK, DK, A, bet);
+  solve_lower<C>(Wt, DK, DK, A, bet);
+  const long long co = chunk_off(p, b, h, n, C * DK);
+  const float* GC = G + (C - 1) * DK;
+  for (int i = threadIdx.x; i < C * DK; i += NT) {
+    const int c = i % DK;
+    p.Ut[co + i] = v[i];
+    p.Wt[co + i] = Wt[i];
+    p.Kh[co + i] = k[i] * __expf(GC[c] - G[i]);
+    p.Qg[co + i] = p.scale * q[i] * __expf(G[i]);
+  }
+  const long long po = chunk_off(p, b, h, n, C * C);
+  for (int i = threadIdx.x; i < C * C; i += NT) p.Pm[po + i] = P[i];
+  for (int c = threadIdx.x; c < DK; c += NT) p.gC[chunk_off(p, b, h, n, DK) + c] = __expf(GC[c]);
+}
+
+// ------------------------------------------------------------------ state fwd
+template <int DK, int C>
+__global__ void __launch_bounds__(NT) state_fwd_kernel(Ptrs p) {
+  extern __shared__ float sm[];
+  float* S = sm;                 // DK x DK
+  float* U = S + DK * DK;        // C x DK
+  float* Wt = U + C * DK;        // C x DK
+  float* X = Wt + C * DK;        // C x DK (Qg, then Kh)
+  float* P = X + C * DK;         // C x C
+  float* O = P + C * C;          // C x DK
+  float* gc = O + C * DK;        // DK
+  const int h = blockIdx.x, b = blockIdx.y;
+  for (int i = threadIdx.x; i < DK * DK; i += NT)
+    S[i] = p.init_state ? p.init_state[((long long)b * p.H + h) * DK * DK + i] : 0.f;
+  __syncthreads();
+  for (int n = 0; n < p.NC; ++n) {
+    const long long co = chunk_off(p, b, h, n, C * DK);
+    const long long so = chunk_off(p, b, h, n, DK * DK);
+    for (int i = threadIdx.x; i < DK * DK; i += NT) p.states[so + i] = S[i];
+    for (int i = threadIdx.x; i < C * DK; i += NT) {
+      U[i] = p.Ut[co + i];
+      Wt[i] = p.Wt[co + i];
+      X[i] = p.Qg[co + i];
+    }
+    for (int i = threadIdx.x; i < C * C; i += NT) P[i] = p.Pm[chunk_off(p, b, h, n, C * C) + i];
+    for (int c = threadIdx.x; c < DK; c += NT) gc[c] = p.gC[chunk_off(p, b, h, n, DK) + c];
+    __syncthreads();
+    // U = Ut - Wt S ;  O = Qg S
+    mm<C, DK, DK, false, false>(U, DK, Wt, DK, S, DK, -1.f, true);
+    mm<C, DK, DK, false, false>(O, DK, X, DK, S, DK, 1.f, false);
+    __syncthreads();
+    // O += P U
+    mm<C, DK, C, false, false>(O, DK, P, C, U, DK, 1.f, true);
+    // Kh into X
+    for (int i = threadIdx.x; i < C * DK; i += NT) X[i] = p.Kh[co + i];
+    __syncthreads();
+    // S = gc * S + Kh^T U
+    for (int e = threadIdx.x; e < DK * DK; e += NT) {
+      const int r = e / DK, c = e % DK;
+      float s = 0.f;
+      for (int t = 0; t < C; ++t) s += X[t * DK + r] * U[t * DK + c];
+      S[e] = gc[r] * S[e] + s;
+    }
+    // write O rows
+    for (int i = threadIdx.x; i < C * DK; i += NT) {
+      const int r = i / DK, c = i % DK;
+      const int t = n * C + r;
+      if (t < p.S) p.o[tok_off(p, b, t, h, DK) + c] = O[i];
+    }
+    __syncthreads();
+  }
+  if (p.final_state)
+    for (int i = threadIdx.x; i < DK * DK; i += NT)
+      p.final_state[((long long)b * p.H + h) * DK * DK + i] = S[i];
+}
+
+// ------------------------------------------------------------------ state bwd
+// dS_prev = gC * dS + Qg^T dO - Wt^T dU,  dU = P^T dO + Kh dS.  dstates[n] = dS at the
+// END of chunk n (gradient flowing into S_C).
+template <int DK, int C>
+__global__ void __launch_bounds__(NT) state_bwd_kernel(Ptrs p) {
+  extern __shared__ float sm[];
+  float* dS = sm;                // DK x DK
+  float* dU = dS + DK * DK;      // C x DK
+  float* dO = dU + C * DK;       // C x DK
+  float* X = dO + C * DK;        // C x DK (Kh, then Qg)
+  float* Wt = X + C * DK;        // C x DK
+  float* P = Wt + C * DK;        // C x C
+  float* gc = P + C * C;         // DK
+  float* T2 = gc + DK;           // DK x DK scratch
+  const int h = blockIdx.x, b = blockIdx.y;
+  for (int i = threadIdx.x; i < DK * DK; i += NT) dS[i] = 0.f;
+  __syncthreads();
+  for (int n = p.NC - 1; n >= 0; --n) {
+    const long long co = chunk_off(p, b, h, n, C * DK);
+    const long long so = chunk_off(p, b, h, n, DK * DK);
+    for (int i = threadIdx.x; i < DK * DK; i += NT) p.dstates[so + i] = dS[i];
+    for (int i = threadIdx.x; i < C * DK; i += NT) {
+      const int r = i / DK, c = i % DK;
+      const int t = n * C + r;
+      dO[i] = t < p.S ? p.dout[tok_off(p, b, t, h, DK) + c] : 0.f;
+      X[i] = p.Kh[co + i];
+      Wt[i] = p.Wt[co + i];
+    }
+    for (int i = threadIdx.x; i < C * C; i += NT) P[i] = p.Pm[chunk_off(p, b, h, n, C * C) + i];
+    for (int c = threadIdx.x; c < DK; c += NT) gc[c] = p.gC[chunk_off(p, b, h, n, DK) + c];
+    __syncthreads();
+    // dU = P^T dO + Kh dS
+    mm<C, DK, C, true, false>(dU, DK, P, C, dO, DK, 1.f, false);
+    __syncthreads();
+    mm<C, DK, DK, false, false>(dU, DK, X, DK, dS, DK, 1.f, true);
+    __syncthreads();
+    for (int i = threadIdx.x; i < C * DK; i += NT) X[i] = p.Qg[co + i];
+    __syncthreads();
+    // T2 = Qg^T dO - Wt^T dU
+    mm<DK, DK, C, true, false>(T2, DK, X, DK, dO, DK, 1.f, false);
+    __syncthreads();
+    mm<DK, DK, C, true, false>(T2, DK, Wt, DK, dU, DK, -1.f, true);
+    __syncthreads();
+    for (int e = threadIdx.x; e < DK * DK; e += NT) dS[e] = gc[e / DK] * dS[e] + T2[e];
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------------ intra bwd
+template <int DK, int C>
+__global__ void __launch_bounds__(NT) intra_bwd_kernel(Ptrs p) {
+  extern __shared__ float sm[];
+  float* q = sm;                 // C x DK
+  float* k = q + C * DK;
+  float* v = k + C * DK;
+  float* G = v + C * DK;
+  float* dO = G + C * DK;
+  float* Ut = dO + C * DK;       // -> U
+  float* Wt = Ut + C * DK;
+  float* X = Wt + C * DK;        // dU -> L^-T dU
+  float* Y = X + C * DK;         // dWt -> L^-T dWt
+  float* dq = Y + C * DK;
+  float* dk = dq + C * DK;
+  float* dG = dk + C * DK;
+  float* S0 = dG + C * DK;       // DK x DK
+  float* dSC = S0 + DK * DK;     // DK x DK
+  float* A = dSC + DK * DK;      // C x C
+  float* P = A + C * C;          // C x C -> dP
+  float* dA = P + C * C;         // C x C
+  float* bet = dA + C * C;       // C
+  float* db2 = bet + C;          // C
+  float* dbt = db2 + C;          // C
+  float* red = dbt + C;          // DK  (dG_C accumulation)
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const float scale = p.scale;
+  load_chunk<DK, C>(p, b, h, n, q, k, v, G, bet);
+  const long long so = chunk_off(p, b, h, n, DK * DK);
+  for (int i = threadIdx.x; i < DK * DK; i += NT) {
+    S0[i] = p.states[so + i];
+    dSC[i] = p.dstates[so + i];
+  }
+  for (int i = threadIdx.x; i < C * DK; i += NT) {
+    const int r = i / DK, c = i % DK;
+    const int t = n * C + r;
+    dO[i] = t < p.S ? p.dout[tok_off(p, b, t, h, DK) + c] : 0.f;
+  }
+  __syncthreads();
+  pair_products<DK, C>(q, k, G, A, P, scale);
+  for (int i = threadIdx.x; i < C * DK; i += NT) {
+    const int r = i / DK;
+    Ut[i] = bet[r] * v[i];
+    Wt[i] = bet[r] * bet[r] * k[i] * __expf(G[i]);
+  }
+  __syncthreads();
+  solve_lower<C>(Ut, DK, DK, A, bet);
+  solve_lower<C>(Wt, DK, DK, A, bet);
+  // U = Ut - Wt S0 (Ut keeps Ut for dL, store U into dq temporarily)
+  float* U = dq;
+  for (int i = threadIdx.x; i < C * DK; i += NT) U[i] = Ut[i];
+  __syncthreads();
+  mm<C, DK, DK, false, false>(U, DK, Wt, DK, S0, DK, -1.f, true);
+  __syncthreads();
+  // dU = P^T dO + Kh dS_C, Kh = k e^{G_C - G}  (X)
+  const float* GC = G + (C - 1) * DK;
+  mm<C, DK, C, true, false>(X, DK, P, C, dO, DK, 1.f, false);
+  __syncthreads();
+  for (int e = threadIdx.x; e < C * DK; e += NT) {
+    const int t = e / DK, vv = e % DK;
+    float s = 0.f;
+    for (int c = 0; c < DK; ++c) s += k[t * DK + c] * __expf(GC[c] - G[t * DK + c]) * dSC[c * DK + vv];
+    X[e] += s;
+  }
+  __syncthreads();
+  // dP = dO U^T (masked s <= t), into P
+  for (int e = threadIdx.x; e < C * C; e += NT) {
+    const int t = e / C, s = e % C;
+    float acc = 0.f;
+    if (s <= t)
+      for (int vv = 0; vv < DK; ++vv) acc += dO[t * DK + vv] * U[s * DK + vv];
+    P[e] = acc;
+  }
+  // dWt = -dU S0^T into Y ; dKh = U dS_C^T (into dk, later scaled) ; dQg = dO S0^T (into dG tmp)
+  mm<C, DK, DK, false, true>(Y, DK, X, DK, S0, DK, -1.f, false);
+  __syncthreads();
+  // dk <- dKh * e^{G_C-G} ;  dG <- -dKh*Kh ;  red <- sum_t dKh*Kh
+  for (int c = threadIdx.x; c < DK; c += NT) red[c] = 0.f;
+  __syncthreads();
+  for (int e = threadIdx.x; e < C * DK; e += NT) {
+    const int t = e / DK, c = e % DK;
+    float s = 0.f;
+    for (int vv = 0; vv < DK; ++vv) s += U[t * DK + vv] * dSC[c * DK + vv];
+    const float dec = __expf(GC[c] - G[e]);
+    const float kh = k[e] * dec;
+    dk[e] = s * dec;
+    dG[e] = -s * kh;
+    atomicAdd(&red[c], s * kh);
+  }
+  __syncthreads();
+  // dQg = dO S0^T:  dq += scale dQg e^G ; dG += dQg * Qg
+  for (int e = threadIdx.x; e < C * DK; e += NT) {
+    const int t = e / DK, c = e % DK;
+    float s = 0.f;
+    for (int vv = 0; vv < DK; ++vv) s += dO[t * DK + vv] * S0[c * DK + vv];
+    const float eg = __expf(G[e]);
+    dG[e] += s * scale * q[e] * eg;
+    U[e] = s * scale * eg;  // U no longer needed after dP/dKh: reuse as dq accumulator
+  }
+  __syncthreads();
+  float* dqa = U;
+  // X <- L^{-T} dU ; Y <- L^{-T} dWt
+  solve_upper_t<C>(X, DK, DK, A, bet);
+  solve_upper_t<C>(Y, DK, DK, A, bet);
+  // dL_ts = -(X Ut^T + Y Wt^T)_ts (s<t) ; dA = b_t^2 dL ; db2_t = sum_s A dL + sum_c Kg Y
+  for (int e = threadIdx.x; e < C * C; e += NT) {
+    const int t = e / C, s = e % C;
+    float dl = 0.f;
+    if (s < t) {
+      for (int c = 0; c < DK; ++c) dl -= X[t * DK + c] * Ut[s * DK + c] + Y[t * DK + c] * Wt[s * DK + c];
+    }
+    dA[e] = dl;  // holds dL for now
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < C; t += NT) {
+    float s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    for (int s = 0; s < t; ++s) s1 += A[t * C + s] * dA[t * C + s];
+    for (int c = 0; c < DK; ++c) {
+      s2 += k[t * DK + c] * __expf(G[t * DK + c]) * Y[t * DK + c];  // Kg . Y
+      s3 += v[t * DK + c] * X[t * DK + c];                          // V . X
+    }
+    db2[t] = s1 + s2;
+    dbt[t] = s3 + 2.f * bet[t] * (s1 + s2);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < C * C; e += NT) dA[e] *= bet[e / C] * bet[e / C];
+  // dv = b X ; dKg = b^2 Y: dk += dKg e^G, dG += dKg Kg
+  for (int e = threadIdx.x; e < C * DK; e += NT) {
+    const int t = e / DK;
+    const float eg = __expf(G[e]);
+    const float dkg = bet[t] * bet[t] * Y[e];
+    dk[e] += dkg * eg;
+    dG[e] += dkg * k[e] * eg;
+    v[e] = bet[t] * X[e];  // v buffer now holds dv
+  }
+  __syncthreads();
+  // pairwise terms (t-side): dq_t += sum_{s<=t} dP_ts scale? (P carries scale: dPm = dP)
+  //   dq_t[c] += scale * sum_s dP_ts k_s e_ts ;  dk_t[c] += sum_{s<t} dA_ts k_s e_ts
+  //   dG_t[c] += q_t[c]*(P-part) + k_t[c]*(A-part)
+  for (int e = threadIdx.x; e < C * DK; e += NT) {
+    const int t = e / DK, c = e % DK;
+    const float gt = G[e];
+    float sp = 0.f, sa = 0.f;
+    for (int s = 0; s <= t; ++s) {
+      const float ks = k[s * DK + c] * __expf(gt - G[s * DK + c]);
+      sp += P[t * C + s] * ks;
+      sa += dA[t * C + s] * ks;
+    }
+    sp *= scale;
+    dqa[e] += sp;
+    dk[e] += sa;
+    dG[e] += q[e] * sp + k[e] * sa;
+  }
+  __syncthreads();
+  // s-side: dk_s[c] += sum_{t>=s} (scale dP_ts q_t + dA_ts k_t) e_ts ; dG_s -= k_s * that
+  for (int e = threadIdx.x; e < C * DK; e += NT) {
+    const int s = e / DK, c = e % DK;
+    const float gs = G[e];
+    float acc = 0.f;
+    for (int t = s; t < C; ++t) {
+      const float ee = __expf(G[t * DK + c] - gs);
+      acc += (scale * P[t * C + s] * q[t * DK + c] + dA[t * C + s] * k[t * DK + c]) * ee;
+    }
+    dk[e] += acc;
+    dG[e] -= k[e] * acc;
+  }
+  __syncthreads();
+  // dG_C += red + dgC * gC, dgC[c] = sum_v dS_C[c][v] S0[c][v]
+  for (int c = threadIdx.x; c < DK; c += NT) {
+    float s = 0.f;
+    for (int vv = 0; vv < DK; ++vv) s += dSC[c * DK + vv] * S0[c * DK + vv];
+    dG[(C - 1) * DK + c] += red[c] + s * __expf(GC[c]);
+  }
+  __syncthreads();
+  // dg = reverse cumsum of dG; write outputs
+  for (int c = threadIdx.x; c < DK; c += NT) {
+    float s = 0.f;
+    for (int r = C - 1; r >= 0; --r) {
+      s += dG[r * DK + c];
+      dG[r * DK + c] = s;
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < C * DK; i += NT) {
+    const int r = i / DK, c = i % DK;
+    const int t = n * C + r;
+    if (t >= p.S) continue;
+    const long long o = tok_off(p, b, t, h, DK) + c;
+    p.dq[o] = dqa[i];
+    p.dk[o] = dk[i];
+    p.dv[o] = v[i];
+    p.dg[o] = dG[i];
+  }
+  for (int r = threadIdx.x; r < C; r += NT) {
+    const int t = n * C + r;
+    if (t < p.S) p.dbeta[((long long)b * p.S + t) * p.H + h] = dbt[r];
+  }
+}
+
+template <int DK, int C>
+constexpr int intra_fwd_smem() { return (5 * C * DK + 2 * C * C + C) * 4; }
+template <int DK, int C>
+constexpr int state_fwd_smem() { return (DK * DK + 4 * C * DK + C * C + DK) * 4; }
+template <int DK, int C>
+constexpr int state_bwd_smem() { return (2 * DK * DK + 4 * C * DK + C * C + DK) * 4; }
+template <int DK, int C>
+constexpr int intra_bwd_smem() { return (12 * C * DK + 2 * DK * DK + 3 * C * C + 3 * C + DK) * 4; }
+
+// ================================================================ front-end
+// One warp per (token, head).  raw: [T, 3*HK] bf16 rows (q | k | v projections);
+// conv weights [HK, 4] fp32 each; outputs fp32 [T, H, K].
+template <int DK>
+__global__ void prep_fwd_kernel(const __nv_bfloat16* __restrict__ raw, long long ld_raw,
+                                const float* __restrict__ wq, const float* __restrict__ wk,
+                                const float* __restrict__ wv, const float* __restrict__ f,
+                                const float* __restrict__ a_log, const float* __restrict__ dt_bias,
+                                const float* __restrict__ braw, int gate_mode, int T, int S, int H,
+                                float* __restrict__ q, float* __restrict__ k, float* __restrict__ v,
+                                float* __restrict__ g, float* __restrict__ beta) {
+  const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+  const int HK = H * DK;
+  constexpr int PL = (DK + 31) / 32;
+  for (long long th = blockIdx.x * (long long)warps + (threadIdx.x >> 5); th < (long long)T * H;
+       th += (long long)gridDim.x * warps) {
+    const int t = th / H, h = th % H;
+    const int pos = t % S;
+    float qv[PL], kv[PL], ssq = 0.f, ssk = 0.f;
+#pragma unroll
+    for (int j = 0; j < PL; ++j) {
+      const int c = lane + 32 * j;
+      if (c >= DK) { qv[j] = kv[j] = 0.f; continue; }
+      const int ch = h * DK + c;
+      float aq = 0.f, ak = 0.f, av = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int sh = 3 - i;
+        if (pos - sh < 0) continue;
+        const __nv_bfloat16* row = raw + (long long)(t - sh) * ld_raw;
+        aq += wq[ch * 4 + i] * __bfloat162float(row[ch]);
+        ak += wk[ch * 4 + i] * __bfloat162float(row[HK + ch]);
+        av += wv[ch * 4 + i] * __bfloat162float(row[2 * HK + ch]);
+      }
+      // the conv result is rounded to the compute dtype (model/kda.py:136, 257-259)
+      aq = __bfloat162float(__float2bfloat16_rn(aq));
+      ak = __bfloat162float(__float2bfloat16_rn(ak));
+      av = __bfloat162float(__float2bfloat16_rn(av));
+      qv[j] = aq / (1.f + __expf(-aq));
+      kv[j] = ak / (1.f + __expf(-ak));
+      const float vs = av / (1.f + __expf(-av));
+      ssq += qv[j] * qv[j];
+      ssk += kv[j] * kv[j];
+      const long long o = (long long)t * HK + ch;
+      v[o] = vs;
+      const float z = f[o] + dt_bias[ch];
+      // softplus(y) = max(y, 0) + log1p(exp(-|y|)) never overflows
+      const float sp = fmaxf(z, 0.f) + log1pf(__expf(-fabsf(z)));
+      const float spn = fmaxf(-z, 0.f) + log1pf(__expf(-fabsf(z)));  // softplus(-z)
+      g[o] = gate_mode == 0 ? -__expf(a_log[h]) * sp : -spn;
+    }
+    ssq = warp_sum(ssq);
+    ssk = warp_sum(ssk);
+    const float rq = rsqrtf(ssq + 1e-6f), rk = rsqrtf(ssk + 1e-6f);
+#pragma unroll
+    for (int j = 0; j < PL; ++j) {
+      const int c = lane + 32 * j;
+      if (c >= DK) continue;
+      const long long o = (long long)t * HK + h * DK + c;
+      q[o] = qv[j] * rq;
+      k[o] = kv[j] * rk;
+    }
+    if (lane == 0) beta[(long long)t * H + h] = 1.f / (1.f + __expf(-braw[(long long)t * H + h]));
+  }
+}
+
+// Backward part 1 (warp per (token, head)): gradients at the conv outputs of
+// q/k/v (fp32, [T, 3*HK]), df [T, HK], dbraw [T, H]; block partials of
+// d a_log and d dt_bias are accumulated with atomics.
+template <int DK>
+__global__ void prep_bwd1_kernel(const __nv_bfloat16* __restrict__ raw, long long ld_raw,
+                                 const float* __restrict__ wq, const float* __restrict__ wk,
+                                 const float* __restrict__ wv, const float* __restrict__ f,
+                                 const float* __restrict__ a_log, const float* __restrict__ dt_bias,
+                                 const float* __restrict__ beta, int gate_mode, int T, int S, int H,
+                                 const float* __restrict__ dq, const float* __restrict__ dk,
+                                 const float* __restrict__ dv, const float* __restrict__ dg,
+                                 const float* __restrict__ dbeta, float* __restrict__ dconv,
+                                 float* __restrict__ df, float* __restrict__ dbraw,
+                                 float* __restrict__ d_alog, float* __restrict__ d_dtb) {
+  const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+  const int HK = H * DK;
+  constexpr int PL = (DK + 31) / 32;
+  for (long long th = blockIdx.x * (long long)warps + (threadIdx.x >> 5); th < (long long)T * H;
+       th += (long long)gridDim.x * warps) {
+    const int t = th / H, h = th % H;
+    const int pos = t % S;
+    float cq[PL], ck[PL], cv[PL], sq[PL], sk[PL];
+    float ssq = 0.f, ssk = 0.f, dotq = 0.f, dotk = 0.f, dal = 0.f;
+#pragma unroll
+    for (int j = 0; j < PL; ++j) {
+      const int c = lane + 32 * j;
+      cq[j] = ck[j] = cv[j] = sq[j] = sk[j] = 0.f;
+      if (c >= DK) continue;
+      const int ch = h * DK + c;
+      float aq = 0.f, ak = 0.f, av = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int sh = 3 - i;
+        if (pos - sh < 0) continue;
+        const __nv_bfloat16* row = raw + (long long)(t - sh) * ld_raw;
+        aq += wq[ch * 4 + i] * __bfloat162float(row[ch]);
+        ak += wk[ch * 4 + i] * __bfloat162float(row[HK + ch]);
+        av += wv[ch * 4 + i] * __bfloat162float(row[2 * HK + ch]);
+      }
+      cq[j] = __bfloat162float(__float2bfloat16_rn(aq));
+      ck[j] = __bfloat162float(__float2bfloat16_rn(ak));
+      cv[j] = __bfloat162float(__float2bfloat16_rn(av));
+      sq[j] = cq[j] / (1.f + __expf(-cq[j]));
+      sk[j] = ck[j] / (1.f + __expf(-ck[j]));
+      ssq += sq[j] * sq[j];
+      ssk += sk[j] * sk[j];
+      const long long o = (long long)t * HK + ch;
+      dotq += dq[o] * sq[j];
+      dotk += dk[o] * sk[j];
+      // gate
+      const float z = f[o] + dt_bias[ch];
+      const float sig = 1.f / (1.f + __expf(-z));
+      float dz;
+      if (gate_mode == 0) {
+        const float A = __expf(a_log[h]);
+        const float sp = fmaxf(z, 0.f) + log1pf(__expf(-fabsf(z)));
+        dz = dg[o] * (-A) * sig;
+        dal += dg[o] * (-A * sp);
+      } else {
+        dz = dg[o] * (1.f - sig);
+      }
+      df[o] = dz;
+      atomicAdd(d_dtb + ch, dz);
+    }
+    ssq = warp_sum(ssq);
+    ssk = warp_sum(ssk);
+    dotq = warp_sum(dotq);
+    dotk = warp_sum(dotk);
+    dal = warp_sum(dal);
+    const float nq = sqrtf(ssq + 1e-6f), nk = sqrtf(ssk + 1e-6f);
+#pragma unroll
+    for (int j = 0; j < PL; ++j) {
+      const int c = lane + 32 * j;
+      if (c >= DK) continue;
+      const int ch = h * DK + c;
+      const long long o = (long long)t * HK + ch;
+      // y = x / n, n = sqrt(|x|^2 + eps): dx = (dy - y (dy . y)) / n
+      const float yq = sq[j] / nq, yk = sk[j] / nk;
+      const float dsq = (dq[o] - yq * (dotq / nq)) / nq;
+      const float dsk = (dk[o] - yk * (dotk / nk)) / nk;
+      auto dsilu = [](float x) {
+        const float s = 1.f / (1.f + __expf(-x));
+        return s * (1.f + x * (1.f - s));
+      };
+      const long long co = (long long)t * 3 * HK + ch;
+      dconv[co] = dsq * dsilu(cq[j]);
+      dconv[co + HK] = dsk * dsilu(ck[j]);
+      dconv[co + 2 * HK] = dv[o] * dsilu(cv[j]);
+    }
+    if (lane == 0) {
+      if (gate_mode == 0) atomicAdd(d_alog + h, dal);
+      const float bt = beta[(long long)t * H + h];
+      dbraw[(long long)t * H + h] = dbeta[(long long)t * H + h] * bt * (1.f - bt);
+    }
+  }
+}
+
+// Backward part 2 (thread per (token, channel) of the 3*HK conv inputs):
+//   draw[t] = sum_i w[i] dconv[t + 3 - i] (same sequence); dw[i] += dconv[t] raw[t-3+i]
+__global__ void prep_bwd2_kernel(const __nv_bfloat16* __restrict__ raw, long long ld_raw,
+                                 const float* __restrict__ wq, const float* __restrict__ wk,
+                                 const float* __restrict__ wv, const float* __restrict__ dconv,
+                                 int T, int S, int HK, __nv_bfloat16* __restrict__ draw,
+                                 float* __restrict__ dwq, float* __restrict__ dwk, float* __restrict__ dwv) {
+  const int C3 = 3 * HK;
+  // each thread: fixed channel, a range of tokens, accumulates dw in registers
+  const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+  if (ch >= C3) return;
+  const int which = ch / HK, cc = ch % HK;
+  const float* w = which == 0 ? wq : (which == 1 ? wk : wv);
+  float* dw = which == 0 ? dwq : (which == 1 ? dwk : dwv);
+  const float w0 = w[cc * 4 + 0], w1 = w[cc * 4 + 1], w2 = w[cc * 4 + 2], w3 = w[cc * 4 + 3];
+  const int tpb = (T + gridDim.y - 1) / gridDim.y;
+  const int tb = blockIdx.y * tpb, te = min(T, tb + tpb);
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  for (int t = tb; t < te; ++t) {
+    const int pos = t % S;
+    float acc = 0.f;
+    // dconv at t + sh contributes through tap i = 3 - sh
+    const float d0 = dconv[(long long)t * C3 + ch];
+    acc += w3 * d0;
+    if (pos + 1 < S && t + 1 < T) acc += w2 * dconv[(long long)(t + 1) * C3 + ch];
+    if (pos + 2 < S && t + 2 < T) acc += w1 * dconv[(long long)(t + 2) * C3 + ch];
+    if (pos + 3 < S && t + 3 < T) acc += w0 * dconv[(long long)(t + 3) * C3 + ch];
+    draw[(long long)t * ld_raw + ch] = __float2bfloat16_rn(acc);
+    // weight grads: out[t] = sum_i w[i] raw[t - 3 + i]
+    const __nv_bfloat16* rr = raw + ch;
+    a3 += d0 * __bfloat162float(rr[(long long)t * ld_raw]);
+    if (pos >= 1) a2 += d0 * __bfloat162float(rr[(long long)(t - 1) * ld_raw]);
+    if (pos >= 2) a1 += d0 * __bfloat162float(rr[(long long)(t - 2) * ld_raw]);
+    if (pos >= 3) a0 += d0 * __bfloat162float(rr[(long long)(t - 3) * ld_raw]);
+  }
+  atomicAdd(dw + cc * 4 + 0, a0);
+  atomicAdd(dw + cc * 4 + 1, a1);
+  atomicAdd(dw + cc * 4 + 2, a2);
+  atomicAdd(dw + cc * 4 + 3, a3);
+}
+
+}  // namespace kda
+
+using kda::Ptrs;
+
+#define KDA_DISPATCH(DKV, ...)                     \
+  if (DKV == 16) {                                 \
+    constexpr int DK = 16;                         \
+    constexpr int C = 32;                          \
+    __VA_ARGS__                                    \
+  } else if (DKV == 32) {                          \
+    constexpr int DK = 32;                         \
+    constexpr int C = 32;                          \
+    __VA_ARGS__                                    \
+  } else if (DKV == 64) {                          \
+    constexpr int DK = 64;                         \
+    constexpr int C = 32;                          \
+    __VA_ARGS__                                    \
+  } else {                                         \
+    HB_CHECK(false, "KDA head_dim must be 16, 32 or 64"); \
+  }
+
+int64_t kda_chunk_size(int64_t dk) { return 32; }
+
+static void set_smem(const void* f, int bytes) {
+  HB_CUDA_CHECK(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+}
+
+// q,k,v,g: [B,S,H,K] fp32; beta [B,S,H]; outputs o [B,S,H,K];
+// scratch: Wt,Ut,Kh,Qg [B,H,NC,C,K], Pm [B,H,NC,C,C], gC [B,H,NC,K], states [B,H,NC,K,K]
+void kda_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
+             double scale, torch::Tensor o, torch::Tensor Wt, torch::Tensor Ut, torch::Tensor Kh,
+             torch::Tensor Qg, torch::Tensor Pm, torch::Tensor gC, torch::Tensor states,
+             c10::optional<torch::Tensor> init_state, c10::optional<torch::Tensor> final_state) {
+  Ptrs p{};
+  p.B = q.size(0);
+  p.S = q.size(1);
+  p.H = q.size(2);
+  const int DKV = q.size(3);
+  p.q = q.data_ptr<float>();
+  p.k = k.data_ptr<float>();
+  p.v = v.data_ptr<float>();
+  p.g = g.data_ptr<float>();
+  p.beta = beta.data_ptr<float>();
+  p.o = o.data_ptr<float>();
+  p.Wt = Wt.data_ptr<float>();
+  p.Ut = Ut.data_ptr<float>();
+  p.Kh = Kh.data_ptr<float>();
+  p.Qg = Qg.data_ptr<float>();
+  p.Pm = Pm.data_ptr<float>();
+  p.gC = gC.data_ptr<float>();
+  p.states = states.data_ptr<float>();
+  p.scale = (float)scale;
+  p.init_state = init_state.has_value() ? init_state->data_ptr<float>() : nullptr;
+  p.final_state = final_state.has_value() ? final_state->data_ptr<float>() : nullptr;
+  KDA_DISPATCH(DKV, {
+    p.NC = (p.S + C - 1) / C;
+    HB_CHECK(Pm.size(-1) == C, "kda_fwd: scratch chunk size mismatch");
+    const int s1 = kda::intra_fwd_smem<DK, C>(), s2 = kda::state_fwd_smem<DK, C>();
+    static bool cfg = false;
+    if (!cfg) {
+      set_smem((const void*)kda::intra_fwd_kernel<DK, C>, s1);
+      set_smem((const void*)kda::state_fwd_kernel<DK, C>, s2);
+      cfg = true;
+    }
+    kda::intra_fwd_kernel<DK, C><<<dim3(p.NC, p.H, p.B), kda::NT, s1, cur_stream()>>>(p);
+    HB_CUDA_CHECK(cudaGetLastError());
+    kda::state_fwd_kernel<DK, C><<<dim3(p.H, p.B), kda::NT, s2, cur_stream()>>>(p);
+    HB_CUDA_CHECK(cudaGetLastError());
+  })
+}
+
+void kda_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
+             double scale, torch::Tensor dout, torch::Tensor Wt, torch::Tensor Kh, torch::Tensor Qg,
+             torch::Tensor Pm, torch::Tensor gC, torch::Tensor states, torch::Tensor dstates,
+             torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor dg, torch::Tensor dbeta) {
+  Ptrs p{};
+  p.B = q.size(0);
+  p.S = q.size(1);
+  p.H = q.size(2);
+  const int DKV = q.size(3);
+  p.q = q.data_ptr<float>();
+  p.k = k.data_ptr<float>();
+  p.v = v.data_ptr<float>();
+  p.g = g.data_ptr<float>();
+  p.beta = beta.data_ptr<float>();
+  p.dout = dout.data_ptr<float>();
+  p.Wt = Wt.data_ptr<float>();
+  p.Kh = Kh.data_ptr<float>();
+  p.Qg = Qg.data_ptr<float>();
+  p.Pm = Pm.data_ptr<float>();
+  p.gC = gC.data_ptr<float>();
+  p.states = states.data_ptr<float>();
+  p.dstates = dstates.data_ptr<float>();
+  p.dq = dq.data_ptr<float>();
+  p.dk = dk.data_ptr<float>();
+  p.dv = dv.data_ptr<float>();
+  p.dg = dg.data_ptr<float>();
+  p.dbeta = dbeta.data_ptr<float>();
+  p.scale = (float)scale;
+  HB_CHECK(dout.is_contiguous(), "kda_bwd: contiguous dout");
+  KDA_DISPATCH(DKV, {
+    p.NC = (p.S + C - 1) / C;
+    const int s1 = kda::state_bwd_smem<DK, C>(), s2 = kda::intra_bwd_smem<DK, C>();
+    static bool cfg = false;
+    if (!cfg) {
+      set_smem((const void*)kda::state_bwd_kernel<DK, C>, s1);
+      set_smem((const void*)kda::intra_bwd_kernel<DK, C>, s2);
+      cfg = true;
+    }
+    kda::state_bwd_kernel<DK, C><<<dim3(p.H, p.B), kda::NT, s1, cur_stream()>>>(p);
+    HB_CUDA_CHECK(cudaGetLastError());
+    kda::intra_bwd_kernel<DK, C><<<dim3(p.NC, p.H, p.B), kda::NT, s2, cur_stream()>>>(p);
+    HB_CUDA_CHECK(cudaGetLastError());
+  })
+}
+
+void kda_prep_fwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::Tensor wv, torch::Tensor f,
+                  torch::Tensor a_log, torch::Tensor dt_bias, torch::Tensor braw, int64_t gate_mode,
+                  int64_t S, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
+                  torch::Tensor beta) {
+  const int T = q.size(0), H = q.size(1), DKV = q.size(2);
+  const long long work = (long long)T * H;
+  const int grid = (int)std::min<long long>((work + 7) / 8, num_sms() * 16);
+  auto launch = [&](auto dk) {
+    constexpr int DK = decltype(dk)::value;
+    kda::prep_fwd_kernel<DK><<<grid, 256, 0, cur_stream()>>>(
+        (const __nv_bfloat16*)raw.data_ptr(), raw.stride(0), wq.data_ptr<float>(), wk.data_ptr<float>(),
+        wv.data_ptr<float>(), f.data_ptr<float>(), a_log.data_ptr<float>(), dt_bias.data_ptr<float>(),
+        braw.data_ptr<float>(), (int)gate_mode, T, (int)S, H, q.data_ptr<float>(), k.data_ptr<float>(),
+        v.data_ptr<float>(), g.data_ptr<float>(), beta.data_ptr<float>());
+  };
+  if (DKV == 16) launch(std::integral_constant<int, 16>{});
+  else if (DKV == 32) launch(std::integral_constant<int, 32>{});
+  else if (DKV == 64) launch(std::integral_constant<int, 64>{});
+  else if (DKV == 128) launch(std::integral_constant<int, 128>{});
+  else HB_CHECK(false, "kda_prep: unsupported head dim");
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+void kda_prep_bwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::Tensor wv, torch::Tensor f,
+                  torch::Tensor a_log, torch::Tensor dt_bias, torch::Tensor beta, int64_t gate_mode,
+                  int64_t S, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor dg,
+                  torch::Tensor dbeta, torch::Tensor dconv, torch::Tensor df, torch::Tensor dbraw,
+                  torch::Tensor d_alog, torch::Tensor d_dtb, torch::Tensor draw, torch::Tensor dwq,
+                  torch::Tensor dwk, torch::Tensor dwv) {
+  const int T = dq.size(0), H = dq.size(1), DKV = dq.size(2);
+  const long long work = (long long)T * H;
+  const int grid = (int)std::min<long long>((work + 7) / 8, num_sms() * 16);
+  auto launch = [&](auto dkc) {
+    constexpr int DK = decltype(dkc)::value;
+    kda::prep_bwd1_kernel<DK><<<grid, 256, 0, cur_stream()>>>(
+        (const __nv_bfloat16*)raw.data_ptr(), raw.stride(0), wq.data_ptr<float>(), wk.data_ptr<float>(),
+        wv.data_ptr<float>(), f.data_ptr<float>(), a_log.data_ptr<float>(), dt_bias.data_ptr<float>(),
+        beta.data_ptr<float>(), (int)gate_mode, T, (int)S, H, dq.data_ptr<float>(), dk.data_ptr<float>(),
+        dv.data_ptr<float>(), dg.data_ptr<float>(), dbeta.data_ptr<float>(), dconv.data_ptr<float>(),
+        df.data_ptr<float>(), dbraw.data_ptr<float>(), d_alog.data_ptr<float>(), d_dtb.data_ptr<float>());
+  };
+  if (DKV == 16) launch(std::integral_constant<int, 16>{});
+  else if (DKV == 32) launch(std::integral_constant<int, 32>{});
+  else if (DKV == 64) launch(std::integral_constant<int, 64>{});
+  else if (DKV == 128) launch(std::integral_constant<int, 128>{});
+  else HB_CHECK(false, "kda_prep: unsupported head dim");
+  HB_CUDA_CHECK(cudaGetLastError());
+  const int HK = H * DKV;
+  dim3 g2((3 * HK + 255) / 256, std::max(1, std::min(64, T / 64)));
+  kda::prep_bwd2_kernel<<<g2, 256, 0, cur_stream()>>>(
+      (const __nv_bfloat16*)raw.data_ptr(), raw.stride(0), wq.data_ptr<float>(), wk.data_ptr<float>(),
+      wv.data_ptr<float>(), dconv.data_ptr<float>(), T, (int)S, HK, (__nv_bfloat16*)draw.data_ptr(),
+      dwq.data_ptr<float>(), dwk.data_ptr<float>(), dwv.data_ptr<float>());
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace hb

@@ -1,0 +1,627 @@
+// MoE router and token dispatch (model/moe.py:37-85, 170-293).
+//
+// router_fwd   fp32 router logits (x @ W_r, fp32 accumulate, W_r staged in smem),
+//              sigmoid(+bias) or softmax scores, top-k selection, renormalised
+//              weights, and per-sequence aux partials (counts, routing-probability
+//              sums, logsumexp^2, entropy) reduced in registers per warp.
+// router_bwd   d(logits) from the gradients of the combine weights, the z-loss
+//              and the sequence-wise balance loss.
+// moe_plan     stable counting sort of the T*K (token, slot) pairs by expert into a
+//              row buffer whose expert segments start at multiples of 128; emits
+//              per-expert starts / counts, the grouped-GEMM tile prefix, and the
+//              row of every (token, slot).
+// moe_gather / moe_scatter_add, moe_combine / moe_combine_bwd  permute and
+//              un-permute rows; the pad rows of every expert segment are zero.
+#include <torch/extension.h>
+
+#include "../common/host.h"
+#include "../common/sm100.cuh"
+
+namespace hb {
+
+namespace {
+
+constexpr int MAXN = 256;  // experts
+constexpr int MAXK = 16;   // top-k
+
+// ------------------------------------------------------------------ router fwd
+// One warp per token; lane e handles experts e, e+32, ... (N <= 256).
+// W_r [D, N] fp32 staged in shared memory in chunks of 64 rows.
+__global__ void router_fwd_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ W,
+                                  const float* __restrict__ bias, int T, int S, int D, int N, int K,
+                                  int softmax_mode, float scaling, float* __restrict__ logits_out,
+                                  int* __restrict__ topi, float* __restrict__ topw,
+                                  float* __restrict__ seq_counts, float* __restrict__ seq_probs,
+                                  float* __restrict__ sums /* [0]=sum lse^2, [1]=sum entropy */) {
+  extern __shared__ float wsh[];  // [64][N]
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int warps = blockDim.x >> 5;
+  const int EPL = (N + 31) / 32;  // experts per lane (<= 8)
+  // Each block handles a contiguous token range.
+  const int per_block = (T + gridDim.x - 1) / gridDim.x;
+  const int t_begin = blockIdx.x * per_block;
+  const int t_end = min(T, t_begin + per_block);
+  float zsum = 0.f, esum = 0.f;
+  // tokens processed in groups of `warps` (one per warp); W streamed per group
+  for (int t0 = t_begin; t0 < t_end; t0 += warps) {
+    const int t = t0 + warp;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int d0 = 0; d0 < D; d0 += 64) {
+      __syncthreads();
+      for (int i = threadIdx.x; i < 64 * N; i += blockDim.x) {
+        const int r = i / N, c = i % N;
+        wsh[i] = (d0 + r < D) ? W[(long long)(d0 + r) * N + c] : 0.f;
+      }
+      __syncthreads();
+      if (t < t_end) {
+        const float xa = (d0 + lane < D) ? __bfloat162float(x[(long long)t * D + d0 + lane]) : 0.f;
+        const float xb = (d0 + 32 + lane < D) ? __bfloat162float(x[(long long)t * D + d0 + 32 + lane]) : 0.f;
+        for (int r = 0; r < 64; ++r) {
+          const float xv = __shfl_sync(0xffffffffu, r < 32 ? xa : xb, r & 31);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            if (i < EPL && lane + 32 * i < N) acc[i] += xv * wsh[r * N + lane + 32 * i];
+        }
+      }
+    }
+    if (t >= t_end) continue;
+    // scores
+    float lg[8], sc[8], ef[8];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane + 32 * i;
+      lg[i] = (i < EPL && e < N) ? acc[i] : -INFINITY;
+      if (i < EPL && e < N) {
+        logits_out[(long long)t * N + e] = lg[i];
+        mx = fmaxf(mx, lg[i]);
+      }
+    }
+    mx = warp_max(mx);
+    float se = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < EPL && lane + 32 * i < N) se += __expf(lg[i] - mx);
+    se = warp_sum(se);
+    const float lse = mx + __logf(se);
+    float ssum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane + 32 * i;
+      if (i < EPL && e < N) {
+        sc[i] = softmax_mode ? __expf(lg[i] - lse) : 1.f / (1.f + __expf(-lg[i]));
+        ef[i] = softmax_mode ? sc[i] : sc[i] + bias[e];
+        ssum += sc[i];
+      } else {
+        sc[i] = 0.f;
+        ef[i] = -INFINITY;
+      }
+    }
+    ssum = warp_sum(ssum);
+    // entropy of probs = s / (sum s + 1e-9)
+    float ent = 0.f;
+    const float inv = 1.f / (ssum + 1e-9f);
+    const int b = t / S;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane + 32 * i;
+      if (i < EPL && e < N) {
+        const float p = sc[i] * inv;
+        ent -= p * __logf(p + 1e-9f);
+        atomicAdd(seq_probs + (long long)b * N + e, p);
+      }
+    }
+    ent = warp_sum(ent);
+    // top-k by repeated warp argmax (ties -> lowest expert id, like top_k)
+    float selsum = 0.f;
+    float selv[MAXK];
+    int seli[MAXK];
+    for (int k = 0; k < K; ++k) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int e = lane + 32 * i;
+        if (i < EPL && e < N && (ef[i] > bv || (ef[i] == bv && e < bi))) {
+          bv = ef[i];
+          bi = e;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      // score of the winner
+      float s_win = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (lane + 32 * i == bi) {
+          s_win = sc[i];
+          ef[i] = -INFINITY;
+        }
+      s_win = warp_sum(s_win);
+      seli[k] = bi;
+      selv[k] = s_win;
+      selsum += s_win;
+    }
+    if (lane == 0) {
+      const float denom = selsum + 1e-9f;
+      for (int k = 0; k < K; ++k) {
+        topi[(long long)t * K + k] = seli[k];
+        topw[(long long)t * K + k] = selv[k] / denom * (softmax_mode ? 1.f : scaling);
+        atomicAdd(seq_counts + (long long)b * N + seli[k], 1.f);
+      }
+      zsum += lse * lse;
+      esum += ent;
+    }
+  }
+  if (lane == 0) {
+    atomicAdd(sums + 0, zsum);
+    atomicAdd(sums + 1, esum);
+  }
+}
+
+// ------------------------------------------------------------------ router bwd
+// dlogits[t, :] from
+//   dtopw [T, K]           gradient of the combine weights
+//   coef_z (device scalar) d(total)/d(lse_t) = coef_z * lse_t  (z-loss)
+//   bal_coef [B, N]        d(total)/d(probs[t, e]) for the balance loss (per seq)
+__global__ void router_bwd_kernel(const float* __restrict__ logits, const int* __restrict__ topi,
+                                  const float* __restrict__ dtopw, const float* __restrict__ bal_coef,
+                                  int T, int S, int N, int K, int softmax_mode, float scaling,
+                                  const float* __restrict__ coef_z_ptr, float* __restrict__ dlogits) {
+  const float coef_z = *coef_z_ptr;
+  const int lane = threadIdx.x & 31;
+  const int warps = blockDim.x >> 5;
+  const int EPL = (N + 31) / 32;
+  for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
+    float lg[8], sc[8], ds[8];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane + 32 * i;
+      lg[i] = (i < EPL && e < N) ? logits[(long long)t * N + e] : -INFINITY;
+      mx = fmaxf(mx, lg[i]);
+      ds[i] = 0.f;
+    }
+    mx = warp_max(mx);
+    float se = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < EPL && lane + 32 * i < N) se += __expf(lg[i] - mx);
+    se = warp_sum(se);
+    const float lse = mx + __logf(se);
+    float ssum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane + 32 * i;
+      sc[i] = (i < EPL && e < N) ? (softmax_mode ? __expf(lg[i] - lse) : 1.f / (1.f + __expf(-lg[i]))) : 0.f;
+      ssum += sc[i];
+    }
+    ssum = warp_sum(ssum);
+    const int b = t / S;
+    // balance loss through probs = s / (sum s + 1e-9)
+    const float Z = ssum + 1e-9f;
+    float dp[8];
+    float dps = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane + 32 * i;
+      dp[i] = (i < EPL && e < N) ? bal_coef[(long long)b * N + e] : 0.f;
+      dps += dp[i] * sc[i];
+    }
+    dps = warp_sum(dps) / (Z * Z);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ds[i] += dp[i] / Z - dps;
+    // combine weights w_k = s_{i_k} / (sum_j s_{i_j} + 1e-9) * scale
+    float selsum = 0.f, wdot = 0.f;
+    for (int k = 0; k < K; ++k) {
+      const int e = topi[(long long)t * K + k];
+      float s_e = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (lane + 32 * i == e) s_e = sc[i];
+      s_e = warp_sum(s_e);
+      selsum += s_e;
+      wdot += dtopw[(long long)t * K + k] * s_e;
+    }
+    const float den = selsum + 1e-9f;
+    const float scl = softmax_mode ? 1.f : scaling;
+    for (int k = 0; k < K; ++k) {
+      const int e = topi[(long long)t * K + k];
+      const float dw = dtopw[(long long)t * K + k];
+      const float g = scl * (dw / den - wdot / (den * den));
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (lane + 32 * i == e) ds[i] += g;
+    }
+    // scores -> logits
+    float sdot = 0.f;
+    if (softmax_mode) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sdot += ds[i] * sc[i];
+      sdot = warp_sum(sdot);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane + 32 * i;
+      if (!(i < EPL && e < N)) continue;
+      float dl = softmax_mode ? sc[i] * (ds[i] - sdot) : ds[i] * sc[i] * (1.f - sc[i]);
+      // z-loss: d lse / d l_e = softmax_e
+      dl += coef_z * lse * __expf(lg[i] - lse);
+      dlogits[(long long)t * N + e] = dl;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ router grads
+// dx[t, d] (+)= sum_e dl[t, e] * W[d, e];  one warp per token, W in smem chunks.
+__global__ void router_dx_kernel(const float* __restrict__ dl, const float* __restrict__ W,
+                                 float* __restrict__ dx, int T, int D, int N) {
+  extern __shared__ float wsh[];  // [128][N]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+  const int per_block = (T + gridDim.x - 1) / gridDim.x;
+  const int tb = blockIdx.x * per_block, te = min(T, tb + per_block);
+  for (int d0 = 0; d0 < D; d0 += 128) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < 128 * N; i += blockDim.x) {
+      const int r = i / N, c = i % N;
+      wsh[i] = (d0 + r < D) ? W[(long long)(d0 + r) * N + c] : 0.f;
+    }
+    __syncthreads();
+    for (int t = tb + warp; t < te; t += warps) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int e = 0; e < N; ++e) {
+        const float g = dl[(long long)t * N + e];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[j] += g * wsh[(lane + 32 * j) * N + e];
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int d = d0 + lane + 32 * j;
+        if (d < D) dx[(long long)t * D + d] += acc[j];
+      }
+    }
+  }
+}
+
+// dW[d, e] += sum_t x[t, d] * dl[t, e]; block = 128 d x N experts, token split.
+__global__ void router_dw_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ dl,
+                                 float* __restrict__ dW, int T, int D, int N, int t_per_block) {
+  extern __shared__ float sh[];  // xs [32][128], ds [32][N]
+  float* xs = sh;
+  float* ds = sh + 32 * 128;
+  const int d0 = blockIdx.x * 128;
+  const int tb = blockIdx.y * t_per_block, te = min(T, tb + t_per_block);
+  // each thread: d = d0 + (tid % 128), experts e = tid / 128 + 2*j
+  const int dl_ = threadIdx.x % 128;
+  const int eo = threadIdx.x / 128;  // 0..1 for 256 threads
+  float acc[MAXN / 2];
+  const int EPT = (N + 1) / 2;
+  for (int j = 0; j < EPT; ++j) acc[j] = 0.f;
+  for (int t0 = tb; t0 < te; t0 += 32) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < 32 * 128; i += blockDim.x) {
+      const int r = i / 128, c = i % 128;
+      xs[i] = (t0 + r < te && d0 + c < D) ? __bfloat162float(x[(long long)(t0 + r) * D + d0 + c]) : 0.f;
+    }
+    for (int i = threadIdx.x; i < 32 * N; i += blockDim.x) {
+      const int r = i / N, c = i % N;
+      ds[i] = (t0 + r < te) ? dl[(long long)(t0 + r) * N + c] : 0.f;
+    }
+    __syncthreads();
+    for (int r = 0; r < 32; ++r) {
+      const float xv = xs[r * 128 + dl_];
+      for (int j = 0; j < EPT; ++j) {
+        const int e = eo + 2 * j;
+        if (e < N) acc[j] += xv * ds[r * N + e];
+      }
+    }
+  }
+  if (d0 + dl_ < D)
+    for (int j = 0; j < EPT; ++j) {
+      const int e = eo + 2 * j;
+      if (e < N) atomicAdd(dW + (long long)(d0 + dl_) * N + e, acc[j]);
+    }
+}
+
+// ------------------------------------------------------------------ plan
+__global__ void hist_kernel(const int* __restrict__ topi, long long n, int N, int* __restrict__ counts) {
+  __shared__ int h[MAXN];
+  for (int i = threadIdx.x; i < N; i += blockDim.x) h[i] = 0;
+  __syncthreads();
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    atomicAdd(&h[topi[i]], 1);
+  __syncthreads();
+  for (int i = threadIdx.x; i < N; i += blockDim.x)
+    if (h[i]) atomicAdd(counts + i, h[i]);
+}
+
+// single block: starts (128-aligned), tile prefix for the grouped GEMM.
+__global__ void plan_scan_kernel(const int* __restrict__ counts, int N, int align, int tiles_n,
+                                 int* __restrict__ starts, int* __restrict__ tile_prefix,
+                                 int* __restrict__ padded_counts, int* __restrict__ total_rows) {
+  if (threadIdx.x == 0) {
+    int s = 0, tp = 0;
+    for (int e = 0; e < N; ++e) {
+      starts[e] = s;
+      tile_prefix[e] = tp;
+      const int c = counts[e];
+      const int pc = (c + align - 1) / align * align;
+      padded_counts[e] = pc;
+      s += pc;
+      tp += (c + 127) / 128 * tiles_n;
+    }
+    tile_prefix[N] = tp;
+    *total_rows = s;
+  }
+}
+
+// grid = N blocks; block e walks the slots in order and assigns stable rows.
+__global__ void assign_kernel(const int* __restrict__ topi, long long n, const int* __restrict__ starts,
+                              int* __restrict__ pos, int* __restrict__ row_src, int K) {
+  const int e = blockIdx.x;
+  __shared__ int warp_tot[32];
+  __shared__ int base;
+  if (threadIdx.x == 0) base = starts[e];
+  __syncthreads();
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (long long c0 = 0; c0 < n; c0 += blockDim.x) {
+    const long long i = c0 + threadIdx.x;
+    const bool hit = i < n && topi[i] == e;
+    const unsigned bal = __ballot_sync(0xffffffffu, hit);
+    const int within = __popc(bal & ((1u << lane) - 1));
+    if (lane == 0) warp_tot[w] = __popc(bal);
+    __syncthreads();
+    int before = 0;
+    for (int j = 0; j < w; ++j) before += warp_tot[j];
+    if (hit) {
+      const int r = base + before + within;
+      pos[i] = r;
+      row_src[r] = (int)i;  // slot id = t * K + k
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int tot = 0;
+      for (int j = 0; j < nw; ++j) tot += warp_tot[j];
+      base += tot;
+    }
+    __syncthreads();
+  }
+}
+
+// xp[r, :] = x[row_src[r] / K, :] or 0 for pad rows (row_src = -1).
+__global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ row_src,
+                                   __nv_bfloat16* __restrict__ xp, long long R, int D, int K) {
+  const int vec = D / 8;  // uint4 of 8 bf16
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < R * vec;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / vec;
+    const int c = i % vec;
+    const int src = row_src[r];
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (src >= 0) v = reinterpret_cast<const uint4*>(x + (long long)(src / K) * D)[c];
+    reinterpret_cast<uint4*>(xp + r * D)[c] = v;
+  }
+}
+
+// dx[t, :] += sum_k dxp[pos[t, k], :]   (fp32 accumulate; dxp bf16 or fp32)
+HB_DEVICE float2 load2(const __nv_bfloat16* p) {
+  const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(p);
+  return make_float2(__bfloat162float(v.x), __bfloat162float(v.y));
+}
+HB_DEVICE float2 load2(const float* p) { return *reinterpret_cast<const float2*>(p); }
+
+template <typename T_>
+__global__ void scatter_add_rows_kernel(const T_* __restrict__ dxp, const int* __restrict__ pos,
+                                        float* __restrict__ dx, int T, int D, int K) {
+  const long long total = (long long)T * (D / 2);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long t = i / (D / 2);
+    const int c = (i % (D / 2)) * 2;
+    float a0 = 0.f, a1 = 0.f;
+    for (int k = 0; k < K; ++k) {
+      const long long r = pos[t * K + k];
+      const float2 v = load2(dxp + r * D + c);
+      a0 += v.x;
+      a1 += v.y;
+    }
+    dx[t * D + c] += a0;
+    dx[t * D + c + 1] += a1;
+  }
+}
+
+// out[t, :] += sum_k bf16(w[t,k]) * y[pos[t,k], :]
+__global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const int* __restrict__ pos,
+                               const float* __restrict__ w, float* __restrict__ out, int T, int D, int K) {
+  const long long total = (long long)T * (D / 2);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long t = i / (D / 2);
+    const int c = (i % (D / 2)) * 2;
+    float a0 = 0.f, a1 = 0.f;
+    for (int k = 0; k < K; ++k) {
+      const long long r = pos[t * K + k];
+      const float wk = __bfloat162float(__float2bfloat16_rn(w[t * K + k]));
+      const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(y + r * D + c);
+      a0 += wk * __bfloat162float(v.x);
+      a1 += wk * __bfloat162float(v.y);
+    }
+    out[t * D + c] += a0;
+    out[t * D + c + 1] += a1;
+  }
+}
+
+// dy[pos[t,k], :] = bf16(w[t,k]) * dout[t, :];  dw[t,k] = <dout[t], y[pos[t,k]]>
+// one warp per token.  Pad rows of dy are zeroed by zero_pad_rows.
+__global__ void combine_bwd_kernel(const float* __restrict__ dout, const __nv_bfloat16* __restrict__ y,
+                                   const int* __restrict__ pos, const float* __restrict__ w,
+                                   __nv_bfloat16* __restrict__ dy, float* __restrict__ dw, int T, int D,
+                                   int K) {
+  const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+  for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
+    for (int k = 0; k < K; ++k) {
+      const long long r = pos[(long long)t * K + k];
+      const float wk = __bfloat162float(__float2bfloat16_rn(w[(long long)t * K + k]));
+      float dot = 0.f;
+      for (int c = lane * 2; c < D; c += 64) {
+        const float g0 = dout[(long long)t * D + c], g1 = dout[(long long)t * D + c + 1];
+        const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(y + r * D + c);
+        dot += g0 * __bfloat162float(v.x) + g1 * __bfloat162float(v.y);
+        *reinterpret_cast<__nv_bfloat162*>(dy + r * D + c) = __floats2bfloat162_rn(wk * g0, wk * g1);
+      }
+      dot = warp_sum(dot);
+      if (lane == 0) dw[(long long)t * K + k] = dot;
+    }
+  }
+}
+
+__global__ void zero_pad_rows_kernel(const int* __restrict__ row_src, __nv_bfloat16* __restrict__ a,
+                                     long long R, int D) {
+  const int vec = D / 8;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < R * vec;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / vec;
+    if (row_src[r] < 0) reinterpret_cast<uint4*>(a + r * D)[i % vec] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+int grid_for(long long work, int per_block) {
+  long long g = (work + per_block - 1) / per_block;
+  long long cap = (long long)num_sms() * 8;
+  return (int)std::max(1LL, std::min(g, cap));
+}
+
+}  // namespace
+
+// ================================================================ host API
+void router_fwd(torch::Tensor x, torch::Tensor W, torch::Tensor bias, int64_t S, int64_t K,
+                bool softmax_mode, double scaling, torch::Tensor logits, torch::Tensor topi,
+                torch::Tensor topw, torch::Tensor seq_counts, torch::Tensor seq_probs,
+                torch::Tensor sums) {
+  check_bf16(x, "x");
+  const int T = x.size(0), D = x.size(1), N = W.size(1);
+  HB_CHECK(N <= MAXN && K <= MAXK && K <= N, "router: N <= 256, K <= 16");
+  if (T == 0) return;
+  const int grid = std::min((T + 7) / 8, num_sms() * 2);
+  const size_t smem = 64 * N * sizeof(float);
+  static bool cfg = false;
+  if (!cfg) {
+    HB_CUDA_CHECK(cudaFuncSetAttribute(router_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * MAXN * 4));
+    cfg = true;
+  }
+  router_fwd_kernel<<<grid, 256, smem, cur_stream()>>>(
+      (const __nv_bfloat16*)x.data_ptr(), W.data_ptr<float>(), bias.data_ptr<float>(), T, (int)S, D,
+      N, (int)K, softmax_mode ? 1 : 0, (float)scaling, logits.data_ptr<float>(), topi.data_ptr<int>(),
+      topw.data_ptr<float>(), seq_counts.data_ptr<float>(), seq_probs.data_ptr<float>(),
+      sums.data_ptr<float>());
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+void router_bwd(torch::Tensor logits, torch::Tensor topi, torch::Tensor dtopw, torch::Tensor bal_coef,
+                int64_t S, bool softmax_mode, double scaling, torch::Tensor coef_z, torch::Tensor dlogits) {
+  const int T = logits.size(0), N = logits.size(1), K = topi.size(1);
+  if (T == 0) return;
+  router_bwd_kernel<<<grid_for(T, 8), 256, 0, cur_stream()>>>(
+      logits.data_ptr<float>(), topi.data_ptr<int>(), dtopw.data_ptr<float>(),
+      bal_coef.data_ptr<float>(), T, (int)S, N, K, softmax_mode ? 1 : 0, (float)scaling,
+      coef_z.data_ptr<float>(), dlogits.data_ptr<float>());
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+void router_grads(torch::Tensor x, torch::Tensor W, torch::Tensor dl, torch::Tensor dx, torch::Tensor dW) {
+  const int T = x.size(0), D = x.size(1), N = W.size(1);
+  if (T == 0) return;
+  {
+    static bool cfg = false;
+    if (!cfg) {
+      HB_CUDA_CHECK(cudaFuncSetAttribute(router_dx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * MAXN * 4));
+      cfg = true;
+    }
+    const int grid = std::min((T + 7) / 8, num_sms() * 2);
+    router_dx_kernel<<<grid, 256, 128 * N * 4, cur_stream()>>>(dl.data_ptr<float>(), W.data_ptr<float>(),
+                                                               dx.data_ptr<float>(), T, D, N);
+    HB_CUDA_CHECK(cudaGetLastError());
+  }
+  {
+    const int tpb = 1024;
+    dim3 grid((D + 127) / 128, (T + tpb - 1) / tpb);
+    const size_t smem = (32 * 128 + 32 * N) * 4;
+    router_dw_kernel<<<grid, 256, smem, cur_stream()>>>((const __nv_bfloat16*)x.data_ptr(),
+                                                        dl.data_ptr<float>(), dW.data_ptr<float>(), T,
+                                                        D, N, tpb);
+    HB_CUDA_CHECK(cudaGetLastError());
+  }
+}
+
+// Returns nothing; fills counts[N], starts[N], tile_prefix[N+1], padded_counts[N],
+// total_rows[1], pos[T*K], row_src[R_max] (pre-filled with -1 by the caller).
+void moe_plan(torch::Tensor topi, int64_t N, int64_t tiles_n, torch::Tensor counts,
+              torch::Tensor starts, torch::Tensor tile_prefix, torch::Tensor padded_counts,
+              torch::Tensor total_rows, torch::Tensor pos, torch::Tensor row_src) {
+  const long long n = topi.numel();
+  const int K = topi.size(-1);
+  HB_CHECK(N <= MAXN, "moe_plan: too many experts");
+  counts.zero_();
+  hist_kernel<<<grid_for(n, 256), 256, 0, cur_stream()>>>(topi.data_ptr<int>(), n, (int)N,
+                                                          counts.data_ptr<int>());
+  plan_scan_kernel<<<1, 32, 0, cur_stream()>>>(counts.data_ptr<int>(), (int)N, 128, (int)tiles_n,
+                                               starts.data_ptr<int>(), tile_prefix.data_ptr<int>(),
+                                               padded_counts.data_ptr<int>(), total_rows.data_ptr<int>());
+  assign_kernel<<<(int)N, 1024, 0, cur_stream()>>>(topi.data_ptr<int>(), n, starts.data_ptr<int>(),
+                                                   pos.data_ptr<int>(), row_src.data_ptr<int>(), K);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+void moe_gather(torch::Tensor x, torch::Tensor row_src, torch::Tensor xp, int64_t K) {
+  const long long R = xp.size(0);
+  const int D = xp.size(1);
+  HB_CHECK(D % 8 == 0, "moe_gather: D % 8");
+  gather_rows_kernel<<<grid_for(R * D / 8, 256), 256, 0, cur_stream()>>>(
+      (const __nv_bfloat16*)x.data_ptr(), row_src.data_ptr<int>(), (__nv_bfloat16*)xp.data_ptr(), R,
+      D, (int)K);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+void moe_scatter_add(torch::Tensor dxp, torch::Tensor pos, torch::Tensor dx) {
+  const int T = pos.size(0), K = pos.size(1), D = dx.size(1);
+  if (dxp.scalar_type() == at::kFloat)
+    scatter_add_rows_kernel<float><<<grid_for((long long)T * D / 2, 256), 256, 0, cur_stream()>>>(
+        dxp.data_ptr<float>(), pos.data_ptr<int>(), dx.data_ptr<float>(), T, D, K);
+  else
+    scatter_add_rows_kernel<__nv_bfloat16><<<grid_for((long long)T * D / 2, 256), 256, 0, cur_stream()>>>(
+        (const __nv_bfloat16*)dxp.data_ptr(), pos.data_ptr<int>(), dx.data_ptr<float>(), T, D, K);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+void moe_combine(torch::Tensor y, torch::Tensor pos, torch::Tensor w, torch::Tensor out) {
+  const int T = pos.size(0), K = pos.size(1), D = out.size(1);
+  combine_kernel<<<grid_for((long long)T * D / 2, 256), 256, 0, cur_stream()>>>(
+      (const __nv_bfloat16*)y.data_ptr(), pos.data_ptr<int>(), w.data_ptr<float>(), out.data_ptr<float>(),
+      T, D, K);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+void moe_combine_bwd(torch::Tensor dout, torch::Tensor y, torch::Tensor pos, torch::Tensor w,
+                     torch::Tensor row_src, torch::Tensor dy, torch::Tensor dw) {
+  const int T = pos.size(0), K = pos.size(1), D = dout.size(1);
+  const long long R = dy.size(0);
+  zero_pad_rows_kernel<<<grid_for(R * D / 8, 256), 256, 0, cur_stream()>>>(
+      row_src.data_ptr<int>(), (__nv_bfloat16*)dy.data_ptr(), R, D);
+  combine_bwd_kernel<<<grid_for(T, 8), 256, 0, cur_stream()>>>(
+      dout.data_ptr<float>(), (const __nv_bfloat16*)y.data_ptr(), pos.data_ptr<int>(), w.data_ptr<float>(),
+      (__nv_bfloat16*)dy.data_ptr(), dw.data_ptr<float>(), T, D, K);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace hb

@@ -53,6 +53,9 @@ class Attention(nn.Module):
     def forward(self, h, cos, sin, dtype, positions=None, cache=None):
         B, S, D = h.shape
         H = self.head_dim
+        if h.is_cuda and cache is None:
+            from ..ops.flash import attention_layer_cuda
+            return attention_layer_cuda(self, h, cos, sin, dtype, positions)
         x2 = h.reshape(B * S, D)
         q = ops.linear(x2, self.wq, compute_dtype=dtype).view(B, S, self.n_q, H)
         k = ops.linear(x2, self.wk, compute_dtype=dtype).view(B, S, self.n_kv, H)

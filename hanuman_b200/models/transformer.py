@@ -86,7 +86,7 @@ class Transformer(nn.Module):
 
     def embed(self, tokens):
         if tokens.is_cuda:
-            from ..ops.embed import embedding_cuda
+            from ..ops.norm import embedding_cuda
             return embedding_cuda(tokens, self.wte)
         return self.wte[tokens].float()
 
@@ -102,8 +102,8 @@ class Transformer(nn.Module):
         return h, merge_aux(aux_list, self.cfg.n_experts, self.n_moe, x.device)
 
     def logits(self, h):
-        return h.float() @ ops.working(self.wte, torch.float32).t() if not h.is_cuda else \
-            ops.linear(h, _Transposed(self.wte), out_dtype=torch.float32, compute_dtype=self.dtype)
+        """Tied fp32-accumulated head ``h @ wte^T`` (model/transformer.py:408-410)."""
+        return ops.linear_t(h.reshape(-1, h.shape[-1]), self.wte).view(*h.shape[:-1], -1)
 
     def loss(self, tokens):
         """Total loss and metrics (train.py:180-217): CE over the full-length
@@ -128,13 +128,6 @@ class Transformer(nn.Module):
 
     def moe_layers(self):
         return [b.ffn for b in self.blocks if b.use_moe]
-
-
-class _Transposed:
-    """Marker: use ``w`` (stored [V, D]) as the ``[D, V]`` right operand."""
-
-    def __init__(self, w):
-        self.w = w
 
 
 def merge_aux(aux_list, n_experts, n_moe, device):

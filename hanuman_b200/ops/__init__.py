@@ -39,10 +39,18 @@ def linear(x: torch.Tensor, w: torch.Tensor, out_dtype: Optional[torch.dtype] = 
            compute_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
     """``x @ w`` with ``w`` stored ``[in, out]`` (reference layout)."""
     if on_gpu(x):
-        from .linear import linear_cuda
+        from .dense import linear_cuda
         return linear_cuda(x, w, out_dtype or compute_dtype, compute_dtype)
     y = x.to(compute_dtype) @ w.to(compute_dtype)
     return y if out_dtype is None else y.to(out_dtype)
+
+
+def linear_t(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """``x @ w^T`` in fp32 output (the tied head: ``w`` is the ``[V, D]`` embedding)."""
+    if on_gpu(x):
+        from .dense import linear_t_cuda
+        return linear_t_cuda(x, w, torch.float32)
+    return x.float() @ w.float().t()
 
 
 # ------------------------------------------------------------------ norms
@@ -56,7 +64,7 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, out_dtype: torch.dtyp
 # ------------------------------------------------------------------ rope
 def apply_rope(q, k, cos, sin, positions=None):
     if on_gpu(q):
-        from .rope import rope_cuda
+        from .norm import rope_cuda
         return rope_cuda(q, k, cos, sin, positions)
     return ref.apply_rope(q, k, cos, sin, positions)
 
@@ -65,7 +73,7 @@ def apply_rope(q, k, cos, sin, positions=None):
 def attention(q, k, v, window: int = 0, q_offset: int = 0):
     """Causal (optionally windowed) GQA; q ``[B,S,Nq,H]``, k/v ``[B,S,Nkv,H]``."""
     if on_gpu(q):
-        from .attention import flash_attention
+        from .flash import flash_attention
         return flash_attention(q, k, v, window, q_offset)
     return ref.causal_attention(q, k, v, window, q_offset=q_offset)
 
@@ -74,7 +82,7 @@ def attention(q, k, v, window: int = 0, q_offset: int = 0):
 def swiglu_act(gu: torch.Tensor) -> torch.Tensor:
     """``silu(g) * u`` for ``gu = [g | u]`` along the last axis."""
     if on_gpu(gu):
-        from .swiglu import swiglu_cuda
+        from .norm import swiglu_cuda
         return swiglu_cuda(gu)
     F = gu.shape[-1] // 2
     return torch.nn.functional.silu(gu[..., :F]) * gu[..., F:]
@@ -88,14 +96,6 @@ def kda_core(q, k, v, g, beta, scale: float, chunk: int):
         return kda_chunked_cuda(q, k, v, g, beta, scale, chunk)
     o, _ = ref.kda_chunked(q, k, v, g, beta, scale, chunk)
     return o
-
-
-def short_conv_silu(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-    """SiLU(causal depthwise conv4(x)) in fp32 (conv result rounded to x.dtype)."""
-    if on_gpu(x):
-        from .kda import conv_silu_cuda
-        return conv_silu_cuda(x, w)
-    return torch.nn.functional.silu(ref.short_conv(x, w).float())
 
 
 # ------------------------------------------------------------------ loss

@@ -1,0 +1,208 @@
+"""MoE layer and dense SwiGLU FFN on the native kernels (model/moe.py).
+
+Forward of one MoE layer (dropless, the reference's ragged dispatch):
+  router kernel   fp32 logits, sigmoid(+bias)/softmax scores, top-k, weights,
+                  per-sequence counts / probability sums / z and entropy sums
+  plan kernels    stable counting sort of (token, slot) by expert into a row
+                  buffer whose expert segments start at multiples of 128
+  gather          Xp[row] = h[token(row)]           (pad rows zero)
+  grouped GEMMs   GU = Xp @ [W_gate | W_up] (per expert), H = silu(G) * U,
+                  Y = H @ W_down                     (tcgen05, grouped over rows)
+  shared expert   dense GEMMs + SwiGLU, fp32 output
+  combine         out[t] += sum_k bf16(w_tk) * Y[row(t, k)]
+Backward mirrors it; expert weight gradients use the grouped-K GEMM (the
+contraction runs over each expert's row segment) accumulating into the
+parameters' fp32 main_grad; the router backward covers the combine weights,
+the z-loss and the sequence-wise balance loss.  No host synchronisation: the
+row buffer is sized for the worst case and the grouped GEMMs read their tile
+counts from device memory.
+"""
+from __future__ import annotations
+
+import torch
+
+from ._ext import ext
+from .dense import _bf16, _work, main_grad
+from .norm import SwiGLUFn
+
+
+def _bn(n: int) -> int:
+    return 256 if n >= 256 else 128
+
+
+class SwiGLUFFNFn(torch.autograd.Function):
+    """down(silu(x @ gate) * (x @ up)) -> fp32."""
+
+    @staticmethod
+    def forward(ctx, x, wg, wu, wd):
+        xb = _bf16(x)
+        g, u, d = _work(wg), _work(wu), _work(wd)
+        T = xb.shape[0]
+        F = g.shape[1]
+        gu = torch.empty(T, 2 * F, dtype=torch.bfloat16, device=x.device)
+        ext().gemm(xb, g, gu[:, :F], False, False, False, 1.0)
+        ext().gemm(xb, u, gu[:, F:], False, False, False, 1.0)
+        hh = torch.empty(T, F, dtype=torch.bfloat16, device=x.device)
+        ext().swiglu_fwd(gu, hh)
+        out = torch.empty(T, d.shape[1], dtype=torch.float32, device=x.device)
+        ext().gemm(hh, d, out, False, False, False, 1.0)
+        ctx.save_for_backward(xb, g, u, d, gu, hh)
+        ctx.params = (wg, wu, wd)
+        ctx.x_dtype = x.dtype
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        xb, g, u, d, gu, hh = ctx.saved_tensors
+        wg, wu, wd = ctx.params
+        F = g.shape[1]
+        db = _bf16(dout)
+        dh = torch.empty_like(hh)
+        ext().gemm(db, d, dh, False, True, False, 1.0)
+        ext().gemm(hh, db, main_grad(wd), True, False, True, 1.0)
+        dgu = torch.empty_like(gu)
+        ext().swiglu_bwd(dh, gu, dgu)
+        dx = torch.empty(xb.shape, dtype=torch.float32, device=xb.device)
+        ext().gemm(dgu[:, :F], g, dx, False, True, False, 1.0)
+        ext().gemm(dgu[:, F:], u, dx, False, True, True, 1.0)
+        ext().gemm(xb, dgu[:, :F], main_grad(wg), True, False, True, 1.0)
+        ext().gemm(xb, dgu[:, F:], main_grad(wu), True, False, True, 1.0)
+        return dx.to(ctx.x_dtype), None, None, None
+
+
+def swiglu_ffn_cuda(x, wg, wu, wd, dtype=torch.bfloat16):
+    return SwiGLUFFNFn.apply(x, wg, wu, wd)
+
+
+class MoEFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, h, mod, B, S):
+        dev = h.device
+        xb = _bf16(h)
+        T, D = xb.shape
+        N, K = mod.n_experts, mod.n_active
+        softmax = mod.router_type == "softmax"
+        Wr = mod.router.detach().float().contiguous()
+        bias = mod.bias.detach().float().contiguous()
+        f32 = dict(dtype=torch.float32, device=dev)
+        i32 = dict(dtype=torch.int32, device=dev)
+        logits = torch.empty(T, N, **f32)
+        topi = torch.empty(T, K, **i32)
+        topw = torch.empty(T, K, **f32)
+        seq_counts = torch.zeros(B, N, **f32)
+        seq_probs = torch.zeros(B, N, **f32)
+        sums = torch.zeros(2, **f32)
+        ext().router_fwd(xb, Wr, bias, S, K, softmax, float(mod.scaling), logits, topi, topw,
+                         seq_counts, seq_probs, sums)
+        # dispatch plan
+        wg, wu, wd = _work(mod.expert_w_gate), _work(mod.expert_w_up), _work(mod.expert_w_down)
+        F = wg.shape[2]
+        R = T * K + N * 127
+        R = (R + 127) // 128 * 128
+        counts = torch.empty(N, **i32)
+        starts = torch.empty(N, **i32)
+        tprefix_f = torch.empty(N + 1, **i32)
+        padded = torch.empty(N, **i32)
+        total = torch.empty(1, **i32)
+        pos = torch.empty(T, K, **i32)
+        row_src = torch.full((R,), -1, **i32)
+        ext().moe_plan(topi, N, (F + _bn(F) - 1) // _bn(F), counts, starts, tprefix_f, padded,
+                       total, pos, row_src)
+        # tile prefix for the D-wide down projection (tiles_n differs)
+        tn_f, tn_d = (F + _bn(F) - 1) // _bn(F), (D + _bn(D) - 1) // _bn(D)
+        tprefix_d = (tprefix_f // tn_f * tn_d).to(torch.int32)
+        xp = torch.empty(R, D, dtype=torch.bfloat16, device=dev)
+        ext().moe_gather(xb, row_src, xp, K)
+        gu = torch.empty(R, 2 * F, dtype=torch.bfloat16, device=dev)
+        ext().grouped_gemm_m(xp, wg, gu[:, :F], starts, counts, tprefix_f, False)
+        ext().grouped_gemm_m(xp, wu, gu[:, F:], starts, counts, tprefix_f, False)
+        hh = torch.empty(R, F, dtype=torch.bfloat16, device=dev)
+        ext().swiglu_fwd(gu, hh, row_src)  # pad rows -> 0 (grouped-K reads them)
+        y = torch.empty(R, D, dtype=torch.bfloat16, device=dev)
+        ext().grouped_gemm_m(hh, wd, y, starts, counts, tprefix_d, False)
+        # shared expert (fp32 out) + combine
+        if mod.n_shared != 1:
+            raise NotImplementedError("GPU MoE supports one shared expert")
+        sg, su, sd = _work(mod.shared_w_gate), _work(mod.shared_w_up), _work(mod.shared_w_down)
+        Fs = sg.shape[1]
+        sgu = torch.empty(T, 2 * Fs, dtype=torch.bfloat16, device=dev)
+        ext().gemm(xb, sg, sgu[:, :Fs], False, False, False, 1.0)
+        ext().gemm(xb, su, sgu[:, Fs:], False, False, False, 1.0)
+        shh = torch.empty(T, Fs, dtype=torch.bfloat16, device=dev)
+        ext().swiglu_fwd(sgu, shh)
+        out = torch.empty(T, D, **f32)
+        ext().gemm(shh, sd, out, False, False, False, 1.0)
+        ext().moe_combine(y, pos, topw, out)
+        # aux (model/moe.py:253-293)
+        z = sums[0] / T
+        ent = sums[1] / T
+        frac = seq_counts / (S * K)
+        mean_probs = seq_probs / S
+        bal = (N * (frac * mean_probs).sum(-1)).mean()
+        expert_counts = seq_counts.sum(0)
+        ctx.save_for_backward(xb, logits, topi, topw, pos, row_src, starts, counts, padded,
+                              tprefix_f, tprefix_d, xp, gu, hh, y, sgu, shh, frac)
+        ctx.mod = mod
+        ctx.meta = (B, S, T, D, N, K, F, Fs, R, softmax)
+        ctx.mark_non_differentiable(ent, expert_counts)
+        return out, z, bal, ent, expert_counts
+
+    @staticmethod
+    def backward(ctx, dout, dz, dbal, dent, dcounts):
+        (xb, logits, topi, topw, pos, row_src, starts, counts, padded, tprefix_f, tprefix_d, xp,
+         gu, hh, y, sgu, shh, frac) = ctx.saved_tensors
+        mod = ctx.mod
+        B, S, T, D, N, K, F, Fs, R, softmax = ctx.meta
+        dev = xb.device
+        dout = dout.float().contiguous()
+        db = dout.to(torch.bfloat16)
+        # shared expert
+        sg, su, sd = _work(mod.shared_w_gate), _work(mod.shared_w_up), _work(mod.shared_w_down)
+        dsh = torch.empty_like(shh)
+        ext().gemm(db, sd, dsh, False, True, False, 1.0)
+        ext().gemm(shh, db, main_grad(mod.shared_w_down), True, False, True, 1.0)
+        dsgu = torch.empty_like(sgu)
+        ext().swiglu_bwd(dsh, sgu, dsgu)
+        dx = torch.empty(T, D, dtype=torch.float32, device=dev)
+        ext().gemm(dsgu[:, :Fs], sg, dx, False, True, False, 1.0)
+        ext().gemm(dsgu[:, Fs:], su, dx, False, True, True, 1.0)
+        ext().gemm(xb, dsgu[:, :Fs], main_grad(mod.shared_w_gate), True, False, True, 1.0)
+        ext().gemm(xb, dsgu[:, Fs:], main_grad(mod.shared_w_up), True, False, True, 1.0)
+        # combine backward
+        dy = torch.empty(R, D, dtype=torch.bfloat16, device=dev)
+        dtopw = torch.empty(T, K, dtype=torch.float32, device=dev)
+        ext().moe_combine_bwd(dout, y, pos, topw, row_src, dy, dtopw)
+        wg, wu, wd = _work(mod.expert_w_gate), _work(mod.expert_w_up), _work(mod.expert_w_down)
+        dhh = torch.empty(R, F, dtype=torch.bfloat16, device=dev)
+        ext().grouped_gemm_m(dy, wd, dhh, starts, counts, tprefix_f, True)
+        ext().grouped_gemm_k(hh, dy, main_grad(mod.expert_w_down), starts, padded, True)
+        dgu = torch.empty_like(gu)
+        ext().swiglu_bwd(dhh, gu, dgu, row_src)  # pad rows -> 0 for the grouped-K GEMMs
+        dxp = torch.empty(R, D, dtype=torch.float32, device=dev)
+        tn_d = (D + _bn(D) - 1) // _bn(D)
+        tn_f = (F + _bn(F) - 1) // _bn(F)
+        tprefix_dx = (tprefix_f // tn_f * tn_d).to(torch.int32)
+        ext().grouped_gemm_m(dgu[:, :F], wg, dxp, starts, counts, tprefix_dx, True, False)
+        ext().grouped_gemm_m(dgu[:, F:], wu, dxp, starts, counts, tprefix_dx, True, True)
+        ext().grouped_gemm_k(xp, dgu[:, :F], main_grad(mod.expert_w_gate), starts, padded, True)
+        ext().grouped_gemm_k(xp, dgu[:, F:], main_grad(mod.expert_w_up), starts, padded, True)
+        ext().moe_scatter_add(dxp, pos, dx)
+        # router backward (z-loss, balance loss, combine weights)
+        dz = torch.zeros((), device=dev) if dz is None else dz
+        dbal = torch.zeros((), device=dev) if dbal is None else dbal
+        coef_z = (dz.float() * 2.0 / T).reshape(1).contiguous()
+        bal_coef = (dbal.float() * N / (B * S) * frac).contiguous()
+        dlogits = torch.empty(T, N, dtype=torch.float32, device=dev)
+        ext().router_bwd(logits, topi, dtopw, bal_coef, S, softmax, float(mod.scaling), coef_z,
+                         dlogits)
+        ext().router_grads(xb, mod.router.detach().float().contiguous(), dlogits, dx,
+                           main_grad(mod.router))
+        return dx.to(torch.bfloat16), None, None, None
+
+
+def moe_layer_cuda(mod, h, dtype):
+    B, S, D = h.shape
+    out, z, bal, ent, counts = MoEFn.apply(h.reshape(B * S, D), mod, B, S)
+    aux = {"router_z_loss": z, "balance_loss": bal, "mean_entropy": ent,
+           "expert_counts": counts}
+    return out.view(B, S, D), aux
