@@ -20,6 +20,7 @@ int epi_of(const torch::Tensor& c, bool accumulate) {
 GemmArgs base_args(const torch::Tensor& c, double alpha,
                    const c10::optional<torch::Tensor>& alpha_t = c10::nullopt) {
   GemmArgs a{};
+  a.k_splits = 1;
   a.C = c.data_ptr();
   a.ldc = c.stride(-2);
   a.alpha = (float)alpha;
@@ -66,8 +67,22 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool trans_a, bool 
   if (K == 0) {
     HB_CHECK(false, "gemm with K == 0 is not supported");
   }
-  const int grid = std::min(args.num_tiles, num_sms());
   const int epi = epi_of(c, accumulate);
+  // Split the K loop when the output has too few tiles to fill the GPU
+  // (weight gradients: small [in, out] output, K = tokens).  fp32 outputs only.
+  args.k_splits = 1;
+  const int sms = num_sms();
+  const int kblocks = (K + GEMM_BK - 1) / GEMM_BK;
+  if (epi != EPI_BF16 && args.num_tiles * 2 <= sms && kblocks >= 16) {
+    int s = std::min(sms / args.num_tiles, kblocks / 8);
+    s = std::max(1, std::min(s, 32));
+    if (s > 1) {
+      if (epi == EPI_F32) c.zero_();  // partials are added atomically
+      args.k_splits = s;
+      args.num_tiles *= s;
+    }
+  }
+  const int grid = std::min(args.num_tiles, sms);
   if (trans_a)
     gemm_dispatch_dense_amn(BN, !trans_b, epi, ta, tb, args, grid);
   else

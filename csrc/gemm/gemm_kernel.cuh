@@ -42,6 +42,7 @@ struct GemmArgs {
   int M, N, K;
   int tiles_m, tiles_n;
   int num_tiles;                // DENSE / GROUPED_K; GROUPED_M reads grp_tile_start[G]
+  int k_splits;                 // DENSE: split the K loop over CTAs (fp32 atomic epilogue)
   int num_groups;
   const int* grp_start;         // GROUPED_M: row start; GROUPED_K: k start
   const int* grp_count;         // rows / k per group
@@ -73,11 +74,16 @@ template <int MODE, int BN>
 __device__ __forceinline__ bool get_tile(const GemmArgs& a, int t, TileInfo& ti) {
   if (MODE == DENSE) {
     if (t >= a.num_tiles) return false;
-    int mb = t / a.tiles_n, nb = t - mb * a.tiles_n;
+    const int split = t % a.k_splits;
+    const int tile = t / a.k_splits;
+    int mb = tile / a.tiles_n, nb = tile - mb * a.tiles_n;
     ti.m0 = mb * GEMM_BM;
     ti.n0 = nb * BN;
-    ti.k0 = 0;
-    ti.k_iters = (a.K + GEMM_BK - 1) / GEMM_BK;
+    const int total_k = (a.K + GEMM_BK - 1) / GEMM_BK;
+    const int per = (total_k + a.k_splits - 1) / a.k_splits;
+    const int kb0 = split * per;
+    ti.k0 = kb0 * GEMM_BK;
+    ti.k_iters = max(0, min(per, total_k - kb0));
     ti.group = 0;
     ti.m_limit = a.M;
     return true;
@@ -304,7 +310,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
         } else {
           float* out = reinterpret_cast<float*>(cbase) + (long long)m * args.ldc + n;
-          if (full) {
+          if (MODE == DENSE && args.k_splits > 1) {
+            // split-K: partial products meet in global memory
+            if (has_k) {
+              if (full) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                  atomicAdd(reinterpret_cast<float4*>(out) + q,
+                            make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]));
+              } else {
+                for (int j = 0; j < 32 && n + j < args.N; ++j) atomicAdd(out + j, v[j]);
+              }
+            }
+          } else if (full) {
             float4* o4 = reinterpret_cast<float4*>(out);
 #pragma unroll
             for (int q = 0; q < 8; ++q) {

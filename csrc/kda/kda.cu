@@ -29,7 +29,15 @@ namespace kda {
 
 constexpr int NT = 256;
 
-// out[m][n] (+)= sum_k A(m,k) B(k,n); A(m,k) = a[m*lda + k] or a[k*lda + m] (TA)
+// Shared-memory matrices use odd row strides (cols + 1) so that a warp reading
+// a column (lanes over rows) or a row (lanes over columns) hits 32 banks.
+template <int DK>
+constexpr int LDK() { return DK + 1; }
+template <int C>
+constexpr int LDC() { return C + 1; }
+
+// out[m][n] (+)= alpha * sum_k A(m,k) B(k,n);  A(m,k) = a[m*lda+k] (or a[k*lda+m] if TA),
+// B(k,n) = b[k*ldb+n] (or b[n*ldb+k] if TB).  Lanes run over n.
 template <int M, int N, int KD, bool TA, bool TB>
 HB_DEVICE void mm(float* out, int ldo, const float* a, int lda, const float* b, int ldb, float alpha,
                   bool acc) {
@@ -65,21 +73,22 @@ HB_DEVICE long long chunk_off(const Ptrs& p, int b, int h, int n, int sz) {
   return ((((long long)b * p.H + h) * p.NC) + n) * sz;
 }
 
-// Shared prologue: load q, k, v, g, beta of one chunk (zeros past S) and
+// Load one chunk's q, k, v, g (zeros past S) into padded smem, beta, and
 // cumulate g -> G in place.
 template <int DK, int C>
 HB_DEVICE void load_chunk(const Ptrs& p, int b, int h, int n, float* q, float* k, float* v, float* G,
                           float* bet) {
+  constexpr int L = LDK<DK>();
   const int t0 = n * C;
   for (int i = threadIdx.x; i < C * DK; i += NT) {
     const int r = i / DK, c = i % DK;
     const int t = t0 + r;
     const bool ok = t < p.S;
     const long long o = ok ? tok_off(p, b, t, h, DK) + c : 0;
-    q[i] = ok ? p.q[o] : 0.f;
-    k[i] = ok ? p.k[o] : 0.f;
-    v[i] = ok ? p.v[o] : 0.f;
-    G[i] = ok ? p.g[o] : 0.f;
+    q[r * L + c] = ok ? p.q[o] : 0.f;
+    k[r * L + c] = ok ? p.k[o] : 0.f;
+    v[r * L + c] = ok ? p.v[o] : 0.f;
+    G[r * L + c] = ok ? p.g[o] : 0.f;
   }
   for (int r = threadIdx.x; r < C; r += NT) {
     const int t = t0 + r;
@@ -89,61 +98,69 @@ HB_DEVICE void load_chunk(const Ptrs& p, int b, int h, int n, float* q, float* k
   for (int c = threadIdx.x; c < DK; c += NT) {
     float s = 0.f;
     for (int r = 0; r < C; ++r) {
-      s += G[r * DK + c];
-      G[r * DK + c] = s;
+      s += G[r * L + c];
+      G[r * L + c] = s;
     }
   }
   __syncthreads();
 }
 
-// A (strict lower) and P (lower incl., scaled) by pairwise log-space decay.
+// A (strict lower) and P (lower incl., scaled) by pairwise log-space decay:
+// one warp per row t, lanes over channels, warp reductions.
 template <int DK, int C>
 HB_DEVICE void pair_products(const float* q, const float* k, const float* G, float* A, float* P,
                              float scale) {
+  constexpr int L = LDK<DK>(), LC = LDC<C>();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int t = warp; t < C; t += NT / 32) {
     for (int s = 0; s < C; ++s) {
       float a = 0.f, pp = 0.f;
       if (s <= t) {
         for (int c = lane; c < DK; c += 32) {
-          const float e = __expf(G[t * DK + c] - G[s * DK + c]);
-          const float ks = k[s * DK + c] * e;
-          a += k[t * DK + c] * ks;
-          pp += q[t * DK + c] * ks;
+          const float e = __expf(G[t * L + c] - G[s * L + c]);
+          const float ks = k[s * L + c] * e;
+          a += k[t * L + c] * ks;
+          pp += q[t * L + c] * ks;
         }
       }
       a = warp_sum(a);
       pp = warp_sum(pp);
       if (lane == 0) {
-        A[t * C + s] = (s < t) ? a : 0.f;
-        P[t * C + s] = (s <= t) ? pp * scale : 0.f;
+        A[t * LC + s] = (s < t) ? a : 0.f;
+        P[t * LC + s] = (s <= t) ? pp * scale : 0.f;
       }
     }
   }
   __syncthreads();
 }
 
-// In-place forward substitution X <- L^{-1} X for L = I + diag(b^2) A (unit lower):
-// X_t -= b_t^2 sum_{s<t} A_ts X_s ; columns independent (one thread per column).
-template <int C>
-HB_DEVICE void solve_lower(float* X, int ncol, int ldx, const float* A, const float* bet) {
-  for (int col = threadIdx.x; col < ncol; col += NT) {
+// In-place forward substitution X <- L^{-1} X, L = I + diag(b^2) A (unit lower),
+// on two column blocks at once (X1, X2: C x DK each); one thread per column.
+template <int DK, int C>
+HB_DEVICE void solve_lower2(float* X1, float* X2, const float* A, const float* bet) {
+  constexpr int L = LDK<DK>(), LC = LDC<C>();
+  for (int col = threadIdx.x; col < 2 * DK; col += NT) {
+    float* X = col < DK ? X1 : X2;
+    const int cc = col < DK ? col : col - DK;
     for (int t = 1; t < C; ++t) {
       float s = 0.f;
-      for (int j = 0; j < t; ++j) s += A[t * C + j] * X[j * ldx + col];
-      X[t * ldx + col] -= bet[t] * bet[t] * s;
+      for (int j = 0; j < t; ++j) s += A[t * LC + j] * X[j * L + cc];
+      X[t * L + cc] -= bet[t] * bet[t] * s;
     }
   }
   __syncthreads();
 }
 // In-place backward substitution X <- L^{-T} X:  X_t -= sum_{s>t} A_st b_s^2 X_s
-template <int C>
-HB_DEVICE void solve_upper_t(float* X, int ncol, int ldx, const float* A, const float* bet) {
-  for (int col = threadIdx.x; col < ncol; col += NT) {
+template <int DK, int C>
+HB_DEVICE void solve_upper_t2(float* X1, float* X2, const float* A, const float* bet) {
+  constexpr int L = LDK<DK>(), LC = LDC<C>();
+  for (int col = threadIdx.x; col < 2 * DK; col += NT) {
+    float* X = col < DK ? X1 : X2;
+    const int cc = col < DK ? col : col - DK;
     for (int t = C - 2; t >= 0; --t) {
       float s = 0.f;
-      for (int j = t + 1; j < C; ++j) s += A[j * C + t] * bet[j] * bet[j] * X[j * ldx + col];
-      X[t * ldx + col] -= s;
+      for (int j = t + 1; j < C; ++j) s += A[j * LC + t] * bet[j] * bet[j] * X[j * L + cc];
+      X[t * L + cc] -= s;
     }
   }
   __syncthreads();
@@ -152,141 +169,165 @@ HB_DEVICE void solve_upper_t(float* X, int ncol, int ldx, const float* A, const 
 // ------------------------------------------------------------------ intra fwd
 template <int DK, int C>
 __global__ void __launch_bounds__(NT) intra_fwd_kernel(Ptrs p) {
+  constexpr int L = LDK<DK>(), LC = LDC<C>();
   extern __shared__ float sm[];
   float* q = sm;
-  float* k = q + C * DK;
-  float* v = k + C * DK;
-  float* G = v + C * DK;
-  float* Wt = G + C * DK;
-  float* A = Wt + C * DK;
-  float* P = A + C * C;
-  float* bet = P + C * C;
+  float* k = q + C * L;
+  float* v = k + C * L;
+  float* G = v + C * L;
+  float* Wt = G + C * L;
+  float* A = Wt + C * L;
+  float* P = A + C * LC;
+  float* bet = P + C * LC;
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   load_chunk<DK, C>(p, b, h, n, q, k, v, G, bet);
   pair_products<DK, C>(q, k, G, A, P, p.scale);
   // right-hand sides: Ut <- b v (in v), Wt <- b^2 k e^G
   for (int i = threadIdx.x; i < C * DK; i += NT) {
-    const int r = i / DK;
-    v[i] *= bet[r];
-    Wt[i] = bet[r] * bet[r] * k[i] * __expf(G[i]);
+    const int r = i / DK, c = i % DK;
+    v[r * L + c] *= bet[r];
+    Wt[r * L + c] = bet[r] * bet[r] * k[r * L + c] * __expf(G[r * L + c]);
   }
   __syncthreads();
-  solve_lower<C>(v, DK, DK, A, bet);
-  solve_lower<C>(Wt, DK, DK, A, bet);
+  solve_lower2<DK, C>(v, Wt, A, bet);
   const long long co = chunk_off(p, b, h, n, C * DK);
-  const float* GC = G + (C - 1) * DK;
+  const float* GC = G + (C - 1) * L;
   for (int i = threadIdx.x; i < C * DK; i += NT) {
-    const int c = i % DK;
-    p.Ut[co + i] = v[i];
-    p.Wt[co + i] = Wt[i];
-    p.Kh[co + i] = k[i] * __expf(GC[c] - G[i]);
-    p.Qg[co + i] = p.scale * q[i] * __expf(G[i]);
+    const int r = i / DK, c = i % DK;
+    const int si = r * L + c;
+    p.Ut[co + i] = v[si];
+    p.Wt[co + i] = Wt[si];
+    p.Kh[co + i] = k[si] * __expf(GC[c] - G[si]);
+    p.Qg[co + i] = p.scale * q[si] * __expf(G[si]);
   }
   const long long po = chunk_off(p, b, h, n, C * C);
-  for (int i = threadIdx.x; i < C * C; i += NT) p.Pm[po + i] = P[i];
+  for (int i = threadIdx.x; i < C * C; i += NT) p.Pm[po + i] = P[(i / C) * LC + (i % C)];
   for (int c = threadIdx.x; c < DK; c += NT) p.gC[chunk_off(p, b, h, n, DK) + c] = __expf(GC[c]);
 }
 
 // ------------------------------------------------------------------ state fwd
-template <int DK, int C>
+// grid (DK / VS, H, B): value columns [vs*VS, vs*VS+VS) of the state.
+template <int DK, int C, int VS>
 __global__ void __launch_bounds__(NT) state_fwd_kernel(Ptrs p) {
+  constexpr int L = LDK<DK>(), LC = LDC<C>(), LV = VS + 1;
   extern __shared__ float sm[];
-  float* S = sm;                 // DK x DK
-  float* U = S + DK * DK;        // C x DK
-  float* Wt = U + C * DK;        // C x DK
-  float* X = Wt + C * DK;        // C x DK (Qg, then Kh)
-  float* P = X + C * DK;         // C x C
-  float* O = P + C * C;          // C x DK
-  float* gc = O + C * DK;        // DK
-  const int h = blockIdx.x, b = blockIdx.y;
-  for (int i = threadIdx.x; i < DK * DK; i += NT)
-    S[i] = p.init_state ? p.init_state[((long long)b * p.H + h) * DK * DK + i] : 0.f;
+  float* S = sm;                 // DK x LV
+  float* U = S + DK * LV;        // C x LV
+  float* O = U + C * LV;         // C x LV
+  float* Wt = O + C * LV;        // C x L
+  float* X = Wt + C * L;         // C x L (Qg, then Kh)
+  float* P = X + C * L;          // C x LC
+  float* gc = P + C * LC;        // DK
+  const int vs = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int v0 = vs * VS;
+  for (int i = threadIdx.x; i < DK * VS; i += NT) {
+    const int r = i / VS, c = i % VS;
+    S[r * LV + c] = p.init_state ? p.init_state[((long long)b * p.H + h) * DK * DK + r * DK + v0 + c] : 0.f;
+  }
   __syncthreads();
   for (int n = 0; n < p.NC; ++n) {
     const long long co = chunk_off(p, b, h, n, C * DK);
     const long long so = chunk_off(p, b, h, n, DK * DK);
-    for (int i = threadIdx.x; i < DK * DK; i += NT) p.states[so + i] = S[i];
-    for (int i = threadIdx.x; i < C * DK; i += NT) {
-      U[i] = p.Ut[co + i];
-      Wt[i] = p.Wt[co + i];
-      X[i] = p.Qg[co + i];
+    for (int i = threadIdx.x; i < DK * VS; i += NT) {
+      const int r = i / VS, c = i % VS;
+      p.states[so + r * DK + v0 + c] = S[r * LV + c];
     }
-    for (int i = threadIdx.x; i < C * C; i += NT) P[i] = p.Pm[chunk_off(p, b, h, n, C * C) + i];
+    for (int i = threadIdx.x; i < C * DK; i += NT) {
+      const int r = i / DK, c = i % DK;
+      Wt[r * L + c] = p.Wt[co + i];
+      X[r * L + c] = p.Qg[co + i];
+    }
+    for (int i = threadIdx.x; i < C * VS; i += NT) {
+      const int r = i / VS, c = i % VS;
+      U[r * LV + c] = p.Ut[co + r * DK + v0 + c];
+    }
+    for (int i = threadIdx.x; i < C * C; i += NT) P[(i / C) * LC + i % C] = p.Pm[chunk_off(p, b, h, n, C * C) + i];
     for (int c = threadIdx.x; c < DK; c += NT) gc[c] = p.gC[chunk_off(p, b, h, n, DK) + c];
     __syncthreads();
     // U = Ut - Wt S ;  O = Qg S
-    mm<C, DK, DK, false, false>(U, DK, Wt, DK, S, DK, -1.f, true);
-    mm<C, DK, DK, false, false>(O, DK, X, DK, S, DK, 1.f, false);
+    mm<C, VS, DK, false, false>(U, LV, Wt, L, S, LV, -1.f, true);
+    mm<C, VS, DK, false, false>(O, LV, X, L, S, LV, 1.f, false);
     __syncthreads();
-    // O += P U
-    mm<C, DK, C, false, false>(O, DK, P, C, U, DK, 1.f, true);
-    // Kh into X
-    for (int i = threadIdx.x; i < C * DK; i += NT) X[i] = p.Kh[co + i];
+    // O += P U (P lower triangular)
+    mm<C, VS, C, false, false>(O, LV, P, LC, U, LV, 1.f, true);
+    for (int i = threadIdx.x; i < C * DK; i += NT) X[(i / DK) * L + i % DK] = p.Kh[co + i];
     __syncthreads();
     // S = gc * S + Kh^T U
-    for (int e = threadIdx.x; e < DK * DK; e += NT) {
-      const int r = e / DK, c = e % DK;
+    for (int e = threadIdx.x; e < DK * VS; e += NT) {
+      const int r = e / VS, c = e % VS;
       float s = 0.f;
-      for (int t = 0; t < C; ++t) s += X[t * DK + r] * U[t * DK + c];
-      S[e] = gc[r] * S[e] + s;
+      for (int t = 0; t < C; ++t) s += X[t * L + r] * U[t * LV + c];
+      S[r * LV + c] = gc[r] * S[r * LV + c] + s;
     }
-    // write O rows
-    for (int i = threadIdx.x; i < C * DK; i += NT) {
-      const int r = i / DK, c = i % DK;
+    for (int i = threadIdx.x; i < C * VS; i += NT) {
+      const int r = i / VS, c = i % VS;
       const int t = n * C + r;
-      if (t < p.S) p.o[tok_off(p, b, t, h, DK) + c] = O[i];
+      if (t < p.S) p.o[tok_off(p, b, t, h, DK) + v0 + c] = O[r * LV + c];
     }
     __syncthreads();
   }
   if (p.final_state)
-    for (int i = threadIdx.x; i < DK * DK; i += NT)
-      p.final_state[((long long)b * p.H + h) * DK * DK + i] = S[i];
+    for (int i = threadIdx.x; i < DK * VS; i += NT) {
+      const int r = i / VS, c = i % VS;
+      p.final_state[((long long)b * p.H + h) * DK * DK + r * DK + v0 + c] = S[r * LV + c];
+    }
 }
 
 // ------------------------------------------------------------------ state bwd
-// dS_prev = gC * dS + Qg^T dO - Wt^T dU,  dU = P^T dO + Kh dS.  dstates[n] = dS at the
-// END of chunk n (gradient flowing into S_C).
-template <int DK, int C>
+// dS_prev = gC * dS + Qg^T dO - Wt^T dU,  dU = P^T dO + Kh dS.  dstates[n] = dS at
+// the END of chunk n.  grid (DK / VS, H, B) over value-column slices.
+template <int DK, int C, int VS>
 __global__ void __launch_bounds__(NT) state_bwd_kernel(Ptrs p) {
+  constexpr int L = LDK<DK>(), LC = LDC<C>(), LV = VS + 1;
   extern __shared__ float sm[];
-  float* dS = sm;                // DK x DK
-  float* dU = dS + DK * DK;      // C x DK
-  float* dO = dU + C * DK;       // C x DK
-  float* X = dO + C * DK;        // C x DK (Kh, then Qg)
-  float* Wt = X + C * DK;        // C x DK
-  float* P = Wt + C * DK;        // C x C
-  float* gc = P + C * C;         // DK
-  float* T2 = gc + DK;           // DK x DK scratch
-  const int h = blockIdx.x, b = blockIdx.y;
-  for (int i = threadIdx.x; i < DK * DK; i += NT) dS[i] = 0.f;
+  float* dS = sm;                // DK x LV
+  float* T2 = dS + DK * LV;      // DK x LV
+  float* dU = T2 + DK * LV;      // C x LV
+  float* dO = dU + C * LV;       // C x LV
+  float* X = dO + C * LV;        // C x L (Kh, then Qg)
+  float* Wt = X + C * L;         // C x L
+  float* P = Wt + C * L;         // C x LC
+  float* gc = P + C * LC;        // DK
+  const int vs = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int v0 = vs * VS;
+  for (int i = threadIdx.x; i < DK * LV; i += NT) dS[i] = 0.f;
   __syncthreads();
   for (int n = p.NC - 1; n >= 0; --n) {
     const long long co = chunk_off(p, b, h, n, C * DK);
     const long long so = chunk_off(p, b, h, n, DK * DK);
-    for (int i = threadIdx.x; i < DK * DK; i += NT) p.dstates[so + i] = dS[i];
+    for (int i = threadIdx.x; i < DK * VS; i += NT) {
+      const int r = i / VS, c = i % VS;
+      p.dstates[so + r * DK + v0 + c] = dS[r * LV + c];
+    }
+    for (int i = threadIdx.x; i < C * VS; i += NT) {
+      const int r = i / VS, c = i % VS;
+      const int t = n * C + r;
+      dO[r * LV + c] = t < p.S ? p.dout[tok_off(p, b, t, h, DK) + v0 + c] : 0.f;
+    }
     for (int i = threadIdx.x; i < C * DK; i += NT) {
       const int r = i / DK, c = i % DK;
-      const int t = n * C + r;
-      dO[i] = t < p.S ? p.dout[tok_off(p, b, t, h, DK) + c] : 0.f;
-      X[i] = p.Kh[co + i];
-      Wt[i] = p.Wt[co + i];
+      X[r * L + c] = p.Kh[co + i];
+      Wt[r * L + c] = p.Wt[co + i];
     }
-    for (int i = threadIdx.x; i < C * C; i += NT) P[i] = p.Pm[chunk_off(p, b, h, n, C * C) + i];
+    for (int i = threadIdx.x; i < C * C; i += NT) P[(i / C) * LC + i % C] = p.Pm[chunk_off(p, b, h, n, C * C) + i];
     for (int c = threadIdx.x; c < DK; c += NT) gc[c] = p.gC[chunk_off(p, b, h, n, DK) + c];
     __syncthreads();
     // dU = P^T dO + Kh dS
-    mm<C, DK, C, true, false>(dU, DK, P, C, dO, DK, 1.f, false);
+    mm<C, VS, C, true, false>(dU, LV, P, LC, dO, LV, 1.f, false);
     __syncthreads();
-    mm<C, DK, DK, false, false>(dU, DK, X, DK, dS, DK, 1.f, true);
+    mm<C, VS, DK, false, false>(dU, LV, X, L, dS, LV, 1.f, true);
     __syncthreads();
-    for (int i = threadIdx.x; i < C * DK; i += NT) X[i] = p.Qg[co + i];
+    for (int i = threadIdx.x; i < C * DK; i += NT) X[(i / DK) * L + i % DK] = p.Qg[co + i];
     __syncthreads();
     // T2 = Qg^T dO - Wt^T dU
-    mm<DK, DK, C, true, false>(T2, DK, X, DK, dO, DK, 1.f, false);
+    mm<DK, VS, C, true, false>(T2, LV, X, L, dO, LV, 1.f, false);
     __syncthreads();
-    mm<DK, DK, C, true, false>(T2, DK, Wt, DK, dU, DK, -1.f, true);
+    mm<DK, VS, C, true, false>(T2, LV, Wt, L, dU, LV, -1.f, true);
     __syncthreads();
-    for (int e = threadIdx.x; e < DK * DK; e += NT) dS[e] = gc[e / DK] * dS[e] + T2[e];
+    for (int e = threadIdx.x; e < DK * VS; e += NT) {
+      const int r = e / VS, c = e % VS;
+      dS[r * LV + c] = gc[r] * dS[r * LV + c] + T2[r * LV + c];
+    }
     __syncthreads();
   }
 }
@@ -294,183 +335,187 @@ __global__ void __launch_bounds__(NT) state_bwd_kernel(Ptrs p) {
 // ------------------------------------------------------------------ intra bwd
 template <int DK, int C>
 __global__ void __launch_bounds__(NT) intra_bwd_kernel(Ptrs p) {
+  constexpr int L = LDK<DK>(), LC = LDC<C>();
   extern __shared__ float sm[];
-  float* q = sm;                 // C x DK
-  float* k = q + C * DK;
-  float* v = k + C * DK;
-  float* G = v + C * DK;
-  float* dO = G + C * DK;
-  float* Ut = dO + C * DK;       // -> U
-  float* Wt = Ut + C * DK;
-  float* X = Wt + C * DK;        // dU -> L^-T dU
-  float* Y = X + C * DK;         // dWt -> L^-T dWt
-  float* dq = Y + C * DK;
-  float* dk = dq + C * DK;
-  float* dG = dk + C * DK;
-  float* S0 = dG + C * DK;       // DK x DK
-  float* dSC = S0 + DK * DK;     // DK x DK
-  float* A = dSC + DK * DK;      // C x C
-  float* P = A + C * C;          // C x C -> dP
-  float* dA = P + C * C;         // C x C
-  float* bet = dA + C * C;       // C
-  float* db2 = bet + C;          // C
-  float* dbt = db2 + C;          // C
+  float* q = sm;                 // C x L each
+  float* k = q + C * L;
+  float* v = k + C * L;          // v, later dv
+  float* G = v + C * L;
+  float* dO = G + C * L;
+  float* Ut = dO + C * L;
+  float* Wt = Ut + C * L;
+  float* X = Wt + C * L;         // dU -> L^-T dU
+  float* Y = X + C * L;          // dWt -> L^-T dWt
+  float* U = Y + C * L;          // U, later dq accumulator
+  float* dk = U + C * L;
+  float* dG = dk + C * L;
+  float* Kh = dG + C * L;        // k e^{G_C - G}
+  float* S0 = Kh + C * L;        // DK x L
+  float* dSC = S0 + DK * L;      // DK x L
+  float* A = dSC + DK * L;       // C x LC
+  float* P = A + C * LC;         // C x LC -> dP
+  float* dA = P + C * LC;        // C x LC
+  float* bet = dA + C * LC;      // C
+  float* dbt = bet + C;          // C
   float* red = dbt + C;          // DK  (dG_C accumulation)
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const float scale = p.scale;
   load_chunk<DK, C>(p, b, h, n, q, k, v, G, bet);
   const long long so = chunk_off(p, b, h, n, DK * DK);
   for (int i = threadIdx.x; i < DK * DK; i += NT) {
-    S0[i] = p.states[so + i];
-    dSC[i] = p.dstates[so + i];
+    const int r = i / DK, c = i % DK;
+    S0[r * L + c] = p.states[so + i];
+    dSC[r * L + c] = p.dstates[so + i];
   }
   for (int i = threadIdx.x; i < C * DK; i += NT) {
     const int r = i / DK, c = i % DK;
     const int t = n * C + r;
-    dO[i] = t < p.S ? p.dout[tok_off(p, b, t, h, DK) + c] : 0.f;
+    dO[r * L + c] = t < p.S ? p.dout[tok_off(p, b, t, h, DK) + c] : 0.f;
   }
+  for (int c = threadIdx.x; c < DK; c += NT) red[c] = 0.f;
   __syncthreads();
   pair_products<DK, C>(q, k, G, A, P, scale);
+  const float* GC = G + (C - 1) * L;
   for (int i = threadIdx.x; i < C * DK; i += NT) {
-    const int r = i / DK;
-    Ut[i] = bet[r] * v[i];
-    Wt[i] = bet[r] * bet[r] * k[i] * __expf(G[i]);
+    const int r = i / DK, c = i % DK;
+    const int si = r * L + c;
+    Ut[si] = bet[r] * v[si];
+    Wt[si] = bet[r] * bet[r] * k[si] * __expf(G[si]);
+    Kh[si] = k[si] * __expf(GC[c] - G[si]);
   }
   __syncthreads();
-  solve_lower<C>(Ut, DK, DK, A, bet);
-  solve_lower<C>(Wt, DK, DK, A, bet);
-  // U = Ut - Wt S0 (Ut keeps Ut for dL, store U into dq temporarily)
-  float* U = dq;
-  for (int i = threadIdx.x; i < C * DK; i += NT) U[i] = Ut[i];
+  solve_lower2<DK, C>(Ut, Wt, A, bet);
+  // U = Ut - Wt S0
+  for (int i = threadIdx.x; i < C * DK; i += NT) U[(i / DK) * L + i % DK] = Ut[(i / DK) * L + i % DK];
   __syncthreads();
-  mm<C, DK, DK, false, false>(U, DK, Wt, DK, S0, DK, -1.f, true);
+  mm<C, DK, DK, false, false>(U, L, Wt, L, S0, L, -1.f, true);
+  // dU = P^T dO + Kh dS_C
+  mm<C, DK, C, true, false>(X, L, P, LC, dO, L, 1.f, false);
   __syncthreads();
-  // dU = P^T dO + Kh dS_C, Kh = k e^{G_C - G}  (X)
-  const float* GC = G + (C - 1) * DK;
-  mm<C, DK, C, true, false>(X, DK, P, C, dO, DK, 1.f, false);
-  __syncthreads();
-  for (int e = threadIdx.x; e < C * DK; e += NT) {
-    const int t = e / DK, vv = e % DK;
-    float s = 0.f;
-    for (int c = 0; c < DK; ++c) s += k[t * DK + c] * __expf(GC[c] - G[t * DK + c]) * dSC[c * DK + vv];
-    X[e] += s;
-  }
+  mm<C, DK, DK, false, false>(X, L, Kh, L, dSC, L, 1.f, true);
+  // dWt = -dU S0^T needs the final dU: after the barrier below
   __syncthreads();
   // dP = dO U^T (masked s <= t), into P
   for (int e = threadIdx.x; e < C * C; e += NT) {
     const int t = e / C, s = e % C;
     float acc = 0.f;
     if (s <= t)
-      for (int vv = 0; vv < DK; ++vv) acc += dO[t * DK + vv] * U[s * DK + vv];
-    P[e] = acc;
+      for (int vv = 0; vv < DK; ++vv) acc += dO[t * L + vv] * U[s * L + vv];
+    P[t * LC + s] = acc;
   }
-  // dWt = -dU S0^T into Y ; dKh = U dS_C^T (into dk, later scaled) ; dQg = dO S0^T (into dG tmp)
-  mm<C, DK, DK, false, true>(Y, DK, X, DK, S0, DK, -1.f, false);
-  __syncthreads();
-  // dk <- dKh * e^{G_C-G} ;  dG <- -dKh*Kh ;  red <- sum_t dKh*Kh
-  for (int c = threadIdx.x; c < DK; c += NT) red[c] = 0.f;
-  __syncthreads();
+  mm<C, DK, DK, false, true>(Y, L, X, L, S0, L, -1.f, false);
+  // dKh = U dS_C^T:  dk = dKh e^{G_C-G};  dG = -dKh Kh;  red += dKh Kh
   for (int e = threadIdx.x; e < C * DK; e += NT) {
     const int t = e / DK, c = e % DK;
     float s = 0.f;
-    for (int vv = 0; vv < DK; ++vv) s += U[t * DK + vv] * dSC[c * DK + vv];
-    const float dec = __expf(GC[c] - G[e]);
-    const float kh = k[e] * dec;
-    dk[e] = s * dec;
-    dG[e] = -s * kh;
+    for (int vv = 0; vv < DK; ++vv) s += U[t * L + vv] * dSC[c * L + vv];
+    const int si = t * L + c;
+    const float kh = Kh[si];
+    dk[si] = s * __expf(GC[c] - G[si]);
+    dG[si] = -s * kh;
     atomicAdd(&red[c], s * kh);
   }
   __syncthreads();
-  // dQg = dO S0^T:  dq += scale dQg e^G ; dG += dQg * Qg
+  // dQg = dO S0^T:  dq = scale dQg e^G (into U);  dG += dQg * scale q e^G
   for (int e = threadIdx.x; e < C * DK; e += NT) {
     const int t = e / DK, c = e % DK;
     float s = 0.f;
-    for (int vv = 0; vv < DK; ++vv) s += dO[t * DK + vv] * S0[c * DK + vv];
-    const float eg = __expf(G[e]);
-    dG[e] += s * scale * q[e] * eg;
-    U[e] = s * scale * eg;  // U no longer needed after dP/dKh: reuse as dq accumulator
+    for (int vv = 0; vv < DK; ++vv) s += dO[t * L + vv] * S0[c * L + vv];
+    const int si = t * L + c;
+    const float eg = __expf(G[si]);
+    dG[si] += s * scale * q[si] * eg;
+    U[si] = s * scale * eg;
   }
   __syncthreads();
   float* dqa = U;
   // X <- L^{-T} dU ; Y <- L^{-T} dWt
-  solve_upper_t<C>(X, DK, DK, A, bet);
-  solve_upper_t<C>(Y, DK, DK, A, bet);
-  // dL_ts = -(X Ut^T + Y Wt^T)_ts (s<t) ; dA = b_t^2 dL ; db2_t = sum_s A dL + sum_c Kg Y
+  solve_upper_t2<DK, C>(X, Y, A, bet);
+  // dL_ts = -(X Ut^T + Y Wt^T)_ts (s<t)
   for (int e = threadIdx.x; e < C * C; e += NT) {
     const int t = e / C, s = e % C;
     float dl = 0.f;
-    if (s < t) {
-      for (int c = 0; c < DK; ++c) dl -= X[t * DK + c] * Ut[s * DK + c] + Y[t * DK + c] * Wt[s * DK + c];
+    if (s < t)
+      for (int c = 0; c < DK; ++c) dl -= X[t * L + c] * Ut[s * L + c] + Y[t * L + c] * Wt[s * L + c];
+    dA[t * LC + s] = dl;  // dL for now
+  }
+  __syncthreads();
+  // db2_t = sum_s A dL + sum_c Kg Y;  dbeta_t = V . X + 2 b_t db2_t   (one warp per t)
+  {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int t = warp; t < C; t += NT / 32) {
+      float s1 = 0.f, s2 = 0.f, s3 = 0.f;
+      for (int s = lane; s < t; s += 32) s1 += A[t * LC + s] * dA[t * LC + s];
+      for (int c = lane; c < DK; c += 32) {
+        const int si = t * L + c;
+        s2 += k[si] * __expf(G[si]) * Y[si];
+        s3 += v[si] * X[si];
+      }
+      s1 = warp_sum(s1);
+      s2 = warp_sum(s2);
+      s3 = warp_sum(s3);
+      if (lane == 0) dbt[t] = s3 + 2.f * bet[t] * (s1 + s2);
     }
-    dA[e] = dl;  // holds dL for now
   }
   __syncthreads();
-  for (int t = threadIdx.x; t < C; t += NT) {
-    float s1 = 0.f, s2 = 0.f, s3 = 0.f;
-    for (int s = 0; s < t; ++s) s1 += A[t * C + s] * dA[t * C + s];
-    for (int c = 0; c < DK; ++c) {
-      s2 += k[t * DK + c] * __expf(G[t * DK + c]) * Y[t * DK + c];  // Kg . Y
-      s3 += v[t * DK + c] * X[t * DK + c];                          // V . X
-    }
-    db2[t] = s1 + s2;
-    dbt[t] = s3 + 2.f * bet[t] * (s1 + s2);
+  for (int e = threadIdx.x; e < C * C; e += NT) {
+    const int t = e / C, s = e % C;
+    dA[t * LC + s] *= bet[t] * bet[t];
   }
-  __syncthreads();
-  for (int e = threadIdx.x; e < C * C; e += NT) dA[e] *= bet[e / C] * bet[e / C];
-  // dv = b X ; dKg = b^2 Y: dk += dKg e^G, dG += dKg Kg
-  for (int e = threadIdx.x; e < C * DK; e += NT) {
-    const int t = e / DK;
-    const float eg = __expf(G[e]);
-    const float dkg = bet[t] * bet[t] * Y[e];
-    dk[e] += dkg * eg;
-    dG[e] += dkg * k[e] * eg;
-    v[e] = bet[t] * X[e];  // v buffer now holds dv
-  }
-  __syncthreads();
-  // pairwise terms (t-side): dq_t += sum_{s<=t} dP_ts scale? (P carries scale: dPm = dP)
-  //   dq_t[c] += scale * sum_s dP_ts k_s e_ts ;  dk_t[c] += sum_{s<t} dA_ts k_s e_ts
-  //   dG_t[c] += q_t[c]*(P-part) + k_t[c]*(A-part)
+  // dv = b X ; dKg = b^2 Y: dk += dKg e^G, dG += dKg k e^G
   for (int e = threadIdx.x; e < C * DK; e += NT) {
     const int t = e / DK, c = e % DK;
-    const float gt = G[e];
+    const int si = t * L + c;
+    const float eg = __expf(G[si]);
+    const float dkg = bet[t] * bet[t] * Y[si];
+    dk[si] += dkg * eg;
+    dG[si] += dkg * k[si] * eg;
+    v[si] = bet[t] * X[si];
+  }
+  __syncthreads();
+  // t-side pairwise terms: dq_t += scale sum_{s<=t} dP_ts k_s e_ts ; dk_t += sum_{s<t} dA_ts k_s e_ts
+  for (int e = threadIdx.x; e < C * DK; e += NT) {
+    const int t = e / DK, c = e % DK;
+    const int si = t * L + c;
+    const float gt = G[si];
     float sp = 0.f, sa = 0.f;
     for (int s = 0; s <= t; ++s) {
-      const float ks = k[s * DK + c] * __expf(gt - G[s * DK + c]);
-      sp += P[t * C + s] * ks;
-      sa += dA[t * C + s] * ks;
+      const float ks = k[s * L + c] * __expf(gt - G[s * L + c]);
+      sp += P[t * LC + s] * ks;
+      sa += dA[t * LC + s] * ks;
     }
     sp *= scale;
-    dqa[e] += sp;
-    dk[e] += sa;
-    dG[e] += q[e] * sp + k[e] * sa;
+    dqa[si] += sp;
+    dk[si] += sa;
+    dG[si] += q[si] * sp + k[si] * sa;
   }
   __syncthreads();
   // s-side: dk_s[c] += sum_{t>=s} (scale dP_ts q_t + dA_ts k_t) e_ts ; dG_s -= k_s * that
   for (int e = threadIdx.x; e < C * DK; e += NT) {
     const int s = e / DK, c = e % DK;
-    const float gs = G[e];
+    const int si = s * L + c;
+    const float gs = G[si];
     float acc = 0.f;
     for (int t = s; t < C; ++t) {
-      const float ee = __expf(G[t * DK + c] - gs);
-      acc += (scale * P[t * C + s] * q[t * DK + c] + dA[t * C + s] * k[t * DK + c]) * ee;
+      const float ee = __expf(G[t * L + c] - gs);
+      acc += (scale * P[t * LC + s] * q[t * L + c] + dA[t * LC + s] * k[t * L + c]) * ee;
     }
-    dk[e] += acc;
-    dG[e] -= k[e] * acc;
+    dk[si] += acc;
+    dG[si] -= k[si] * acc;
   }
   __syncthreads();
   // dG_C += red + dgC * gC, dgC[c] = sum_v dS_C[c][v] S0[c][v]
   for (int c = threadIdx.x; c < DK; c += NT) {
     float s = 0.f;
-    for (int vv = 0; vv < DK; ++vv) s += dSC[c * DK + vv] * S0[c * DK + vv];
-    dG[(C - 1) * DK + c] += red[c] + s * __expf(GC[c]);
+    for (int vv = 0; vv < DK; ++vv) s += dSC[c * L + vv] * S0[c * L + vv];
+    dG[(C - 1) * L + c] += red[c] + s * __expf(GC[c]);
   }
   __syncthreads();
   // dg = reverse cumsum of dG; write outputs
   for (int c = threadIdx.x; c < DK; c += NT) {
     float s = 0.f;
     for (int r = C - 1; r >= 0; --r) {
-      s += dG[r * DK + c];
-      dG[r * DK + c] = s;
+      s += dG[r * L + c];
+      dG[r * L + c] = s;
     }
   }
   __syncthreads();
@@ -479,10 +524,11 @@ __global__ void __launch_bounds__(NT) intra_bwd_kernel(Ptrs p) {
     const int t = n * C + r;
     if (t >= p.S) continue;
     const long long o = tok_off(p, b, t, h, DK) + c;
-    p.dq[o] = dqa[i];
-    p.dk[o] = dk[i];
-    p.dv[o] = v[i];
-    p.dg[o] = dG[i];
+    const int si = r * L + c;
+    p.dq[o] = dqa[si];
+    p.dk[o] = dk[si];
+    p.dv[o] = v[si];
+    p.dg[o] = dG[si];
   }
   for (int r = threadIdx.x; r < C; r += NT) {
     const int t = n * C + r;
@@ -491,13 +537,19 @@ __global__ void __launch_bounds__(NT) intra_bwd_kernel(Ptrs p) {
 }
 
 template <int DK, int C>
-constexpr int intra_fwd_smem() { return (5 * C * DK + 2 * C * C + C) * 4; }
+constexpr int intra_fwd_smem() { return (5 * C * LDK<DK>() + 2 * C * LDC<C>() + C) * 4; }
+template <int DK, int C, int VS>
+constexpr int state_fwd_smem() {
+  return (DK * (VS + 1) + 2 * C * (VS + 1) + 2 * C * LDK<DK>() + C * LDC<C>() + DK) * 4;
+}
+template <int DK, int C, int VS>
+constexpr int state_bwd_smem() {
+  return (2 * DK * (VS + 1) + 2 * C * (VS + 1) + 2 * C * LDK<DK>() + C * LDC<C>() + DK) * 4;
+}
 template <int DK, int C>
-constexpr int state_fwd_smem() { return (DK * DK + 4 * C * DK + C * C + DK) * 4; }
-template <int DK, int C>
-constexpr int state_bwd_smem() { return (2 * DK * DK + 4 * C * DK + C * C + DK) * 4; }
-template <int DK, int C>
-constexpr int intra_bwd_smem() { return (12 * C * DK + 2 * DK * DK + 3 * C * C + 3 * C + DK) * 4; }
+constexpr int intra_bwd_smem() {
+  return (13 * C * LDK<DK>() + 2 * DK * LDK<DK>() + 3 * C * LDC<C>() + 2 * C + DK) * 4;
+}
 
 // ================================================================ front-end
 // One warp per (token, head).  raw: [T, 3*HK] bf16 rows (q | k | v projections);
@@ -760,16 +812,17 @@ void kda_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
   KDA_DISPATCH(DKV, {
     p.NC = (p.S + C - 1) / C;
     HB_CHECK(Pm.size(-1) == C, "kda_fwd: scratch chunk size mismatch");
-    const int s1 = kda::intra_fwd_smem<DK, C>(), s2 = kda::state_fwd_smem<DK, C>();
+    constexpr int VS = DK >= 32 ? 16 : DK;
+    const int s1 = kda::intra_fwd_smem<DK, C>(), s2 = kda::state_fwd_smem<DK, C, VS>();
     static bool cfg = false;
     if (!cfg) {
       set_smem((const void*)kda::intra_fwd_kernel<DK, C>, s1);
-      set_smem((const void*)kda::state_fwd_kernel<DK, C>, s2);
+      set_smem((const void*)kda::state_fwd_kernel<DK, C, VS>, s2);
       cfg = true;
     }
     kda::intra_fwd_kernel<DK, C><<<dim3(p.NC, p.H, p.B), kda::NT, s1, cur_stream()>>>(p);
     HB_CUDA_CHECK(cudaGetLastError());
-    kda::state_fwd_kernel<DK, C><<<dim3(p.H, p.B), kda::NT, s2, cur_stream()>>>(p);
+    kda::state_fwd_kernel<DK, C, VS><<<dim3(DK / VS, p.H, p.B), kda::NT, s2, cur_stream()>>>(p);
     HB_CUDA_CHECK(cudaGetLastError());
   })
 }
@@ -805,14 +858,15 @@ void kda_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
   HB_CHECK(dout.is_contiguous(), "kda_bwd: contiguous dout");
   KDA_DISPATCH(DKV, {
     p.NC = (p.S + C - 1) / C;
-    const int s1 = kda::state_bwd_smem<DK, C>(), s2 = kda::intra_bwd_smem<DK, C>();
+    constexpr int VS = DK >= 32 ? 16 : DK;
+    const int s1 = kda::state_bwd_smem<DK, C, VS>(), s2 = kda::intra_bwd_smem<DK, C>();
     static bool cfg = false;
     if (!cfg) {
-      set_smem((const void*)kda::state_bwd_kernel<DK, C>, s1);
+      set_smem((const void*)kda::state_bwd_kernel<DK, C, VS>, s1);
       set_smem((const void*)kda::intra_bwd_kernel<DK, C>, s2);
       cfg = true;
     }
-    kda::state_bwd_kernel<DK, C><<<dim3(p.H, p.B), kda::NT, s1, cur_stream()>>>(p);
+    kda::state_bwd_kernel<DK, C, VS><<<dim3(DK / VS, p.H, p.B), kda::NT, s1, cur_stream()>>>(p);
     HB_CUDA_CHECK(cudaGetLastError());
     kda::intra_bwd_kernel<DK, C><<<dim3(p.NC, p.H, p.B), kda::NT, s2, cur_stream()>>>(p);
     HB_CUDA_CHECK(cudaGetLastError());

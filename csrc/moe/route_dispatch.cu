@@ -25,56 +25,66 @@ constexpr int MAXN = 256;  // experts
 constexpr int MAXK = 16;   // top-k
 
 // ------------------------------------------------------------------ router fwd
-// One warp per token; lane e handles experts e, e+32, ... (N <= 256).
-// W_r [D, N] fp32 staged in shared memory in chunks of 64 rows.
+// Block = RT_TOK consecutive tokens.  The router weight W_r [D, N] is staged in
+// shared memory in row chunks of DC rows (the whole matrix when it fits) and
+// every token's logits are accumulated in a shared [RT_TOK][N] array; one warp
+// per token, lane e owns experts e, e+32, ...
+constexpr int RT_TOK = 64;
+constexpr int RT_SMEM_W = 160 * 1024;
+
 __global__ void router_fwd_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ W,
                                   const float* __restrict__ bias, int T, int S, int D, int N, int K,
-                                  int softmax_mode, float scaling, float* __restrict__ logits_out,
+                                  int softmax_mode, float scaling, int DC, float* __restrict__ logits_out,
                                   int* __restrict__ topi, float* __restrict__ topw,
                                   float* __restrict__ seq_counts, float* __restrict__ seq_probs,
                                   float* __restrict__ sums /* [0]=sum lse^2, [1]=sum entropy */) {
-  extern __shared__ float wsh[];  // [64][N]
+  extern __shared__ float sh[];
+  float* wsh = sh;              // [DC][N]
+  float* acc = sh + DC * N;     // [RT_TOK][N]
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int warps = blockDim.x >> 5;
   const int EPL = (N + 31) / 32;  // experts per lane (<= 8)
-  // Each block handles a contiguous token range.
-  const int per_block = (T + gridDim.x - 1) / gridDim.x;
-  const int t_begin = blockIdx.x * per_block;
-  const int t_end = min(T, t_begin + per_block);
-  float zsum = 0.f, esum = 0.f;
-  // tokens processed in groups of `warps` (one per warp); W streamed per group
-  for (int t0 = t_begin; t0 < t_end; t0 += warps) {
-    const int t = t0 + warp;
-    float acc[8];
+  const int t_begin = blockIdx.x * RT_TOK;
+  const int t_end = min(T, t_begin + RT_TOK);
+  for (int i = threadIdx.x; i < RT_TOK * N; i += blockDim.x) acc[i] = 0.f;
+  for (int d0 = 0; d0 < D; d0 += DC) {
+    const int dn = min(DC, D - d0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < dn * N; i += blockDim.x) wsh[i] = W[(long long)d0 * N + i];
+    __syncthreads();
+    for (int t = t_begin + warp; t < t_end; t += warps) {
+      float a[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-    for (int d0 = 0; d0 < D; d0 += 64) {
-      __syncthreads();
-      for (int i = threadIdx.x; i < 64 * N; i += blockDim.x) {
-        const int r = i / N, c = i % N;
-        wsh[i] = (d0 + r < D) ? W[(long long)(d0 + r) * N + c] : 0.f;
-      }
-      __syncthreads();
-      if (t < t_end) {
-        const float xa = (d0 + lane < D) ? __bfloat162float(x[(long long)t * D + d0 + lane]) : 0.f;
-        const float xb = (d0 + 32 + lane < D) ? __bfloat162float(x[(long long)t * D + d0 + 32 + lane]) : 0.f;
-        for (int r = 0; r < 64; ++r) {
-          const float xv = __shfl_sync(0xffffffffu, r < 32 ? xa : xb, r & 31);
+      for (int i = 0; i < 8; ++i) a[i] = 0.f;
+      const __nv_bfloat16* xr = x + (long long)t * D + d0;
+      for (int r0 = 0; r0 < dn; r0 += 32) {
+        const float xv_l = (r0 + lane < dn) ? __bfloat162float(xr[r0 + lane]) : 0.f;
+        const int rn = min(32, dn - r0);
+        for (int r = 0; r < rn; ++r) {
+          const float xv = __shfl_sync(0xffffffffu, xv_l, r);
+          const float* wr = wsh + (r0 + r) * N;
 #pragma unroll
           for (int i = 0; i < 8; ++i)
-            if (i < EPL && lane + 32 * i < N) acc[i] += xv * wsh[r * N + lane + 32 * i];
+            if (i < EPL && lane + 32 * i < N) a[i] += xv * wr[lane + 32 * i];
         }
       }
+      float* ar = acc + (t - t_begin) * N;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (i < EPL && lane + 32 * i < N) ar[lane + 32 * i] += a[i];
     }
-    if (t >= t_end) continue;
-    // scores
+  }
+  __syncthreads();
+  float zsum = 0.f, esum = 0.f;
+  for (int t = t_begin + warp; t < t_end; t += warps) {
+    const float* ar = acc + (t - t_begin) * N;
     float lg[8], sc[8], ef[8];
     float mx = -INFINITY;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int e = lane + 32 * i;
-      lg[i] = (i < EPL && e < N) ? acc[i] : -INFINITY;
+      lg[i] = (i < EPL && e < N) ? ar[e] : -INFINITY;
       if (i < EPL && e < N) {
         logits_out[(long long)t * N + e] = lg[i];
         mx = fmaxf(mx, lg[i]);
@@ -101,7 +111,6 @@ __global__ void router_fwd_kernel(const __nv_bfloat16* __restrict__ x, const flo
       }
     }
     ssum = warp_sum(ssum);
-    // entropy of probs = s / (sum s + 1e-9)
     float ent = 0.f;
     const float inv = 1.f / (ssum + 1e-9f);
     const int b = t / S;
@@ -109,9 +118,9 @@ __global__ void router_fwd_kernel(const __nv_bfloat16* __restrict__ x, const flo
     for (int i = 0; i < 8; ++i) {
       const int e = lane + 32 * i;
       if (i < EPL && e < N) {
-        const float p = sc[i] * inv;
-        ent -= p * __logf(p + 1e-9f);
-        atomicAdd(seq_probs + (long long)b * N + e, p);
+        const float pr = sc[i] * inv;
+        ent -= pr * __logf(pr + 1e-9f);
+        atomicAdd(seq_probs + (long long)b * N + e, pr);
       }
     }
     ent = warp_sum(ent);
@@ -119,7 +128,7 @@ __global__ void router_fwd_kernel(const __nv_bfloat16* __restrict__ x, const flo
     float selsum = 0.f;
     float selv[MAXK];
     int seli[MAXK];
-    for (int k = 0; k < K; ++k) {
+    for (int kk = 0; kk < K; ++kk) {
       float bv = -INFINITY;
       int bi = 0x7fffffff;
 #pragma unroll
@@ -139,7 +148,6 @@ __global__ void router_fwd_kernel(const __nv_bfloat16* __restrict__ x, const flo
           bi = oi;
         }
       }
-      // score of the winner
       float s_win = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i)
@@ -148,16 +156,16 @@ __global__ void router_fwd_kernel(const __nv_bfloat16* __restrict__ x, const flo
           ef[i] = -INFINITY;
         }
       s_win = warp_sum(s_win);
-      seli[k] = bi;
-      selv[k] = s_win;
+      seli[kk] = bi;
+      selv[kk] = s_win;
       selsum += s_win;
     }
     if (lane == 0) {
       const float denom = selsum + 1e-9f;
-      for (int k = 0; k < K; ++k) {
-        topi[(long long)t * K + k] = seli[k];
-        topw[(long long)t * K + k] = selv[k] / denom * (softmax_mode ? 1.f : scaling);
-        atomicAdd(seq_counts + (long long)b * N + seli[k], 1.f);
+      for (int kk = 0; kk < K; ++kk) {
+        topi[(long long)t * K + kk] = seli[kk];
+        topw[(long long)t * K + kk] = selv[kk] / denom * (softmax_mode ? 1.f : scaling);
+        atomicAdd(seq_counts + (long long)b * N + seli[kk], 1.f);
       }
       zsum += lse * lse;
       esum += ent;
@@ -263,31 +271,46 @@ __global__ void router_bwd_kernel(const float* __restrict__ logits, const int* _
 }
 
 // ------------------------------------------------------------------ router grads
-// dx[t, d] (+)= sum_e dl[t, e] * W[d, e];  one warp per token, W in smem chunks.
+// dx[t, d] (+)= sum_e dl[t, e] * W[d, e].  W is staged expert-major
+// (wsh[e][d], d contiguous) so lanes read consecutive addresses; one warp per
+// token, lane owns d = lane + 32 j; the token's dl row is held in registers.
 __global__ void router_dx_kernel(const float* __restrict__ dl, const float* __restrict__ W,
-                                 float* __restrict__ dx, int T, int D, int N) {
-  extern __shared__ float wsh[];  // [128][N]
+                                 float* __restrict__ dx, int T, int D, int N, int DCH) {
+  extern __shared__ float wsh[];  // [N][DCH]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
-  const int per_block = (T + gridDim.x - 1) / gridDim.x;
-  const int tb = blockIdx.x * per_block, te = min(T, tb + per_block);
-  for (int d0 = 0; d0 < D; d0 += 128) {
+  const int tb = blockIdx.x * RT_TOK, te = min(T, tb + RT_TOK);
+  const int EPL = (N + 31) / 32;
+  for (int d0 = 0; d0 < D; d0 += DCH) {
+    const int dn = min(DCH, D - d0);
     __syncthreads();
-    for (int i = threadIdx.x; i < 128 * N; i += blockDim.x) {
-      const int r = i / N, c = i % N;
-      wsh[i] = (d0 + r < D) ? W[(long long)(d0 + r) * N + c] : 0.f;
+    for (int i = threadIdx.x; i < dn * N; i += blockDim.x) {
+      const int d = i / N, e = i % N;
+      wsh[e * DCH + d] = W[(long long)(d0 + d) * N + e];
     }
     __syncthreads();
     for (int t = tb + warp; t < te; t += warps) {
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int e = 0; e < N; ++e) {
-        const float g = dl[(long long)t * N + e];
+      float g[8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[j] += g * wsh[(lane + 32 * j) * N + e];
-      }
+      for (int i = 0; i < 8; ++i) g[i] = (i < EPL && lane + 32 * i < N) ? dl[(long long)t * N + lane + 32 * i] : 0.f;
+      for (int c0 = 0; c0 < dn; c0 += 128) {
+        float a[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int e = 0; e < N; ++e) {
+          const int gi = e >> 5;
+          float src = g[0];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int d = d0 + lane + 32 * j;
-        if (d < D) dx[(long long)t * D + d] += acc[j];
+          for (int i = 1; i < 8; ++i)
+            if (gi == i) src = g[i];
+          const float ge = __shfl_sync(0xffffffffu, src, e & 31);
+          const float* wr = wsh + e * DCH + c0;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (c0 + lane + 32 * j < dn) a[j] += ge * wr[lane + 32 * j];
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int d = d0 + c0 + lane + 32 * j;
+          if (c0 + lane + 32 * j < dn) dx[(long long)t * D + d] += a[j];
+        }
       }
     }
   }
@@ -513,16 +536,18 @@ void router_fwd(torch::Tensor x, torch::Tensor W, torch::Tensor bias, int64_t S,
   const int T = x.size(0), D = x.size(1), N = W.size(1);
   HB_CHECK(N <= MAXN && K <= MAXK && K <= N, "router: N <= 256, K <= 16");
   if (T == 0) return;
-  const int grid = std::min((T + 7) / 8, num_sms() * 2);
-  const size_t smem = 64 * N * sizeof(float);
+  const int grid = (T + RT_TOK - 1) / RT_TOK;
+  const int DC = std::max(32, std::min(D, (int)(RT_SMEM_W / (N * sizeof(float)))) / 32 * 32);
+  const size_t smem = (size_t)(DC * N + RT_TOK * N) * sizeof(float);
   static bool cfg = false;
   if (!cfg) {
-    HB_CUDA_CHECK(cudaFuncSetAttribute(router_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * MAXN * 4));
+    HB_CUDA_CHECK(cudaFuncSetAttribute(router_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       RT_SMEM_W + RT_TOK * MAXN * 4));
     cfg = true;
   }
   router_fwd_kernel<<<grid, 256, smem, cur_stream()>>>(
       (const __nv_bfloat16*)x.data_ptr(), W.data_ptr<float>(), bias.data_ptr<float>(), T, (int)S, D,
-      N, (int)K, softmax_mode ? 1 : 0, (float)scaling, logits.data_ptr<float>(), topi.data_ptr<int>(),
+      N, (int)K, softmax_mode ? 1 : 0, (float)scaling, DC, logits.data_ptr<float>(), topi.data_ptr<int>(),
       topw.data_ptr<float>(), seq_counts.data_ptr<float>(), seq_probs.data_ptr<float>(),
       sums.data_ptr<float>());
   HB_CUDA_CHECK(cudaGetLastError());
@@ -545,12 +570,13 @@ void router_grads(torch::Tensor x, torch::Tensor W, torch::Tensor dl, torch::Ten
   {
     static bool cfg = false;
     if (!cfg) {
-      HB_CUDA_CHECK(cudaFuncSetAttribute(router_dx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * MAXN * 4));
+      HB_CUDA_CHECK(cudaFuncSetAttribute(router_dx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, RT_SMEM_W));
       cfg = true;
     }
-    const int grid = std::min((T + 7) / 8, num_sms() * 2);
-    router_dx_kernel<<<grid, 256, 128 * N * 4, cur_stream()>>>(dl.data_ptr<float>(), W.data_ptr<float>(),
-                                                               dx.data_ptr<float>(), T, D, N);
+    const int DCH = std::max(128, std::min(D, (int)(RT_SMEM_W / (N * sizeof(float)))) / 128 * 128);
+    const int grid = (T + RT_TOK - 1) / RT_TOK;
+    router_dx_kernel<<<grid, 256, (size_t)N * DCH * 4, cur_stream()>>>(
+        dl.data_ptr<float>(), W.data_ptr<float>(), dx.data_ptr<float>(), T, D, N, DCH);
     HB_CUDA_CHECK(cudaGetLastError());
   }
   {

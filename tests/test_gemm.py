@@ -15,7 +15,8 @@ def _rel_err(x, ref):
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 200, 136), (304, 200, 136), (1024, 1024, 1024),
-                                   (4096, 768, 1024), (77, 64, 520), (2048, 3072, 512)])
+                                   (4096, 768, 1024), (77, 64, 520), (2048, 3072, 512),
+                                   (256, 256, 8192), (1024, 64, 20000)])
 @pytest.mark.parametrize("ta,tb", [(False, False), (False, True), (True, False), (True, True)])
 def test_dense_gemm(M, N, K, ta, tb):
     # TMA needs 16-byte row strides: the contiguous dimension of each operand
