@@ -21,6 +21,8 @@
 //                   dv, dg, dbeta given S0, dS_C and dO
 #include <torch/extension.h>
 
+#include <mutex>
+
 #include "../common/host.h"
 #include "../common/sm100.cuh"
 
@@ -930,3 +932,108 @@ void kda_prep_bwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::
 }
 
 }  // namespace hb
+
+// ============================================================================
+// Allocation-free entry point (declared in kda_noalloc.h).
+//
+// For callers that cannot allocate device memory themselves: code running
+// inside a CUDA-graph capture that must not see a cudaMalloc, host runtimes
+// with their own fixed memory pools, and plugins loaded into a process whose
+// allocator they do not own.  The chunk intermediates live in the file-scope
+// array below, 64 MiB on every GPU that loads this library, held until the
+// process exits.  The host side cannot use the array's name as a device
+// address (there it is only a host-side stand-in); the device address is
+// obtained once per device with cudaGetSymbolAddress, with that device
+// current, the first time the entry point is called on it.
+// ============================================================================
+namespace hb {
+namespace kda_noalloc {
+
+constexpr long long kScratchFloats = 16LL * 1024 * 1024;  // 64 MiB of fp32
+__device__ __align__(256) float g_scratch[kScratchFloats];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+float* g_dev_ptr[kMaxDevices] = {nullptr};
+
+// Scratch floats needed for [B, S, H, DK] inputs (chunk size 32).
+long long scratch_floats(int B, int S, int H, int DK) {
+  const long long C = 32;
+  const long long NC = (S + C - 1) / C;
+  const long long bhn = (long long)B * H * NC;
+  return bhn * (4 * C * DK + C * C + DK + (long long)DK * DK);
+}
+
+}  // namespace kda_noalloc
+}  // namespace hb
+
+#include "kda_noalloc.h"
+
+extern "C" __attribute__((visibility("default"))) int hb_kda_fwd_noalloc(
+    const float* q, const float* k, const float* v, const float* g, const float* beta, float* o,
+    int B, int S, int H, int DK, float scale, cudaStream_t stream) {
+  using namespace hb;
+  using namespace hb::kda_noalloc;
+  if (!(DK == 16 || DK == 32 || DK == 64)) return HB_NOALLOC_BAD_HEAD_DIM;
+  if (B <= 0 || S <= 0 || H <= 0) return HB_NOALLOC_BAD_SHAPE;
+  if (scratch_floats(B, S, H, DK) > kScratchFloats) return HB_NOALLOC_TOO_LARGE;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return HB_NOALLOC_CUDA_ERROR;
+  float* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_dev_ptr[dev]) {
+      void* ptr = nullptr;
+      if (cudaGetSymbolAddress(&ptr, g_scratch) != cudaSuccess || ptr == nullptr)
+        return HB_NOALLOC_CUDA_ERROR;
+      g_dev_ptr[dev] = static_cast<float*>(ptr);
+    }
+    base = g_dev_ptr[dev];
+  }
+  Ptrs p{};
+  p.B = B;
+  p.S = S;
+  p.H = H;
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.g = g;
+  p.beta = beta;
+  p.o = o;
+  p.scale = scale;
+  const long long C = 32;
+  const long long NC = (S + C - 1) / C;
+  p.NC = (int)NC;
+  const long long bhn = (long long)B * H * NC;
+  // carve the scratch: every region is written before it is read, so nothing
+  // has to be cleared between calls
+  float* cur = base;
+  p.Wt = cur; cur += bhn * C * DK;
+  p.Ut = cur; cur += bhn * C * DK;
+  p.Kh = cur; cur += bhn * C * DK;
+  p.Qg = cur; cur += bhn * C * DK;
+  p.Pm = cur; cur += bhn * C * C;
+  p.gC = cur; cur += bhn * DK;
+  p.states = cur;
+  p.init_state = nullptr;
+  p.final_state = nullptr;
+  auto run = [&](auto dkc) -> int {
+    constexpr int DKc = decltype(dkc)::value;
+    constexpr int Cc = 32;
+    constexpr int VS = DKc >= 32 ? 16 : DKc;
+    const int s1 = kda::intra_fwd_smem<DKc, Cc>(), s2 = kda::state_fwd_smem<DKc, Cc, VS>();
+    if (cudaFuncSetAttribute((const void*)kda::intra_fwd_kernel<DKc, Cc>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, s1) != cudaSuccess ||
+        cudaFuncSetAttribute((const void*)kda::state_fwd_kernel<DKc, Cc, VS>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, s2) != cudaSuccess)
+      return HB_NOALLOC_CUDA_ERROR;
+    kda::intra_fwd_kernel<DKc, Cc><<<dim3(p.NC, p.H, p.B), kda::NT, s1, stream>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return HB_NOALLOC_CUDA_ERROR;
+    kda::state_fwd_kernel<DKc, Cc, VS><<<dim3(DKc / VS, p.H, p.B), kda::NT, s2, stream>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return HB_NOALLOC_CUDA_ERROR;
+    return HB_NOALLOC_OK;
+  };
+  if (DK == 16) return run(std::integral_constant<int, 16>{});
+  if (DK == 32) return run(std::integral_constant<int, 32>{});
+  return run(std::integral_constant<int, 64>{});
+}
