@@ -228,6 +228,7 @@ def main():
                        "per_gpu_batch": B, "micro_batch": cfg.micro_batch,
                        "parallelism": f"dp{world}" if world > 1 else "single",
                        "optimizer": cfg.optimizer,
+                       "grad_transport": getattr(trainer.engine, "transport", "local"),
                        "l2": "working set per step is tens of GB (> 126 MB L2); no flush needed"},
             "mfu": mfu, "model_tflop_per_step": model_fl / 1e12,
             "peak_tflops_per_gpu": peak / 1e12, "loss": loss_v,

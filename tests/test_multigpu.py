@@ -1,0 +1,75 @@
+"""Data parallel on 2 GPUs: the fused peer-memory transport (reduce-scatter in a
+kernel reading peers over NVLink, optimizer storing the new weights into every
+peer) must match the NCCL baseline.  Skipped with fewer than 2 GPUs."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, out_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    from hanuman_b200.config import get_config
+    from hanuman_b200.ops._ext import ext
+    from hanuman_b200.parallel.mesh import init_distributed
+    from hanuman_b200.train import Trainer
+    ctx = init_distributed(timeout_s=120)
+    try:
+        res = {}
+        for fused in (False, True):
+            c = get_config("tiny_hybrid").replace(dtype="bf16", batch_size=4, seq_len=128,
+                                                  fused_comm=fused)
+            tr = Trainer(c, dist_ctx=ctx)
+            assert tr.engine.transport == ("p2p" if fused else "nccl")
+            per = c.batch_size // world
+            losses = []
+            for step in range(3):
+                g = torch.Generator().manual_seed(step)
+                toks = torch.randint(0, c.vocab_size, (c.batch_size, c.seq_len), generator=g)
+                losses.append(float(tr.step(toks[rank * per:(rank + 1) * per])))
+            st = tr.engine.master_state()
+            res[fused] = (losses, {k: v.float().cpu() for k, v in st.items()})
+            del tr
+        torch.cuda.synchronize()
+        assert ext().read_status() == 0
+        if rank == 0:
+            torch.save(res, out_path)
+    finally:
+        ctx.shutdown()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_p2p_transport_matches_nccl(tmp_path):
+    ctx = mp.get_context("spawn")
+    port = _port()
+    out = str(tmp_path / "res.pt")
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+        assert p.exitcode == 0
+    res = torch.load(out)
+    (l0, s0), (l1, s1) = res[False], res[True]
+    for a, b in zip(l0, l1):
+        assert abs(a - b) < 1e-3 * abs(a), (l0, l1)
+    # The embedding gradient is summed with atomics, so the two runs differ in the
+    # last bits; AdamW's first steps are sign-like (|update| ~ lr per step), so an
+    # element can move by up to 2 * lr per step between runs (lr = 3e-4, 3 steps).
+    for k in s0:
+        diff = (s0[k] - s1[k]).abs()
+        assert diff.max().item() <= 6 * 3e-4 + 1e-5, (k, diff.max().item())
+        assert diff.mean().item() < 2e-5, (k, diff.mean().item())
