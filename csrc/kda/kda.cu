@@ -39,20 +39,73 @@ template <int C>
 constexpr int LDC() { return C + 1; }
 
 // out[m][n] (+)= alpha * sum_k A(m,k) B(k,n);  A(m,k) = a[m*lda+k] (or a[k*lda+m] if TA),
-// B(k,n) = b[k*ldb+n] (or b[n*ldb+k] if TB).  Lanes run over n.
+// B(k,n) = b[k*ldb+n] (or b[n*ldb+k] if TB).  Shared-memory operands, fp32 out.
+//
+// Tensor cores: mma.sync m16n8k8 with tf32 inputs, each fp32 operand split as
+// x = hi + lo (hi, lo tf32) and the product formed as hi*hi + hi*lo + lo*hi,
+// which keeps fp32-level accuracy (the state recurrence accumulates over the
+// whole sequence).  Output tiles of 16 x 8 are spread over the 8 warps.
+HB_DEVICE uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+HB_DEVICE void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+  hi = to_tf32(x);
+  lo = to_tf32(x - __uint_as_float(hi));
+}
+HB_DEVICE void mma_tf32(float* c, const uint32_t* a, const uint32_t* b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
 template <int M, int N, int KD, bool TA, bool TB>
 HB_DEVICE void mm(float* out, int ldo, const float* a, int lda, const float* b, int ldb, float alpha,
                   bool acc) {
-  for (int e = threadIdx.x; e < M * N; e += NT) {
-    const int m = e / N, n = e % N;
-    float s = 0.f;
-#pragma unroll 8
-    for (int k = 0; k < KD; ++k) {
-      const float av = TA ? a[k * lda + m] : a[m * lda + k];
-      const float bv = TB ? b[n * ldb + k] : b[k * ldb + n];
-      s += av * bv;
+  static_assert(M % 16 == 0 && N % 8 == 0 && KD % 8 == 0, "mm tile shape");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  constexpr int TM = M / 16, TN = N / 8;
+  for (int tile = warp; tile < TM * TN; tile += NT / 32) {
+    const int m0 = (tile / TN) * 16, n0 = (tile % TN) * 8;
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
+    for (int k0 = 0; k0 < KD; k0 += 8) {
+      float af[4], bf[2];
+      auto A = [&](int m, int k) { return TA ? a[k * lda + m] : a[m * lda + k]; };
+      auto B = [&](int k, int n) { return TB ? b[n * ldb + k] : b[k * ldb + n]; };
+      af[0] = A(m0 + g, k0 + t);
+      af[1] = A(m0 + g + 8, k0 + t);
+      af[2] = A(m0 + g, k0 + t + 4);
+      af[3] = A(m0 + g + 8, k0 + t + 4);
+      bf[0] = B(k0 + t, n0 + g);
+      bf[1] = B(k0 + t + 4, n0 + g);
+      uint32_t ah[4], al[4], bh[2], bl[2];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) split_tf32(af[i], ah[i], al[i]);
+      split_tf32(bf[0], bh[0], bl[0]);
+      split_tf32(bf[1], bh[1], bl[1]);
+      mma_tf32(c, al, bh);
+      mma_tf32(c, ah, bl);
+      mma_tf32(c, ah, bh);
     }
-    out[m * ldo + n] = acc ? out[m * ldo + n] + alpha * s : alpha * s;
+    const int r0 = m0 + g, cc = n0 + 2 * t;
+    float* o0 = out + r0 * ldo + cc;
+    float* o1 = out + (r0 + 8) * ldo + cc;
+    if (acc) {
+      o0[0] += alpha * c[0];
+      o0[1] += alpha * c[1];
+      o1[0] += alpha * c[2];
+      o1[1] += alpha * c[3];
+    } else {
+      o0[0] = alpha * c[0];
+      o0[1] = alpha * c[1];
+      o1[0] = alpha * c[2];
+      o1[1] = alpha * c[3];
+    }
   }
 }
 
@@ -115,22 +168,24 @@ HB_DEVICE void pair_products(const float* q, const float* k, const float* G, flo
   constexpr int L = LDK<DK>(), LC = LDC<C>();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int t = warp; t < C; t += NT / 32) {
-    for (int s = 0; s < C; ++s) {
+    for (int s = 0; s <= t; ++s) {
       float a = 0.f, pp = 0.f;
-      if (s <= t) {
-        for (int c = lane; c < DK; c += 32) {
-          const float e = __expf(G[t * L + c] - G[s * L + c]);
-          const float ks = k[s * L + c] * e;
-          a += k[t * L + c] * ks;
-          pp += q[t * L + c] * ks;
-        }
+      for (int c = lane; c < DK; c += 32) {
+        const float e = __expf(G[t * L + c] - G[s * L + c]);
+        const float ks = k[s * L + c] * e;
+        a += k[t * L + c] * ks;
+        pp += q[t * L + c] * ks;
       }
       a = warp_sum(a);
       pp = warp_sum(pp);
       if (lane == 0) {
         A[t * LC + s] = (s < t) ? a : 0.f;
-        P[t * LC + s] = (s <= t) ? pp * scale : 0.f;
+        P[t * LC + s] = pp * scale;
       }
+    }
+    for (int s = t + 1 + lane; s < C; s += 32) {
+      A[t * LC + s] = 0.f;
+      P[t * LC + s] = 0.f;
     }
   }
   __syncthreads();
@@ -220,6 +275,7 @@ __global__ void __launch_bounds__(NT) state_fwd_kernel(Ptrs p) {
   float* X = Wt + C * L;         // C x L (Qg, then Kh)
   float* P = X + C * L;          // C x LC
   float* gc = P + C * LC;        // DK
+  float* Tn = gc + DK;           // DK x LV
   const int vs = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int v0 = vs * VS;
   for (int i = threadIdx.x; i < DK * VS; i += NT) {
@@ -255,11 +311,11 @@ __global__ void __launch_bounds__(NT) state_fwd_kernel(Ptrs p) {
     for (int i = threadIdx.x; i < C * DK; i += NT) X[(i / DK) * L + i % DK] = p.Kh[co + i];
     __syncthreads();
     // S = gc * S + Kh^T U
+    mm<DK, VS, C, true, false>(Tn, LV, X, L, U, LV, 1.f, false);
+    __syncthreads();
     for (int e = threadIdx.x; e < DK * VS; e += NT) {
       const int r = e / VS, c = e % VS;
-      float s = 0.f;
-      for (int t = 0; t < C; ++t) s += X[t * L + r] * U[t * LV + c];
-      S[r * LV + c] = gc[r] * S[r * LV + c] + s;
+      S[r * LV + c] = gc[r] * S[r * LV + c] + Tn[r * LV + c];
     }
     for (int i = threadIdx.x; i < C * VS; i += NT) {
       const int r = i / VS, c = i % VS;
@@ -352,7 +408,9 @@ __global__ void __launch_bounds__(NT) intra_bwd_kernel(Ptrs p) {
   float* dk = U + C * L;
   float* dG = dk + C * L;
   float* Kh = dG + C * L;        // k e^{G_C - G}
-  float* S0 = Kh + C * L;        // DK x L
+  float* T1 = Kh + C * L;        // C x L scratch products
+  float* T2 = T1 + C * L;        // C x L
+  float* S0 = T2 + C * L;        // DK x L
   float* dSC = S0 + DK * L;      // DK x L
   float* A = dSC + DK * L;       // C x LC
   float* P = A + C * LC;         // C x LC -> dP
@@ -374,7 +432,6 @@ __global__ void __launch_bounds__(NT) intra_bwd_kernel(Ptrs p) {
     const int t = n * C + r;
     dO[r * L + c] = t < p.S ? p.dout[tok_off(p, b, t, h, DK) + c] : 0.f;
   }
-  for (int c = threadIdx.x; c < DK; c += NT) red[c] = 0.f;
   __syncthreads();
   pair_products<DK, C>(q, k, G, A, P, scale);
   const float* GC = G + (C - 1) * L;
@@ -397,48 +454,46 @@ __global__ void __launch_bounds__(NT) intra_bwd_kernel(Ptrs p) {
   mm<C, DK, DK, false, false>(X, L, Kh, L, dSC, L, 1.f, true);
   // dWt = -dU S0^T needs the final dU: after the barrier below
   __syncthreads();
-  // dP = dO U^T (masked s <= t), into P
+  // dP = dO U^T (masked to s <= t below), into P
+  mm<C, C, DK, false, true>(P, LC, dO, L, U, L, 1.f, false);
+  mm<C, DK, DK, false, true>(Y, L, X, L, S0, L, -1.f, false);
+  // T1 = dKh = U dS_C^T ;  T2 = dQg = dO S0^T
+  mm<C, DK, DK, false, true>(T1, L, U, L, dSC, L, 1.f, false);
+  mm<C, DK, DK, false, true>(T2, L, dO, L, S0, L, 1.f, false);
+  __syncthreads();
   for (int e = threadIdx.x; e < C * C; e += NT) {
     const int t = e / C, s = e % C;
-    float acc = 0.f;
-    if (s <= t)
-      for (int vv = 0; vv < DK; ++vv) acc += dO[t * L + vv] * U[s * L + vv];
-    P[t * LC + s] = acc;
+    if (s > t) P[t * LC + s] = 0.f;
   }
-  mm<C, DK, DK, false, true>(Y, L, X, L, S0, L, -1.f, false);
-  // dKh = U dS_C^T:  dk = dKh e^{G_C-G};  dG = -dKh Kh;  red += dKh Kh
+  // dk = dKh e^{G_C-G};  dG = -dKh Kh + dQg scale q e^G;  dq = scale dQg e^G (into U)
   for (int e = threadIdx.x; e < C * DK; e += NT) {
     const int t = e / DK, c = e % DK;
-    float s = 0.f;
-    for (int vv = 0; vv < DK; ++vv) s += U[t * L + vv] * dSC[c * L + vv];
     const int si = t * L + c;
+    const float dkh = T1[si], dqg = T2[si];
     const float kh = Kh[si];
-    dk[si] = s * __expf(GC[c] - G[si]);
-    dG[si] = -s * kh;
-    atomicAdd(&red[c], s * kh);
-  }
-  __syncthreads();
-  // dQg = dO S0^T:  dq = scale dQg e^G (into U);  dG += dQg * scale q e^G
-  for (int e = threadIdx.x; e < C * DK; e += NT) {
-    const int t = e / DK, c = e % DK;
-    float s = 0.f;
-    for (int vv = 0; vv < DK; ++vv) s += dO[t * L + vv] * S0[c * L + vv];
-    const int si = t * L + c;
     const float eg = __expf(G[si]);
-    dG[si] += s * scale * q[si] * eg;
-    U[si] = s * scale * eg;
+    dk[si] = dkh * __expf(GC[c] - G[si]);
+    dG[si] = -dkh * kh + dqg * scale * q[si] * eg;
+    U[si] = dqg * scale * eg;
+  }
+  // red[c] = sum_t dKh Kh (column sums)
+  for (int c = threadIdx.x; c < DK; c += NT) {
+    float s = 0.f;
+    for (int t = 0; t < C; ++t) s += T1[t * L + c] * Kh[t * L + c];
+    red[c] = s;
   }
   __syncthreads();
   float* dqa = U;
   // X <- L^{-T} dU ; Y <- L^{-T} dWt
   solve_upper_t2<DK, C>(X, Y, A, bet);
-  // dL_ts = -(X Ut^T + Y Wt^T)_ts (s<t)
+  // dL_ts = -(X Ut^T + Y Wt^T)_ts, kept for s < t (into dA for now)
+  mm<C, C, DK, false, true>(dA, LC, X, L, Ut, L, -1.f, false);
+  __syncthreads();
+  mm<C, C, DK, false, true>(dA, LC, Y, L, Wt, L, -1.f, true);
+  __syncthreads();
   for (int e = threadIdx.x; e < C * C; e += NT) {
     const int t = e / C, s = e % C;
-    float dl = 0.f;
-    if (s < t)
-      for (int c = 0; c < DK; ++c) dl -= X[t * L + c] * Ut[s * L + c] + Y[t * L + c] * Wt[s * L + c];
-    dA[t * LC + s] = dl;  // dL for now
+    if (s >= t) dA[t * LC + s] = 0.f;
   }
   __syncthreads();
   // db2_t = sum_s A dL + sum_c Kg Y;  dbeta_t = V . X + 2 b_t db2_t   (one warp per t)
@@ -542,7 +597,7 @@ template <int DK, int C>
 constexpr int intra_fwd_smem() { return (5 * C * LDK<DK>() + 2 * C * LDC<C>() + C) * 4; }
 template <int DK, int C, int VS>
 constexpr int state_fwd_smem() {
-  return (DK * (VS + 1) + 2 * C * (VS + 1) + 2 * C * LDK<DK>() + C * LDC<C>() + DK) * 4;
+  return (2 * DK * (VS + 1) + 2 * C * (VS + 1) + 2 * C * LDK<DK>() + C * LDC<C>() + DK) * 4;
 }
 template <int DK, int C, int VS>
 constexpr int state_bwd_smem() {
@@ -550,7 +605,7 @@ constexpr int state_bwd_smem() {
 }
 template <int DK, int C>
 constexpr int intra_bwd_smem() {
-  return (13 * C * LDK<DK>() + 2 * DK * LDK<DK>() + 3 * C * LDC<C>() + 2 * C + DK) * 4;
+  return (15 * C * LDK<DK>() + 2 * DK * LDK<DK>() + 3 * C * LDC<C>() + 2 * C + DK) * 4;
 }
 
 // ================================================================ front-end

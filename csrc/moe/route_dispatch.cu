@@ -30,7 +30,8 @@ constexpr int MAXK = 16;   // top-k
 // every token's logits are accumulated in a shared [RT_TOK][N] array; one warp
 // per token, lane e owns experts e, e+32, ...
 constexpr int RT_TOK = 64;
-constexpr int RT_SMEM_W = 160 * 1024;
+constexpr int RT_SMEM_W = 32 * 1024;   // router-weight chunk staged per block
+constexpr int RT_NSEQ = 4;             // sequences a block reduces in shared memory
 
 __global__ void router_fwd_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ W,
                                   const float* __restrict__ bias, int T, int S, int D, int N, int K,
@@ -39,15 +40,19 @@ __global__ void router_fwd_kernel(const __nv_bfloat16* __restrict__ x, const flo
                                   float* __restrict__ seq_counts, float* __restrict__ seq_probs,
                                   float* __restrict__ sums /* [0]=sum lse^2, [1]=sum entropy */) {
   extern __shared__ float sh[];
-  float* wsh = sh;              // [DC][N]
-  float* acc = sh + DC * N;     // [RT_TOK][N]
+  float* wsh = sh;                      // [DC][N]
+  float* acc = sh + DC * N;             // [RT_TOK][N]
+  float* scnt = acc + RT_TOK * N;       // [RT_NSEQ][N] per-sequence counts of this block
+  float* sprb = scnt + RT_NSEQ * N;     // [RT_NSEQ][N] per-sequence probability sums
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int warps = blockDim.x >> 5;
   const int EPL = (N + 31) / 32;  // experts per lane (<= 8)
   const int t_begin = blockIdx.x * RT_TOK;
   const int t_end = min(T, t_begin + RT_TOK);
+  const int b_first = t_begin / S;
   for (int i = threadIdx.x; i < RT_TOK * N; i += blockDim.x) acc[i] = 0.f;
+  for (int i = threadIdx.x; i < 2 * RT_NSEQ * N; i += blockDim.x) scnt[i] = 0.f;
   for (int d0 = 0; d0 < D; d0 += DC) {
     const int dn = min(DC, D - d0);
     __syncthreads();
@@ -120,7 +125,8 @@ __global__ void router_fwd_kernel(const __nv_bfloat16* __restrict__ x, const flo
       if (i < EPL && e < N) {
         const float pr = sc[i] * inv;
         ent -= pr * __logf(pr + 1e-9f);
-        atomicAdd(seq_probs + (long long)b * N + e, pr);
+        if (b - b_first < RT_NSEQ) atomicAdd(sprb + (b - b_first) * N + e, pr);
+        else atomicAdd(seq_probs + (long long)b * N + e, pr);
       }
     }
     ent = warp_sum(ent);
@@ -165,7 +171,8 @@ __global__ void router_fwd_kernel(const __nv_bfloat16* __restrict__ x, const flo
       for (int kk = 0; kk < K; ++kk) {
         topi[(long long)t * K + kk] = seli[kk];
         topw[(long long)t * K + kk] = selv[kk] / denom * (softmax_mode ? 1.f : scaling);
-        atomicAdd(seq_counts + (long long)b * N + seli[kk], 1.f);
+        if (b - b_first < RT_NSEQ) atomicAdd(scnt + (b - b_first) * N + seli[kk], 1.f);
+        else atomicAdd(seq_counts + (long long)b * N + seli[kk], 1.f);
       }
       zsum += lse * lse;
       esum += ent;
@@ -174,6 +181,14 @@ __global__ void router_fwd_kernel(const __nv_bfloat16* __restrict__ x, const flo
   if (lane == 0) {
     atomicAdd(sums + 0, zsum);
     atomicAdd(sums + 1, esum);
+  }
+  __syncthreads();
+  const int nb = min(RT_NSEQ, (t_end - 1) / S - b_first + 1);
+  for (int i = threadIdx.x; i < nb * N; i += blockDim.x) {
+    const int bl = i / N, e = i % N;
+    const long long gi = (long long)(b_first + bl) * N + e;
+    if (scnt[i] != 0.f) atomicAdd(seq_counts + gi, scnt[i]);
+    if (sprb[i] != 0.f) atomicAdd(seq_probs + gi, sprb[i]);
   }
 }
 
@@ -280,7 +295,8 @@ __global__ void router_dx_kernel(const float* __restrict__ dl, const float* __re
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
   const int tb = blockIdx.x * RT_TOK, te = min(T, tb + RT_TOK);
   const int EPL = (N + 31) / 32;
-  for (int d0 = 0; d0 < D; d0 += DCH) {
+  {
+    const int d0 = blockIdx.y * DCH;
     const int dn = min(DCH, D - d0);
     __syncthreads();
     for (int i = threadIdx.x; i < dn * N; i += blockDim.x) {
@@ -538,11 +554,11 @@ void router_fwd(torch::Tensor x, torch::Tensor W, torch::Tensor bias, int64_t S,
   if (T == 0) return;
   const int grid = (T + RT_TOK - 1) / RT_TOK;
   const int DC = std::max(32, std::min(D, (int)(RT_SMEM_W / (N * sizeof(float)))) / 32 * 32);
-  const size_t smem = (size_t)(DC * N + RT_TOK * N) * sizeof(float);
+  const size_t smem = (size_t)(DC * N + RT_TOK * N + 2 * RT_NSEQ * N) * sizeof(float);
   static bool cfg = false;
   if (!cfg) {
     HB_CUDA_CHECK(cudaFuncSetAttribute(router_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       RT_SMEM_W + RT_TOK * MAXN * 4));
+                                       RT_SMEM_W + (RT_TOK + 2 * RT_NSEQ) * MAXN * 4 + 32 * MAXN * 4));
     cfg = true;
   }
   router_fwd_kernel<<<grid, 256, smem, cur_stream()>>>(
@@ -574,7 +590,7 @@ void router_grads(torch::Tensor x, torch::Tensor W, torch::Tensor dl, torch::Ten
       cfg = true;
     }
     const int DCH = std::max(128, std::min(D, (int)(RT_SMEM_W / (N * sizeof(float)))) / 128 * 128);
-    const int grid = (T + RT_TOK - 1) / RT_TOK;
+    const dim3 grid((T + RT_TOK - 1) / RT_TOK, (D + DCH - 1) / DCH);
     router_dx_kernel<<<grid, 256, (size_t)N * DCH * 4, cur_stream()>>>(
         dl.data_ptr<float>(), W.data_ptr<float>(), dx.data_ptr<float>(), T, D, N, DCH);
     HB_CUDA_CHECK(cudaGetLastError());
