@@ -79,6 +79,17 @@ void p2p_update_bcast(torch::Tensor p, torch::Tensor g, torch::Tensor m, c10::op
                       torch::Tensor decay, torch::Tensor work_peers, int64_t world, int64_t off,
                       bool work_bf16, int64_t mode, double lr, double wd, double b1, double b2, double eps,
                       int64_t step, torch::Tensor coef);
+// expert parallel
+void ep_scatter(torch::Tensor x, c10::optional<torch::Tensor> dout, c10::optional<torch::Tensor> w,
+                c10::optional<torch::Tensor> ret, c10::optional<torch::Tensor> dw, torch::Tensor topi,
+                torch::Tensor pos, torch::Tensor starts, torch::Tensor peers, int64_t me, int64_t E,
+                int64_t Nl, int64_t cap, bool backward);
+void ep_zero_pads(torch::Tensor counts, torch::Tensor peers, c10::optional<torch::Tensor> count_peers,
+                  int64_t D, int64_t me, int64_t E, int64_t Nl, int64_t cap);
+void ep_return(torch::Tensor rows, torch::Tensor cnt, torch::Tensor peers, int64_t me, int64_t E, int64_t Nl,
+               int64_t cap);
+void ep_combine(torch::Tensor ret, c10::optional<torch::Tensor> w, torch::Tensor topi, torch::Tensor pos,
+                torch::Tensor starts, torch::Tensor out, int64_t cap);
 }  // namespace hb
 
 static int64_t read_status() {
@@ -130,4 +141,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_barrier", &hb::p2p_barrier);
   m.def("p2p_reduce_scatter", &hb::p2p_reduce_scatter);
   m.def("p2p_update_bcast", &hb::p2p_update_bcast);
+  m.def("ep_scatter", &hb::ep_scatter);
+  m.def("ep_zero_pads", &hb::ep_zero_pads);
+  m.def("ep_return", &hb::ep_return);
+  m.def("ep_combine", &hb::ep_combine);
 }

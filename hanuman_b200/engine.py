@@ -64,6 +64,7 @@ class FlatGroup:
     lo: int = 0
     hi: int = 0
     trainable: torch.Tensor = None  # 1.0 where the element receives updates
+    local: bool = False             # expert-parallel slice owned by this rank only
 
 
 def _build_group(named, dtype, device, world, rank, master_init) -> Optional[FlatGroup]:
@@ -121,11 +122,16 @@ class Engine:
         self.units = self._units(model)
         self.groups: list[FlatGroup] = []
         for unit in self.units:
-            mats = [(n, p) for n, p in unit if _is_matrix(n, p)]
-            smalls = [(n, p) for n, p in unit if not _is_matrix(n, p)]
-            for named, dt in ((mats, cdt), (smalls, torch.float32)):
-                g = _build_group(named, dt, self.device, world, rank, master_init)
+            local = [(n, p) for n, p in unit if getattr(p, "_ep_local", False)]
+            rest = [(n, p) for n, p in unit if not getattr(p, "_ep_local", False)]
+            mats = [(n, p) for n, p in rest if _is_matrix(n, p)]
+            smalls = [(n, p) for n, p in rest if not _is_matrix(n, p)]
+            for named, dt, loc in ((mats, cdt, False), (smalls, torch.float32, False),
+                                   (local, cdt, True)):
+                g = _build_group(named, dt, self.device, 1 if loc else world, 0 if loc else rank,
+                                 master_init)
                 if g is not None:
+                    g.local = loc
                     self.groups.append(g)
         mdt = torch.bfloat16 if (cfg.optimizer == "lion" and cfg.opt_state_dtype == "bf16") \
             else torch.float32
@@ -216,16 +222,26 @@ class Engine:
 
     # ------------------------------------------------------------------
     def master_state(self) -> dict:
-        """Full fp32 master weights by reference-tree name (gathers shards)."""
+        """Full fp32 master weights by reference-tree name (gathers shards; the
+        expert-parallel slices are concatenated along the expert axis)."""
         out = {}
         for g in self.groups:
             full = self._gather_master(g)
             for n, o, p in zip(g.names, g.offsets, g.params):
-                out[n] = full[o:o + p.numel()].view(p.shape).clone()
+                if g.local and self.world > 1:
+                    parts = [full[r][o:o + p.numel()].view(p.shape) for r in range(self.world)]
+                    out[n] = torch.cat(parts, 0).clone()
+                else:
+                    out[n] = full[o:o + p.numel()].view(p.shape).clone()
         return out
 
-    def _gather_master(self, g: FlatGroup) -> torch.Tensor:
-        if self.world == 1:
+    def _gather_master(self, g: FlatGroup):
+        if g.local and self.world > 1:
+            import torch.distributed as dist
+            parts = [torch.empty_like(g.master) for _ in range(self.world)]
+            dist.all_gather(parts, g.master)
+            return parts
+        if self.world == 1 or g.local:
             return g.master
         import torch.distributed as dist
         full = torch.empty(g.numel, dtype=torch.float32, device=self.device)
@@ -236,7 +252,11 @@ class Engine:
         for g in self.groups:
             full = torch.zeros(g.numel, dtype=torch.float32, device=self.device)
             for n, o, p in zip(g.names, g.offsets, g.params):
-                full[o:o + p.numel()] = state[n].reshape(-1).to(self.device, torch.float32)
+                v = state[n]
+                if g.local and tuple(v.shape) != tuple(p.shape):  # full tensor -> own experts
+                    nl = p.shape[0]
+                    v = v[self.rank * nl:(self.rank + 1) * nl]
+                full[o:o + p.numel()] = v.reshape(-1).to(self.device, torch.float32)
             g.master.copy_(full[g.lo:g.hi])
             g.work.copy_(full.to(g.work.dtype))
 

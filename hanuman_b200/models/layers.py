@@ -215,8 +215,27 @@ class MoE(nn.Module):
                                    self.shared_w_down[i].to(dtype)).float()
         return out / self.n_shared
 
+    def make_expert_parallel(self, rank: int, world: int):
+        """Keep only this rank's experts (global ids rank*N/E .. (rank+1)*N/E - 1)."""
+        if self.n_experts % world:
+            raise ValueError(f"{self.n_experts} experts do not split over {world} ranks")
+        nl = self.n_experts // world
+        for name in ("expert_w_gate", "expert_w_up", "expert_w_down"):
+            p = getattr(self, name)
+            p.data = p.data[rank * nl:(rank + 1) * nl].clone()
+            p._ep_local = True
+        self.ep_rank, self.ep_world = rank, world
+        self.ep_ctx = None
+
     def forward(self, h, dtype):
         """h ``[B,S,D]`` (compute dtype) -> (fp32 output, aux dict)."""
+        if h.is_cuda and getattr(self, "ep_world", 1) > 1:
+            from ..ops.moe_ep import EPContext, moe_ep_layer_cuda
+            if self.ep_ctx is None:
+                self.ep_ctx = EPContext(self, h.shape[0] * h.shape[1], h.shape[2],
+                                        self.expert_w_gate.shape[2], self.ep_dist,
+                                        self.capacity_factor)
+            return moe_ep_layer_cuda(self, h, dtype)
         if h.is_cuda:
             from ..ops.moe import moe_layer_cuda
             return moe_layer_cuda(self, h, dtype)

@@ -55,10 +55,15 @@ class FSDPEngine(Engine):
     def reduce_grads(self, loss, counts):
         """Mean gradient over ranks into each group's shard; global counts/loss."""
         w = self.world
+        for g in self.groups:
+            if g.local:  # expert-parallel slice: the owner saw every token; mean over ranks
+                g.grad.mul_(1.0 / w)
         if self.p2p is not None:
             self.p2p.reduce_scatter_grads()
         else:
             for g in self.groups:
+                if g.local:
+                    continue
                 shard = g.grad[g.lo:g.hi]
                 if self.ctx.backend == "nccl":
                     dist.reduce_scatter_tensor(shard, g.grad, op=dist.ReduceOp.SUM)
@@ -73,7 +78,12 @@ class FSDPEngine(Engine):
 
     def grad_sq_sum(self):
         if self.p2p is not None and self.p2p.sumsq is not None:
-            return self.p2p.sumsq.reshape(())
+            tot = self.p2p.sumsq.reshape(())
+            loc = [g.grad for g in self.groups if g.local]
+            if loc:
+                from ..ops.optim import sumsq_cuda
+                tot = tot + sumsq_cuda(loc)
+            return tot
         return super().grad_sq_sum()
 
     def allreduce_scalar(self, x):
@@ -86,6 +96,10 @@ class FSDPEngine(Engine):
             lr = self.schedule(self.step_count)
             self.step_count += 1
             self.p2p.update_and_broadcast(self.cfg, lr, self.step_count, coef)
+            from ..ops.optim import fused_update_cuda
+            for g in self.groups:
+                if g.local:
+                    fused_update_cuda(g, self.cfg, lr, self.step_count, coef)
             return lr
         lr = super().apply_update(coef)
         self.gather_work()
@@ -93,6 +107,8 @@ class FSDPEngine(Engine):
 
     def gather_work(self):
         for g in self.groups:
+            if g.local:
+                continue
             dist.all_gather_into_tensor(g.work, g.work[g.lo:g.hi].clone()
                                         if self.device.type == "cpu" else g.work[g.lo:g.hi])
 

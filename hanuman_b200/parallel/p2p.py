@@ -27,7 +27,8 @@ class P2PComm:
         self.world, self.rank = ctx.world, ctx.rank
         dev = eng.device
         group = dist.group.WORLD
-        groups = eng.groups
+        groups = [g for g in eng.groups if not g.local]
+        self.groups = groups
         # one symmetric allocation per buffer kind
         gtot = sum(g.numel for g in groups)
         self.gbuf = symm.empty(gtot, dtype=torch.float32, device=dev)
@@ -84,7 +85,7 @@ class P2PComm:
     def reduce_scatter_grads(self):
         self.barrier()                      # every rank's backward is complete
         self.sumsq = torch.zeros(1, dtype=torch.float32, device=self.eng.device)
-        for g, (gp, _) in zip(self.eng.groups, self.layout):
+        for g, (gp, _) in zip(self.groups, self.layout):
             ext().p2p_reduce_scatter(gp, self.world, g.lo, g.hi - g.lo, g.grad[g.lo:g.hi],
                                      1.0 / self.world, self.sumsq)
         self.barrier()                      # nobody reads a peer's gradients any more
@@ -94,7 +95,7 @@ class P2PComm:
         b1 = cfg.adam_b1 if mode == 0 else cfg.lion_b1
         b2 = cfg.adam_b2 if mode == 0 else cfg.lion_b2
         c = coef.reshape(1).float().contiguous()
-        for g, (_, wp) in zip(self.eng.groups, self.layout):
+        for g, (_, wp) in zip(self.groups, self.layout):
             ext().p2p_update_bcast(g.master, g.grad[g.lo:g.hi], g.m, g.v, g.decay, wp, self.world,
                                    g.lo, g.work.dtype == torch.bfloat16, mode, float(lr),
                                    float(cfg.weight_decay), float(b1), float(b2),
