@@ -31,12 +31,14 @@ namespace kda {
 
 constexpr int NT = 256;
 
-// Shared-memory matrices use odd row strides (cols + 1) so that a warp reading
-// a column (lanes over rows) or a row (lanes over columns) hits 32 banks.
+// Shared-memory matrices use row strides = cols + 4 (a multiple of 4 that is
+// 4 mod 32 for the widths used): the tensor-core fragment loads of a row-major
+// operand (lanes over 8 rows x 4 columns) then touch 32 distinct banks, the
+// transposed ones at most 2-way, and the SIMT loops (lanes over columns) none.
 template <int DK>
-constexpr int LDK() { return DK + 1; }
+constexpr int LDK() { return DK + 4; }
 template <int C>
-constexpr int LDC() { return C + 1; }
+constexpr int LDC() { return C + 4; }
 
 // out[m][n] (+)= alpha * sum_k A(m,k) B(k,n);  A(m,k) = a[m*lda+k] (or a[k*lda+m] if TA),
 // B(k,n) = b[k*ldb+n] (or b[n*ldb+k] if TB).  Shared-memory operands, fp32 out.
@@ -266,7 +268,7 @@ __global__ void __launch_bounds__(NT) intra_fwd_kernel(Ptrs p) {
 // grid (DK / VS, H, B): value columns [vs*VS, vs*VS+VS) of the state.
 template <int DK, int C, int VS>
 __global__ void __launch_bounds__(NT) state_fwd_kernel(Ptrs p) {
-  constexpr int L = LDK<DK>(), LC = LDC<C>(), LV = VS + 1;
+  constexpr int L = LDK<DK>(), LC = LDC<C>(), LV = VS + 4;
   extern __shared__ float sm[];
   float* S = sm;                 // DK x LV
   float* U = S + DK * LV;        // C x LV
@@ -336,7 +338,7 @@ __global__ void __launch_bounds__(NT) state_fwd_kernel(Ptrs p) {
 // the END of chunk n.  grid (DK / VS, H, B) over value-column slices.
 template <int DK, int C, int VS>
 __global__ void __launch_bounds__(NT) state_bwd_kernel(Ptrs p) {
-  constexpr int L = LDK<DK>(), LC = LDC<C>(), LV = VS + 1;
+  constexpr int L = LDK<DK>(), LC = LDC<C>(), LV = VS + 4;
   extern __shared__ float sm[];
   float* dS = sm;                // DK x LV
   float* T2 = dS + DK * LV;      // DK x LV
@@ -597,11 +599,11 @@ template <int DK, int C>
 constexpr int intra_fwd_smem() { return (5 * C * LDK<DK>() + 2 * C * LDC<C>() + C) * 4; }
 template <int DK, int C, int VS>
 constexpr int state_fwd_smem() {
-  return (2 * DK * (VS + 1) + 2 * C * (VS + 1) + 2 * C * LDK<DK>() + C * LDC<C>() + DK) * 4;
+  return (2 * DK * (VS + 4) + 2 * C * (VS + 4) + 2 * C * LDK<DK>() + C * LDC<C>() + DK) * 4;
 }
 template <int DK, int C, int VS>
 constexpr int state_bwd_smem() {
-  return (2 * DK * (VS + 1) + 2 * C * (VS + 1) + 2 * C * LDK<DK>() + C * LDC<C>() + DK) * 4;
+  return (2 * DK * (VS + 4) + 2 * C * (VS + 4) + 2 * C * LDK<DK>() + C * LDC<C>() + DK) * 4;
 }
 template <int DK, int C>
 constexpr int intra_bwd_smem() {

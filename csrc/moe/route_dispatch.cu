@@ -33,6 +33,7 @@ constexpr int RT_TOK = 64;
 constexpr int RT_SMEM_W = 32 * 1024;   // router-weight chunk staged per block
 constexpr int RT_NSEQ = 4;             // sequences a block reduces in shared memory
 
+template <int EPL>
 __global__ void router_fwd_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ W,
                                   const float* __restrict__ bias, int T, int S, int D, int N, int K,
                                   int softmax_mode, float scaling, int DC, float* __restrict__ logits_out,
@@ -47,7 +48,7 @@ __global__ void router_fwd_kernel(const __nv_bfloat16* __restrict__ x, const flo
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int warps = blockDim.x >> 5;
-  const int EPL = (N + 31) / 32;  // experts per lane (<= 8)
+  // EPL (template): experts per lane, ceil(N / 32)
   const int t_begin = blockIdx.x * RT_TOK;
   const int t_end = min(T, t_begin + RT_TOK);
   const int b_first = t_begin / S;
@@ -59,25 +60,27 @@ __global__ void router_fwd_kernel(const __nv_bfloat16* __restrict__ x, const flo
     for (int i = threadIdx.x; i < dn * N; i += blockDim.x) wsh[i] = W[(long long)d0 * N + i];
     __syncthreads();
     for (int t = t_begin + warp; t < t_end; t += warps) {
-      float a[8];
+      float a[EPL];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) a[i] = 0.f;
+      for (int i = 0; i < EPL; ++i) a[i] = 0.f;
       const __nv_bfloat16* xr = x + (long long)t * D + d0;
+      const bool full = (N % 32) == 0;
       for (int r0 = 0; r0 < dn; r0 += 32) {
         const float xv_l = (r0 + lane < dn) ? __bfloat162float(xr[r0 + lane]) : 0.f;
         const int rn = min(32, dn - r0);
+#pragma unroll 8
         for (int r = 0; r < rn; ++r) {
           const float xv = __shfl_sync(0xffffffffu, xv_l, r);
-          const float* wr = wsh + (r0 + r) * N;
+          const float* wr = wsh + (r0 + r) * N + lane;
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            if (i < EPL && lane + 32 * i < N) a[i] += xv * wr[lane + 32 * i];
+          for (int i = 0; i < EPL; ++i)
+            if (full || lane + 32 * i < N) a[i] += xv * wr[32 * i];
         }
       }
       float* ar = acc + (t - t_begin) * N;
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (i < EPL && lane + 32 * i < N) ar[lane + 32 * i] += a[i];
+      for (int i = 0; i < EPL; ++i)
+        if (lane + 32 * i < N) ar[lane + 32 * i] += a[i];
     }
   }
   __syncthreads();
@@ -555,13 +558,11 @@ void router_fwd(torch::Tensor x, torch::Tensor W, torch::Tensor bias, int64_t S,
   const int grid = (T + RT_TOK - 1) / RT_TOK;
   const int DC = std::max(32, std::min(D, (int)(RT_SMEM_W / (N * sizeof(float)))) / 32 * 32);
   const size_t smem = (size_t)(DC * N + RT_TOK * N + 2 * RT_NSEQ * N) * sizeof(float);
-  static bool cfg = false;
-  if (!cfg) {
-    HB_CUDA_CHECK(cudaFuncSetAttribute(router_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       RT_SMEM_W + (RT_TOK + 2 * RT_NSEQ) * MAXN * 4 + 32 * MAXN * 4));
-    cfg = true;
-  }
-  router_fwd_kernel<<<grid, 256, smem, cur_stream()>>>(
+  const int epl = (N + 31) / 32;
+  auto kern = epl == 1 ? router_fwd_kernel<1> : epl == 2 ? router_fwd_kernel<2>
+            : epl <= 4 ? router_fwd_kernel<4> : router_fwd_kernel<8>;
+  HB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  kern<<<grid, 256, smem, cur_stream()>>>(
       (const __nv_bfloat16*)x.data_ptr(), W.data_ptr<float>(), bias.data_ptr<float>(), T, (int)S, D,
       N, (int)K, softmax_mode ? 1 : 0, (float)scaling, DC, logits.data_ptr<float>(), topi.data_ptr<int>(),
       topw.data_ptr<float>(), seq_counts.data_ptr<float>(), seq_probs.data_ptr<float>(),

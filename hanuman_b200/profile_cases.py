@@ -1,0 +1,164 @@
+"""Small, self-contained kernel cases for device profiling (ncu) and timing.
+
+    python -m hanuman_b200.profile_cases <case> [--time]
+
+Each case builds inputs on the current GPU (a few GB at most; operands larger
+than the 126 MB L2 where the kernel is memory-bound), runs the kernel a few
+times and exits.  With ``--time`` it prints the CUDA-event time of one launch
+and the achieved TFLOP/s or GB/s.  Cases: gemm_fwd, gemm_dw, grouped_fwd,
+kda_fwd, kda_bwd, flash_fwd, flash_bwd, router_fwd, p2p_rs_emulated.
+"""
+from __future__ import annotations
+
+import math
+import sys
+
+import torch
+
+from .ops._ext import ext
+
+
+def _time(fn, n=5):
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(n):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / n
+
+
+def case_gemm_fwd():
+    x = torch.randn(32768, 1024, device="cuda").bfloat16()
+    w = torch.randn(1024, 3200, device="cuda").bfloat16()
+    y = torch.empty(32768, 3200, device="cuda", dtype=torch.bfloat16)
+    return (lambda: ext().gemm(x, w, y, False, False, False, 1.0)), 2 * 32768 * 1024 * 3200, "flop"
+
+
+def case_gemm_dw():
+    x = torch.randn(32768, 1024, device="cuda").bfloat16()
+    dy = torch.randn(32768, 1024, device="cuda").bfloat16()
+    g = torch.zeros(1024, 1024, device="cuda")
+    return (lambda: ext().gemm(x, dy, g, True, False, True, 1.0)), 2 * 32768 * 1024 * 1024, "flop"
+
+
+def case_grouped_fwd():
+    T, K, N, D, F = 32768, 4, 32, 1024, 768
+    counts = [T * K // N] * N
+    starts = [i * ((T * K // N + 127) // 128 * 128) for i in range(N)]
+    R = starts[-1] + counts[-1]
+    xp = torch.randn(R, D, device="cuda").bfloat16()
+    w = torch.randn(N, D, F, device="cuda").bfloat16()
+    y = torch.empty(R, F, device="cuda", dtype=torch.bfloat16)
+    tiles_n = (F + 255) // 256
+    tp = [0]
+    for c in counts:
+        tp.append(tp[-1] + (c + 127) // 128 * tiles_n)
+    i32 = lambda v: torch.tensor(v, dtype=torch.int32, device="cuda")
+    gs, gc, gt = i32(starts), i32(counts), i32(tp)
+    return (lambda: ext().grouped_gemm_m(xp, w, y, gs, gc, gt, False)), 2 * T * K * D * F, "flop"
+
+
+def _kda_inputs(B=8, S=4096, H=16, K=64):
+    g = torch.Generator(device="cuda").manual_seed(0)
+    n = lambda x: x / torch.sqrt((x * x).sum(-1, keepdim=True) + 1e-6)
+    q = n(torch.randn(B, S, H, K, device="cuda", generator=g))
+    k = n(torch.randn(B, S, H, K, device="cuda", generator=g))
+    v = torch.randn(B, S, H, K, device="cuda", generator=g)
+    gg = torch.nn.functional.logsigmoid(torch.randn(B, S, H, K, device="cuda", generator=g))
+    beta = torch.sigmoid(torch.randn(B, S, H, device="cuda", generator=g))
+    return q, k, v, gg, beta
+
+
+def case_kda_fwd():
+    from .ops.kda import KdaCoreFn
+    ins = _kda_inputs()
+    B, S, H, K = ins[0].shape
+    flops = 8 * H * K * K * B * S   # reference FLOP model of the recurrence
+    return (lambda: KdaCoreFn.apply(*ins, 1 / math.sqrt(K))), flops, "flop"
+
+
+def case_kda_bwd():
+    from .ops.kda import KdaCoreFn
+    ins = [t.requires_grad_() for t in _kda_inputs()]
+    B, S, H, K = ins[0].shape
+    def run():
+        o = KdaCoreFn.apply(*ins, 1 / math.sqrt(K))
+        o.backward(torch.ones_like(o))
+    return run, 3 * 8 * H * K * K * B * S, "flop"
+
+
+def _attn_inputs(B=8, S=4096, Nq=16, Nkv=4, H=64):
+    q = torch.randn(B, S, Nq, H, device="cuda").bfloat16()
+    k = torch.randn(B, S, Nkv, H, device="cuda").bfloat16()
+    v = torch.randn(B, S, Nkv, H, device="cuda").bfloat16()
+    return q, k, v
+
+
+def case_flash_fwd():
+    q, k, v = _attn_inputs()
+    B, S, Nq, H = q.shape
+    out = torch.empty_like(q)
+    lse = torch.empty(B, Nq, S, device="cuda")
+    return (lambda: ext().flash_fwd(q, k, v, out, lse, 0)), 4 * B * Nq * H * S * (S + 1) / 2, "flop"
+
+
+def case_flash_bwd():
+    q, k, v = _attn_inputs()
+    B, S, Nq, H = q.shape
+    out = torch.empty_like(q)
+    lse = torch.empty(B, Nq, S, device="cuda")
+    ext().flash_fwd(q, k, v, out, lse, 0)
+    do = torch.randn_like(q)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    delta = torch.empty(B, Nq, S, device="cuda")
+    return (lambda: ext().flash_bwd(q, k, v, out, do, lse, delta, dq, dk, dv, 0)), \
+        2.5 * 4 * B * Nq * H * S * (S + 1) / 2, "flop"
+
+
+def case_router_fwd():
+    T, D, N, K = 32768, 1024, 32, 4
+    x = torch.randn(T, D, device="cuda").bfloat16()
+    W = torch.randn(D, N, device="cuda") * 0.01
+    bias = torch.zeros(N, device="cuda")
+    lg = torch.empty(T, N, device="cuda")
+    ti = torch.empty(T, K, dtype=torch.int32, device="cuda")
+    tw = torch.empty(T, K, device="cuda")
+    sc, sp = torch.zeros(8, N, device="cuda"), torch.zeros(8, N, device="cuda")
+    su = torch.zeros(2, device="cuda")
+    return (lambda: ext().router_fwd(x, W, bias, 4096, K, False, 2.5, lg, ti, tw, sc, sp, su)), \
+        T * D * 2 + D * N * 4, "byte"
+
+
+def case_p2p_rs_emulated():
+    """The fused reduce-scatter kernel on one GPU: both 'peers' are local
+    buffers (the kernel and its memory traffic without NVLink)."""
+    n = 64 * 1024 * 1024
+    a = torch.randn(2 * n, device="cuda")
+    out = torch.empty(n // 2, device="cuda")
+    s = torch.zeros(1, device="cuda")
+    peers = torch.tensor([a.data_ptr(), a.data_ptr() + n * 4], dtype=torch.int64, device="cuda")
+    return (lambda: ext().p2p_reduce_scatter(peers, 2, 0, n // 2, out, 0.5, s)), \
+        3 * (n // 2) * 4, "byte"
+
+
+CASES = {k[5:]: v for k, v in globals().items() if k.startswith("case_")}
+
+
+def main(argv=None):
+    argv = sys.argv[1:] if argv is None else argv
+    name = argv[0]
+    fn, work, unit = CASES[name]()
+    ms = _time(fn)
+    if "--time" in argv:
+        rate = work / (ms / 1e3)
+        print(f"{name}: {ms:.3f} ms  " + (f"{rate/1e12:.1f} TFLOP/s" if unit == "flop"
+                                          else f"{rate/1e9:.0f} GB/s"))
+    assert ext().read_status() == 0
+
+
+if __name__ == "__main__":
+    main()

@@ -144,12 +144,20 @@ def train(config: Config, use_random_data: bool = True, save: bool = True, dist_
     model_fl, hw_fl = fl.step_flops(config)
     peak = fl.peak_flops_per_device() * world if trainer.device.type == "cuda" else 0.0
     log(f"[train] {model_fl/1e12:.2f} TFLOP/step model, {hw_fl/1e12:.2f} with remat")
+    wd = None
+    if dist_ctx is not None and world > 1:
+        import torch.distributed as dist
+        from .parallel.watchdog import Watchdog
+        wd = Watchdog(dist.distributed_c10d._get_default_store(), rank, world)
     losses = []
     it = iter(loader)
     ev0 = ev1 = None
     steps_win = 0
     t_win = time.time()
     for step in range(start_step, config.train_steps):
+        if wd is not None:       # between steps: nothing of ours is in flight
+            wd.tick(step)
+            wd.check()
         batch = next(it)
         if trainer.device.type == "cuda" and ev0 is None:
             ev0 = torch.cuda.Event(enable_timing=True)
@@ -203,6 +211,8 @@ def train(config: Config, use_random_data: bool = True, save: bool = True, dist_
     if save:
         save_checkpoint(trainer, config, config.train_steps, dist_ctx,
                         extra={"loader": loader.state_dict()})
+    if wd is not None:
+        wd.close()
     if losses:
         log(f"[train] Done. First loss={losses[0]:.4f}, last loss={losses[-1]:.4f}")
     return trainer, losses

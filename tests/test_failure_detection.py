@@ -1,0 +1,119 @@
+"""Failure detection without faulting a GPU.
+
+* CPU (gloo) ranks: a rank that stops heart-beating is reported to the others
+  by the watchdog; a rank that never joins a collective makes the others'
+  collective end with an error after the process-group timeout (no hang).
+* GPU: the device barrier waits on a flag that nothing sets; the bounded wait
+  runs out, the kernel records kErrTimeoutPeer in the status word and returns,
+  and the context stays usable.
+"""
+import os
+import socket
+import time
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _wd_worker(rank, world, port, out_path):
+    import datetime
+    import torch.distributed as dist
+    from hanuman_b200.parallel.watchdog import PeerFailure, Watchdog
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=20))
+    store = dist.distributed_c10d._get_default_store()
+    wd = Watchdog(store, rank, world, timeout_s=2.0, interval_s=0.2)
+    if rank == 1:
+        wd.close()          # rank 1 dies between steps: it stops beating and exits
+        return
+    result = "no-failure"
+    for step in range(100):
+        wd.tick(step)
+        try:
+            wd.check()
+        except PeerFailure as e:
+            result = f"detected:{e}"
+            break
+        time.sleep(0.1)
+    wd.close()
+    with open(out_path, "w") as f:
+        f.write(result)
+    os._exit(0)  # do not wait for the departed peer in destroy_process_group
+
+
+def test_watchdog_reports_silent_rank(tmp_path):
+    ctx = mp.get_context("spawn")
+    out = str(tmp_path / "wd.txt")
+    port = _port()
+    ps = [ctx.Process(target=_wd_worker, args=(r, 2, port, out)) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(timeout=120)
+    assert open(out).read().startswith("detected:")
+    assert "[1]" in open(out).read()
+
+
+def _timeout_worker(rank, world, port, out_path):
+    import datetime
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=3))
+    if rank == 1:
+        time.sleep(8)       # never joins the collective below in time
+        os._exit(0)
+    t0 = time.time()
+    try:
+        dist.all_reduce(torch.ones(4))
+        res = "completed"
+    except Exception as e:  # gloo raises once the timeout expires
+        res = f"error after {time.time() - t0:.1f}s: {type(e).__name__}"
+    with open(out_path, "w") as f:
+        f.write(res)
+    os._exit(0)
+
+
+def test_collective_with_missing_rank_errors_instead_of_hanging(tmp_path):
+    ctx = mp.get_context("spawn")
+    out = str(tmp_path / "to.txt")
+    port = _port()
+    ps = [ctx.Process(target=_timeout_worker, args=(r, 2, port, out)) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(timeout=120)
+    assert open(out).read().startswith("error after")
+
+
+@pytest.mark.gpu
+def test_device_barrier_times_out_with_error_status():
+    from hanuman_b200.ops._ext import ext
+    e = ext()
+    e.clear_status()
+    # two "ranks" whose signal pads are both this GPU's buffer: slot 1 is never set
+    pad = torch.zeros(32, dtype=torch.int32, device="cuda")
+    pads = torch.tensor([pad.data_ptr(), pad.data_ptr()], dtype=torch.int64, device="cuda")
+    e.set_wait_budget_ns(200_000_000)           # 0.2 s
+    try:
+        t0 = time.time()
+        e.p2p_barrier(pads, 0, 2, 1)
+        torch.cuda.synchronize()
+        assert time.time() - t0 < 10
+        assert e.read_status() == 4             # kErrTimeoutPeer
+    finally:
+        e.set_wait_budget_ns(4_000_000_000)
+        e.clear_status()
+    # the context is still usable
+    x = torch.randn(64, 64, device="cuda")
+    assert torch.isfinite((x @ x).sum())
