@@ -71,7 +71,7 @@ HB_DEVICE void mm(float* out, int ldo, const float* a, int lda, const float* b, 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   constexpr int TM = M / 16, TN = N / 8;
-  for (int tile = warp; tile < TM * TN; tile += NT / 32) {
+  for (int tile = warp; tile < TM * TN; tile += (int)(blockDim.x >> 5)) {
     const int m0 = (tile / TN) * 16, n0 = (tile % TN) * 8;
     float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 2
@@ -130,138 +130,184 @@ HB_DEVICE long long chunk_off(const Ptrs& p, int b, int h, int n, int sz) {
   return ((((long long)b * p.H + h) * p.NC) + n) * sz;
 }
 
-// Load one chunk's q, k, v, g (zeros past S) into padded smem, beta, and
-// cumulate g -> G in place.
+// 16-byte shared/global accesses (every row offset used below is a multiple of 4 floats).
+HB_DEVICE float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+HB_DEVICE void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+
+// Thread count of the intra-chunk kernels: 256 up to head dim 64 (two or more
+// blocks per SM), 512 for head dim 128 (one block per SM with 205 KB of tiles).
+template <int DK>
+constexpr int NTB() { return DK >= 128 ? 512 : 256; }
+
+// Load one chunk's rows of [B, S, H, DK] x (zeros past S) into padded smem.
+template <int DK, int C>
+HB_DEVICE void load_rows(const Ptrs& p, const float* x, int b, int h, int n, float* dst) {
+  constexpr int L = LDK<DK>(), D4 = DK / 4;
+  for (int i = threadIdx.x; i < C * D4; i += blockDim.x) {
+    const int r = i / D4, c = (i % D4) * 4;
+    const int t = n * C + r;
+    float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (t < p.S) z = ld4(x + tok_off(p, b, t, h, DK) + c);
+    st4(dst + r * L + c, z);
+  }
+}
+
+// q, k, v, g and beta of one chunk; g is cumulated in place into G
+// (registers per column, so the 32 loads of a column are independent).
 template <int DK, int C>
 HB_DEVICE void load_chunk(const Ptrs& p, int b, int h, int n, float* q, float* k, float* v, float* G,
                           float* bet) {
   constexpr int L = LDK<DK>();
-  const int t0 = n * C;
-  for (int i = threadIdx.x; i < C * DK; i += NT) {
-    const int r = i / DK, c = i % DK;
-    const int t = t0 + r;
-    const bool ok = t < p.S;
-    const long long o = ok ? tok_off(p, b, t, h, DK) + c : 0;
-    q[r * L + c] = ok ? p.q[o] : 0.f;
-    k[r * L + c] = ok ? p.k[o] : 0.f;
-    v[r * L + c] = ok ? p.v[o] : 0.f;
-    G[r * L + c] = ok ? p.g[o] : 0.f;
-  }
-  for (int r = threadIdx.x; r < C; r += NT) {
-    const int t = t0 + r;
+  load_rows<DK, C>(p, p.q, b, h, n, q);
+  load_rows<DK, C>(p, p.k, b, h, n, k);
+  load_rows<DK, C>(p, p.v, b, h, n, v);
+  load_rows<DK, C>(p, p.g, b, h, n, G);
+  for (int r = threadIdx.x; r < C; r += blockDim.x) {
+    const int t = n * C + r;
     bet[r] = t < p.S ? p.beta[((long long)b * p.S + t) * p.H + h] : 0.f;
   }
   __syncthreads();
-  for (int c = threadIdx.x; c < DK; c += NT) {
-    float s = 0.f;
-    for (int r = 0; r < C; ++r) {
-      s += G[r * L + c];
-      G[r * L + c] = s;
+  for (int c = threadIdx.x; c < DK; c += blockDim.x) {
+    float x[C];
+#pragma unroll
+    for (int r = 0; r < C; ++r) x[r] = G[r * L + c];
+#pragma unroll
+    for (int r = 1; r < C; ++r) x[r] += x[r - 1];
+#pragma unroll
+    for (int r = 0; r < C; ++r) G[r * L + c] = x[r];
+  }
+  __syncthreads();
+}
+
+// Pairwise products with log-space decay, for rows t >= columns s:
+//   A_ts = sum_c k_t k_s e^{G_t-G_s} (s < t, else 0),  N = diag(b^2) A,
+//   P_ts = scale sum_c q_t k_s e^{G_t-G_s} (s <= t, else 0).
+// Lane = row t (C == 32); warp w owns columns s = w, w + nw, ...  Each lane
+// streams its own row in 16-byte pieces and accumulates against the warp's
+// columns (broadcast reads): no cross-lane reductions.  Pairs with s > t are
+// computed and discarded by a select, never multiplied in.
+template <int DK, int C, bool WRITE_A>
+HB_DEVICE void pair_products(const float* q, const float* k, const float* G, const float* bet, float* A,
+                             float* N, float* P, float scale) {
+  static_assert(C == 32, "one lane per chunk row");
+  constexpr int L = LDK<DK>(), LC = LDC<C>();
+  constexpr int MS = 4;
+  const int nw = blockDim.x >> 5, warp = threadIdx.x >> 5, t = threadIdx.x & 31;
+  for (int s0 = warp; s0 < C; s0 += nw * MS) {
+    float a[MS], pp[MS];
+#pragma unroll
+    for (int j = 0; j < MS; ++j) a[j] = pp[j] = 0.f;
+    for (int c = 0; c < DK; c += 4) {
+      const float4 kt = ld4(k + t * L + c), gt = ld4(G + t * L + c), qt = ld4(q + t * L + c);
+#pragma unroll
+      for (int j = 0; j < MS; ++j) {
+        const int s = s0 + j * nw;
+        if (s >= C) break;
+        const float4 ks = ld4(k + s * L + c), gs = ld4(G + s * L + c);
+        const float e0 = __expf(gt.x - gs.x) * ks.x, e1 = __expf(gt.y - gs.y) * ks.y;
+        const float e2 = __expf(gt.z - gs.z) * ks.z, e3 = __expf(gt.w - gs.w) * ks.w;
+        a[j] += kt.x * e0 + kt.y * e1 + kt.z * e2 + kt.w * e3;
+        pp[j] += qt.x * e0 + qt.y * e1 + qt.z * e2 + qt.w * e3;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < MS; ++j) {
+      const int s = s0 + j * nw;
+      if (s >= C) break;
+      const float av = s < t ? a[j] : 0.f;
+      if (WRITE_A) A[t * LC + s] = av;
+      N[t * LC + s] = bet[t] * bet[t] * av;
+      P[t * LC + s] = s <= t ? pp[j] * scale : 0.f;
     }
   }
   __syncthreads();
 }
 
-// A (strict lower) and P (lower incl., scaled) by pairwise log-space decay:
-// one warp per row t, lanes over channels, warp reductions.
-template <int DK, int C>
-HB_DEVICE void pair_products(const float* q, const float* k, const float* G, float* A, float* P,
-                             float scale) {
-  constexpr int L = LDK<DK>(), LC = LDC<C>();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int t = warp; t < C; t += NT / 32) {
-    for (int s = 0; s <= t; ++s) {
-      float a = 0.f, pp = 0.f;
-      for (int c = lane; c < DK; c += 32) {
-        const float e = __expf(G[t * L + c] - G[s * L + c]);
-        const float ks = k[s * L + c] * e;
-        a += k[t * L + c] * ks;
-        pp += q[t * L + c] * ks;
-      }
-      a = warp_sum(a);
-      pp = warp_sum(pp);
-      if (lane == 0) {
-        A[t * LC + s] = (s < t) ? a : 0.f;
-        P[t * LC + s] = pp * scale;
-      }
-    }
-    for (int s = t + 1 + lane; s < C; s += 32) {
-      A[t * LC + s] = 0.f;
-      P[t * LC + s] = 0.f;
-    }
+// x <- (I + N)^{-1} x for one column held in registers (N strictly lower):
+// right-looking substitution, each step's updates are independent.
+template <int C>
+HB_DEVICE void col_solve_lower(float (&x)[C], const float* N) {
+  constexpr int LC = LDC<C>();
+#pragma unroll
+  for (int p = 0; p < C - 1; ++p) {
+#pragma unroll
+    for (int t = p + 1; t < C; ++t) x[t] = fmaf(-N[t * LC + p], x[p], x[t]);
   }
-  __syncthreads();
+}
+// x <- (I + N)^{-T} x
+template <int C>
+HB_DEVICE void col_solve_upper_t(float (&x)[C], const float* N) {
+  constexpr int LC = LDC<C>();
+#pragma unroll
+  for (int t = C - 1; t > 0; --t) {
+#pragma unroll
+    for (int s = 0; s < t; ++s) x[s] = fmaf(-N[t * LC + s], x[t], x[s]);
+  }
 }
 
-// In-place forward substitution X <- L^{-1} X, L = I + diag(b^2) A (unit lower),
-// on two column blocks at once (X1, X2: C x DK each); one thread per column.
-template <int DK, int C>
-HB_DEVICE void solve_lower2(float* X1, float* X2, const float* A, const float* bet) {
-  constexpr int L = LDK<DK>(), LC = LDC<C>();
-  for (int col = threadIdx.x; col < 2 * DK; col += NT) {
-    float* X = col < DK ? X1 : X2;
-    const int cc = col < DK ? col : col - DK;
-    for (int t = 1; t < C; ++t) {
-      float s = 0.f;
-      for (int j = 0; j < t; ++j) s += A[t * LC + j] * X[j * L + cc];
-      X[t * L + cc] -= bet[t] * bet[t] * s;
-    }
+// For each of `ncols` columns: x_t = ld(t, col); solve; st(t, col, x_t).
+// Each thread owns whole columns, so dst may alias src.
+template <int C, bool UPPER_T, class Ld, class St>
+HB_DEVICE void solve_cols(int ncols, const float* N, Ld ld, St st) {
+  for (int col = threadIdx.x; col < ncols; col += blockDim.x) {
+    float x[C];
+#pragma unroll
+    for (int t = 0; t < C; ++t) x[t] = ld(t, col);
+    if (UPPER_T) col_solve_upper_t<C>(x, N);
+    else col_solve_lower<C>(x, N);
+#pragma unroll
+    for (int t = 0; t < C; ++t) st(t, col, x[t]);
   }
-  __syncthreads();
-}
-// In-place backward substitution X <- L^{-T} X:  X_t -= sum_{s>t} A_st b_s^2 X_s
-template <int DK, int C>
-HB_DEVICE void solve_upper_t2(float* X1, float* X2, const float* A, const float* bet) {
-  constexpr int L = LDK<DK>(), LC = LDC<C>();
-  for (int col = threadIdx.x; col < 2 * DK; col += NT) {
-    float* X = col < DK ? X1 : X2;
-    const int cc = col < DK ? col : col - DK;
-    for (int t = C - 2; t >= 0; --t) {
-      float s = 0.f;
-      for (int j = t + 1; j < C; ++j) s += A[j * LC + t] * bet[j] * bet[j] * X[j * L + cc];
-      X[t * L + cc] -= s;
-    }
-  }
-  __syncthreads();
 }
 
 // ------------------------------------------------------------------ intra fwd
 template <int DK, int C>
-__global__ void __launch_bounds__(NT) intra_fwd_kernel(Ptrs p) {
-  constexpr int L = LDK<DK>(), LC = LDC<C>();
+__global__ void __launch_bounds__(256) intra_fwd_kernel(Ptrs p) {
+  constexpr int L = LDK<DK>(), LC = LDC<C>(), D4 = DK / 4;
   extern __shared__ float sm[];
   float* q = sm;
   float* k = q + C * L;
-  float* v = k + C * L;
+  float* v = k + C * L;          // v, then Ut
   float* G = v + C * L;
   float* Wt = G + C * L;
-  float* A = Wt + C * L;
-  float* P = A + C * LC;
-  float* bet = P + C * LC;
+  float* N = Wt + C * L;         // C x LC
+  float* P = N + C * LC;         // C x LC
+  float* bet = P + C * LC;       // C
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   load_chunk<DK, C>(p, b, h, n, q, k, v, G, bet);
-  pair_products<DK, C>(q, k, G, A, P, p.scale);
-  // right-hand sides: Ut <- b v (in v), Wt <- b^2 k e^G
-  for (int i = threadIdx.x; i < C * DK; i += NT) {
-    const int r = i / DK, c = i % DK;
-    v[r * L + c] *= bet[r];
-    Wt[r * L + c] = bet[r] * bet[r] * k[r * L + c] * __expf(G[r * L + c]);
-  }
+  pair_products<DK, C, false>(q, k, G, bet, nullptr, N, P, p.scale);
+  // Ut = L^{-1} b v (in place),  Wt = L^{-1} b^2 k e^G
+  solve_cols<C, false>(
+      2 * DK, N,
+      [&](int t, int col) {
+        return col < DK ? bet[t] * v[t * L + col]
+                        : bet[t] * bet[t] * k[t * L + col - DK] * __expf(G[t * L + col - DK]);
+      },
+      [&](int t, int col, float x) {
+        if (col < DK) v[t * L + col] = x;
+        else Wt[t * L + col - DK] = x;
+      });
   __syncthreads();
-  solve_lower2<DK, C>(v, Wt, A, bet);
   const long long co = chunk_off(p, b, h, n, C * DK);
   const float* GC = G + (C - 1) * L;
-  for (int i = threadIdx.x; i < C * DK; i += NT) {
-    const int r = i / DK, c = i % DK;
+  for (int i = threadIdx.x; i < C * D4; i += blockDim.x) {
+    const int r = i / D4, c = (i % D4) * 4;
     const int si = r * L + c;
-    p.Ut[co + i] = v[si];
-    p.Wt[co + i] = Wt[si];
-    p.Kh[co + i] = k[si] * __expf(GC[c] - G[si]);
-    p.Qg[co + i] = p.scale * q[si] * __expf(G[si]);
+    const float4 kk = ld4(k + si), gg = ld4(G + si), qq = ld4(q + si), gc = ld4(GC + c);
+    st4(p.Ut + co + r * DK + c, ld4(v + si));
+    st4(p.Wt + co + r * DK + c, ld4(Wt + si));
+    st4(p.Kh + co + r * DK + c, make_float4(kk.x * __expf(gc.x - gg.x), kk.y * __expf(gc.y - gg.y),
+                                            kk.z * __expf(gc.z - gg.z), kk.w * __expf(gc.w - gg.w)));
+    const float sc = p.scale;
+    st4(p.Qg + co + r * DK + c, make_float4(sc * qq.x * __expf(gg.x), sc * qq.y * __expf(gg.y),
+                                            sc * qq.z * __expf(gg.z), sc * qq.w * __expf(gg.w)));
   }
   const long long po = chunk_off(p, b, h, n, C * C);
-  for (int i = threadIdx.x; i < C * C; i += NT) p.Pm[po + i] = P[(i / C) * LC + (i % C)];
-  for (int c = threadIdx.x; c < DK; c += NT) p.gC[chunk_off(p, b, h, n, DK) + c] = __expf(GC[c]);
+  for (int i = threadIdx.x; i < C * C / 4; i += blockDim.x) {
+    const int r = i / (C / 4), c = (i % (C / 4)) * 4;
+    st4(p.Pm + po + r * C + c, ld4(P + r * LC + c));
+  }
+  for (int c = threadIdx.x; c < DK; c += blockDim.x) p.gC[chunk_off(p, b, h, n, DK) + c] = __expf(GC[c]);
 }
 
 // ------------------------------------------------------------------ state fwd
@@ -393,146 +439,180 @@ __global__ void __launch_bounds__(NT) state_bwd_kernel(Ptrs p) {
 }
 
 // ------------------------------------------------------------------ intra bwd
+// Rows of the [DK, DK] state matrices streamed per step (two panels in smem).
+template <int DK>
+constexpr int PANEL() { return DK >= 128 ? 16 : 8; }
+
+// Recomputes the chunk (A, N, P, Ut, Wt, U) and emits dq, dk, dv, dg, dbeta
+// given S0 (state entering the chunk), dS_C (gradient of the state leaving
+// it) and dO.  S0 and dS_C are read in row panels, twice (the second pass
+// needs the completed U and dU):
+//   pass 1: U -= Wt S0,  dU += Kh dS_C,  dQg = dO S0^T,  dgC = rowsum(dS_C * S0)
+//   pass 2: dWt = -dU S0^T,  dKh = U dS_C^T
 template <int DK, int C>
-__global__ void __launch_bounds__(NT) intra_bwd_kernel(Ptrs p) {
-  constexpr int L = LDK<DK>(), LC = LDC<C>();
+__global__ void __launch_bounds__(NTB<DK>(), DK >= 128 ? 1 : 2) intra_bwd_kernel(Ptrs p) {
+  constexpr int L = LDK<DK>(), LC = LDC<C>(), D4 = DK / 4, PR = PANEL<DK>();
   extern __shared__ float sm[];
   float* q = sm;                 // C x L each
   float* k = q + C * L;
   float* v = k + C * L;          // v, later dv
   float* G = v + C * L;
-  float* dO = G + C * L;
-  float* Ut = dO + C * L;
-  float* Wt = Ut + C * L;
-  float* X = Wt + C * L;         // dU -> L^-T dU
-  float* Y = X + C * L;          // dWt -> L^-T dWt
-  float* U = Y + C * L;          // U, later dq accumulator
-  float* dk = U + C * L;
-  float* dG = dk + C * L;
-  float* Kh = dG + C * L;        // k e^{G_C - G}
-  float* T1 = Kh + C * L;        // C x L scratch products
-  float* T2 = T1 + C * L;        // C x L
-  float* S0 = T2 + C * L;        // DK x L
-  float* dSC = S0 + DK * L;      // DK x L
-  float* A = dSC + DK * L;       // C x LC
-  float* P = A + C * LC;         // C x LC -> dP
+  float* dO = G + C * L;         // dO, later X = L^{-T} dU
+  float* U = dO + C * L;         // Ut -> U, later dG
+  float* dU = U + C * L;         // dU, later Y = L^{-T} dWt
+  float* T0 = dU + C * L;        // Wt -> dWt -> Ut / Wt (recomputed)
+  float* T1 = T0 + C * L;        // Kh -> dKh -> dk
+  float* T2 = T1 + C * L;        // dQg -> dq
+  float* S0p = T2 + C * L;       // PR x L
+  float* dSp = S0p + PR * L;     // PR x L
+  float* A = dSp + PR * L;       // C x LC
+  float* N = A + C * LC;         // C x LC
+  float* P = N + C * LC;         // C x LC, later dP
   float* dA = P + C * LC;        // C x LC
   float* bet = dA + C * LC;      // C
   float* dbt = bet + C;          // C
-  float* red = dbt + C;          // DK  (dG_C accumulation)
+  float* red = dbt + C;          // DK
+  float* dgc = red + DK;         // DK
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const float scale = p.scale;
+  load_rows<DK, C>(p, p.dout, b, h, n, dO);
   load_chunk<DK, C>(p, b, h, n, q, k, v, G, bet);
-  const long long so = chunk_off(p, b, h, n, DK * DK);
-  for (int i = threadIdx.x; i < DK * DK; i += NT) {
-    const int r = i / DK, c = i % DK;
-    S0[r * L + c] = p.states[so + i];
-    dSC[r * L + c] = p.dstates[so + i];
-  }
-  for (int i = threadIdx.x; i < C * DK; i += NT) {
-    const int r = i / DK, c = i % DK;
-    const int t = n * C + r;
-    dO[r * L + c] = t < p.S ? p.dout[tok_off(p, b, t, h, DK) + c] : 0.f;
-  }
-  __syncthreads();
-  pair_products<DK, C>(q, k, G, A, P, scale);
+  pair_products<DK, C, true>(q, k, G, bet, A, N, P, scale);
   const float* GC = G + (C - 1) * L;
-  for (int i = threadIdx.x; i < C * DK; i += NT) {
-    const int r = i / DK, c = i % DK;
-    const int si = r * L + c;
-    Ut[si] = bet[r] * v[si];
-    Wt[si] = bet[r] * bet[r] * k[si] * __expf(G[si]);
-    Kh[si] = k[si] * __expf(GC[c] - G[si]);
+  // Ut -> U, Wt -> T0;  Kh -> T1
+  solve_cols<C, false>(
+      2 * DK, N,
+      [&](int t, int col) {
+        return col < DK ? bet[t] * v[t * L + col]
+                        : bet[t] * bet[t] * k[t * L + col - DK] * __expf(G[t * L + col - DK]);
+      },
+      [&](int t, int col, float x) {
+        if (col < DK) U[t * L + col] = x;
+        else T0[t * L + col - DK] = x;
+      });
+  for (int e = threadIdx.x; e < C * DK; e += blockDim.x) {
+    const int t = e / DK, c = e % DK;
+    T1[t * L + c] = k[t * L + c] * __expf(GC[c] - G[t * L + c]);
   }
   __syncthreads();
-  solve_lower2<DK, C>(Ut, Wt, A, bet);
-  // U = Ut - Wt S0
-  for (int i = threadIdx.x; i < C * DK; i += NT) U[(i / DK) * L + i % DK] = Ut[(i / DK) * L + i % DK];
+  // dU = P^T dO
+  mm<C, DK, C, true, false>(dU, L, P, LC, dO, L, 1.f, false);
   __syncthreads();
-  mm<C, DK, DK, false, false>(U, L, Wt, L, S0, L, -1.f, true);
-  // dU = P^T dO + Kh dS_C
-  mm<C, DK, C, true, false>(X, L, P, LC, dO, L, 1.f, false);
-  __syncthreads();
-  mm<C, DK, DK, false, false>(X, L, Kh, L, dSC, L, 1.f, true);
-  // dWt = -dU S0^T needs the final dU: after the barrier below
-  __syncthreads();
-  // dP = dO U^T (masked to s <= t below), into P
+  const long long so = chunk_off(p, b, h, n, DK * DK);
+  auto load_panels = [&](int kp) {
+    for (int i = threadIdx.x; i < PR * D4; i += blockDim.x) {
+      const int r = i / D4, c = (i % D4) * 4;
+      const long long g = so + (long long)(kp + r) * DK + c;
+      st4(S0p + r * L + c, ld4(p.states + g));
+      st4(dSp + r * L + c, ld4(p.dstates + g));
+    }
+  };
+  for (int kp = 0; kp < DK; kp += PR) {
+    load_panels(kp);
+    __syncthreads();
+    mm<C, DK, PR, false, false>(U, L, T0 + kp, L, S0p, L, -1.f, true);
+    mm<C, DK, PR, false, false>(dU, L, T1 + kp, L, dSp, L, 1.f, true);
+    mm<C, PR, DK, false, true>(T2 + kp, L, dO, L, S0p, L, 1.f, false);
+    for (int r = warp; r < PR; r += nw) {
+      float s = 0.f;
+      for (int c = lane; c < DK; c += 32) s += dSp[r * L + c] * S0p[r * L + c];
+      s = warp_sum(s);
+      if (lane == 0) dgc[kp + r] = s;
+    }
+    __syncthreads();
+  }
+  // dP = dO U^T (into P; masked to s <= t below)
   mm<C, C, DK, false, true>(P, LC, dO, L, U, L, 1.f, false);
-  mm<C, DK, DK, false, true>(Y, L, X, L, S0, L, -1.f, false);
-  // T1 = dKh = U dS_C^T ;  T2 = dQg = dO S0^T
-  mm<C, DK, DK, false, true>(T1, L, U, L, dSC, L, 1.f, false);
-  mm<C, DK, DK, false, true>(T2, L, dO, L, S0, L, 1.f, false);
-  __syncthreads();
-  for (int e = threadIdx.x; e < C * C; e += NT) {
+  for (int kp = 0; kp < DK; kp += PR) {
+    load_panels(kp);
+    __syncthreads();
+    mm<C, PR, DK, false, true>(T0 + kp, L, dU, L, S0p, L, -1.f, false);
+    mm<C, PR, DK, false, true>(T1 + kp, L, U, L, dSp, L, 1.f, false);
+    __syncthreads();
+  }
+  for (int e = threadIdx.x; e < C * C; e += blockDim.x) {
     const int t = e / C, s = e % C;
     if (s > t) P[t * LC + s] = 0.f;
   }
-  // dk = dKh e^{G_C-G};  dG = -dKh Kh + dQg scale q e^G;  dq = scale dQg e^G (into U)
-  for (int e = threadIdx.x; e < C * DK; e += NT) {
-    const int t = e / DK, c = e % DK;
-    const int si = t * L + c;
-    const float dkh = T1[si], dqg = T2[si];
-    const float kh = Kh[si];
-    const float eg = __expf(G[si]);
-    dk[si] = dkh * __expf(GC[c] - G[si]);
-    dG[si] = -dkh * kh + dqg * scale * q[si] * eg;
-    U[si] = dqg * scale * eg;
-  }
-  // red[c] = sum_t dKh Kh (column sums)
-  for (int c = threadIdx.x; c < DK; c += NT) {
+  // red[c] = sum_t dKh Kh
+  for (int c = threadIdx.x; c < DK; c += blockDim.x) {
     float s = 0.f;
-    for (int t = 0; t < C; ++t) s += T1[t * L + c] * Kh[t * L + c];
+#pragma unroll 8
+    for (int t = 0; t < C; ++t) s += T1[t * L + c] * k[t * L + c] * __expf(GC[c] - G[t * L + c]);
     red[c] = s;
   }
   __syncthreads();
-  float* dqa = U;
-  // X <- L^{-T} dU ; Y <- L^{-T} dWt
-  solve_upper_t2<DK, C>(X, Y, A, bet);
-  // dL_ts = -(X Ut^T + Y Wt^T)_ts, kept for s < t (into dA for now)
-  mm<C, C, DK, false, true>(dA, LC, X, L, Ut, L, -1.f, false);
+  // dk = dKh e^{G_C-G} (T1);  dG = -dKh Kh + dQg scale q e^G (U);  dq = dQg scale e^G (T2)
+  for (int e = threadIdx.x; e < C * DK; e += blockDim.x) {
+    const int t = e / DK, c = e % DK;
+    const int si = t * L + c;
+    const float dkh = T1[si], dqg = T2[si];
+    const float ed = __expf(GC[c] - G[si]), eg = __expf(G[si]);
+    T1[si] = dkh * ed;
+    U[si] = -dkh * k[si] * ed + dqg * scale * q[si] * eg;
+    T2[si] = dqg * scale * eg;
+  }
+  // X = L^{-T} dU (into dO)
+  solve_cols<C, true>(
+      DK, N, [&](int t, int c) { return dU[t * L + c]; }, [&](int t, int c, float x) { dO[t * L + c] = x; });
   __syncthreads();
-  mm<C, C, DK, false, true>(dA, LC, Y, L, Wt, L, -1.f, true);
+  // Y = L^{-T} dWt (into dU)
+  solve_cols<C, true>(
+      DK, N, [&](int t, int c) { return T0[t * L + c]; }, [&](int t, int c, float x) { dU[t * L + c] = x; });
   __syncthreads();
-  for (int e = threadIdx.x; e < C * C; e += NT) {
+  float* X = dO;
+  float* Y = dU;
+  // dL_ts = -(X Ut^T + Y Wt^T)_ts for s < t; Ut and Wt are recomputed into T0
+  solve_cols<C, false>(
+      DK, N, [&](int t, int c) { return bet[t] * v[t * L + c]; },
+      [&](int t, int c, float x) { T0[t * L + c] = x; });
+  __syncthreads();
+  mm<C, C, DK, false, true>(dA, LC, X, L, T0, L, -1.f, false);
+  __syncthreads();
+  solve_cols<C, false>(
+      DK, N, [&](int t, int c) { return bet[t] * bet[t] * k[t * L + c] * __expf(G[t * L + c]); },
+      [&](int t, int c, float x) { T0[t * L + c] = x; });
+  __syncthreads();
+  mm<C, C, DK, false, true>(dA, LC, Y, L, T0, L, -1.f, true);
+  __syncthreads();
+  for (int e = threadIdx.x; e < C * C; e += blockDim.x) {
     const int t = e / C, s = e % C;
     if (s >= t) dA[t * LC + s] = 0.f;
   }
   __syncthreads();
-  // db2_t = sum_s A dL + sum_c Kg Y;  dbeta_t = V . X + 2 b_t db2_t   (one warp per t)
-  {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int t = warp; t < C; t += NT / 32) {
-      float s1 = 0.f, s2 = 0.f, s3 = 0.f;
-      for (int s = lane; s < t; s += 32) s1 += A[t * LC + s] * dA[t * LC + s];
-      for (int c = lane; c < DK; c += 32) {
-        const int si = t * L + c;
-        s2 += k[si] * __expf(G[si]) * Y[si];
-        s3 += v[si] * X[si];
-      }
-      s1 = warp_sum(s1);
-      s2 = warp_sum(s2);
-      s3 = warp_sum(s3);
-      if (lane == 0) dbt[t] = s3 + 2.f * bet[t] * (s1 + s2);
+  // dbeta_t = v_t . X_t + 2 b_t (sum_s A_ts dL_ts + sum_c k e^G Y)   (one warp per t)
+  for (int t = warp; t < C; t += nw) {
+    float s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    for (int s = lane; s < t; s += 32) s1 += A[t * LC + s] * dA[t * LC + s];
+    for (int c = lane; c < DK; c += 32) {
+      const int si = t * L + c;
+      s2 += k[si] * __expf(G[si]) * Y[si];
+      s3 += v[si] * X[si];
     }
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    s3 = warp_sum(s3);
+    if (lane == 0) dbt[t] = s3 + 2.f * bet[t] * (s1 + s2);
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < C * C; e += NT) {
+  for (int e = threadIdx.x; e < C * C; e += blockDim.x) {
     const int t = e / C, s = e % C;
     dA[t * LC + s] *= bet[t] * bet[t];
   }
   // dv = b X ; dKg = b^2 Y: dk += dKg e^G, dG += dKg k e^G
-  for (int e = threadIdx.x; e < C * DK; e += NT) {
+  for (int e = threadIdx.x; e < C * DK; e += blockDim.x) {
     const int t = e / DK, c = e % DK;
     const int si = t * L + c;
     const float eg = __expf(G[si]);
     const float dkg = bet[t] * bet[t] * Y[si];
-    dk[si] += dkg * eg;
-    dG[si] += dkg * k[si] * eg;
+    T1[si] += dkg * eg;
+    U[si] += dkg * k[si] * eg;
     v[si] = bet[t] * X[si];
   }
   __syncthreads();
-  // t-side pairwise terms: dq_t += scale sum_{s<=t} dP_ts k_s e_ts ; dk_t += sum_{s<t} dA_ts k_s e_ts
-  for (int e = threadIdx.x; e < C * DK; e += NT) {
+  // t-side: dq_t += scale sum_{s<=t} dP_ts k_s e_ts ; dk_t += sum_{s<t} dA_ts k_s e_ts
+  for (int e = threadIdx.x; e < C * DK; e += blockDim.x) {
     const int t = e / DK, c = e % DK;
     const int si = t * L + c;
     const float gt = G[si];
@@ -543,13 +623,13 @@ __global__ void __launch_bounds__(NT) intra_bwd_kernel(Ptrs p) {
       sa += dA[t * LC + s] * ks;
     }
     sp *= scale;
-    dqa[si] += sp;
-    dk[si] += sa;
-    dG[si] += q[si] * sp + k[si] * sa;
+    T2[si] += sp;
+    T1[si] += sa;
+    U[si] += q[si] * sp + k[si] * sa;
   }
   __syncthreads();
-  // s-side: dk_s[c] += sum_{t>=s} (scale dP_ts q_t + dA_ts k_t) e_ts ; dG_s -= k_s * that
-  for (int e = threadIdx.x; e < C * DK; e += NT) {
+  // s-side: dk_s += sum_{t>=s} (scale dP_ts q_t + dA_ts k_t) e_ts ; dG_s -= k_s * that
+  for (int e = threadIdx.x; e < C * DK; e += blockDim.x) {
     const int s = e / DK, c = e % DK;
     const int si = s * L + c;
     const float gs = G[si];
@@ -558,38 +638,34 @@ __global__ void __launch_bounds__(NT) intra_bwd_kernel(Ptrs p) {
       const float ee = __expf(G[t * L + c] - gs);
       acc += (scale * P[t * LC + s] * q[t * L + c] + dA[t * LC + s] * k[t * L + c]) * ee;
     }
-    dk[si] += acc;
-    dG[si] -= k[si] * acc;
+    T1[si] += acc;
+    U[si] -= k[si] * acc;
   }
   __syncthreads();
-  // dG_C += red + dgC * gC, dgC[c] = sum_v dS_C[c][v] S0[c][v]
-  for (int c = threadIdx.x; c < DK; c += NT) {
-    float s = 0.f;
-    for (int vv = 0; vv < DK; ++vv) s += dSC[c * L + vv] * S0[c * L + vv];
-    dG[(C - 1) * L + c] += red[c] + s * __expf(GC[c]);
+  // dG_C += red + dgC e^{G_C};  dg = reverse cumsum of dG
+  for (int c = threadIdx.x; c < DK; c += blockDim.x) {
+    float x[C];
+#pragma unroll
+    for (int r = 0; r < C; ++r) x[r] = U[r * L + c];
+    x[C - 1] += red[c] + dgc[c] * __expf(GC[c]);
+#pragma unroll
+    for (int r = C - 2; r >= 0; --r) x[r] += x[r + 1];
+#pragma unroll
+    for (int r = 0; r < C; ++r) U[r * L + c] = x[r];
   }
   __syncthreads();
-  // dg = reverse cumsum of dG; write outputs
-  for (int c = threadIdx.x; c < DK; c += NT) {
-    float s = 0.f;
-    for (int r = C - 1; r >= 0; --r) {
-      s += dG[r * L + c];
-      dG[r * L + c] = s;
-    }
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < C * DK; i += NT) {
-    const int r = i / DK, c = i % DK;
+  for (int i = threadIdx.x; i < C * D4; i += blockDim.x) {
+    const int r = i / D4, c = (i % D4) * 4;
     const int t = n * C + r;
     if (t >= p.S) continue;
     const long long o = tok_off(p, b, t, h, DK) + c;
     const int si = r * L + c;
-    p.dq[o] = dqa[si];
-    p.dk[o] = dk[si];
-    p.dv[o] = v[si];
-    p.dg[o] = dG[si];
+    st4(p.dq + o, ld4(T2 + si));
+    st4(p.dk + o, ld4(T1 + si));
+    st4(p.dv + o, ld4(v + si));
+    st4(p.dg + o, ld4(U + si));
   }
-  for (int r = threadIdx.x; r < C; r += NT) {
+  for (int r = threadIdx.x; r < C; r += blockDim.x) {
     const int t = n * C + r;
     if (t < p.S) p.dbeta[((long long)b * p.S + t) * p.H + h] = dbt[r];
   }
@@ -607,7 +683,7 @@ constexpr int state_bwd_smem() {
 }
 template <int DK, int C>
 constexpr int intra_bwd_smem() {
-  return (15 * C * LDK<DK>() + 2 * DK * LDK<DK>() + 3 * C * LDC<C>() + 2 * C + DK) * 4;
+  return (10 * C * LDK<DK>() + 2 * PANEL<DK>() * LDK<DK>() + 4 * C * LDC<C>() + 2 * C + 2 * DK) * 4;
 }
 
 // ================================================================ front-end
@@ -831,11 +907,17 @@ using kda::Ptrs;
     constexpr int DK = 64;                         \
     constexpr int C = 32;                          \
     __VA_ARGS__                                    \
+  } else if (DKV == 128) {                         \
+    constexpr int DK = 128;                        \
+    constexpr int C = 32;                          \
+    __VA_ARGS__                                    \
   } else {                                         \
-    HB_CHECK(false, "KDA head_dim must be 16, 32 or 64"); \
+    HB_CHECK(false, "KDA head_dim must be 16, 32, 64 or 128"); \
   }
 
 int64_t kda_chunk_size(int64_t dk) { return 32; }
+
+static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 static void set_smem(const void* f, int bytes) {
   HB_CUDA_CHECK(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
@@ -868,6 +950,9 @@ void kda_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
   p.scale = (float)scale;
   p.init_state = init_state.has_value() ? init_state->data_ptr<float>() : nullptr;
   p.final_state = final_state.has_value() ? final_state->data_ptr<float>() : nullptr;
+  HB_CHECK(al16(p.q) && al16(p.k) && al16(p.v) && al16(p.g) && al16(p.o) && al16(p.Wt) && al16(p.Ut) &&
+               al16(p.Kh) && al16(p.Qg) && al16(p.Pm) && al16(p.states),
+           "kda_fwd: 16-byte aligned buffers required");
   KDA_DISPATCH(DKV, {
     p.NC = (p.S + C - 1) / C;
     HB_CHECK(Pm.size(-1) == C, "kda_fwd: scratch chunk size mismatch");
@@ -915,6 +1000,9 @@ void kda_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
   p.dbeta = dbeta.data_ptr<float>();
   p.scale = (float)scale;
   HB_CHECK(dout.is_contiguous(), "kda_bwd: contiguous dout");
+  HB_CHECK(al16(p.q) && al16(p.k) && al16(p.v) && al16(p.g) && al16(p.dout) && al16(p.states) &&
+               al16(p.dstates) && al16(p.dq) && al16(p.dk) && al16(p.dv) && al16(p.dg),
+           "kda_bwd: 16-byte aligned buffers required");
   KDA_DISPATCH(DKV, {
     p.NC = (p.S + C - 1) / C;
     constexpr int VS = DK >= 32 ? 16 : DK;
@@ -927,7 +1015,7 @@ void kda_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
     }
     kda::state_bwd_kernel<DK, C, VS><<<dim3(DK / VS, p.H, p.B), kda::NT, s1, cur_stream()>>>(p);
     HB_CUDA_CHECK(cudaGetLastError());
-    kda::intra_bwd_kernel<DK, C><<<dim3(p.NC, p.H, p.B), kda::NT, s2, cur_stream()>>>(p);
+    kda::intra_bwd_kernel<DK, C><<<dim3(p.NC, p.H, p.B), kda::NTB<DK>(), s2, cur_stream()>>>(p);
     HB_CUDA_CHECK(cudaGetLastError());
   })
 }
@@ -1033,6 +1121,8 @@ extern "C" __attribute__((visibility("default"))) int hb_kda_fwd_noalloc(
   using namespace hb::kda_noalloc;
   if (!(DK == 16 || DK == 32 || DK == 64)) return HB_NOALLOC_BAD_HEAD_DIM;
   if (B <= 0 || S <= 0 || H <= 0) return HB_NOALLOC_BAD_SHAPE;
+  for (const void* ptr : {(const void*)q, (const void*)k, (const void*)v, (const void*)g, (const void*)o})
+    if (reinterpret_cast<uintptr_t>(ptr) & 15) return HB_NOALLOC_BAD_SHAPE;
   if (scratch_floats(B, S, H, DK) > kScratchFloats) return HB_NOALLOC_TOO_LARGE;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return HB_NOALLOC_CUDA_ERROR;

@@ -8,7 +8,8 @@
 //
 //   o = KDA(q, k, v, g, beta)   all fp32, q/k/v/g/o [B, S, H, DK], beta [B, S, H]
 //
-// The caller passes device pointers to the inputs and the output and a stream.
+// The caller passes device pointers to the inputs and the output and a stream;
+// q, k, v, g and o must be 16-byte aligned (HB_NOALLOC_BAD_SHAPE otherwise).
 // The chunk intermediates live in a file-scope __device__ array of 64 MiB
 // (16 Mi floats) that every GPU which loads the library holds until the
 // process exits; inputs needing more (B * H * ceil(S / 32) * (4*32*DK + 32*32 +

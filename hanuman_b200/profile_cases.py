@@ -6,7 +6,7 @@ Each case builds inputs on the current GPU (a few GB at most; operands larger
 than the 126 MB L2 where the kernel is memory-bound), runs the kernel a few
 times and exits.  With ``--time`` it prints the CUDA-event time of one launch
 and the achieved TFLOP/s or GB/s.  Cases: gemm_fwd, gemm_dw, grouped_fwd,
-kda_fwd, kda_bwd, flash_fwd, flash_bwd, router_fwd, p2p_rs_emulated.
+kda_fwd, kda_bwd, kda128_fwd, kda128_bwd, flash_fwd, flash_bwd, router_fwd, p2p_rs_emulated.
 """
 from __future__ import annotations
 
@@ -84,6 +84,24 @@ def case_kda_fwd():
 def case_kda_bwd():
     from .ops.kda import KdaCoreFn
     ins = [t.requires_grad_() for t in _kda_inputs()]
+    B, S, H, K = ins[0].shape
+    def run():
+        o = KdaCoreFn.apply(*ins, 1 / math.sqrt(K))
+        o.backward(torch.ones_like(o))
+    return run, 3 * 8 * H * K * K * B * S, "flop"
+
+
+def case_kda128_fwd():
+    """KDA-layer microbench shape: 16 heads of head dim 128, 2 x 32768 tokens."""
+    from .ops.kda import KdaCoreFn
+    ins = _kda_inputs(B=2, S=32768, H=16, K=128)
+    B, S, H, K = ins[0].shape
+    return (lambda: KdaCoreFn.apply(*ins, 1 / math.sqrt(K))), 8 * H * K * K * B * S, "flop"
+
+
+def case_kda128_bwd():
+    from .ops.kda import KdaCoreFn
+    ins = [t.requires_grad_() for t in _kda_inputs(B=2, S=32768, H=16, K=128)]
     B, S, H, K = ins[0].shape
     def run():
         o = KdaCoreFn.apply(*ins, 1 / math.sqrt(K))

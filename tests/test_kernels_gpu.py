@@ -139,7 +139,8 @@ def _kda_inputs(B, S, H, K, gscale, seed=5, dtype=torch.float32):
     return q, k, v, g, beta
 
 
-@pytest.mark.parametrize("K,S,gscale", [(64, 100, 1.0), (64, 64, 20.0), (32, 77, 1.0), (16, 40, 5.0)])
+@pytest.mark.parametrize("K,S,gscale", [(64, 100, 1.0), (64, 64, 20.0), (32, 77, 1.0), (16, 40, 5.0),
+                                         (128, 70, 1.0), (128, 96, 8.0)])
 def test_kda_core_fwd_bwd(K, S, gscale):
     from hanuman_b200.ops.kda import kda_chunked_cuda
     B, H = 2, 3
