@@ -29,6 +29,11 @@ void sumsq(torch::Tensor a, torch::Tensor out);
 void fused_update(torch::Tensor p, torch::Tensor g, torch::Tensor m, c10::optional<torch::Tensor> v,
                   torch::Tensor decay, torch::Tensor work, int64_t mode, double lr, double wd,
                   double b1, double b2, double eps, int64_t step, torch::Tensor coef);
+void add_norm_fwd(torch::Tensor x, torch::Tensor a, torch::Tensor rs, torch::Tensor w, double eps,
+                  torch::Tensor xn, torch::Tensor h, torch::Tensor rstd);
+void add_norm_bwd(c10::optional<torch::Tensor> g, torch::Tensor dh, torch::Tensor xn, torch::Tensor a,
+                  torch::Tensor rs, torch::Tensor w, torch::Tensor rstd, torch::Tensor dx, torch::Tensor da,
+                  torch::Tensor drs, torch::Tensor dw);
 // moe
 void router_fwd(torch::Tensor x, torch::Tensor W, torch::Tensor bias, int64_t S, int64_t K,
                 bool softmax_mode, double scaling, torch::Tensor logits, torch::Tensor topi,
@@ -52,6 +57,11 @@ void flash_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor 
                torch::Tensor lse, torch::Tensor delta, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv,
                int64_t window);
 // kda
+void kda_out_gate_fwd(torch::Tensor o, torch::Tensor gl, torch::Tensor w, torch::Tensor gb, double eps,
+                      torch::Tensor y, torch::Tensor rstd);
+void kda_out_gate_bwd(torch::Tensor dy, torch::Tensor o, torch::Tensor gl, torch::Tensor w, torch::Tensor gb,
+                      torch::Tensor rstd, torch::Tensor dO, torch::Tensor dgl, torch::Tensor dw,
+                      torch::Tensor dgb);
 int64_t kda_chunk_size(int64_t dk);
 void kda_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
              double scale, torch::Tensor o, torch::Tensor Wt, torch::Tensor Ut, torch::Tensor Kh,
@@ -123,6 +133,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_fwd_bwd", &hb::ce_fwd_bwd);
   m.def("sumsq", &hb::sumsq);
   m.def("fused_update", &hb::fused_update);
+  m.def("add_norm_fwd", &hb::add_norm_fwd);
+  m.def("add_norm_bwd", &hb::add_norm_bwd);
+  m.def("kda_out_gate_fwd", &hb::kda_out_gate_fwd);
+  m.def("kda_out_gate_bwd", &hb::kda_out_gate_bwd);
   m.def("router_fwd", &hb::router_fwd);
   m.def("router_bwd", &hb::router_bwd);
   m.def("router_grads", &hb::router_grads);

@@ -766,12 +766,42 @@ __global__ void prep_bwd1_kernel(const __nv_bfloat16* __restrict__ raw, long lon
                                  const float* __restrict__ dbeta, float* __restrict__ dconv,
                                  float* __restrict__ df, float* __restrict__ dbraw,
                                  float* __restrict__ d_alog, float* __restrict__ d_dtb) {
+  // block partials of d dt_bias [HK] and d a_log [H]: one global atomic per
+  // element and block instead of one per token
+  extern __shared__ float s_acc[];
   const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
   const int HK = H * DK;
+  float* s_dtb = s_acc;
+  float* s_al = s_acc + HK;
+  for (int i = threadIdx.x; i < HK + H; i += blockDim.x) s_acc[i] = 0.f;
+  __syncthreads();
   constexpr int PL = (DK + 31) / 32;
+  // per-warp register partials for the current head, flushed to shared
+  // memory when the warp's head changes (with a grid stride that is a
+  // multiple of H it never does)
+  float acc_dtb[PL];
+  float acc_al = 0.f;
+  int cur_h = -1;
+#pragma unroll
+  for (int j = 0; j < PL; ++j) acc_dtb[j] = 0.f;
+  auto flush = [&]() {
+    if (cur_h < 0) return;
+#pragma unroll
+    for (int j = 0; j < PL; ++j) {
+      const int c = lane + 32 * j;
+      if (c < DK) atomicAdd(s_dtb + cur_h * DK + c, acc_dtb[j]);
+      acc_dtb[j] = 0.f;
+    }
+    if (lane == 0) atomicAdd(s_al + cur_h, acc_al);
+    acc_al = 0.f;
+  };
   for (long long th = blockIdx.x * (long long)warps + (threadIdx.x >> 5); th < (long long)T * H;
        th += (long long)gridDim.x * warps) {
     const int t = th / H, h = th % H;
+    if (h != cur_h) {
+      flush();
+      cur_h = h;
+    }
     const int pos = t % S;
     float cq[PL], ck[PL], cv[PL], sq[PL], sk[PL];
     float ssq = 0.f, ssk = 0.f, dotq = 0.f, dotk = 0.f, dal = 0.f;
@@ -814,7 +844,7 @@ __global__ void prep_bwd1_kernel(const __nv_bfloat16* __restrict__ raw, long lon
         dz = dg[o] * (1.f - sig);
       }
       df[o] = dz;
-      atomicAdd(d_dtb + ch, dz);
+      acc_dtb[j] += dz;
     }
     ssq = warp_sum(ssq);
     ssk = warp_sum(ssk);
@@ -842,11 +872,17 @@ __global__ void prep_bwd1_kernel(const __nv_bfloat16* __restrict__ raw, long lon
       dconv[co + 2 * HK] = dv[o] * dsilu(cv[j]);
     }
     if (lane == 0) {
-      if (gate_mode == 0) atomicAdd(d_alog + h, dal);
+      if (gate_mode == 0) acc_al += dal;
       const float bt = beta[(long long)t * H + h];
       dbraw[(long long)t * H + h] = dbeta[(long long)t * H + h] * bt * (1.f - bt);
     }
   }
+  flush();
+  __syncthreads();
+  for (int i = threadIdx.x; i < HK; i += blockDim.x)
+    if (s_dtb[i] != 0.f) atomicAdd(d_dtb + i, s_dtb[i]);
+  for (int i = threadIdx.x; i < H; i += blockDim.x)
+    if (s_al[i] != 0.f) atomicAdd(d_alog + i, s_al[i]);
 }
 
 // Backward part 2 (thread per (token, channel) of the 3*HK conv inputs):
@@ -1051,10 +1087,13 @@ void kda_prep_bwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::
                   torch::Tensor dwk, torch::Tensor dwv) {
   const int T = dq.size(0), H = dq.size(1), DKV = dq.size(2);
   const long long work = (long long)T * H;
+  // a multiple of H warps per grid stride keeps each warp on one head
   const int grid = (int)std::min<long long>((work + 7) / 8, num_sms() * 16);
+  const size_t acc_smem = (size_t)(H * DKV + H) * 4;
+  HB_CHECK(acc_smem <= 48 * 1024, "kda_prep_bwd: too many channels");
   auto launch = [&](auto dkc) {
     constexpr int DK = decltype(dkc)::value;
-    kda::prep_bwd1_kernel<DK><<<grid, 256, 0, cur_stream()>>>(
+    kda::prep_bwd1_kernel<DK><<<grid, 256, acc_smem, cur_stream()>>>(
         (const __nv_bfloat16*)raw.data_ptr(), raw.stride(0), wq.data_ptr<float>(), wk.data_ptr<float>(),
         wv.data_ptr<float>(), f.data_ptr<float>(), a_log.data_ptr<float>(), dt_bias.data_ptr<float>(),
         beta.data_ptr<float>(), (int)gate_mode, T, (int)S, H, dq.data_ptr<float>(), dk.data_ptr<float>(),

@@ -1,9 +1,14 @@
 // MoE router and token dispatch (model/moe.py:37-85, 170-293).
 //
-// router_fwd   fp32 router logits (x @ W_r, fp32 accumulate, W_r staged in smem),
-//              sigmoid(+bias) or softmax scores, top-k selection, renormalised
-//              weights, and per-sequence aux partials (counts, routing-probability
-//              sums, logsumexp^2, entropy) reduced in registers per warp.
+// router_fwd   fp32 router logits, sigmoid(+bias) or softmax scores, top-k
+//              selection, renormalised weights, and per-sequence aux partials
+//              (counts, routing-probability sums, logsumexp^2, entropy).  The
+//              logits run on the tcgen05 GEMM: the fp32 weight is split into three
+//              bf16 terms (hi + mid + lo) and x (bf16, exact) multiplies all three
+//              with fp32 accumulation, which reproduces the fp32 product of the
+//              reference (model/moe.py:177-181); a SIMT kernel covers shapes whose
+//              rows are not 16-byte aligned.
+// router_grads dx and dW of the router GEMM, also as split-bf16 tensor-core GEMMs.
 // router_bwd   d(logits) from the gradients of the combine weights, the z-loss
 //              and the sequence-wise balance loss.
 // moe_plan     stable counting sort of the T*K (token, slot) pairs by expert into a
@@ -32,6 +37,127 @@ constexpr int MAXK = 16;   // top-k
 constexpr int RT_TOK = 64;
 constexpr int RT_SMEM_W = 32 * 1024;   // router-weight chunk staged per block
 constexpr int RT_NSEQ = 4;             // sequences a block reduces in shared memory
+
+// Per-token routing from the logits lg (lane e holds experts e, e+32, ...):
+// scores, aux partials, top-k and the renormalised combine weights.
+template <int EPL>
+HB_DEVICE void route_token(int t, float (&lg)[8], const float* __restrict__ bias, int S, int N, int K,
+                           int softmax_mode, float scaling, int b_first, float* __restrict__ logits_out,
+                           int* __restrict__ topi, float* __restrict__ topw, float* __restrict__ seq_counts,
+                           float* __restrict__ seq_probs, float* scnt, float* sprb, float& zsum,
+                           float& esum) {
+  const int lane = threadIdx.x & 31;
+  float sc[8], ef[8];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int e = lane + 32 * i;
+    if (i < EPL && e < N) {
+      logits_out[(long long)t * N + e] = lg[i];
+      mx = fmaxf(mx, lg[i]);
+    }
+  }
+  mx = warp_max(mx);
+  float se = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (i < EPL && lane + 32 * i < N) se += __expf(lg[i] - mx);
+  se = warp_sum(se);
+  const float lse = mx + __logf(se);
+  float ssum = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int e = lane + 32 * i;
+    if (i < EPL && e < N) {
+      sc[i] = softmax_mode ? __expf(lg[i] - lse) : 1.f / (1.f + __expf(-lg[i]));
+      ef[i] = softmax_mode ? sc[i] : sc[i] + bias[e];
+      ssum += sc[i];
+    } else {
+      sc[i] = 0.f;
+      ef[i] = -INFINITY;
+    }
+  }
+  ssum = warp_sum(ssum);
+  float ent = 0.f;
+  const float inv = 1.f / (ssum + 1e-9f);
+  const int b = t / S;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int e = lane + 32 * i;
+    if (i < EPL && e < N) {
+      const float pr = sc[i] * inv;
+      ent -= pr * __logf(pr + 1e-9f);
+      if (b - b_first < RT_NSEQ) atomicAdd(sprb + (b - b_first) * N + e, pr);
+      else atomicAdd(seq_probs + (long long)b * N + e, pr);
+    }
+  }
+  ent = warp_sum(ent);
+  // top-k by repeated warp argmax (ties -> lowest expert id, like top_k)
+  float selsum = 0.f;
+  float selv[MAXK];
+  int seli[MAXK];
+  for (int kk = 0; kk < K; ++kk) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane + 32 * i;
+      if (i < EPL && e < N && (ef[i] > bv || (ef[i] == bv && e < bi))) {
+        bv = ef[i];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    float s_win = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (lane + 32 * i == bi) {
+        s_win = sc[i];
+        ef[i] = -INFINITY;
+      }
+    s_win = warp_sum(s_win);
+    seli[kk] = bi;
+    selv[kk] = s_win;
+    selsum += s_win;
+  }
+  if (lane == 0) {
+    const float denom = selsum + 1e-9f;
+    for (int kk = 0; kk < K; ++kk) {
+      topi[(long long)t * K + kk] = seli[kk];
+      topw[(long long)t * K + kk] = selv[kk] / denom * (softmax_mode ? 1.f : scaling);
+      if (b - b_first < RT_NSEQ) atomicAdd(scnt + (b - b_first) * N + seli[kk], 1.f);
+      else atomicAdd(seq_counts + (long long)b * N + seli[kk], 1.f);
+    }
+    zsum += lse * lse;
+    esum += ent;
+  }
+}
+
+// Block-level flush of the per-sequence partials and the z / entropy sums.
+HB_DEVICE void route_flush(int t_begin, int t_end, int S, int N, int b_first, float* __restrict__ seq_counts,
+                           float* __restrict__ seq_probs, const float* scnt, const float* sprb, float zsum,
+                           float esum, float* __restrict__ sums) {
+  if ((threadIdx.x & 31) == 0) {
+    atomicAdd(sums + 0, zsum);
+    atomicAdd(sums + 1, esum);
+  }
+  __syncthreads();
+  const int nb = min(RT_NSEQ, (t_end - 1) / S - b_first + 1);
+  for (int i = threadIdx.x; i < nb * N; i += blockDim.x) {
+    const int bl = i / N, e = i % N;
+    const long long gi = (long long)(b_first + bl) * N + e;
+    if (scnt[i] != 0.f) atomicAdd(seq_counts + gi, scnt[i]);
+    if (sprb[i] != 0.f) atomicAdd(seq_probs + gi, sprb[i]);
+  }
+}
 
 template <int EPL>
 __global__ void router_fwd_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ W,
@@ -87,111 +213,87 @@ __global__ void router_fwd_kernel(const __nv_bfloat16* __restrict__ x, const flo
   float zsum = 0.f, esum = 0.f;
   for (int t = t_begin + warp; t < t_end; t += warps) {
     const float* ar = acc + (t - t_begin) * N;
-    float lg[8], sc[8], ef[8];
-    float mx = -INFINITY;
+    float lg[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int e = lane + 32 * i;
       lg[i] = (i < EPL && e < N) ? ar[e] : -INFINITY;
-      if (i < EPL && e < N) {
-        logits_out[(long long)t * N + e] = lg[i];
-        mx = fmaxf(mx, lg[i]);
-      }
     }
-    mx = warp_max(mx);
-    float se = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (i < EPL && lane + 32 * i < N) se += __expf(lg[i] - mx);
-    se = warp_sum(se);
-    const float lse = mx + __logf(se);
-    float ssum = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int e = lane + 32 * i;
-      if (i < EPL && e < N) {
-        sc[i] = softmax_mode ? __expf(lg[i] - lse) : 1.f / (1.f + __expf(-lg[i]));
-        ef[i] = softmax_mode ? sc[i] : sc[i] + bias[e];
-        ssum += sc[i];
-      } else {
-        sc[i] = 0.f;
-        ef[i] = -INFINITY;
-      }
-    }
-    ssum = warp_sum(ssum);
-    float ent = 0.f;
-    const float inv = 1.f / (ssum + 1e-9f);
-    const int b = t / S;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int e = lane + 32 * i;
-      if (i < EPL && e < N) {
-        const float pr = sc[i] * inv;
-        ent -= pr * __logf(pr + 1e-9f);
-        if (b - b_first < RT_NSEQ) atomicAdd(sprb + (b - b_first) * N + e, pr);
-        else atomicAdd(seq_probs + (long long)b * N + e, pr);
-      }
-    }
-    ent = warp_sum(ent);
-    // top-k by repeated warp argmax (ties -> lowest expert id, like top_k)
-    float selsum = 0.f;
-    float selv[MAXK];
-    int seli[MAXK];
-    for (int kk = 0; kk < K; ++kk) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int e = lane + 32 * i;
-        if (i < EPL && e < N && (ef[i] > bv || (ef[i] == bv && e < bi))) {
-          bv = ef[i];
-          bi = e;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) {
-          bv = ov;
-          bi = oi;
-        }
-      }
-      float s_win = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (lane + 32 * i == bi) {
-          s_win = sc[i];
-          ef[i] = -INFINITY;
-        }
-      s_win = warp_sum(s_win);
-      seli[kk] = bi;
-      selv[kk] = s_win;
-      selsum += s_win;
-    }
-    if (lane == 0) {
-      const float denom = selsum + 1e-9f;
-      for (int kk = 0; kk < K; ++kk) {
-        topi[(long long)t * K + kk] = seli[kk];
-        topw[(long long)t * K + kk] = selv[kk] / denom * (softmax_mode ? 1.f : scaling);
-        if (b - b_first < RT_NSEQ) atomicAdd(scnt + (b - b_first) * N + seli[kk], 1.f);
-        else atomicAdd(seq_counts + (long long)b * N + seli[kk], 1.f);
-      }
-      zsum += lse * lse;
-      esum += ent;
-    }
+    route_token<EPL>(t, lg, bias, S, N, K, softmax_mode, scaling, b_first, logits_out, topi, topw,
+                     seq_counts, seq_probs, scnt, sprb, zsum, esum);
   }
-  if (lane == 0) {
-    atomicAdd(sums + 0, zsum);
-    atomicAdd(sums + 1, esum);
-  }
+  route_flush(t_begin, t_end, S, N, b_first, seq_counts, seq_probs, scnt, sprb, zsum, esum, sums);
+}
+
+// Router on precomputed partial logits: l3 [T, 3N] holds x @ [W_hi | W_mid | W_lo]
+// (three bf16 terms of the fp32 router weight, products accumulated in fp32 by
+// the tensor-core GEMM); the logits are their sum.  Block = RT_TOK tokens.
+template <int EPL>
+__global__ void router_select_kernel(const float* __restrict__ l3, const float* __restrict__ bias,
+                                     int T, int S, int N, int K, int softmax_mode, float scaling,
+                                     float* __restrict__ logits_out, int* __restrict__ topi,
+                                     float* __restrict__ topw, float* __restrict__ seq_counts,
+                                     float* __restrict__ seq_probs, float* __restrict__ sums) {
+  __shared__ float scnt[RT_NSEQ * MAXN];
+  __shared__ float sprb[RT_NSEQ * MAXN];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+  const int t_begin = blockIdx.x * RT_TOK;
+  const int t_end = min(T, t_begin + RT_TOK);
+  const int b_first = t_begin / S;
+  for (int i = threadIdx.x; i < RT_NSEQ * N; i += blockDim.x) scnt[i] = sprb[i] = 0.f;
   __syncthreads();
-  const int nb = min(RT_NSEQ, (t_end - 1) / S - b_first + 1);
-  for (int i = threadIdx.x; i < nb * N; i += blockDim.x) {
-    const int bl = i / N, e = i % N;
-    const long long gi = (long long)(b_first + bl) * N + e;
-    if (scnt[i] != 0.f) atomicAdd(seq_counts + gi, scnt[i]);
-    if (sprb[i] != 0.f) atomicAdd(seq_probs + gi, sprb[i]);
+  float zsum = 0.f, esum = 0.f;
+  for (int t = t_begin + warp; t < t_end; t += warps) {
+    const float* r = l3 + (long long)t * 3 * N;
+    float lg[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane + 32 * i;
+      lg[i] = (i < EPL && e < N) ? (r[e] + r[N + e]) + r[2 * N + e] : -INFINITY;
+    }
+    route_token<EPL>(t, lg, bias, S, N, K, softmax_mode, scaling, b_first, logits_out, topi, topw,
+                     seq_counts, seq_probs, scnt, sprb, zsum, esum);
+  }
+  route_flush(t_begin, t_end, S, N, b_first, seq_counts, seq_probs, scnt, sprb, zsum, esum, sums);
+}
+
+// W [D, N] fp32 -> w3 = [hi | mid | lo] and w3x = [hi | hi | mid], both [D, 3N]
+// bf16, with hi = bf16(W), mid = bf16(W - hi), lo = bf16(W - hi - mid).
+__global__ void router_split_w_kernel(const float* __restrict__ W, long long n, int N,
+                                      __nv_bfloat16* __restrict__ w3, __nv_bfloat16* __restrict__ w3x) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long d = i / N;
+    const int e = i % N;
+    const float w = W[i];
+    const __nv_bfloat16 hi = __float2bfloat16_rn(w);
+    const float r = w - __bfloat162float(hi);
+    const __nv_bfloat16 mid = __float2bfloat16_rn(r);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(r - __bfloat162float(mid));
+    __nv_bfloat16* o = w3 + d * 3 * N + e;
+    o[0] = hi;
+    o[N] = mid;
+    o[2 * N] = lo;
+    __nv_bfloat16* ox = w3x + d * 3 * N + e;
+    ox[0] = hi;
+    ox[N] = hi;
+    ox[2 * N] = mid;
+  }
+}
+
+// dl [T, N] fp32 -> a3 [T, 3N] bf16 = [hi | lo | hi]:  a3 @ [hi | hi | mid]^T
+// = dl_hi W_hi + dl_lo W_hi + dl_hi W_mid (16-bit-mantissa accurate product).
+__global__ void router_split_dl_kernel(const float* __restrict__ dl, long long n, int N,
+                                       __nv_bfloat16* __restrict__ a3) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long t = i / N;
+    const int e = i % N;
+    const float v = dl[i];
+    const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+    __nv_bfloat16* o = a3 + t * 3 * N + e;
+    o[0] = hi;
+    o[N] = lo;
+    o[2 * N] = hi;
   }
 }
 
@@ -547,6 +649,26 @@ int grid_for(long long work, int per_block) {
 }  // namespace
 
 // ================================================================ host API
+void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool trans_a, bool trans_b,
+          bool accumulate, double alpha, c10::optional<torch::Tensor> alpha_t);
+
+// The tensor-core route needs 16-byte rows for every GEMM operand.
+static bool router_tc_ok(const torch::Tensor& x, int N) {
+  return N % 8 == 0 && x.size(1) % 8 == 0 && x.stride(1) == 1 && x.stride(0) % 8 == 0;
+}
+
+// W [D, N] fp32 -> (w3 = [hi | mid | lo], w3x = [hi | hi | mid]) bf16 [D, 3N].
+static std::pair<torch::Tensor, torch::Tensor> router_split_w(const torch::Tensor& W) {
+  const int D = W.size(0), N = W.size(1);
+  auto opt = W.options().dtype(torch::kBFloat16);
+  auto w3 = torch::empty({D, 3 * N}, opt), w3x = torch::empty({D, 3 * N}, opt);
+  const long long n = (long long)D * N;
+  router_split_w_kernel<<<grid_for(n, 256), 256, 0, cur_stream()>>>(
+      W.data_ptr<float>(), n, N, (__nv_bfloat16*)w3.data_ptr(), (__nv_bfloat16*)w3x.data_ptr());
+  HB_CUDA_CHECK(cudaGetLastError());
+  return {w3, w3x};
+}
+
 void router_fwd(torch::Tensor x, torch::Tensor W, torch::Tensor bias, int64_t S, int64_t K,
                 bool softmax_mode, double scaling, torch::Tensor logits, torch::Tensor topi,
                 torch::Tensor topw, torch::Tensor seq_counts, torch::Tensor seq_probs,
@@ -554,11 +676,26 @@ void router_fwd(torch::Tensor x, torch::Tensor W, torch::Tensor bias, int64_t S,
   check_bf16(x, "x");
   const int T = x.size(0), D = x.size(1), N = W.size(1);
   HB_CHECK(N <= MAXN && K <= MAXK && K <= N, "router: N <= 256, K <= 16");
+  HB_CHECK(W.is_contiguous() && W.scalar_type() == torch::kFloat32, "router: fp32 contiguous W");
   if (T == 0) return;
   const int grid = (T + RT_TOK - 1) / RT_TOK;
+  const int epl = (N + 31) / 32;
+  if (router_tc_ok(x, N)) {
+    // fp32-accurate logits on the tensor cores: x @ [hi | mid | lo], summed in the select kernel
+    auto w3 = router_split_w(W).first;
+    auto l3 = torch::empty({T, 3 * N}, x.options().dtype(torch::kFloat32));
+    gemm(x, w3, l3, false, false, false, 1.0, c10::nullopt);
+    auto kern = epl == 1 ? router_select_kernel<1> : epl == 2 ? router_select_kernel<2>
+              : epl <= 4 ? router_select_kernel<4> : router_select_kernel<8>;
+    kern<<<grid, 256, 0, cur_stream()>>>(
+        l3.data_ptr<float>(), bias.data_ptr<float>(), T, (int)S, N, (int)K, softmax_mode ? 1 : 0,
+        (float)scaling, logits.data_ptr<float>(), topi.data_ptr<int>(), topw.data_ptr<float>(),
+        seq_counts.data_ptr<float>(), seq_probs.data_ptr<float>(), sums.data_ptr<float>());
+    HB_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   const int DC = std::max(32, std::min(D, (int)(RT_SMEM_W / (N * sizeof(float)))) / 32 * 32);
   const size_t smem = (size_t)(DC * N + RT_TOK * N + 2 * RT_NSEQ * N) * sizeof(float);
-  const int epl = (N + 31) / 32;
   auto kern = epl == 1 ? router_fwd_kernel<1> : epl == 2 ? router_fwd_kernel<2>
             : epl <= 4 ? router_fwd_kernel<4> : router_fwd_kernel<8>;
   HB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -584,6 +721,21 @@ void router_bwd(torch::Tensor logits, torch::Tensor topi, torch::Tensor dtopw, t
 void router_grads(torch::Tensor x, torch::Tensor W, torch::Tensor dl, torch::Tensor dx, torch::Tensor dW) {
   const int T = x.size(0), D = x.size(1), N = W.size(1);
   if (T == 0) return;
+  HB_CHECK(dx.scalar_type() == torch::kFloat32 && dW.scalar_type() == torch::kFloat32 &&
+               dl.is_contiguous(), "router_grads: fp32 dx / dW, contiguous dl");
+  if (router_tc_ok(x, N) && dx.stride(1) == 1 && dx.stride(0) % 4 == 0 && dW.is_contiguous()) {
+    // dx += [dl_hi | dl_lo | dl_hi] @ [W_hi | W_hi | W_mid]^T ;  dW += x^T dl_hi + x^T dl_lo
+    auto w3x = router_split_w(W).second;
+    auto a3 = torch::empty({T, 3 * N}, x.options());
+    const long long n = (long long)T * N;
+    router_split_dl_kernel<<<grid_for(n, 256), 256, 0, cur_stream()>>>(dl.data_ptr<float>(), n, N,
+                                                                      (__nv_bfloat16*)a3.data_ptr());
+    HB_CUDA_CHECK(cudaGetLastError());
+    gemm(a3, w3x, dx, false, true, true, 1.0, c10::nullopt);
+    gemm(x, a3.narrow(1, 0, N), dW, true, false, true, 1.0, c10::nullopt);
+    gemm(x, a3.narrow(1, N, N), dW, true, false, true, 1.0, c10::nullopt);
+    return;
+  }
   {
     static bool cfg = false;
     if (!cfg) {

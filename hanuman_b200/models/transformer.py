@@ -39,20 +39,25 @@ class Block(nn.Module):
             self.ffn = DenseFFN(cfg.d_model, cfg.d_ff_shared, gen)
         self.residual_scale = nn.Parameter(torch.tensor(float(cfg.residual_scale_init)))
 
+    def mix(self, h, cos, sin, dtype, positions=None, cache=None):
+        """Token mixer (attention or KDA) on the normed input."""
+        if self.attention_type == "kda":
+            return self.attn(h, dtype, state=None if cache is None else cache.kda_state(self.layer))
+        return self.attn(h, cos, sin, dtype, positions=positions,
+                         cache=None if cache is None else cache.kv(self.layer))
+
+    def feed_forward(self, h, dtype):
+        if self.use_moe:
+            return self.ffn(h, dtype)
+        return self.ffn(h, dtype), {}
+
     def forward(self, x, cos, sin, dtype, positions=None, cache=None):
         rs = self.residual_scale.float()
         h = self.norm1(x, dtype)
-        if self.attention_type == "kda":
-            a = self.attn(h, dtype, state=None if cache is None else cache.kda_state(self.layer))
-        else:
-            a = self.attn(h, cos, sin, dtype, positions=positions,
-                          cache=None if cache is None else cache.kv(self.layer))
+        a = self.mix(h, cos, sin, dtype, positions, cache)
         x = x + rs * a
         h = self.norm2(x, dtype)
-        if self.use_moe:
-            f, aux = self.ffn(h, dtype)
-        else:
-            f, aux = self.ffn(h, dtype), {}
+        f, aux = self.feed_forward(h, dtype)
         x = x + rs * f
         return x, aux
 
@@ -90,9 +95,34 @@ class Transformer(nn.Module):
             return embedding_cuda(tokens, self.wte)
         return self.wte[tokens].float()
 
+    def _fused_residual_ok(self, x, cache) -> bool:
+        D = self.cfg.d_model
+        return (x.is_cuda and cache is None and self.dtype == torch.bfloat16 and D % 4 == 0
+                and D <= 2048)
+
+    def _forward_fused(self, x, positions):
+        """CUDA path: every residual add is fused with the RMSNorm that follows
+        it (norm2 of the same block, norm1 of the next block, or norm_f)."""
+        from ..ops.norm import add_rms_norm_cuda
+        dtype = self.dtype
+        aux_list = []
+        h = self.blocks[0].norm1(x, dtype)
+        nb = len(self.blocks)
+        for i, blk in enumerate(self.blocks):
+            a = blk.mix(h, self.rope_cos, self.rope_sin, dtype, positions)
+            x, h = add_rms_norm_cuda(x, a, blk.residual_scale, blk.norm2.weight, blk.norm2.eps)
+            f, aux = blk.feed_forward(h, dtype)
+            if aux:
+                aux_list.append(aux)
+            nxt = self.blocks[i + 1].norm1 if i + 1 < nb else self.norm_f
+            x, h = add_rms_norm_cuda(x, f, blk.residual_scale, nxt.weight, nxt.eps)
+        return h, merge_aux(aux_list, self.cfg.n_experts, self.n_moe, x.device)
+
     def forward(self, tokens, positions=None, cache=None):
         dtype = self.dtype
         x = self.embed(tokens)
+        if self._fused_residual_ok(x, cache):
+            return self._forward_fused(x, positions)
         aux_list = []
         for blk in self.blocks:
             x, aux = blk(x, self.rope_cos, self.rope_sin, dtype, positions, cache)

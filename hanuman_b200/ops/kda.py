@@ -4,7 +4,7 @@
     braw = h @ wb;  f = f0 @ f_proj1;  gl = g0 @ g_proj1  (fp32 outputs)
     q, k, v, g, beta = prep(...)   conv4 + SiLU (+ L2 norm for q, k), decay, sigmoid
     o = chunked gated delta rule (fp32)
-    y = RMSNorm_V(o) * o_norm * sigmoid(gl + bias) @ wo
+    y = RMSNorm_V(o) * o_norm * sigmoid(gl + bias) @ wo   (norm and gate in one kernel)
 """
 from __future__ import annotations
 
@@ -106,6 +106,34 @@ class KdaPrepFn(torch.autograd.Function):
         return (draw, df, dbraw, dwq, dwk, dwv, d_alog, d_dtb, None, None, None, None)
 
 
+class KdaOutGateFn(torch.autograd.Function):
+    """y = RMSNorm_K(o) * o_norm * sigmoid(gl + g_bias) as bf16 (one fused kernel each way)."""
+
+    @staticmethod
+    def forward(ctx, o, gl, w, gb):
+        T, H, K = o.shape
+        o = o.contiguous()
+        gl = gl.float().contiguous()
+        y = torch.empty(T, H * K, dtype=torch.bfloat16, device=o.device)
+        rstd = torch.empty(T * H, dtype=torch.float32, device=o.device)
+        wf, gbf = w.float().contiguous(), gb.float().contiguous()
+        ext().kda_out_gate_fwd(o, gl, wf, gbf, 1e-5, y, rstd)
+        ctx.save_for_backward(o, gl, wf, gbf, rstd)
+        ctx.dtypes = (w.dtype, gb.dtype)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        o, gl, wf, gbf, rstd = ctx.saved_tensors
+        dy = dy.to(torch.bfloat16).contiguous()
+        do = torch.empty_like(o)
+        dgl = torch.empty_like(gl)
+        dw = torch.zeros_like(wf)
+        dgb = torch.zeros_like(gbf)
+        ext().kda_out_gate_bwd(dy, o, gl, wf, gbf, rstd, do, dgl, dw, dgb)
+        return do, dgl, dw.to(ctx.dtypes[0]), dgb.to(ctx.dtypes[1])
+
+
 def kda_layer_cuda(mod, h, dtype):
     B, S, D = h.shape
     T = B * S
@@ -122,9 +150,12 @@ def kda_layer_cuda(mod, h, dtype):
                                        mod.v_conv.weight, mod.a_log, mod.dt_bias, gate_mode, S, H, K)
     o = KdaCoreFn.apply(q.view(B, S, H, K), k.view(B, S, H, K), v.view(B, S, H, K),
                         g.view(B, S, H, K), beta.view(B, S, H), 1.0 / math.sqrt(K))
-    var = (o * o).mean(-1, keepdim=True)
-    on = o * torch.rsqrt(var + 1e-5) * mod.o_norm
-    gate = torch.sigmoid(gl + mod.g_proj1_bias).view(B, S, H, K)
-    y = (on * gate).reshape(T, HK).to(torch.bfloat16)
+    if K in (32, 64, 128):
+        y = KdaOutGateFn.apply(o.view(T, H, K), gl, mod.o_norm, mod.g_proj1_bias)
+    else:
+        var = (o * o).mean(-1, keepdim=True)
+        on = o * torch.rsqrt(var + 1e-5) * mod.o_norm
+        gate = torch.sigmoid(gl + mod.g_proj1_bias).view(B, S, H, K)
+        y = (on * gate).reshape(T, HK).to(torch.bfloat16)
     out = linear_fused(y, [mod.wo], torch.float32)
     return out.view(B, S, D)

@@ -33,6 +33,48 @@ def rms_norm_cuda(x, w, eps, out_dtype):
     return RMSNormFn.apply(x, w, eps, out_dtype)
 
 
+class AddNormFn(torch.autograd.Function):
+    """``x_new = x + rs * a`` and ``h = RMSNorm(x_new) * w`` (bf16) in one kernel
+    each way; ``rs`` is the block's residual-scale parameter (read on the
+    device, no host synchronisation)."""
+
+    @staticmethod
+    def forward(ctx, x, a, rs, w, eps):
+        shape = x.shape
+        D = shape[-1]
+        x2 = x.float().reshape(-1, D).contiguous()
+        a2 = a.float().reshape(-1, D).contiguous()
+        T = x2.shape[0]
+        xn = torch.empty_like(x2)
+        h = torch.empty(T, D, dtype=torch.bfloat16, device=x.device)
+        rstd = torch.empty(T, dtype=torch.float32, device=x.device)
+        rsf = rs.detach().float().reshape(1).contiguous()
+        wf = w.detach().float().contiguous()
+        ext().add_norm_fwd(x2, a2, rsf, wf, eps, xn, h, rstd)
+        ctx.save_for_backward(xn, a2, rsf, wf, rstd)
+        ctx.meta = (shape, rs.dtype, w.dtype)
+        return xn.view(shape), h.view(shape)
+
+    @staticmethod
+    def backward(ctx, g, dh):
+        xn, a2, rsf, wf, rstd = ctx.saved_tensors
+        shape, rs_dtype, w_dtype = ctx.meta
+        D = shape[-1]
+        dh = (torch.zeros(xn.shape, dtype=torch.bfloat16, device=xn.device) if dh is None
+              else dh.reshape(-1, D).to(torch.bfloat16).contiguous())
+        g = None if g is None else g.reshape(-1, D).float().contiguous()
+        dx = torch.empty_like(xn)
+        da = torch.empty_like(xn)
+        drs = torch.zeros(1, dtype=torch.float32, device=xn.device)
+        dw = torch.zeros(D, dtype=torch.float32, device=xn.device)
+        ext().add_norm_bwd(g, dh, xn, a2, rsf, wf, rstd, dx, da, drs, dw)
+        return dx.view(shape), da.view(shape), drs.reshape(()).to(rs_dtype), dw.to(w_dtype), None
+
+
+def add_rms_norm_cuda(x, a, rs, w, eps):
+    return AddNormFn.apply(x, a, rs, w, eps)
+
+
 class RopeFn(torch.autograd.Function):
     """In-place rotary embedding of ``x [B, S, N, H]`` (bf16)."""
 

@@ -279,3 +279,72 @@ def test_no_kernel_reported_errors():
     from hanuman_b200.ops._ext import ext
     torch.cuda.synchronize()
     assert ext().read_status() == 0
+
+
+@pytest.mark.parametrize("N", [32, 12])
+def test_router_logits_and_grads_match_fp32(N):
+    """N=32 runs the split-bf16 tensor-core GEMM route, N=12 the SIMT route."""
+    from hanuman_b200.ops._ext import ext
+    torch.manual_seed(11)
+    T, D, S, K = 1024, 512, 256, 4
+    x = torch.randn(T, D, device=DEV).bfloat16()
+    W = torch.randn(D, N, device=DEV) * 0.02
+    bias = torch.zeros(N, device=DEV)
+    lg = torch.empty(T, N, device=DEV)
+    ti = torch.empty(T, K, dtype=torch.int32, device=DEV)
+    tw = torch.empty(T, K, device=DEV)
+    sc, sp = torch.zeros(T // S, N, device=DEV), torch.zeros(T // S, N, device=DEV)
+    su = torch.zeros(2, device=DEV)
+    ext().router_fwd(x, W, bias, S, K, False, 2.5, lg, ti, tw, sc, sp, su)
+    ref_lg = x.double() @ W.double()
+    assert (lg.double() - ref_lg).abs().max().item() < 1e-5
+    want = torch.topk(torch.sigmoid(ref_lg), K, dim=-1).indices
+    assert torch.equal(ti.long().sort(-1)[0], want.sort(-1)[0])
+    assert torch.equal(sc.sum(0), torch.bincount(ti.flatten().long(), minlength=N).float())
+    dl = torch.randn(T, N, device=DEV)
+    dx = torch.randn(T, D, device=DEV)
+    dx0 = dx.clone()
+    dW = torch.zeros(D, N, device=DEV)
+    ext().router_grads(x, W, dl, dx, dW)
+    assert rel(dx - dx0, dl @ W.t()) < 1e-4
+    assert rel(dW, x.float().t() @ dl) < 1e-4
+
+
+def test_add_norm_fwd_bwd():
+    from hanuman_b200.ops.norm import add_rms_norm_cuda
+    torch.manual_seed(12)
+    B, S, D = 2, 100, 1024
+    x = torch.randn(B, S, D, device=DEV, requires_grad=True)
+    a = torch.randn(B, S, D, device=DEV, requires_grad=True)
+    rs = torch.tensor(0.7, device=DEV, requires_grad=True)
+    w = (1 + 0.1 * torch.randn(D, device=DEV)).requires_grad_()
+    xn, h = add_rms_norm_cuda(x, a, rs, w, 1e-6)
+    xr = [t.detach().clone().requires_grad_() for t in (x, a, rs, w)]
+    xnr = xr[0] + xr[2] * xr[1]
+    hr = xnr * torch.rsqrt((xnr * xnr).mean(-1, keepdim=True) + 1e-6) * xr[3]
+    assert rel(xn, xnr) < 1e-6 and rel(h, hr) < 1e-2
+    g1, g2 = torch.randn_like(xnr), torch.randn_like(hr)
+    ((xn * g1).sum() + (h.float() * g2).sum()).backward()
+    ((xnr * g1).sum() + (hr * g2.bfloat16().float()).sum()).backward()
+    for got, want, name in zip((x, a, rs, w), xr, "x a rs w".split()):
+        assert rel(got.grad, want.grad) < 1e-3, name
+
+
+def test_kda_out_gate_fwd_bwd():
+    from hanuman_b200.ops.kda import KdaOutGateFn
+    torch.manual_seed(13)
+    T, H, K = 300, 4, 64
+    o = torch.randn(T, H, K, device=DEV, requires_grad=True)
+    gl = torch.randn(T, H * K, device=DEV, requires_grad=True)
+    w = (1 + 0.1 * torch.randn(K, device=DEV)).requires_grad_()
+    gb = (0.1 * torch.randn(H * K, device=DEV)).requires_grad_()
+    y = KdaOutGateFn.apply(o, gl, w, gb)
+    r = [t.detach().clone().requires_grad_() for t in (o, gl, w, gb)]
+    on = r[0] * torch.rsqrt((r[0] * r[0]).mean(-1, keepdim=True) + 1e-5) * r[2]
+    yr = (on * torch.sigmoid(r[1] + r[3]).view(T, H, K)).reshape(T, H * K)
+    assert rel(y, yr) < 1e-2
+    g = torch.randn_like(yr)
+    (y.float() * g).sum().backward()
+    (yr * g.bfloat16().float()).sum().backward()
+    for got, want, name in zip((o, gl, w, gb), r, "o gl w gb".split()):
+        assert rel(got.grad, want.grad) < 1e-3, name
