@@ -115,6 +115,34 @@ HB_DEVICE void tma_load_3d(uint32_t dst, const CUtensorMap* d, uint32_t mbar, in
       : "memory");
 }
 
+// TMA store of a 3-D box from shared memory (bulk-group completion).
+HB_DEVICE void tma_store_3d(const CUtensorMap* d, uint32_t src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(d)),
+               "r"(src), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+HB_DEVICE void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until every committed bulk store of this thread has completed its writes.
+HB_DEVICE void bulk_wait_group_0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders global-memory accesses of the async proxy (TMA) against the generic proxy.
+HB_DEVICE void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+HB_DEVICE int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+HB_DEVICE int ld_relaxed_gpu(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// With relaxed loads that observed released values, gives them acquire semantics.
+HB_DEVICE void fence_acquire_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+HB_DEVICE void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // ------------------------------------------------------------------- tcgen05
 // TMEM allocation (whole warp).  Writes the TMEM base address to *dst_smem.
 HB_DEVICE void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {

@@ -56,6 +56,91 @@ struct GemmArgs {
   unsigned long long budget_ns;
 };
 
+// Fused all-gather of the B operand (FSDP expert weights), GROUPED_M only.
+// B[g] lives on rank g / groups_per_rank (its shard of groups); every B tile
+// (group, k-block, n-block) is fetched ONCE per GPU (over NVLink unless this
+// GPU owns it): the first CTA that needs it claims flags[tile] (0 -> 1), TMA-loads it
+// from the owner's memory into its smem stage (plain TMA load, no multicast),
+// feeds it to the MMA and TMA-stores the same stage into the local gathered
+// copy, then publishes flags[tile] = 2.  Every other CTA waits (bounded) for
+// 2 and loads the tile from the local copy.  The claimant never waits on
+// anyone, so the scheme cannot deadlock.
+constexpr int GATHER_MAX_PEERS = 8;
+struct alignas(64) GatherMaps {
+  CUtensorMap peer[GATHER_MAX_PEERS];  // rank r's shard of B: [groups_per_rank, K, N]
+  CUtensorMap local;                   // gathered copy on this GPU: [G, K, N]
+  const __nv_bfloat16* src[GATHER_MAX_PEERS];  // the same shards as plain pointers
+  __nv_bfloat16* dst;                  // the gathered copy
+  int* flags;                          // [G][tiles_n][k_blocks]
+  int rank, world, groups_per_rank;
+};
+
+// Copy-ahead of the gathered B tiles by two extra warps (warps 6-7 of the
+// gathered variant), concurrent with the producer, MMA and epilogue.  CTA i takes tiles
+// i, i + grid, ... in the order the tile schedule needs them, claims each with
+// the same flag protocol as the producer (so a tile is copied exactly once)
+// and moves it with 16-byte peer loads / local stores.  Groups without rows
+// are skipped.
+constexpr int GATHER_COPY_THREADS = 64;  // two extra warps in the gathered variant
+
+template <int BN>
+__device__ void gather_copy_ahead(const GemmArgs& args, const GatherMaps& gm) {
+  constexpr int CT = GATHER_COPY_THREADS;
+  constexpr int PER = 16;                        // 16-byte pieces in flight per thread
+  constexpr int ROUNDS = GEMM_BK * BN / 8 / CT / PER;
+  static_assert(ROUNDS * PER * CT * 8 == GEMM_BK * BN, "copy split");
+  __shared__ int s_claim[2];
+  const int tid = threadIdx.x - (GEMM_THREADS);  // 0..CT-1
+  const int K = args.K, N = args.N, TN = args.tiles_n;
+  const int KB = (K + GEMM_BK - 1) / GEMM_BK;
+  const long long total = (long long)args.num_groups * KB * TN;
+  int it = 0;
+  for (long long c = blockIdx.x; c < total; c += gridDim.x) {
+    const int nb = c % TN;
+    const int kb = (c / TN) % KB;
+    const int g = c / ((long long)TN * KB);
+    if (__ldg(args.grp_count + g) == 0) continue;
+    int* flag = gm.flags + ((long long)g * TN + nb) * KB + kb;
+    // claim broadcast through alternating slots: one barrier per tile
+    if (tid == 0) s_claim[it & 1] = ld_acquire_gpu(flag) == 0 && atomicCAS(flag, 0, 1) == 0;
+    asm volatile("bar.sync 1, %0;" ::"n"(CT) : "memory");
+    const bool won = s_claim[it & 1];
+    ++it;
+    if (!won) continue;
+    const int owner = g / gm.groups_per_rank;
+    const int k0 = kb * GEMM_BK, n0 = nb * BN;
+    const int rows = min(GEMM_BK, K - k0), cols = min(BN, N - n0);
+    const __nv_bfloat16* src = gm.src[owner] + ((long long)(g - owner * gm.groups_per_rank) * K + k0) * N + n0;
+    __nv_bfloat16* dst = gm.dst + ((long long)g * K + k0) * N + n0;
+    const int c8 = cols / 8;  // N % 8 == 0: 16-byte pieces
+    const int n8 = rows * c8;
+#pragma unroll 1
+    for (int rd = 0; rd < ROUNDS; ++rd) {
+      uint4 v[PER];
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {  // every load of the round in flight before the stores
+        const int i = tid + CT * (rd * PER + j);
+        if (i < n8) {
+          const int r = i / c8, q = i - r * c8;
+          v[j] = *reinterpret_cast<const uint4*>(src + (long long)r * N + 8 * q);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {
+        const int i = tid + CT * (rd * PER + j);
+        if (i < n8) {
+          const int r = i / c8, q = i - r * c8;
+          *reinterpret_cast<uint4*>(dst + (long long)r * N + 8 * q) = v[j];
+        }
+      }
+    }
+    __threadfence();
+    fence_proxy_async_global();
+    asm volatile("bar.sync 1, %0;" ::"n"(CT) : "memory");
+    if (tid == 0) st_release_gpu(flag, 2);
+  }
+}
+
 template <int BN>
 struct GemmCfg {
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
@@ -119,10 +204,11 @@ __device__ __forceinline__ bool get_tile(const GemmArgs& a, int t, TileInfo& ti)
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int MODE, int EPI>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+template <int BN, bool A_MN, bool B_MN, int MODE, int EPI, bool GATHER = false>
+__global__ void __launch_bounds__(GATHER ? GEMM_THREADS + GATHER_COPY_THREADS : GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmArgs args) {
+                   const GemmArgs args, const __grid_constant__ GatherMaps gm) {
+  static_assert(!GATHER || (MODE == GROUPED_M && B_MN), "gathered B: grouped-M, MN-major B");
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -170,6 +256,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       for (int t = blockIdx.x; ok; t += gridDim.x) {
         TileInfo ti;
         if (!get_tile<MODE, BN>(args, t, ti)) break;
+        // gathered B: one parallel read of the tile column's flags; when all
+        // are published the k-loop loads from the local copy without checks
+        int* fcol = nullptr;
+        bool col_ready = false;
+        if (GATHER) {
+          fcol = gm.flags + ((long long)ti.group * args.tiles_n + ti.n0 / BN) * ti.k_iters;
+          int nr = 0;
+#pragma unroll 8
+          for (int kb = 0; kb < ti.k_iters; ++kb) nr += ld_relaxed_gpu(fcol + kb) == 2;
+          col_ready = nr == ti.k_iters;
+          if (col_ready) {
+            fence_acquire_gpu();
+            fence_proxy_async_global();
+          }
+        }
         for (int kb = 0; kb < ti.k_iters; ++kb) {
           if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, args.status, kErrTimeoutProducer,
                          args.budget_ns)) {
@@ -187,7 +288,49 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
             for (int i = 0; i < GEMM_BM / 64; ++i) tma_load_2d(sa + i * 8192, &tmA, fb, ti.m0 + 64 * i, kc);
           }
-          if (MODE == GROUPED_M) {
+          if (GATHER) {
+            // own experts go through the same claim / copy path (a local copy),
+            // so the gathered buffer is complete for the backward
+            const int g = ti.group;
+            const int owner = g / gm.groups_per_rank;
+            if (col_ready) {
+#pragma unroll
+              for (int i = 0; i < BN / 64; ++i) tma_load_3d(sb + i * 8192, &gm.local, fb, ti.n0 + 64 * i, kc, g);
+            } else {
+              int* flag = fcol + kb;
+              const bool won = ld_acquire_gpu(flag) == 0 && atomicCAS(flag, 0, 1) == 0;
+              if (won) {
+#pragma unroll
+                for (int i = 0; i < BN / 64; ++i)
+                  tma_load_3d(sb + i * 8192, &gm.peer[owner], fb, ti.n0 + 64 * i, kc,
+                              g - owner * gm.groups_per_rank);
+                // the stage also feeds the MMA; wait for it here and copy it out
+                if (!mbar_wait(fb, phase, args.status, kErrTimeoutProducer, args.budget_ns)) {
+                  ok = false;
+                  break;
+                }
+#pragma unroll
+                for (int i = 0; i < BN / 64; ++i) tma_store_3d(&gm.local, sb + i * 8192, ti.n0 + 64 * i, kc, g);
+                bulk_commit_group();
+                bulk_wait_group_0();
+                fence_proxy_async_global();
+                st_release_gpu(flag, 2);
+              } else {
+                const uint64_t t0 = globaltimer();
+                while (ld_acquire_gpu(flag) != 2) {
+                  if (globaltimer() - t0 > args.budget_ns) {
+                    set_error(args.status, kErrTimeoutPeer);
+                    ok = false;
+                    break;
+                  }
+                }
+                if (!ok) break;
+                fence_proxy_async_global();
+#pragma unroll
+                for (int i = 0; i < BN / 64; ++i) tma_load_3d(sb + i * 8192, &gm.local, fb, ti.n0 + 64 * i, kc, g);
+              }
+            }
+          } else if (MODE == GROUPED_M) {
             if (!B_MN) {
               tma_load_3d(sb, &tmB, fb, kc, ti.n0, ti.group);
             } else {
@@ -262,6 +405,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (acc == 0) acc_phase ^= 1;
       }
     }
+  } else if (GATHER && warp >= GEMM_THREADS / 32) {
+    // ------------------------------------------------------------ copy warps
+    gather_copy_ahead<BN>(args, gm);
   } else {
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;  // TMEM lane quadrant accessible to this warp
@@ -354,16 +500,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 }
 
 
-template <int BN, bool A_MN, bool B_MN, int MODE, int EPI>
-void gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid) {
+template <int BN, bool A_MN, bool B_MN, int MODE, int EPI, bool GATHER = false>
+void gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
+                 const GatherMaps* gm = nullptr) {
   using Cfg = GemmCfg<BN>;
-  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, MODE, EPI>;
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, MODE, EPI, GATHER>;
   static bool configured = false;  // one static per instantiation
   if (!configured) {
     HB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
     configured = true;
   }
-  kern<<<grid, GEMM_THREADS, Cfg::SMEM, cur_stream()>>>(ta, tb, args);
+  static const GatherMaps none{};
+  kern<<<grid, GATHER ? GEMM_THREADS + GATHER_COPY_THREADS : GEMM_THREADS, Cfg::SMEM, cur_stream()>>>(
+      ta, tb, args, gm ? *gm : none);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -374,5 +523,6 @@ void gemm_dispatch_dense_amn(int bn, bool b_mn, int epi, const CUtensorMap& ta, 
                              const GemmArgs& args, int grid);
 void gemm_dispatch_grouped(int mode, int bn, bool a_mn, bool b_mn, int epi, const CUtensorMap& ta,
                            const CUtensorMap& tb, const GemmArgs& args, int grid);
+void gemm_dispatch_gather(int bn, const CUtensorMap& ta, const GemmArgs& args, const GatherMaps& gm, int grid);
 
 }  // namespace hb

@@ -140,6 +140,12 @@ class Config:
     micro_batch: int = 0
     # Use the hand-written fused compute+collective paths when world > 1.
     fused_comm: bool = True
+    # MoE expert weights under data parallelism (no expert axis): "replicated"
+    # keeps the full bf16 working copy on every rank (the optimizer stores each
+    # updated shard into every peer); "fused_gather" keeps only the rank's own
+    # experts current and pulls the others inside the first grouped GEMM that
+    # consumes them (all-gather fused with the GEMM, over peer memory).
+    expert_weights: str = "replicated"
     seed: int = 0
 
     # ------------------------------------------------------------------

@@ -65,6 +65,8 @@ class FlatGroup:
     hi: int = 0
     trainable: torch.Tensor = None  # 1.0 where the element receives updates
     local: bool = False             # expert-parallel slice owned by this rank only
+    gathered: bool = False          # one expert-weight tensor, shards = whole experts,
+                                    # gathered by the consuming grouped GEMM
 
 
 def _build_group(named, dtype, device, world, rank, master_init) -> Optional[FlatGroup]:
@@ -124,6 +126,12 @@ class Engine:
         for unit in self.units:
             local = [(n, p) for n, p in unit if getattr(p, "_ep_local", False)]
             rest = [(n, p) for n, p in unit if not getattr(p, "_ep_local", False)]
+            gath = [(n, p) for n, p in rest if getattr(p, "_fsdp_gather", False)]
+            rest = [(n, p) for n, p in rest if not getattr(p, "_fsdp_gather", False)]
+            for n, p in gath:   # one group per tensor: the shards are whole experts
+                g = _build_group([(n, p)], cdt, self.device, world, rank, master_init)
+                g.gathered = g.numel == p.numel() and p.shape[0] % world == 0
+                self.groups.append(g)
             mats = [(n, p) for n, p in rest if _is_matrix(n, p)]
             smalls = [(n, p) for n, p in rest if not _is_matrix(n, p)]
             for named, dt, loc in ((mats, cdt, False), (smalls, torch.float32, False),

@@ -26,6 +26,7 @@ def _apply_overrides(config, args):
         "optimizer": "optimizer", "router_type": "router_type",
         "capacity_factor": "capacity_factor", "micro_batch": "micro_batch",
         "checkpoint_every": "checkpoint_every", "fused_comm": "fused_comm",
+        "expert_weights": "expert_weights",
     }
     for a, f in mapping.items():
         v = getattr(args, a, None)
@@ -103,6 +104,7 @@ def build_parser():
                    choices=["full", "dots", "dots_no_batch", "experts", "none"])
     t.add_argument("--optimizer", default=None, choices=["lion", "adamw"])
     t.add_argument("--router_type", default=None, choices=["sigmoid_bias", "softmax"])
+    t.add_argument("--expert_weights", default=None, choices=["replicated", "fused_gather"])
     t.add_argument("--random_data", action="store_true")
     t.add_argument("--no_save", action="store_true")
     t.add_argument("--resume", action="store_true", help="continue from the latest checkpoint")

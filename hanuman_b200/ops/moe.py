@@ -74,6 +74,25 @@ def swiglu_ffn_cuda(x, wg, wu, wd, dtype=torch.bfloat16):
     return SwiGLUFFNFn.apply(x, wg, wu, wd)
 
 
+class ExpertGather:
+    """Per-MoE-layer state of the fused expert-weight all-gather: every rank's
+    shard address of each expert tensor, the local gathered copies and the
+    tile flags shared by the three GEMMs (they run one after another)."""
+
+    def __init__(self, ptrs: dict, rank: int, groups_per_rank: int, shapes: dict, device):
+        self.ptrs, self.rank, self.gpr = ptrs, rank, groups_per_rank
+        self.bufs = {k: torch.empty(s, dtype=torch.bfloat16, device=device) for k, s in shapes.items()}
+        n = 0
+        for s in shapes.values():
+            G, Kd, Nd = s
+            n = max(n, G * ((Kd + 63) // 64) * ((Nd + _bn(Nd) - 1) // _bn(Nd)))
+        self.flags = torch.zeros(n, dtype=torch.int32, device=device)
+
+    def gemm(self, a, name, c, starts, counts, tprefix):
+        ext().grouped_gemm_m_gather(a, self.ptrs[name], self.rank, self.gpr, self.bufs[name],
+                                    self.flags, c, starts, counts, tprefix)
+
+
 class MoEFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, h, mod, B, S):
@@ -114,12 +133,23 @@ class MoEFn(torch.autograd.Function):
         xp = torch.empty(R, D, dtype=torch.bfloat16, device=dev)
         ext().moe_gather(xb, row_src, xp, K)
         gu = torch.empty(R, 2 * F, dtype=torch.bfloat16, device=dev)
-        ext().grouped_gemm_m(xp, wg, gu[:, :F], starts, counts, tprefix_f, False)
-        ext().grouped_gemm_m(xp, wu, gu[:, F:], starts, counts, tprefix_f, False)
+        gat = getattr(mod, "_gather", None)
+        if gat is not None:
+            # FSDP expert weights: the all-gather runs inside these GEMMs (peer
+            # tiles land in gat.bufs, which the backward then reads)
+            wg, wu, wd = (gat.bufs[k] for k in ("expert_w_gate", "expert_w_up", "expert_w_down"))
+            gat.gemm(xp, "expert_w_gate", gu[:, :F], starts, counts, tprefix_f)
+            gat.gemm(xp, "expert_w_up", gu[:, F:], starts, counts, tprefix_f)
+        else:
+            ext().grouped_gemm_m(xp, wg, gu[:, :F], starts, counts, tprefix_f, False)
+            ext().grouped_gemm_m(xp, wu, gu[:, F:], starts, counts, tprefix_f, False)
         hh = torch.empty(R, F, dtype=torch.bfloat16, device=dev)
         ext().swiglu_fwd(gu, hh, row_src)  # pad rows -> 0 (grouped-K reads them)
         y = torch.empty(R, D, dtype=torch.bfloat16, device=dev)
-        ext().grouped_gemm_m(hh, wd, y, starts, counts, tprefix_d, False)
+        if gat is not None:
+            gat.gemm(hh, "expert_w_down", y, starts, counts, tprefix_d)
+        else:
+            ext().grouped_gemm_m(hh, wd, y, starts, counts, tprefix_d, False)
         # shared expert (fp32 out) + combine
         if mod.n_shared != 1:
             raise NotImplementedError("GPU MoE supports one shared expert")
@@ -143,6 +173,7 @@ class MoEFn(torch.autograd.Function):
         ctx.save_for_backward(xb, logits, topi, topw, pos, row_src, starts, counts, padded,
                               tprefix_f, tprefix_d, xp, gu, hh, y, sgu, shh, frac)
         ctx.mod = mod
+        ctx.expert_w = (wg, wu, wd)
         ctx.meta = (B, S, T, D, N, K, F, Fs, R, softmax)
         ctx.mark_non_differentiable(ent, expert_counts)
         return out, z, bal, ent, expert_counts
@@ -172,7 +203,7 @@ class MoEFn(torch.autograd.Function):
         dy = torch.empty(R, D, dtype=torch.bfloat16, device=dev)
         dtopw = torch.empty(T, K, dtype=torch.float32, device=dev)
         ext().moe_combine_bwd(dout, y, pos, topw, row_src, dy, dtopw)
-        wg, wu, wd = _work(mod.expert_w_gate), _work(mod.expert_w_up), _work(mod.expert_w_down)
+        wg, wu, wd = ctx.expert_w
         dhh = torch.empty(R, F, dtype=torch.bfloat16, device=dev)
         ext().grouped_gemm_m(dy, wd, dhh, starts, counts, tprefix_f, True)
         ext().grouped_gemm_k(hh, dy, main_grad(mod.expert_w_down), starts, padded, True)

@@ -22,6 +22,10 @@ Two transports implement the two collectives:
   working values into EVERY peer's working copy with peer stores, so the
   all-gather disappears into the optimizer.  Selected with ``cfg.fused_comm``
   when symmetric memory is available; otherwise NCCL.
+* ``expert_weights = "fused_gather"`` (with ``p2p``): the MoE expert tensors
+  are sharded by expert and only their owner updates them; the forward's
+  grouped GEMMs pull the other experts' tiles from the owners' memory
+  (model/moe.py:202-245 gathers them with ``all_gather(tiled)`` instead).
 
 With 180 GB per GPU the full working copy stays resident (no re-gather in the
 backward), which is what makes the all-gather a once-per-step operation.
@@ -50,6 +54,31 @@ class FSDPEngine(Engine):
                 if ctx.rank == 0:
                     print(f"[fsdp] fused peer-memory transport unavailable ({e}); using NCCL")
                 self.p2p = None
+        self._attach_expert_gather()
+
+    def _attach_expert_gather(self):
+        """Hand each MoE layer the shard addresses of its gathered expert tensors."""
+        gathered = [g for g in self.groups if g.gathered]
+        if not gathered:
+            return
+        if self.p2p is None:
+            # no peer memory: these groups fall back to the NCCL all-gather
+            for g in gathered:
+                g.gathered = False
+            return
+        from ..ops.moe import ExpertGather
+        by_layer = {}
+        for g in gathered:
+            name = g.names[0]
+            layer, leaf = name.rsplit(".", 1)
+            by_layer.setdefault(layer, {})[leaf] = (self.p2p.gather_ptrs[name], g.params[0])
+        for layer, d in by_layer.items():
+            mod = self.model.get_submodule(layer)
+            if set(d) != {"expert_w_gate", "expert_w_up", "expert_w_down"}:
+                raise RuntimeError(f"{layer}: expert tensors must all be gathered")
+            N = d["expert_w_gate"][1].shape[0]
+            mod._gather = ExpertGather({k: v[0] for k, v in d.items()}, self.rank, N // self.world,
+                                       {k: tuple(v[1].shape) for k, v in d.items()}, self.device)
 
     # ------------------------------------------------------------------
     def reduce_grads(self, loss, counts):

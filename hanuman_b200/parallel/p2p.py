@@ -11,6 +11,12 @@ kernels per flat group and three device-side barriers per step:
 
 No host synchronisation and no NCCL call is on this path except the one-float
 all-reduce of the squared gradient norm.
+
+Expert-weight tensors marked for the fused gather (``expert_weights =
+"fused_gather"``) are updated in place on their owner only; their forward
+consumers pull the other ranks' experts over NVLink inside the grouped GEMM
+(``grouped_gemm_m_gather``), so for them the all-gather moves from the
+optimizer into the first GEMM that needs the weights.
 """
 from __future__ import annotations
 
@@ -51,6 +57,7 @@ class P2PComm:
         # re-home every group and re-point the parameters
         goff, woff = 0, {dt: 0 for dt in kinds}
         self.layout = []
+        self.gather_ptrs = {}   # gathered tensor name -> every rank's shard address
         for g in groups:
             dt = g.work.dtype
             new_grad = self.gbuf[goff:goff + g.numel]
@@ -67,8 +74,14 @@ class P2PComm:
             esz_w = torch.tensor([], dtype=dt).element_size()
             gp = torch.tensor([int(self.ghdl.buffer_ptrs[r]) + goff * 4 for r in range(self.world)],
                               dtype=torch.int64, device=dev)
-            wp = torch.tensor([int(self.whdl[dt].buffer_ptrs[r]) + woff[dt] * esz_w
-                               for r in range(self.world)], dtype=torch.int64, device=dev)
+            bases = [int(self.whdl[dt].buffer_ptrs[r]) + woff[dt] * esz_w for r in range(self.world)]
+            if g.gathered:
+                # the update stays local; peers pull this shard in their forward
+                wp = torch.tensor([bases[self.rank]], dtype=torch.int64, device=dev)
+                shard = g.numel // self.world
+                self.gather_ptrs[g.names[0]] = [bases[r] + r * shard * esz_w for r in range(self.world)]
+            else:
+                wp = torch.tensor(bases, dtype=torch.int64, device=dev)
             self.layout.append((gp, wp))
             goff += g.numel
             woff[dt] += g.numel
@@ -96,7 +109,8 @@ class P2PComm:
         b2 = cfg.adam_b2 if mode == 0 else cfg.lion_b2
         c = coef.reshape(1).float().contiguous()
         for g, (_, wp) in zip(self.groups, self.layout):
-            ext().p2p_update_bcast(g.master, g.grad[g.lo:g.hi], g.m, g.v, g.decay, wp, self.world,
+            ext().p2p_update_bcast(g.master, g.grad[g.lo:g.hi], g.m, g.v, g.decay, wp,
+                                   1 if g.gathered else self.world,
                                    g.lo, g.work.dtype == torch.bfloat16, mode, float(lr),
                                    float(cfg.weight_decay), float(b1), float(b2),
                                    float(cfg.adam_eps), int(step), c)

@@ -6,7 +6,7 @@ Each case builds inputs on the current GPU (a few GB at most; operands larger
 than the 126 MB L2 where the kernel is memory-bound), runs the kernel a few
 times and exits.  With ``--time`` it prints the CUDA-event time of one launch
 and the achieved TFLOP/s or GB/s.  Cases: gemm_fwd, gemm_dw, grouped_fwd,
-kda_fwd, kda_bwd, kda128_fwd, kda128_bwd, flash_fwd, flash_bwd, router_fwd, p2p_rs_emulated.
+gather_gemm_emulated, kda_fwd, kda_bwd, kda128_fwd, kda128_bwd, flash_fwd, flash_bwd, router_fwd, p2p_rs_emulated.
 """
 from __future__ import annotations
 
@@ -60,6 +60,31 @@ def case_grouped_fwd():
     i32 = lambda v: torch.tensor(v, dtype=torch.int32, device="cuda")
     gs, gc, gt = i32(starts), i32(counts), i32(tp)
     return (lambda: ext().grouped_gemm_m(xp, w, y, gs, gc, gt, False)), 2 * T * K * D * F, "flop"
+
+
+def case_gather_gemm_emulated():
+    """Fused expert-weight all-gather + grouped GEMM on one GPU: the 8 "ranks'"
+    expert shards are local buffers (the kernel's tile claiming, copy-out and
+    waiting, without NVLink).  Flagship MoE shape: 32 experts, D 1024, F 768."""
+    T, K, N, D, F, W = 32768, 4, 32, 1024, 768, 8
+    counts = [T * K // N] * N
+    starts = [i * ((T * K // N + 127) // 128 * 128) for i in range(N)]
+    R = starts[-1] + counts[-1]
+    xp = torch.randn(R, D, device="cuda").bfloat16()
+    w = torch.randn(N, D, F, device="cuda").bfloat16()
+    shards = [w[r * (N // W):(r + 1) * (N // W)].clone() for r in range(W)]
+    y = torch.empty(R, F, device="cuda", dtype=torch.bfloat16)
+    gathered = torch.empty_like(w)
+    tiles_n = (F + 255) // 256
+    flags = torch.zeros(N * (D // 64) * tiles_n, dtype=torch.int32, device="cuda")
+    tp = [0]
+    for c in counts:
+        tp.append(tp[-1] + (c + 127) // 128 * tiles_n)
+    i32 = lambda v: torch.tensor(v, dtype=torch.int32, device="cuda")
+    gs, gc, gt = i32(starts), i32(counts), i32(tp)
+    ptrs = [s.data_ptr() for s in shards]
+    return (lambda: ext().grouped_gemm_m_gather(xp, ptrs, 0, N // W, gathered, flags, y, gs, gc, gt)), \
+        2 * T * K * D * F, "flop"
 
 
 def _kda_inputs(B=8, S=4096, H=16, K=64):

@@ -42,6 +42,13 @@ class Trainer:
                 m.make_expert_parallel(rank, world)
                 m.ep_dist = dist_ctx
                 m.capacity_factor = cfg.capacity_factor
+        if (dist_ctx is not None and world > 1 and cfg.mesh_expert_axis <= 1
+                and cfg.expert_weights == "fused_gather" and cfg.fused_comm
+                and self.device.type == "cuda" and cfg.n_experts % world == 0):
+            # expert weights sharded by expert; gathered inside the grouped GEMMs
+            for m in self.model.moe_layers():
+                for p in (m.expert_w_gate, m.expert_w_up, m.expert_w_down):
+                    p._fsdp_gather = True
         if dist_ctx is not None and world > 1:
             from .parallel.fsdp import FSDPEngine
             self.engine = FSDPEngine(self.model, cfg, self.device, dist_ctx)

@@ -102,3 +102,43 @@ def test_grouped_k(acc):
         if acc:
             ref = ref + c0[g]
         assert _rel_err(c[g], ref) < 1e-5 or (n == 0 and torch.equal(c[g], ref))
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_grouped_gemm_fused_gather_emulated(world):
+    """The fused all-gather GEMM on one GPU: each "rank's" expert shard is a
+    separate local buffer; the output must equal the plain grouped GEMM on the
+    full weight, and the gathered copy must hold every expert that has rows."""
+    torch.manual_seed(3)
+    dev = "cuda"
+    G, K, N = 8, 512, 768
+    counts = [130, 0, 7, 256, 300, 64, 1, 200]
+    starts, R = _groups(counts)
+    a = torch.randn(R, K, device=dev).bfloat16()
+    b = torch.randn(G, K, N, device=dev).bfloat16()
+    gpr = G // world
+    shards = [b[r * gpr:(r + 1) * gpr].clone() for r in range(world)]
+    BN = 256 if N >= 256 else 128
+    tiles_n = (N + BN - 1) // BN
+    tstart = [0]
+    for cnt in counts:
+        tstart.append(tstart[-1] + (cnt + 127) // 128 * tiles_n)
+    gs = torch.tensor(starts, dtype=torch.int32, device=dev)
+    gc = torch.tensor(counts, dtype=torch.int32, device=dev)
+    gt = torch.tensor(tstart, dtype=torch.int32, device=dev)
+    ref = torch.full((R, N), float("nan"), device=dev).bfloat16()
+    _ext().grouped_gemm_m(a, b, ref, gs, gc, gt, False)
+    for rank in range(world):
+        gathered = torch.zeros(G, K, N, device=dev).bfloat16()
+        flags = torch.zeros(G * (K // 64) * tiles_n, dtype=torch.int32, device=dev)
+        for _ in range(2):   # the flags are re-armed on every call
+            c = torch.full((R, N), float("nan"), device=dev).bfloat16()
+            _ext().grouped_gemm_m_gather(a, [s.data_ptr() for s in shards], rank, gpr, gathered,
+                                         flags, c, gs, gc, gt)
+            torch.cuda.synchronize()
+            for g in range(G):
+                s, n = starts[g], counts[g]
+                if n:
+                    assert torch.equal(c[s:s + n], ref[s:s + n]), (rank, g)
+                    assert torch.equal(gathered[g], b[g]), (rank, g)
+        assert _ext().read_status() == 0

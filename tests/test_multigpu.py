@@ -1,6 +1,7 @@
 """Data parallel on 2 GPUs: the fused peer-memory transport (reduce-scatter in a
 kernel reading peers over NVLink, optimizer storing the new weights into every
-peer) must match the NCCL baseline.  Skipped with fewer than 2 GPUs."""
+peer) must match the NCCL baseline, and so must the fused expert-weight
+all-gather inside the grouped GEMMs.  Skipped with fewer than 2 GPUs."""
 import os
 import socket
 
@@ -29,11 +30,15 @@ def _worker(rank, world, port, out_path):
     ctx = init_distributed(timeout_s=120)
     try:
         res = {}
-        for fused in (False, True):
+        for fused in (False, True, "gather"):
             c = get_config("tiny_hybrid").replace(dtype="bf16", batch_size=4, seq_len=128,
-                                                  fused_comm=fused)
+                                                  fused_comm=bool(fused))
+            if fused == "gather":
+                c = c.replace(expert_weights="fused_gather")
             tr = Trainer(c, dist_ctx=ctx)
             assert tr.engine.transport == ("p2p" if fused else "nccl")
+            if fused == "gather":
+                assert all(getattr(m, "_gather", None) is not None for m in tr.model.moe_layers())
             per = c.batch_size // world
             losses = []
             for step in range(3):
@@ -63,6 +68,14 @@ def test_p2p_transport_matches_nccl(tmp_path):
         p.join(timeout=600)
         assert p.exitcode == 0
     res = torch.load(out)
+    # the fused expert-weight gather (P1) computes exactly what the replicated
+    # weights compute: same tiles, same kernels, only the source of B differs
+    (lg, sg), (lp, sp) = res["gather"], res[True]
+    for a, b in zip(lg, lp):
+        assert abs(a - b) < 1e-3 * abs(a), (lg, lp)
+    for k in sp:
+        diff = (sg[k] - sp[k]).abs()
+        assert diff.max().item() <= 6 * 3e-4 + 1e-5, (k, diff.max().item())
     (l0, s0), (l1, s1) = res[False], res[True]
     for a, b in zip(l0, l1):
         assert abs(a - b) < 1e-3 * abs(a), (l0, l1)
