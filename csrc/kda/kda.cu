@@ -44,17 +44,15 @@ constexpr int LDC() { return C + 4; }
 // B(k,n) = b[k*ldb+n] (or b[n*ldb+k] if TB).  Shared-memory operands, fp32 out.
 //
 // Tensor cores: mma.sync m16n8k8 with tf32 inputs, each fp32 operand split as
-// x = hi + lo (hi, lo tf32) and the product formed as hi*hi + hi*lo + lo*hi,
-// which keeps fp32-level accuracy (the state recurrence accumulates over the
-// whole sequence).  Output tiles of 16 x 8 are spread over the 8 warps.
-HB_DEVICE uint32_t to_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
-}
+// x = hi + lo with hi = x truncated to tf32 (exact) and lo = x - hi (exact in
+// fp32; the tensor core reads its top 19 bits), product hi*hi + hi*lo + lo*hi:
+// about 2^-19 relative error per product, fp32-level for the recurrence that
+// accumulates over the whole sequence.  A warp owns a 16 x 8*NS output tile
+// (NS = 2 when that still gives every warp a tile, so one A fragment feeds two
+// n-subtiles).
 HB_DEVICE void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
-  hi = to_tf32(x);
-  lo = to_tf32(x - __uint_as_float(hi));
+  hi = __float_as_uint(x) & 0xffffe000u;
+  lo = __float_as_uint(x - __uint_as_float(hi));
 }
 HB_DEVICE void mma_tf32(float* c, const uint32_t* a, const uint32_t* b) {
   asm volatile(
@@ -69,44 +67,51 @@ HB_DEVICE void mm(float* out, int ldo, const float* a, int lda, const float* b, 
                   bool acc) {
   static_assert(M % 16 == 0 && N % 8 == 0 && KD % 8 == 0, "mm tile shape");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nw = blockDim.x >> 5;
   const int g = lane >> 2, t = lane & 3;
-  constexpr int TM = M / 16, TN = N / 8;
-  for (int tile = warp; tile < TM * TN; tile += (int)(blockDim.x >> 5)) {
-    const int m0 = (tile / TN) * 16, n0 = (tile % TN) * 8;
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
+  constexpr int TM = M / 16;
+  constexpr int NS = ((N / 8) % 2 == 0 && TM * (N / 16) >= 8) ? 2 : 1;
+  constexpr int TN = N / (8 * NS);
+  auto A = [&](int m, int k) { return TA ? a[k * lda + m] : a[m * lda + k]; };
+  auto B = [&](int k, int n) { return TB ? b[n * ldb + k] : b[k * ldb + n]; };
+  for (int tile = warp; tile < TM * TN; tile += nw) {
+    const int m0 = (tile / TN) * 16, n0 = (tile % TN) * 8 * NS;
+    float c[NS][4];
+#pragma unroll
+    for (int j = 0; j < NS; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = 0.f;
 #pragma unroll 2
     for (int k0 = 0; k0 < KD; k0 += 8) {
-      float af[4], bf[2];
-      auto A = [&](int m, int k) { return TA ? a[k * lda + m] : a[m * lda + k]; };
-      auto B = [&](int k, int n) { return TB ? b[n * ldb + k] : b[k * ldb + n]; };
-      af[0] = A(m0 + g, k0 + t);
-      af[1] = A(m0 + g + 8, k0 + t);
-      af[2] = A(m0 + g, k0 + t + 4);
-      af[3] = A(m0 + g + 8, k0 + t + 4);
-      bf[0] = B(k0 + t, n0 + g);
-      bf[1] = B(k0 + t + 4, n0 + g);
-      uint32_t ah[4], al[4], bh[2], bl[2];
+      uint32_t ah[4], al[4];
+      split_tf32(A(m0 + g, k0 + t), ah[0], al[0]);
+      split_tf32(A(m0 + g + 8, k0 + t), ah[1], al[1]);
+      split_tf32(A(m0 + g, k0 + t + 4), ah[2], al[2]);
+      split_tf32(A(m0 + g + 8, k0 + t + 4), ah[3], al[3]);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) split_tf32(af[i], ah[i], al[i]);
-      split_tf32(bf[0], bh[0], bl[0]);
-      split_tf32(bf[1], bh[1], bl[1]);
-      mma_tf32(c, al, bh);
-      mma_tf32(c, ah, bl);
-      mma_tf32(c, ah, bh);
+      for (int j = 0; j < NS; ++j) {
+        uint32_t bh[2], bl[2];
+        split_tf32(B(k0 + t, n0 + 8 * j + g), bh[0], bl[0]);
+        split_tf32(B(k0 + t + 4, n0 + 8 * j + g), bh[1], bl[1]);
+        mma_tf32(c[j], al, bh);
+        mma_tf32(c[j], ah, bl);
+        mma_tf32(c[j], ah, bh);
+      }
     }
-    const int r0 = m0 + g, cc = n0 + 2 * t;
-    float* o0 = out + r0 * ldo + cc;
-    float* o1 = out + (r0 + 8) * ldo + cc;
-    if (acc) {
-      o0[0] += alpha * c[0];
-      o0[1] += alpha * c[1];
-      o1[0] += alpha * c[2];
-      o1[1] += alpha * c[3];
-    } else {
-      o0[0] = alpha * c[0];
-      o0[1] = alpha * c[1];
-      o1[0] = alpha * c[2];
-      o1[1] = alpha * c[3];
+#pragma unroll
+    for (int j = 0; j < NS; ++j) {
+      const int r0 = m0 + g, cc = n0 + 8 * j + 2 * t;
+      float* o0 = out + r0 * ldo + cc;
+      float* o1 = out + (r0 + 8) * ldo + cc;
+      if (acc) {
+        o0[0] += alpha * c[j][0];
+        o0[1] += alpha * c[j][1];
+        o1[0] += alpha * c[j][2];
+        o1[1] += alpha * c[j][3];
+      } else {
+        o0[0] = alpha * c[j][0];
+        o0[1] = alpha * c[j][1];
+        o1[0] = alpha * c[j][2];
+        o1[1] = alpha * c[j][3];
+      }
     }
   }
 }
@@ -687,8 +692,40 @@ constexpr int intra_bwd_smem() {
 }
 
 // ================================================================ front-end
-// One warp per (token, head).  raw: [T, 3*HK] bf16 rows (q | k | v projections);
-// conv weights [HK, 4] fp32 each; outputs fp32 [T, H, K].
+// One warp per token (all heads), two adjacent channels per lane: bf16x2 loads
+// of the projection taps, float4 loads of the conv taps, float2 stores.
+// raw: [T, 3*HK] bf16 rows (q | k | v projections, row stride ld_raw); conv
+// weights [HK, 4] fp32 each; outputs fp32 [T, H, K].
+HB_DEVICE float2 ld_bf2(const __nv_bfloat16* p) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+}
+HB_DEVICE float tap(const float4& w, int i) { return i == 0 ? w.x : i == 1 ? w.y : i == 2 ? w.z : w.w; }
+HB_DEVICE float rbf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+HB_DEVICE float silu_f(float x) { return x / (1.f + __expf(-x)); }
+HB_DEVICE float dsilu_f(float x) {
+  const float s = 1.f / (1.f + __expf(-x));
+  return s * (1.f + x * (1.f - s));
+}
+// softplus(y) = max(y, 0) + log1p(exp(-|y|)) never overflows
+HB_DEVICE float softplus_f(float y) { return fmaxf(y, 0.f) + log1pf(__expf(-fabsf(y))); }
+
+// Causal 4-tap conv of channels (ch, ch+1) of projection `which` at token t;
+// rows[i] is the row of token t - 3 + i (nullptr before the sequence start).
+// The result is rounded to the compute dtype (model/kda.py:136, 257-259).
+HB_DEVICE float2 conv2(const __nv_bfloat16* const (&rows)[4], int off, const float* w, int ch) {
+  const float4 wa = *reinterpret_cast<const float4*>(w + ch * 4);
+  const float4 wb = *reinterpret_cast<const float4*>(w + ch * 4 + 4);
+  float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (!rows[i]) continue;
+    const float2 x = ld_bf2(rows[i] + off);
+    a0 += tap(wa, i) * x.x;
+    a1 += tap(wb, i) * x.y;
+  }
+  return make_float2(rbf(a0), rbf(a1));
+}
+
 template <int DK>
 __global__ void prep_fwd_kernel(const __nv_bfloat16* __restrict__ raw, long long ld_raw,
                                 const float* __restrict__ wq, const float* __restrict__ wk,
@@ -697,64 +734,62 @@ __global__ void prep_fwd_kernel(const __nv_bfloat16* __restrict__ raw, long long
                                 const float* __restrict__ braw, int gate_mode, int T, int S, int H,
                                 float* __restrict__ q, float* __restrict__ k, float* __restrict__ v,
                                 float* __restrict__ g, float* __restrict__ beta) {
+  constexpr int NP = (DK + 63) / 64;
   const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
   const int HK = H * DK;
-  constexpr int PL = (DK + 31) / 32;
-  for (long long th = blockIdx.x * (long long)warps + (threadIdx.x >> 5); th < (long long)T * H;
-       th += (long long)gridDim.x * warps) {
-    const int t = th / H, h = th % H;
+  for (long long t = blockIdx.x * (long long)warps + (threadIdx.x >> 5); t < T; t += (long long)gridDim.x * warps) {
     const int pos = t % S;
-    float qv[PL], kv[PL], ssq = 0.f, ssk = 0.f;
+    const __nv_bfloat16* rows[4];
 #pragma unroll
-    for (int j = 0; j < PL; ++j) {
-      const int c = lane + 32 * j;
-      if (c >= DK) { qv[j] = kv[j] = 0.f; continue; }
-      const int ch = h * DK + c;
-      float aq = 0.f, ak = 0.f, av = 0.f;
+    for (int i = 0; i < 4; ++i) rows[i] = pos - (3 - i) >= 0 ? raw + (t - (3 - i)) * ld_raw : nullptr;
+    for (int h = 0; h < H; ++h) {
+      float2 qv[NP], kv[NP];
+      float ssq = 0.f, ssk = 0.f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int sh = 3 - i;
-        if (pos - sh < 0) continue;
-        const __nv_bfloat16* row = raw + (long long)(t - sh) * ld_raw;
-        aq += wq[ch * 4 + i] * __bfloat162float(row[ch]);
-        ak += wk[ch * 4 + i] * __bfloat162float(row[HK + ch]);
-        av += wv[ch * 4 + i] * __bfloat162float(row[2 * HK + ch]);
+      for (int j = 0; j < NP; ++j) {
+        const int c = 2 * lane + 64 * j;
+        qv[j] = kv[j] = make_float2(0.f, 0.f);
+        if (c >= DK) continue;
+        const int ch = h * DK + c;
+        const float2 cq = conv2(rows, ch, wq, ch), ck = conv2(rows, HK + ch, wk, ch),
+                     cv = conv2(rows, 2 * HK + ch, wv, ch);
+        qv[j] = make_float2(silu_f(cq.x), silu_f(cq.y));
+        kv[j] = make_float2(silu_f(ck.x), silu_f(ck.y));
+        ssq += qv[j].x * qv[j].x + qv[j].y * qv[j].y;
+        ssk += kv[j].x * kv[j].x + kv[j].y * kv[j].y;
+        const long long o = t * HK + ch;
+        *reinterpret_cast<float2*>(v + o) = make_float2(silu_f(cv.x), silu_f(cv.y));
+        const float2 fz = *reinterpret_cast<const float2*>(f + o);
+        const float2 db = *reinterpret_cast<const float2*>(dt_bias + ch);
+        const float z0 = fz.x + db.x, z1 = fz.y + db.y;
+        float2 gg;
+        if (gate_mode == 0) {
+          const float A = -__expf(a_log[h]);
+          gg = make_float2(A * softplus_f(z0), A * softplus_f(z1));
+        } else {
+          gg = make_float2(-softplus_f(-z0), -softplus_f(-z1));
+        }
+        *reinterpret_cast<float2*>(g + o) = gg;
       }
-      // the conv result is rounded to the compute dtype (model/kda.py:136, 257-259)
-      aq = __bfloat162float(__float2bfloat16_rn(aq));
-      ak = __bfloat162float(__float2bfloat16_rn(ak));
-      av = __bfloat162float(__float2bfloat16_rn(av));
-      qv[j] = aq / (1.f + __expf(-aq));
-      kv[j] = ak / (1.f + __expf(-ak));
-      const float vs = av / (1.f + __expf(-av));
-      ssq += qv[j] * qv[j];
-      ssk += kv[j] * kv[j];
-      const long long o = (long long)t * HK + ch;
-      v[o] = vs;
-      const float z = f[o] + dt_bias[ch];
-      // softplus(y) = max(y, 0) + log1p(exp(-|y|)) never overflows
-      const float sp = fmaxf(z, 0.f) + log1pf(__expf(-fabsf(z)));
-      const float spn = fmaxf(-z, 0.f) + log1pf(__expf(-fabsf(z)));  // softplus(-z)
-      g[o] = gate_mode == 0 ? -__expf(a_log[h]) * sp : -spn;
-    }
-    ssq = warp_sum(ssq);
-    ssk = warp_sum(ssk);
-    const float rq = rsqrtf(ssq + 1e-6f), rk = rsqrtf(ssk + 1e-6f);
+      ssq = warp_sum(ssq);
+      ssk = warp_sum(ssk);
+      const float rq = rsqrtf(ssq + 1e-6f), rk = rsqrtf(ssk + 1e-6f);
 #pragma unroll
-    for (int j = 0; j < PL; ++j) {
-      const int c = lane + 32 * j;
-      if (c >= DK) continue;
-      const long long o = (long long)t * HK + h * DK + c;
-      q[o] = qv[j] * rq;
-      k[o] = kv[j] * rk;
+      for (int j = 0; j < NP; ++j) {
+        const int c = 2 * lane + 64 * j;
+        if (c >= DK) continue;
+        const long long o = t * HK + h * DK + c;
+        *reinterpret_cast<float2*>(q + o) = make_float2(qv[j].x * rq, qv[j].y * rq);
+        *reinterpret_cast<float2*>(k + o) = make_float2(kv[j].x * rk, kv[j].y * rk);
+      }
+      if (lane == 0) beta[t * H + h] = 1.f / (1.f + __expf(-braw[t * H + h]));
     }
-    if (lane == 0) beta[(long long)t * H + h] = 1.f / (1.f + __expf(-braw[(long long)t * H + h]));
   }
 }
 
-// Backward part 1 (warp per (token, head)): gradients at the conv outputs of
-// q/k/v (fp32, [T, 3*HK]), df [T, HK], dbraw [T, H]; block partials of
-// d a_log and d dt_bias are accumulated with atomics.
+// Backward part 1 (warp per token, all heads): gradients at the conv outputs of
+// q/k/v (fp32, [T, 3*HK]), df [T, HK], dbraw [T, H]; d a_log and d dt_bias are
+// block partials in shared memory, flushed with one atomic per element.
 template <int DK>
 __global__ void prep_bwd1_kernel(const __nv_bfloat16* __restrict__ raw, long long ld_raw,
                                  const float* __restrict__ wq, const float* __restrict__ wk,
@@ -766,8 +801,7 @@ __global__ void prep_bwd1_kernel(const __nv_bfloat16* __restrict__ raw, long lon
                                  const float* __restrict__ dbeta, float* __restrict__ dconv,
                                  float* __restrict__ df, float* __restrict__ dbraw,
                                  float* __restrict__ d_alog, float* __restrict__ d_dtb) {
-  // block partials of d dt_bias [HK] and d a_log [H]: one global atomic per
-  // element and block instead of one per token
+  constexpr int NP = (DK + 63) / 64;
   extern __shared__ float s_acc[];
   const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
   const int HK = H * DK;
@@ -775,109 +809,82 @@ __global__ void prep_bwd1_kernel(const __nv_bfloat16* __restrict__ raw, long lon
   float* s_al = s_acc + HK;
   for (int i = threadIdx.x; i < HK + H; i += blockDim.x) s_acc[i] = 0.f;
   __syncthreads();
-  constexpr int PL = (DK + 31) / 32;
-  // per-warp register partials for the current head, flushed to shared
-  // memory when the warp's head changes (with a grid stride that is a
-  // multiple of H it never does)
-  float acc_dtb[PL];
-  float acc_al = 0.f;
-  int cur_h = -1;
-#pragma unroll
-  for (int j = 0; j < PL; ++j) acc_dtb[j] = 0.f;
-  auto flush = [&]() {
-    if (cur_h < 0) return;
-#pragma unroll
-    for (int j = 0; j < PL; ++j) {
-      const int c = lane + 32 * j;
-      if (c < DK) atomicAdd(s_dtb + cur_h * DK + c, acc_dtb[j]);
-      acc_dtb[j] = 0.f;
-    }
-    if (lane == 0) atomicAdd(s_al + cur_h, acc_al);
-    acc_al = 0.f;
-  };
-  for (long long th = blockIdx.x * (long long)warps + (threadIdx.x >> 5); th < (long long)T * H;
-       th += (long long)gridDim.x * warps) {
-    const int t = th / H, h = th % H;
-    if (h != cur_h) {
-      flush();
-      cur_h = h;
-    }
+  for (long long t = blockIdx.x * (long long)warps + (threadIdx.x >> 5); t < T; t += (long long)gridDim.x * warps) {
     const int pos = t % S;
-    float cq[PL], ck[PL], cv[PL], sq[PL], sk[PL];
-    float ssq = 0.f, ssk = 0.f, dotq = 0.f, dotk = 0.f, dal = 0.f;
+    const __nv_bfloat16* rows[4];
 #pragma unroll
-    for (int j = 0; j < PL; ++j) {
-      const int c = lane + 32 * j;
-      cq[j] = ck[j] = cv[j] = sq[j] = sk[j] = 0.f;
-      if (c >= DK) continue;
-      const int ch = h * DK + c;
-      float aq = 0.f, ak = 0.f, av = 0.f;
+    for (int i = 0; i < 4; ++i) rows[i] = pos - (3 - i) >= 0 ? raw + (t - (3 - i)) * ld_raw : nullptr;
+    for (int h = 0; h < H; ++h) {
+      float2 cq[NP], ck[NP], sq[NP], sk[NP], gq[NP], gk[NP];
+      float ssq = 0.f, ssk = 0.f, dotq = 0.f, dotk = 0.f, dal = 0.f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int sh = 3 - i;
-        if (pos - sh < 0) continue;
-        const __nv_bfloat16* row = raw + (long long)(t - sh) * ld_raw;
-        aq += wq[ch * 4 + i] * __bfloat162float(row[ch]);
-        ak += wk[ch * 4 + i] * __bfloat162float(row[HK + ch]);
-        av += wv[ch * 4 + i] * __bfloat162float(row[2 * HK + ch]);
+      for (int j = 0; j < NP; ++j) {
+        const int c = 2 * lane + 64 * j;
+        cq[j] = ck[j] = sq[j] = sk[j] = gq[j] = gk[j] = make_float2(0.f, 0.f);
+        if (c >= DK) continue;
+        const int ch = h * DK + c;
+        const long long o = t * HK + ch;
+        cq[j] = conv2(rows, ch, wq, ch);
+        ck[j] = conv2(rows, HK + ch, wk, ch);
+        const float2 cv = conv2(rows, 2 * HK + ch, wv, ch);
+        sq[j] = make_float2(silu_f(cq[j].x), silu_f(cq[j].y));
+        sk[j] = make_float2(silu_f(ck[j].x), silu_f(ck[j].y));
+        ssq += sq[j].x * sq[j].x + sq[j].y * sq[j].y;
+        ssk += sk[j].x * sk[j].x + sk[j].y * sk[j].y;
+        gq[j] = *reinterpret_cast<const float2*>(dq + o);
+        gk[j] = *reinterpret_cast<const float2*>(dk + o);
+        dotq += gq[j].x * sq[j].x + gq[j].y * sq[j].y;
+        dotk += gk[j].x * sk[j].x + gk[j].y * sk[j].y;
+        const float2 gv = *reinterpret_cast<const float2*>(dv + o);
+        const long long co = t * 3 * HK + ch;
+        *reinterpret_cast<float2*>(dconv + co + 2 * HK) = make_float2(gv.x * dsilu_f(cv.x), gv.y * dsilu_f(cv.y));
+        // decay gate
+        const float2 fz = *reinterpret_cast<const float2*>(f + o);
+        const float2 db = *reinterpret_cast<const float2*>(dt_bias + ch);
+        const float2 gg = *reinterpret_cast<const float2*>(dg + o);
+        const float z[2] = {fz.x + db.x, fz.y + db.y}, dgv[2] = {gg.x, gg.y};
+        float dz[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float sig = 1.f / (1.f + __expf(-z[e]));
+          if (gate_mode == 0) {
+            const float A = __expf(a_log[h]);
+            dz[e] = dgv[e] * (-A) * sig;
+            dal += dgv[e] * (-A * softplus_f(z[e]));
+          } else {
+            dz[e] = dgv[e] * (1.f - sig);
+          }
+        }
+        *reinterpret_cast<float2*>(df + o) = make_float2(dz[0], dz[1]);
+        atomicAdd(s_dtb + ch, dz[0]);
+        atomicAdd(s_dtb + ch + 1, dz[1]);
       }
-      cq[j] = __bfloat162float(__float2bfloat16_rn(aq));
-      ck[j] = __bfloat162float(__float2bfloat16_rn(ak));
-      cv[j] = __bfloat162float(__float2bfloat16_rn(av));
-      sq[j] = cq[j] / (1.f + __expf(-cq[j]));
-      sk[j] = ck[j] / (1.f + __expf(-ck[j]));
-      ssq += sq[j] * sq[j];
-      ssk += sk[j] * sk[j];
-      const long long o = (long long)t * HK + ch;
-      dotq += dq[o] * sq[j];
-      dotk += dk[o] * sk[j];
-      // gate
-      const float z = f[o] + dt_bias[ch];
-      const float sig = 1.f / (1.f + __expf(-z));
-      float dz;
-      if (gate_mode == 0) {
-        const float A = __expf(a_log[h]);
-        const float sp = fmaxf(z, 0.f) + log1pf(__expf(-fabsf(z)));
-        dz = dg[o] * (-A) * sig;
-        dal += dg[o] * (-A * sp);
-      } else {
-        dz = dg[o] * (1.f - sig);
-      }
-      df[o] = dz;
-      acc_dtb[j] += dz;
-    }
-    ssq = warp_sum(ssq);
-    ssk = warp_sum(ssk);
-    dotq = warp_sum(dotq);
-    dotk = warp_sum(dotk);
-    dal = warp_sum(dal);
-    const float nq = sqrtf(ssq + 1e-6f), nk = sqrtf(ssk + 1e-6f);
+      ssq = warp_sum(ssq);
+      ssk = warp_sum(ssk);
+      dotq = warp_sum(dotq);
+      dotk = warp_sum(dotk);
+      dal = warp_sum(dal);
+      const float nq = sqrtf(ssq + 1e-6f), nk = sqrtf(ssk + 1e-6f);
 #pragma unroll
-    for (int j = 0; j < PL; ++j) {
-      const int c = lane + 32 * j;
-      if (c >= DK) continue;
-      const int ch = h * DK + c;
-      const long long o = (long long)t * HK + ch;
-      // y = x / n, n = sqrt(|x|^2 + eps): dx = (dy - y (dy . y)) / n
-      const float yq = sq[j] / nq, yk = sk[j] / nk;
-      const float dsq = (dq[o] - yq * (dotq / nq)) / nq;
-      const float dsk = (dk[o] - yk * (dotk / nk)) / nk;
-      auto dsilu = [](float x) {
-        const float s = 1.f / (1.f + __expf(-x));
-        return s * (1.f + x * (1.f - s));
-      };
-      const long long co = (long long)t * 3 * HK + ch;
-      dconv[co] = dsq * dsilu(cq[j]);
-      dconv[co + HK] = dsk * dsilu(ck[j]);
-      dconv[co + 2 * HK] = dv[o] * dsilu(cv[j]);
-    }
-    if (lane == 0) {
-      if (gate_mode == 0) acc_al += dal;
-      const float bt = beta[(long long)t * H + h];
-      dbraw[(long long)t * H + h] = dbeta[(long long)t * H + h] * bt * (1.f - bt);
+      for (int j = 0; j < NP; ++j) {
+        const int c = 2 * lane + 64 * j;
+        if (c >= DK) continue;
+        const long long co = t * 3 * HK + h * DK + c;
+        // y = x / n, n = sqrt(|x|^2 + eps): dx = (dy - y (dy . y)) / n
+        const float dq0 = (gq[j].x - sq[j].x / nq * (dotq / nq)) / nq;
+        const float dq1 = (gq[j].y - sq[j].y / nq * (dotq / nq)) / nq;
+        const float dk0 = (gk[j].x - sk[j].x / nk * (dotk / nk)) / nk;
+        const float dk1 = (gk[j].y - sk[j].y / nk * (dotk / nk)) / nk;
+        *reinterpret_cast<float2*>(dconv + co) = make_float2(dq0 * dsilu_f(cq[j].x), dq1 * dsilu_f(cq[j].y));
+        *reinterpret_cast<float2*>(dconv + co + HK) = make_float2(dk0 * dsilu_f(ck[j].x), dk1 * dsilu_f(ck[j].y));
+      }
+      if (lane == 0) {
+        if (gate_mode == 0) atomicAdd(s_al + h, dal);
+        const float bt = beta[t * H + h];
+        dbraw[t * H + h] = dbeta[t * H + h] * bt * (1.f - bt);
+      }
     }
   }
-  flush();
   __syncthreads();
   for (int i = threadIdx.x; i < HK; i += blockDim.x)
     if (s_dtb[i] != 0.f) atomicAdd(d_dtb + i, s_dtb[i]);
@@ -885,40 +892,53 @@ __global__ void prep_bwd1_kernel(const __nv_bfloat16* __restrict__ raw, long lon
     if (s_al[i] != 0.f) atomicAdd(d_alog + i, s_al[i]);
 }
 
-// Backward part 2 (thread per (token, channel) of the 3*HK conv inputs):
+// Backward part 2 (thread per channel of the 3*HK conv inputs, a run of tokens):
 //   draw[t] = sum_i w[i] dconv[t + 3 - i] (same sequence); dw[i] += dconv[t] raw[t-3+i]
+// dconv and raw are held in 4-deep register windows, so each element is loaded once.
 __global__ void prep_bwd2_kernel(const __nv_bfloat16* __restrict__ raw, long long ld_raw,
                                  const float* __restrict__ wq, const float* __restrict__ wk,
                                  const float* __restrict__ wv, const float* __restrict__ dconv,
                                  int T, int S, int HK, __nv_bfloat16* __restrict__ draw,
                                  float* __restrict__ dwq, float* __restrict__ dwk, float* __restrict__ dwv) {
   const int C3 = 3 * HK;
-  // each thread: fixed channel, a range of tokens, accumulates dw in registers
   const int ch = blockIdx.x * blockDim.x + threadIdx.x;
   if (ch >= C3) return;
   const int which = ch / HK, cc = ch % HK;
   const float* w = which == 0 ? wq : (which == 1 ? wk : wv);
   float* dw = which == 0 ? dwq : (which == 1 ? dwk : dwv);
-  const float w0 = w[cc * 4 + 0], w1 = w[cc * 4 + 1], w2 = w[cc * 4 + 2], w3 = w[cc * 4 + 3];
+  const float4 wt = *reinterpret_cast<const float4*>(w + cc * 4);
   const int tpb = (T + gridDim.y - 1) / gridDim.y;
   const int tb = blockIdx.y * tpb, te = min(T, tb + tpb);
+  if (tb >= te) return;
   float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  const float* dcol = dconv + ch;
+  const __nv_bfloat16* rcol = raw + ch;
+  auto dc = [&](int t) { return t < T ? dcol[(long long)t * C3] : 0.f; };
+  auto rw = [&](int t) { return t >= 0 ? __bfloat162float(rcol[(long long)t * ld_raw]) : 0.f; };
+  // windows: d0..d3 = dconv[t..t+3], r1..r3 = raw[t-1..t-3]
+  float d0 = dc(tb), d1 = dc(tb + 1), d2 = dc(tb + 2), d3 = dc(tb + 3);
+  float r1 = rw(tb - 1), r2 = rw(tb - 2), r3 = rw(tb - 3);
+  int pos = tb % S;
   for (int t = tb; t < te; ++t) {
-    const int pos = t % S;
-    float acc = 0.f;
-    // dconv at t + sh contributes through tap i = 3 - sh
-    const float d0 = dconv[(long long)t * C3 + ch];
-    acc += w3 * d0;
-    if (pos + 1 < S && t + 1 < T) acc += w2 * dconv[(long long)(t + 1) * C3 + ch];
-    if (pos + 2 < S && t + 2 < T) acc += w1 * dconv[(long long)(t + 2) * C3 + ch];
-    if (pos + 3 < S && t + 3 < T) acc += w0 * dconv[(long long)(t + 3) * C3 + ch];
+    const float r0 = rw(t);
+    const float dn = dc(t + 4);
+    float acc = wt.w * d0;
+    if (pos + 1 < S) acc += wt.z * d1;
+    if (pos + 2 < S) acc += wt.y * d2;
+    if (pos + 3 < S) acc += wt.x * d3;
     draw[(long long)t * ld_raw + ch] = __float2bfloat16_rn(acc);
-    // weight grads: out[t] = sum_i w[i] raw[t - 3 + i]
-    const __nv_bfloat16* rr = raw + ch;
-    a3 += d0 * __bfloat162float(rr[(long long)t * ld_raw]);
-    if (pos >= 1) a2 += d0 * __bfloat162float(rr[(long long)(t - 1) * ld_raw]);
-    if (pos >= 2) a1 += d0 * __bfloat162float(rr[(long long)(t - 2) * ld_raw]);
-    if (pos >= 3) a0 += d0 * __bfloat162float(rr[(long long)(t - 3) * ld_raw]);
+    a3 += d0 * r0;
+    if (pos >= 1) a2 += d0 * r1;
+    if (pos >= 2) a1 += d0 * r2;
+    if (pos >= 3) a0 += d0 * r3;
+    d0 = d1;
+    d1 = d2;
+    d2 = d3;
+    d3 = dn;
+    r3 = r2;
+    r2 = r1;
+    r1 = r0;
+    if (++pos == S) pos = 0;
   }
   atomicAdd(dw + cc * 4 + 0, a0);
   atomicAdd(dw + cc * 4 + 1, a1);
@@ -1061,8 +1081,8 @@ void kda_prep_fwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::
                   int64_t S, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
                   torch::Tensor beta) {
   const int T = q.size(0), H = q.size(1), DKV = q.size(2);
-  const long long work = (long long)T * H;
-  const int grid = (int)std::min<long long>((work + 7) / 8, num_sms() * 16);
+  HB_CHECK(raw.stride(0) % 2 == 0 && DKV % 2 == 0, "kda_prep: even row stride and head dim");
+  const int grid = (int)std::min<long long>(((long long)T + 7) / 8, num_sms() * 16);
   auto launch = [&](auto dk) {
     constexpr int DK = decltype(dk)::value;
     kda::prep_fwd_kernel<DK><<<grid, 256, 0, cur_stream()>>>(
@@ -1086,9 +1106,8 @@ void kda_prep_bwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::
                   torch::Tensor d_alog, torch::Tensor d_dtb, torch::Tensor draw, torch::Tensor dwq,
                   torch::Tensor dwk, torch::Tensor dwv) {
   const int T = dq.size(0), H = dq.size(1), DKV = dq.size(2);
-  const long long work = (long long)T * H;
-  // a multiple of H warps per grid stride keeps each warp on one head
-  const int grid = (int)std::min<long long>((work + 7) / 8, num_sms() * 16);
+  HB_CHECK(raw.stride(0) % 2 == 0 && DKV % 2 == 0, "kda_prep: even row stride and head dim");
+  const int grid = (int)std::min<long long>(((long long)T + 7) / 8, num_sms() * 8);
   const size_t acc_smem = (size_t)(H * DKV + H) * 4;
   HB_CHECK(acc_smem <= 48 * 1024, "kda_prep_bwd: too many channels");
   auto launch = [&](auto dkc) {

@@ -6,7 +6,7 @@ Each case builds inputs on the current GPU (a few GB at most; operands larger
 than the 126 MB L2 where the kernel is memory-bound), runs the kernel a few
 times and exits.  With ``--time`` it prints the CUDA-event time of one launch
 and the achieved TFLOP/s or GB/s.  Cases: gemm_fwd, gemm_dw, grouped_fwd,
-gather_gemm_emulated, kda_fwd, kda_bwd, kda128_fwd, kda128_bwd, flash_fwd, flash_bwd, router_fwd, p2p_rs_emulated.
+gather_gemm_emulated, kda_layer, kda_fwd, kda_bwd, kda128_fwd, kda128_bwd, flash_fwd, flash_bwd, router_fwd, p2p_rs_emulated.
 """
 from __future__ import annotations
 
@@ -114,6 +114,19 @@ def case_kda_bwd():
         o = KdaCoreFn.apply(*ins, 1 / math.sqrt(K))
         o.backward(torch.ones_like(o))
     return run, 3 * 8 * H * K * K * B * S, "flop"
+
+
+def case_kda_layer():
+    """Whole KDA layer (projections, conv/gate front-end, chunked core, output
+    gate, wo) forward + backward at the flagship shape: 8 x 4096 tokens, d 1024,
+    16 heads of 64."""
+    from .models.layers import KDA
+    m = KDA(1024, 16, 64, torch.Generator().manual_seed(0)).cuda()
+    h = torch.randn(8, 4096, 1024, device="cuda").bfloat16().requires_grad_()
+    def run():
+        y = m(h, torch.bfloat16)
+        y.backward(torch.ones_like(y))
+    return run, 3 * 2 * 8 * 4096 * (1024 * 16 * 64 * 4 + 8 * 16 * 64 * 64), "flop"
 
 
 def case_kda128_fwd():
