@@ -316,69 +316,111 @@ __global__ void __launch_bounds__(256) intra_fwd_kernel(Ptrs p) {
 }
 
 // ------------------------------------------------------------------ state fwd
-// grid (DK / VS, H, B): value columns [vs*VS, vs*VS+VS) of the state.
+// grid (DK / VS, H, B): value columns [vs*VS, vs*VS+VS) of the state, chunks in
+// order.  The next chunk's operands (Wt, Qg, the Ut slice, P, gC) are fetched
+// with cp.async into the second half of a double buffer while the current
+// chunk computes; Kh (needed last) has one buffer, refilled right after its
+// use for the following chunk.
+HB_DEVICE void cp_async16(float* smem, const float* gmem, bool valid = true) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+HB_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+HB_DEVICE void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// rows x cols fp32 (cols % 4 == 0) from global (row stride gs) to smem (row stride ls)
+template <int ROWS, int COLS>
+HB_DEVICE void cp_tile(float* s, int ls, const float* g, long long gs) {
+  constexpr int C4 = COLS / 4;
+  for (int i = threadIdx.x; i < ROWS * C4; i += blockDim.x) {
+    const int r = i / C4, c = (i % C4) * 4;
+    cp_async16(s + r * ls + c, g + r * gs + c);
+  }
+}
+
+template <int DK, int C, int VS>
+struct StateFwdSmem {
+  static constexpr int L = LDK<DK>(), LC = LDC<C>(), LV = VS + 4;
+  static constexpr int BUF = 2 * C * L + C * LV + C * LC + DK;  // Wt, Qg, Ut slice, P, gC
+  static constexpr int FLOATS = 2 * DK * LV + 2 * C * LV + C * L + 2 * BUF;
+};
+
 template <int DK, int C, int VS>
 __global__ void __launch_bounds__(NT) state_fwd_kernel(Ptrs p) {
-  constexpr int L = LDK<DK>(), LC = LDC<C>(), LV = VS + 4;
+  using SM = StateFwdSmem<DK, C, VS>;
+  constexpr int L = SM::L, LC = SM::LC, LV = SM::LV;
   extern __shared__ float sm[];
   float* S = sm;                 // DK x LV
-  float* U = S + DK * LV;        // C x LV
+  float* Tn = S + DK * LV;       // DK x LV
+  float* U = Tn + DK * LV;       // C x LV
   float* O = U + C * LV;         // C x LV
-  float* Wt = O + C * LV;        // C x L
-  float* X = Wt + C * L;         // C x L (Qg, then Kh)
-  float* P = X + C * L;          // C x LC
-  float* gc = P + C * LC;        // DK
-  float* Tn = gc + DK;           // DK x LV
+  float* Kh = O + C * LV;        // C x L
+  float* buf0 = Kh + C * L;      // two operand sets
   const int vs = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int v0 = vs * VS;
-  for (int i = threadIdx.x; i < DK * VS; i += NT) {
+  auto set = [&](int n) { return buf0 + (n & 1) * SM::BUF; };
+  auto fetch = [&](int n) {
+    float* bs = set(n);
+    const long long co = chunk_off(p, b, h, n, C * DK);
+    cp_tile<C, DK>(bs, L, p.Wt + co, DK);
+    cp_tile<C, DK>(bs + C * L, L, p.Qg + co, DK);
+    cp_tile<C, VS>(bs + 2 * C * L, LV, p.Ut + co + v0, DK);
+    cp_tile<C, C>(bs + 2 * C * L + C * LV, LC, p.Pm + chunk_off(p, b, h, n, C * C), C);
+    cp_tile<1, DK>(bs + 2 * C * L + C * LV + C * LC, DK, p.gC + chunk_off(p, b, h, n, DK), DK);
+  };
+  for (int i = threadIdx.x; i < DK * VS; i += blockDim.x) {
     const int r = i / VS, c = i % VS;
     S[r * LV + c] = p.init_state ? p.init_state[((long long)b * p.H + h) * DK * DK + r * DK + v0 + c] : 0.f;
   }
-  __syncthreads();
+  fetch(0);
+  cp_tile<C, DK>(Kh, L, p.Kh + chunk_off(p, b, h, 0, C * DK), DK);
+  cp_async_commit();
   for (int n = 0; n < p.NC; ++n) {
-    const long long co = chunk_off(p, b, h, n, C * DK);
+    cp_async_wait_all();
+    __syncthreads();
+    if (n + 1 < p.NC) {  // the next chunk's operands land during this chunk's math
+      fetch(n + 1);
+      cp_async_commit();
+    }
+    const float* bs = set(n);
+    const float* Wt = bs;
+    const float* Qg = bs + C * L;
+    const float* Ut = bs + 2 * C * L;
+    const float* P = Ut + C * LV;
+    const float* gc = P + C * LC;
     const long long so = chunk_off(p, b, h, n, DK * DK);
-    for (int i = threadIdx.x; i < DK * VS; i += NT) {
-      const int r = i / VS, c = i % VS;
-      p.states[so + r * DK + v0 + c] = S[r * LV + c];
+    for (int i = threadIdx.x; i < DK * VS / 4; i += blockDim.x) {
+      const int r = i / (VS / 4), c = (i % (VS / 4)) * 4;
+      st4(p.states + so + r * DK + v0 + c, ld4(S + r * LV + c));
     }
-    for (int i = threadIdx.x; i < C * DK; i += NT) {
-      const int r = i / DK, c = i % DK;
-      Wt[r * L + c] = p.Wt[co + i];
-      X[r * L + c] = p.Qg[co + i];
-    }
-    for (int i = threadIdx.x; i < C * VS; i += NT) {
-      const int r = i / VS, c = i % VS;
-      U[r * LV + c] = p.Ut[co + r * DK + v0 + c];
-    }
-    for (int i = threadIdx.x; i < C * C; i += NT) P[(i / C) * LC + i % C] = p.Pm[chunk_off(p, b, h, n, C * C) + i];
-    for (int c = threadIdx.x; c < DK; c += NT) gc[c] = p.gC[chunk_off(p, b, h, n, DK) + c];
+    for (int i = threadIdx.x; i < C * VS; i += blockDim.x) U[(i / VS) * LV + i % VS] = Ut[(i / VS) * LV + i % VS];
     __syncthreads();
     // U = Ut - Wt S ;  O = Qg S
     mm<C, VS, DK, false, false>(U, LV, Wt, L, S, LV, -1.f, true);
-    mm<C, VS, DK, false, false>(O, LV, X, L, S, LV, 1.f, false);
+    mm<C, VS, DK, false, false>(O, LV, Qg, L, S, LV, 1.f, false);
     __syncthreads();
-    // O += P U (P lower triangular)
+    // O += P U (P lower triangular);  Tn = Kh^T U
     mm<C, VS, C, false, false>(O, LV, P, LC, U, LV, 1.f, true);
-    for (int i = threadIdx.x; i < C * DK; i += NT) X[(i / DK) * L + i % DK] = p.Kh[co + i];
+    mm<DK, VS, C, true, false>(Tn, LV, Kh, L, U, LV, 1.f, false);
     __syncthreads();
-    // S = gc * S + Kh^T U
-    mm<DK, VS, C, true, false>(Tn, LV, X, L, U, LV, 1.f, false);
-    __syncthreads();
-    for (int e = threadIdx.x; e < DK * VS; e += NT) {
+    if (n + 1 < p.NC) {
+      cp_tile<C, DK>(Kh, L, p.Kh + chunk_off(p, b, h, n + 1, C * DK), DK);
+      cp_async_commit();
+    }
+    for (int e = threadIdx.x; e < DK * VS; e += blockDim.x) {
       const int r = e / VS, c = e % VS;
       S[r * LV + c] = gc[r] * S[r * LV + c] + Tn[r * LV + c];
     }
-    for (int i = threadIdx.x; i < C * VS; i += NT) {
-      const int r = i / VS, c = i % VS;
+    for (int i = threadIdx.x; i < C * VS / 4; i += blockDim.x) {
+      const int r = i / (VS / 4), c = (i % (VS / 4)) * 4;
       const int t = n * C + r;
-      if (t < p.S) p.o[tok_off(p, b, t, h, DK) + v0 + c] = O[r * LV + c];
+      if (t < p.S) st4(p.o + tok_off(p, b, t, h, DK) + v0 + c, ld4(O + r * LV + c));
     }
-    __syncthreads();
   }
+  __syncthreads();
   if (p.final_state)
-    for (int i = threadIdx.x; i < DK * VS; i += NT) {
+    for (int i = threadIdx.x; i < DK * VS; i += blockDim.x) {
       const int r = i / VS, c = i % VS;
       p.final_state[((long long)b * p.H + h) * DK * DK + r * DK + v0 + c] = S[r * LV + c];
     }
@@ -386,60 +428,80 @@ __global__ void __launch_bounds__(NT) state_fwd_kernel(Ptrs p) {
 
 // ------------------------------------------------------------------ state bwd
 // dS_prev = gC * dS + Qg^T dO - Wt^T dU,  dU = P^T dO + Kh dS.  dstates[n] = dS at
-// the END of chunk n.  grid (DK / VS, H, B) over value-column slices.
+// the END of chunk n.  grid (DK / VS, H, B) over value-column slices, chunks in
+// reverse order, every operand of the next (earlier) chunk prefetched with
+// cp.async into the other half of a double buffer.
+template <int DK, int C, int VS>
+struct StateBwdSmem {
+  static constexpr int L = LDK<DK>(), LC = LDC<C>(), LV = VS + 4;
+  static constexpr int BUF = 3 * C * L + C * LV + C * LC + DK;  // Kh, Wt, Qg, dO slice, P, gC
+  static constexpr int FLOATS = 2 * DK * LV + C * LV + 2 * BUF;
+};
+
 template <int DK, int C, int VS>
 __global__ void __launch_bounds__(NT) state_bwd_kernel(Ptrs p) {
-  constexpr int L = LDK<DK>(), LC = LDC<C>(), LV = VS + 4;
+  using SM = StateBwdSmem<DK, C, VS>;
+  constexpr int L = SM::L, LC = SM::LC, LV = SM::LV;
   extern __shared__ float sm[];
   float* dS = sm;                // DK x LV
   float* T2 = dS + DK * LV;      // DK x LV
   float* dU = T2 + DK * LV;      // C x LV
-  float* dO = dU + C * LV;       // C x LV
-  float* X = dO + C * LV;        // C x L (Kh, then Qg)
-  float* Wt = X + C * L;         // C x L
-  float* P = Wt + C * L;         // C x LC
-  float* gc = P + C * LC;        // DK
+  float* buf0 = dU + C * LV;
   const int vs = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int v0 = vs * VS;
-  for (int i = threadIdx.x; i < DK * LV; i += NT) dS[i] = 0.f;
-  __syncthreads();
-  for (int n = p.NC - 1; n >= 0; --n) {
+  auto set = [&](int n) { return buf0 + (n & 1) * SM::BUF; };
+  auto fetch = [&](int n) {
+    float* bs = set(n);
     const long long co = chunk_off(p, b, h, n, C * DK);
-    const long long so = chunk_off(p, b, h, n, DK * DK);
-    for (int i = threadIdx.x; i < DK * VS; i += NT) {
-      const int r = i / VS, c = i % VS;
-      p.dstates[so + r * DK + v0 + c] = dS[r * LV + c];
-    }
-    for (int i = threadIdx.x; i < C * VS; i += NT) {
-      const int r = i / VS, c = i % VS;
+    cp_tile<C, DK>(bs, L, p.Kh + co, DK);
+    cp_tile<C, DK>(bs + C * L, L, p.Wt + co, DK);
+    cp_tile<C, DK>(bs + 2 * C * L, L, p.Qg + co, DK);
+    float* dO = bs + 3 * C * L;
+    constexpr int V4 = VS / 4;
+    for (int i = threadIdx.x; i < C * V4; i += blockDim.x) {
+      const int r = i / V4, c = (i % V4) * 4;
       const int t = n * C + r;
-      dO[r * LV + c] = t < p.S ? p.dout[tok_off(p, b, t, h, DK) + v0 + c] : 0.f;
+      const bool ok = t < p.S;
+      cp_async16(dO + r * LV + c, ok ? p.dout + tok_off(p, b, t, h, DK) + v0 + c : p.dout, ok);
     }
-    for (int i = threadIdx.x; i < C * DK; i += NT) {
-      const int r = i / DK, c = i % DK;
-      X[r * L + c] = p.Kh[co + i];
-      Wt[r * L + c] = p.Wt[co + i];
-    }
-    for (int i = threadIdx.x; i < C * C; i += NT) P[(i / C) * LC + i % C] = p.Pm[chunk_off(p, b, h, n, C * C) + i];
-    for (int c = threadIdx.x; c < DK; c += NT) gc[c] = p.gC[chunk_off(p, b, h, n, DK) + c];
+    cp_tile<C, C>(dO + C * LV, LC, p.Pm + chunk_off(p, b, h, n, C * C), C);
+    cp_tile<1, DK>(dO + C * LV + C * LC, DK, p.gC + chunk_off(p, b, h, n, DK), DK);
+  };
+  for (int i = threadIdx.x; i < DK * LV; i += blockDim.x) dS[i] = 0.f;
+  fetch(p.NC - 1);
+  cp_async_commit();
+  for (int n = p.NC - 1; n >= 0; --n) {
+    cp_async_wait_all();
     __syncthreads();
-    // dU = P^T dO + Kh dS
+    if (n > 0) {
+      fetch(n - 1);
+      cp_async_commit();
+    }
+    const float* bs = set(n);
+    const float* Kh = bs;
+    const float* Wt = bs + C * L;
+    const float* Qg = bs + 2 * C * L;
+    const float* dO = bs + 3 * C * L;
+    const float* P = dO + C * LV;
+    const float* gc = P + C * LC;
+    const long long so = chunk_off(p, b, h, n, DK * DK);
+    for (int i = threadIdx.x; i < DK * VS / 4; i += blockDim.x) {
+      const int r = i / (VS / 4), c = (i % (VS / 4)) * 4;
+      st4(p.dstates + so + r * DK + v0 + c, ld4(dS + r * LV + c));
+    }
+    // dU = P^T dO + Kh dS ;  T2 = Qg^T dO
     mm<C, VS, C, true, false>(dU, LV, P, LC, dO, LV, 1.f, false);
+    mm<DK, VS, C, true, false>(T2, LV, Qg, L, dO, LV, 1.f, false);
     __syncthreads();
-    mm<C, VS, DK, false, false>(dU, LV, X, L, dS, LV, 1.f, true);
+    mm<C, VS, DK, false, false>(dU, LV, Kh, L, dS, LV, 1.f, true);
     __syncthreads();
-    for (int i = threadIdx.x; i < C * DK; i += NT) X[(i / DK) * L + i % DK] = p.Qg[co + i];
-    __syncthreads();
-    // T2 = Qg^T dO - Wt^T dU
-    mm<DK, VS, C, true, false>(T2, LV, X, L, dO, LV, 1.f, false);
-    __syncthreads();
+    // T2 -= Wt^T dU
     mm<DK, VS, C, true, false>(T2, LV, Wt, L, dU, LV, -1.f, true);
     __syncthreads();
-    for (int e = threadIdx.x; e < DK * VS; e += NT) {
+    for (int e = threadIdx.x; e < DK * VS; e += blockDim.x) {
       const int r = e / VS, c = e % VS;
       dS[r * LV + c] = gc[r] * dS[r * LV + c] + T2[r * LV + c];
     }
-    __syncthreads();
   }
 }
 
@@ -679,13 +741,9 @@ __global__ void __launch_bounds__(NTB<DK>(), DK >= 128 ? 1 : 2) intra_bwd_kernel
 template <int DK, int C>
 constexpr int intra_fwd_smem() { return (5 * C * LDK<DK>() + 2 * C * LDC<C>() + C) * 4; }
 template <int DK, int C, int VS>
-constexpr int state_fwd_smem() {
-  return (2 * DK * (VS + 4) + 2 * C * (VS + 4) + 2 * C * LDK<DK>() + C * LDC<C>() + DK) * 4;
-}
+constexpr int state_fwd_smem() { return StateFwdSmem<DK, C, VS>::FLOATS * 4; }
 template <int DK, int C, int VS>
-constexpr int state_bwd_smem() {
-  return (2 * DK * (VS + 4) + 2 * C * (VS + 4) + 2 * C * LDK<DK>() + C * LDC<C>() + DK) * 4;
-}
+constexpr int state_bwd_smem() { return StateBwdSmem<DK, C, VS>::FLOATS * 4; }
 template <int DK, int C>
 constexpr int intra_bwd_smem() {
   return (10 * C * LDK<DK>() + 2 * PANEL<DK>() * LDK<DK>() + 4 * C * LDC<C>() + 2 * C + 2 * DK) * 4;
@@ -1012,7 +1070,7 @@ void kda_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
   KDA_DISPATCH(DKV, {
     p.NC = (p.S + C - 1) / C;
     HB_CHECK(Pm.size(-1) == C, "kda_fwd: scratch chunk size mismatch");
-    constexpr int VS = DK >= 32 ? 16 : DK;
+    constexpr int VS = DK >= 32 ? 32 : DK;
     const int s1 = kda::intra_fwd_smem<DK, C>(), s2 = kda::state_fwd_smem<DK, C, VS>();
     static bool cfg = false;
     if (!cfg) {
@@ -1061,7 +1119,7 @@ void kda_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
            "kda_bwd: 16-byte aligned buffers required");
   KDA_DISPATCH(DKV, {
     p.NC = (p.S + C - 1) / C;
-    constexpr int VS = DK >= 32 ? 16 : DK;
+    constexpr int VS = DK >= 32 ? 32 : DK;
     const int s1 = kda::state_bwd_smem<DK, C, VS>(), s2 = kda::intra_bwd_smem<DK, C>();
     static bool cfg = false;
     if (!cfg) {
@@ -1225,7 +1283,7 @@ extern "C" __attribute__((visibility("default"))) int hb_kda_fwd_noalloc(
   auto run = [&](auto dkc) -> int {
     constexpr int DKc = decltype(dkc)::value;
     constexpr int Cc = 32;
-    constexpr int VS = DKc >= 32 ? 16 : DKc;
+    constexpr int VS = DKc >= 32 ? 32 : DKc;
     const int s1 = kda::intra_fwd_smem<DKc, Cc>(), s2 = kda::state_fwd_smem<DKc, Cc, VS>();
     if (cudaFuncSetAttribute((const void*)kda::intra_fwd_kernel<DKc, Cc>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, s1) != cudaSuccess ||
