@@ -526,8 +526,8 @@ __global__ void __launch_bounds__(NTB<DK>(), DK >= 128 ? 1 : 2) intra_bwd_kernel
   float* G = v + C * L;
   float* dO = G + C * L;         // dO, later X = L^{-T} dU
   float* U = dO + C * L;         // Ut -> U, later dG
-  float* dU = U + C * L;         // dU, later Y = L^{-T} dWt
-  float* T0 = dU + C * L;        // Wt -> dWt -> Ut / Wt (recomputed)
+  float* dU = U + C * L;         // dU, later Ut / Wt (recomputed)
+  float* T0 = dU + C * L;        // Wt -> dWt -> Y = L^{-T} dWt
   float* T1 = T0 + C * L;        // Kh -> dKh -> dk
   float* T2 = T1 + C * L;        // dQg -> dq
   float* S0p = T2 + C * L;       // PR x L
@@ -567,17 +567,30 @@ __global__ void __launch_bounds__(NTB<DK>(), DK >= 128 ? 1 : 2) intra_bwd_kernel
   mm<C, DK, C, true, false>(dU, L, P, LC, dO, L, 1.f, false);
   __syncthreads();
   const long long so = chunk_off(p, b, h, n, DK * DK);
-  auto load_panels = [&](int kp) {
-    for (int i = threadIdx.x; i < PR * D4; i += blockDim.x) {
-      const int r = i / D4, c = (i % D4) * 4;
-      const long long g = so + (long long)(kp + r) * DK + c;
-      st4(S0p + r * L + c, ld4(p.states + g));
-      st4(dSp + r * L + c, ld4(p.dstates + g));
+  // panel rows are fetched into registers one panel ahead (the loads overlap
+  // the current panel's math) and stored to shared memory between barriers
+  static_assert(PR * D4 <= NTB<DK>(), "one 16-byte piece of each panel per thread");
+  const bool pl = threadIdx.x < PR * D4;
+  const int pr = threadIdx.x / D4, pc = (threadIdx.x % D4) * 4;
+  float4 nx_s = make_float4(0.f, 0.f, 0.f, 0.f), nx_d = nx_s;
+  auto fetch_panel = [&](int kp) {
+    if (pl && kp < DK) {
+      const long long g = so + (long long)(kp + pr) * DK + pc;
+      nx_s = ld4(p.states + g);
+      nx_d = ld4(p.dstates + g);
     }
   };
+  auto put_panel = [&]() {
+    if (pl) {
+      st4(S0p + pr * L + pc, nx_s);
+      st4(dSp + pr * L + pc, nx_d);
+    }
+  };
+  fetch_panel(0);
   for (int kp = 0; kp < DK; kp += PR) {
-    load_panels(kp);
+    put_panel();
     __syncthreads();
+    fetch_panel(kp + PR < DK ? kp + PR : 0);  // pass 2 starts again at panel 0
     mm<C, DK, PR, false, false>(U, L, T0 + kp, L, S0p, L, -1.f, true);
     mm<C, DK, PR, false, false>(dU, L, T1 + kp, L, dSp, L, 1.f, true);
     mm<C, PR, DK, false, true>(T2 + kp, L, dO, L, S0p, L, 1.f, false);
@@ -592,8 +605,9 @@ __global__ void __launch_bounds__(NTB<DK>(), DK >= 128 ? 1 : 2) intra_bwd_kernel
   // dP = dO U^T (into P; masked to s <= t below)
   mm<C, C, DK, false, true>(P, LC, dO, L, U, L, 1.f, false);
   for (int kp = 0; kp < DK; kp += PR) {
-    load_panels(kp);
+    put_panel();
     __syncthreads();
+    fetch_panel(kp + PR);
     mm<C, PR, DK, false, true>(T0 + kp, L, dU, L, S0p, L, -1.f, false);
     mm<C, PR, DK, false, true>(T1 + kp, L, U, L, dSp, L, 1.f, false);
     __syncthreads();
@@ -620,28 +634,28 @@ __global__ void __launch_bounds__(NTB<DK>(), DK >= 128 ? 1 : 2) intra_bwd_kernel
     U[si] = -dkh * k[si] * ed + dqg * scale * q[si] * eg;
     T2[si] = dqg * scale * eg;
   }
-  // X = L^{-T} dU (into dO)
+  // X = L^{-T} dU (into dO) and Y = L^{-T} dWt (in place in T0), one phase
   solve_cols<C, true>(
-      DK, N, [&](int t, int c) { return dU[t * L + c]; }, [&](int t, int c, float x) { dO[t * L + c] = x; });
-  __syncthreads();
-  // Y = L^{-T} dWt (into dU)
-  solve_cols<C, true>(
-      DK, N, [&](int t, int c) { return T0[t * L + c]; }, [&](int t, int c, float x) { dU[t * L + c] = x; });
+      2 * DK, N, [&](int t, int col) { return col < DK ? dU[t * L + col] : T0[t * L + col - DK]; },
+      [&](int t, int col, float x) {
+        if (col < DK) dO[t * L + col] = x;
+        else T0[t * L + col - DK] = x;
+      });
   __syncthreads();
   float* X = dO;
-  float* Y = dU;
-  // dL_ts = -(X Ut^T + Y Wt^T)_ts for s < t; Ut and Wt are recomputed into T0
+  float* Y = T0;
+  // dL_ts = -(X Ut^T + Y Wt^T)_ts for s < t; Ut is recomputed into dU, then Wt
   solve_cols<C, false>(
       DK, N, [&](int t, int c) { return bet[t] * v[t * L + c]; },
-      [&](int t, int c, float x) { T0[t * L + c] = x; });
+      [&](int t, int c, float x) { dU[t * L + c] = x; });
   __syncthreads();
-  mm<C, C, DK, false, true>(dA, LC, X, L, T0, L, -1.f, false);
+  mm<C, C, DK, false, true>(dA, LC, X, L, dU, L, -1.f, false);
   __syncthreads();
   solve_cols<C, false>(
       DK, N, [&](int t, int c) { return bet[t] * bet[t] * k[t * L + c] * __expf(G[t * L + c]); },
-      [&](int t, int c, float x) { T0[t * L + c] = x; });
+      [&](int t, int c, float x) { dU[t * L + c] = x; });
   __syncthreads();
-  mm<C, C, DK, false, true>(dA, LC, Y, L, T0, L, -1.f, true);
+  mm<C, C, DK, false, true>(dA, LC, Y, L, dU, L, -1.f, true);
   __syncthreads();
   for (int e = threadIdx.x; e < C * C; e += blockDim.x) {
     const int t = e / C, s = e % C;
