@@ -1,10 +1,32 @@
 // Host entry points of the tcgen05 GEMM: operand checks, TMA descriptors,
 // tile counts, and dispatch to the instantiation units.
+#include <cstdlib>
+#include <string>
+
 #include "gemm_kernel.cuh"
+#include "gemm_pair.cuh"
 
 namespace hb {
 
 namespace {
+
+// CTA-pair kernel selection: HB_GEMM_PAIR=0 disables it, =force uses it for
+// every supported shape (tests), default uses it when the 256 x 256 pair tiles
+// fill at least one wave of SM pairs.
+int pair_mode() {
+  static int m = [] {
+    const char* e = std::getenv("HB_GEMM_PAIR");
+    if (e && std::string(e) == "0") return 0;
+    if (e && std::string(e) == "force") return 2;
+    return 1;
+  }();
+  return m;
+}
+bool use_pair(long long pair_tiles) {
+  const int pm = pair_mode();
+  return pm == 2 || (pm == 1 && pair_tiles >= num_sms() / 2);
+}
+
 
 int pick_bn(int N) { return N >= 256 ? 256 : 128; }
 
@@ -68,6 +90,20 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool trans_a, bool 
     HB_CHECK(false, "gemm with K == 0 is not supported");
   }
   const int epi = epi_of(c, accumulate);
+  if (M >= 128 && N >= 256 && !(trans_a && trans_b)) {
+    const long long ptiles = (long long)((M + PAIR_BM - 1) / PAIR_BM) * ((N + PAIR_BN - 1) / PAIR_BN);
+    if (use_pair(ptiles)) {
+      GemmArgs pa = args;
+      pa.tiles_m = (M + PAIR_BM - 1) / PAIR_BM;
+      pa.tiles_n = (N + PAIR_BN - 1) / PAIR_BN;
+      pa.num_tiles = pa.tiles_m * pa.tiles_n;
+      pa.k_splits = 1;
+      CUtensorMap tbp = trans_b ? tmap_bf16_2d(b.data_ptr(), N, K, b.stride(0), 64, 128) : tb;
+      const int grid = 2 * std::min(pa.num_tiles, num_sms() / 2);
+      gemm_dispatch_pair(DENSE, trans_a, !trans_b, epi, ta, tbp, pa, grid);
+      return;
+    }
+  }
   // Split the K loop when the output has too few tiles to fill the GPU
   // (weight gradients: small [in, out] output, K = tokens).  fp32 outputs only.
   args.k_splits = 1;
@@ -156,8 +192,20 @@ void grouped_gemm_k(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Te
   args.num_groups = G;
   args.grp_start = grp_start.data_ptr<int>();
   args.grp_count = grp_count.data_ptr<int>();
-  const int grid = std::min(args.num_tiles, num_sms());
   const int epi = epi_of(c, accumulate);
+  if (M >= 128 && N >= 256 && epi != EPI_BF16) {
+    const long long ptiles = (long long)G * ((M + PAIR_BM - 1) / PAIR_BM) * ((N + PAIR_BN - 1) / PAIR_BN);
+    if (use_pair(ptiles)) {
+      GemmArgs pa = args;
+      pa.tiles_m = (M + PAIR_BM - 1) / PAIR_BM;
+      pa.tiles_n = (N + PAIR_BN - 1) / PAIR_BN;
+      pa.num_tiles = G * pa.tiles_m * pa.tiles_n;
+      const int grid = 2 * std::min(pa.num_tiles, num_sms() / 2);
+      gemm_dispatch_pair(GROUPED_K, true, true, epi, ta, tb, pa, grid);
+      return;
+    }
+  }
+  const int grid = std::min(args.num_tiles, num_sms());
   gemm_dispatch_grouped(GROUPED_K, BN, true, true, epi, ta, tb, args, grid);
 }
 

@@ -142,3 +142,60 @@ def test_grouped_gemm_fused_gather_emulated(world):
                     assert torch.equal(c[s:s + n], ref[s:s + n]), (rank, g)
                     assert torch.equal(gathered[g], b[g]), (rank, g)
         assert _ext().read_status() == 0
+
+
+_PAIR_SCRIPT = r"""
+import torch
+from hanuman_b200.ops._ext import ext
+def rel(x, r):
+    return ((x.float() - r).norm() / r.norm().clamp_min(1e-12)).item()
+torch.manual_seed(0)
+for (M, N, K, ta, tb) in [(4096, 768, 1024, False, False), (300, 512, 136, False, True), (1024, 3072, 512, False, False),
+                          (768, 1024, 4096, True, False), (2048, 256, 64, False, True), (520, 1000, 200, True, False)]:
+    a = (torch.randn(K, M, device="cuda") if ta else torch.randn(M, K, device="cuda")).bfloat16()
+    b = (torch.randn(N, K, device="cuda") if tb else torch.randn(K, N, device="cuda")).bfloat16()
+    A = a.float().t() if ta else a.float()
+    B = b.float().t() if tb else b.float()
+    ref = A @ B
+    for dt, acc in ((torch.float32, False), (torch.bfloat16, False), (torch.float32, True)):
+        c = torch.randn(M, N, device="cuda").to(dt)
+        c0 = c.float().clone()
+        ext().gemm(a, b, c, ta, tb, acc, 0.5)
+        torch.cuda.synchronize()
+        want = 0.5 * ref + (c0 if acc else 0)
+        e = rel(c, want)
+        assert e < (1e-2 if dt == torch.bfloat16 else 1e-5), (M, N, K, ta, tb, dt, acc, e)
+# grouped over K
+G, M, N = 5, 512, 768
+counts = [128, 0, 384, 128, 1024]
+starts, s = [], 0
+for c_ in counts:
+    starts.append(s); s += c_
+a = torch.randn(s, M, device="cuda").bfloat16()
+b = torch.randn(s, N, device="cuda").bfloat16()
+c = torch.randn(G, M, N, device="cuda")
+c0 = c.clone()
+gs = torch.tensor(starts, dtype=torch.int32, device="cuda")
+gc = torch.tensor(counts, dtype=torch.int32, device="cuda")
+ext().grouped_gemm_k(a, b, c, gs, gc, True)
+torch.cuda.synchronize()
+for g in range(G):
+    st, n = starts[g], counts[g]
+    r = a[st:st + n].float().t() @ b[st:st + n].float() + c0[g]
+    assert rel(c[g], r) < 1e-5, g
+assert ext().read_status() == 0
+print("PAIR_OK")
+"""
+
+
+def test_pair_gemm_forced():
+    """The CTA-pair (cta_group::2) kernel on every supported shape, forced on
+    (it normally runs only when the pair tiles fill a wave)."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, HB_GEMM_PAIR="force", PYTHONPATH=root)
+    r = subprocess.run([sys.executable, "-c", _PAIR_SCRIPT], env=env, capture_output=True, text=True,
+                       timeout=600)
+    assert "PAIR_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]
