@@ -230,11 +230,11 @@ class MoE(nn.Module):
     def forward(self, h, dtype):
         """h ``[B,S,D]`` (compute dtype) -> (fp32 output, aux dict)."""
         if h.is_cuda and getattr(self, "ep_world", 1) > 1:
-            from ..ops.moe_ep import EPContext, moe_ep_layer_cuda
-            if self.ep_ctx is None:
-                self.ep_ctx = EPContext(self, h.shape[0] * h.shape[1], h.shape[2],
-                                        self.expert_w_gate.shape[2], self.ep_dist,
-                                        self.capacity_factor)
+            from ..ops.moe_ep import moe_ep_layer_cuda, shared_ep_context
+            T = h.shape[0] * h.shape[1]
+            if self.ep_ctx is None or self.ep_ctx.T != T:
+                self.ep_ctx = shared_ep_context(self, T, h.shape[2], self.expert_w_gate.shape[2],
+                                                self.ep_dist, self.capacity_factor)
             return moe_ep_layer_cuda(self, h, dtype)
         if h.is_cuda:
             from ..ops.moe import moe_layer_cuda

@@ -231,6 +231,27 @@ class MoEEPFn(torch.autograd.Function):
         return dx.to(torch.bfloat16), None, None, None, None
 
 
+_SHARED_CTX: dict = {}
+
+
+def shared_ep_context(layer, T: int, D: int, F: int, ctx, capacity_factor: float) -> EPContext:
+    """One set of symmetric dispatch / return buffers per layer shape, shared by
+    every MoE layer: each use is fenced by device barriers and everything the
+    backward needs is copied out of the buffers, so layers never hold them."""
+    key = (T, D, F, layer.n_experts, layer.n_active, float(capacity_factor), ctx.world, ctx.rank,
+           torch.cuda.current_device())
+    ep = _SHARED_CTX.get(key)
+    if ep is None:
+        ep = EPContext(layer, T, D, F, ctx, capacity_factor)
+        _SHARED_CTX[key] = ep
+    return ep
+
+
+def release_shared_contexts():
+    """Drop the shared buffers (before the process group is destroyed)."""
+    _SHARED_CTX.clear()
+
+
 def moe_ep_layer_cuda(mod, h, dtype):
     B, S, D = h.shape
     ep = mod.ep_ctx
