@@ -12,6 +12,9 @@
 // Tiles that the causal / window mask removes entirely are skipped.
 #include <torch/extension.h>
 
+#include <cstdlib>
+#include <string>
+
 #include "../common/host.h"
 #include "../common/sm100.cuh"
 
@@ -603,9 +606,25 @@ static void check_qkv(const torch::Tensor& q, const torch::Tensor& k, const torc
 }
 
 // q [B,S,Nq,H], k/v [B,S,Nkv,H] -> out [B,S,Nq,H], lse [B,Nq,S] (log2 units)
+void flash_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
+                  int64_t window);
+
+// Head dim 64 runs on the tcgen05 forward (flash_tc.cu) unless HB_FA_TC=0.
+static bool use_fwd_tc(int H) {
+  static const bool on = [] {
+    const char* e = std::getenv("HB_FA_TC");
+    return !(e && std::string(e) == "0");
+  }();
+  return on && H == 64;
+}
+
 void flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                int64_t window) {
   check_qkv(q, k, v);
+  if (use_fwd_tc(q.size(3))) {
+    flash_fwd_tc(q, k, v, out, lse, window);
+    return;
+  }
   Params p = make_params(q, k, window);
   p.q = (const __nv_bfloat16*)q.data_ptr();
   p.k = (const __nv_bfloat16*)k.data_ptr();

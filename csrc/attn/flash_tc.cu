@@ -1,0 +1,346 @@
+// Causal / sliding-window GQA attention forward on the 5th-generation tensor
+// cores (tcgen05 + TMEM), head dim 64 (model/attention.py:136-224 semantics:
+// query i sees key j iff j <= i and, with a window W > 0, i - j < W).
+//
+// CTA = 128 query rows of one head; key/value tiles of 64.  Warp roles:
+//   warp 0     TMA producer: Q once, then K_j / V_j into a 3-deep ring
+//   warp 1     MMA issuer (one elected lane):
+//                S_j  = Q K_j^T   M 128 x N 64 x K 64   -> TMEM S buffer j % 2
+//                O   += P_j V_j   M 128 x N 64 x K 64   -> TMEM O
+//              S_{j+2} is issued as soon as softmax j has consumed S_j, so the
+//              tensor core computes the next score tile during the softmax
+//   warps 2-9  softmax / epilogue, two threads per query row (32 keys each):
+//              read S from TMEM (tcgen05.ld), online softmax in the exp2 domain
+//              (row max exchanged through shared memory), write P_j (bf16) into
+//              P buffer j % 2, a 128B-swizzled shared tile that is the A operand
+//              of the P V MMA; at the end O / l -> bf16 and the row lse (log2).
+// The running max used for the exponentials is raised only when a tile's max
+// exceeds it by more than 8 (log2 units), so P <= 256 and O in TMEM is
+// rescaled (tcgen05.ld / st, warp-uniform: the whole warp takes that path when
+// any of its rows needs it) only on those rare steps.  Double-buffered
+// barriers (s_full, p_full, pv_done per buffer) keep every mbarrier at most
+// one phase ahead of its waiter.  Two CTAs share an SM (97 KB of shared memory,
+// 256 TMEM columns each).  Every wait is bounded (status word).
+#include <torch/extension.h>
+
+#include "../common/host.h"
+#include "../common/sm100.cuh"
+
+namespace hb {
+namespace fatc {
+
+constexpr int H = 64;
+constexpr int BQ = 128;
+constexpr int BK = 64;
+constexpr int THREADS = 320;   // producer, MMA, 8 softmax warps
+constexpr int Q_BYTES = BQ * H * 2;          // 16 KB
+constexpr int K_BYTES = BK * H * 2;          // 8 KB
+constexpr int V_BYTES = BK * H * 2;          // 8 KB
+constexpr int P_BYTES = BQ * BK * 2;         // 16 KB
+constexpr int KV_STAGES = 3;
+constexpr int SMEM = Q_BYTES + KV_STAGES * (K_BYTES + V_BYTES) + 2 * P_BYTES + 1024 + 256 + 6 * BQ * 4;
+constexpr int TMEM_COLS = 256;
+constexpr int S_COL = 0, O_COL = 128;   // S buffers at columns 0 and 64
+
+// 2^x on the special-function unit (PTX ex2.approx, flush-to-zero).
+HB_DEVICE float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float LOG2E = 1.4426950408889634f;
+
+struct TcParams {
+  int B, S, Nq, Nkv, window;
+  float sl2;            // scale * log2(e)
+  long long q_row;      // elements between consecutive tokens of q / out
+  __nv_bfloat16* out;
+  float* lse;
+  int* status;
+  unsigned long long budget_ns;
+};
+
+HB_DEVICE bool visible(const TcParams& p, int qi, int kj) {
+  return kj <= qi && (p.window <= 0 || qi - kj < p.window) && kj < p.S && qi < p.S;
+}
+
+__global__ void __launch_bounds__(THREADS, 2)
+    fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const __grid_constant__ CUtensorMap tmV, const TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sQ = smem_u32(smem);
+  const uint32_t sK0 = sQ + Q_BYTES;                 // KV_STAGES stages of K, then of V
+  const uint32_t sV0 = sK0 + KV_STAGES * K_BYTES;
+  const uint32_t sP0 = sV0 + KV_STAGES * V_BYTES;    // two P buffers
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Q_BYTES + KV_STAGES * (K_BYTES + V_BYTES) + 2 * P_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;                 // [KV_STAGES]
+  uint64_t* kv_empty = kv_full + KV_STAGES;     // [KV_STAGES]
+  uint64_t* s_full = kv_empty + KV_STAGES;      // [2]
+  uint64_t* p_full = s_full + 2;                // [2]
+  uint64_t* pv_done = p_full + 2;               // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nqt = (p.S + BQ - 1) / BQ;
+  const int qt = nqt - 1 - blockIdx.x;  // longest causal rows first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (p.Nq / p.Nkv);
+  const int q0 = qt * BQ;
+  const int hi = min(p.S, q0 + BQ);
+  const int lo = p.window > 0 ? max(0, q0 - p.window + 1) : 0;
+  const int jb0 = lo / BK, jb1 = (hi + BK - 1) / BK;
+  const int nkt = jb1 - jb0;
+  const int row0 = b * p.S;  // first token row of this sequence in the 2-D views
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(q_full), 1);
+    for (int s = 0; s < KV_STAGES; ++s) {
+      mbar_init(smem_u32(&kv_full[s]), 1);
+      mbar_init(smem_u32(&kv_empty[s]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&s_full[i]), 1);
+      mbar_init(smem_u32(&p_full[i]), 256);
+      mbar_init(smem_u32(&pv_done[i]), 1);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one()) {
+      mbar_expect_tx(smem_u32(q_full), Q_BYTES);
+      tma_load_2d(sQ, &tmQ, smem_u32(q_full), h * H, row0 + q0);
+      for (int j = 0; j < nkt; ++j) {
+        const int st = j % KV_STAGES;
+        if (!mbar_wait(smem_u32(&kv_empty[st]), ((j / KV_STAGES) & 1) ^ 1, p.status, kErrTimeoutProducer,
+                       p.budget_ns))
+          break;
+        const uint32_t fb = smem_u32(&kv_full[st]);
+        mbar_expect_tx(fb, K_BYTES + V_BYTES);
+        const int k0 = (jb0 + j) * BK;
+        tma_load_2d(sK0 + st * K_BYTES, &tmK, fb, hk * H, row0 + k0);
+        tma_load_2d(sV0 + st * V_BYTES, &tmV, fb, hk * H, row0 + k0);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(BQ, BK, false, false);
+      constexpr uint32_t idesc_o = make_idesc_bf16(BQ, H, false, true);
+      bool ok = mbar_wait(smem_u32(q_full), 0, p.status, kErrTimeoutMma, p.budget_ns);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % KV_STAGES;
+        if (!mbar_wait(smem_u32(&kv_full[st]), (j / KV_STAGES) & 1, p.status, kErrTimeoutMma, p.budget_ns))
+          return false;
+        tc_fence_after();
+        const uint32_t sk = sK0 + st * K_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < H / 16; ++kk)
+          umma_f16(tmem + S_COL + (j & 1) * BK, make_smem_desc(sQ + kk * 32, 16, 1024),
+                   make_smem_desc(sk + kk * 32, 16, 1024), idesc_s, kk != 0 ? 1u : 0u);
+        umma_commit(smem_u32(&s_full[j & 1]));
+        return true;
+      };
+      if (ok && nkt > 0) ok = issue_s(0);
+      if (ok && nkt > 1) ok = issue_s(1);
+      for (int j = 0; ok && j < nkt; ++j) {
+        if (!mbar_wait(smem_u32(&p_full[j & 1]), (j >> 1) & 1, p.status, kErrTimeoutMma, p.budget_ns)) break;
+        tc_fence_after();
+        const uint32_t sv = sV0 + (j % KV_STAGES) * V_BYTES;
+        const uint32_t sp = sP0 + (j & 1) * P_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint64_t ad = make_smem_desc(sp + kk * 32, 16, 1024);
+          const uint64_t bd = make_smem_desc(sv + kk * 2048, 8192, 1024);
+          umma_f16(tmem + O_COL, ad, bd, idesc_o, (j | kk) != 0 ? 1u : 0u);
+        }
+        umma_commit(smem_u32(&pv_done[j & 1]));
+        umma_commit(smem_u32(&kv_empty[j % KV_STAGES]));
+        if (j + 2 < nkt) ok = issue_s(j + 2);   // S buffer j % 2 was consumed by softmax j
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax / epilogue
+    // Warps 2-9: two threads per query row.  Warp w reads TMEM lane quadrant
+    // w % 4 (rows 32 (w % 4) ..) and owns key / output columns half * 32 ..,
+    // half = (w - 2) / 4.  The two halves of a row exchange their maxima
+    // through xmax (double-buffered by tile parity, one named barrier per tile).
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int r = quad * 32 + lane;     // row of the tile == TMEM lane
+    const int qi = q0 + r;
+    const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
+    float* xmax = reinterpret_cast<float*>(tmem_slot + 4);   // [2 parity][2 half][BQ]
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkt; ++j) {
+      // After a timeout the loop keeps running without waiting, so every warp
+      // still reaches the named barriers below; nothing is written at the end.
+      if (ok) ok = mbar_wait(smem_u32(&s_full[j & 1]), (j >> 1) & 1, p.status, kErrTimeoutEpilogue, p.budget_ns);
+      ok = __all_sync(0xffffffffu, ok);
+      tc_fence_after();
+      const int k0 = (jb0 + j) * BK + half * 32;   // this thread's 32 keys
+      const bool need_mask = (k0 + 32 > q0) || p.window > 0 || (k0 + 32 > p.S);
+      uint32_t sv[32];
+      tmem_ld_32x32b_x32(trow + S_COL + (j & 1) * BK + half * 32, sv);
+      tmem_ld_wait();
+      // pass 1: row max of the raw scores (the scale is positive), both halves
+      float mraw = -INFINITY;
+      if (!need_mask) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) mraw = fmaxf(mraw, __uint_as_float(sv[e]));
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (visible(p, qi, k0 + e)) mraw = fmaxf(mraw, __uint_as_float(sv[e]));
+      }
+      xmax[((j & 1) * 2 + half) * BQ + r] = mraw;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      mraw = fmaxf(mraw, xmax[((j & 1) * 2 + (half ^ 1)) * BQ + r]);
+      const float mt = mraw * p.sl2;
+      float alpha = 1.f;
+      const bool raise = mt > m_used + 8.f;
+      if (raise) {
+        alpha = m_used == -INFINITY ? 0.f : ex2(m_used - mt);
+        m_used = mt;
+        l *= alpha;
+      }
+      // tcgen05.ld / st are warp-collective: the rescale runs for the whole warp
+      const bool warp_raise = __any_sync(0xffffffffu, raise);
+      // O rescale: needs P V_{j-1} complete (and P V_j not yet issued)
+      if (warp_raise && j > 0) {
+        if (ok)
+          ok = mbar_wait(smem_u32(&pv_done[(j - 1) & 1]), ((j - 1) >> 1) & 1, p.status, kErrTimeoutEpilogue,
+                         p.budget_ns);
+        ok = __all_sync(0xffffffffu, ok);
+        tc_fence_after();
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(trow + O_COL + half * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+        tmem_st_32x32b_x32(trow + O_COL + half * 32, v);
+        tmem_st_wait();
+      }
+      // P buffer j % 2 is free once P V_{j-2} is complete
+      if (j >= 2) {
+        if (ok) ok = mbar_wait(smem_u32(&pv_done[j & 1]), ((j - 2) >> 1) & 1, p.status, kErrTimeoutEpilogue, p.budget_ns);
+        ok = __all_sync(0xffffffffu, ok);
+      }
+      // pass 2: P = exp2(s * scale * log2e - m_used) -> bf16 into the swizzled A tile
+      {
+        const float nm = -m_used;
+        const bool live = m_used != -INFINITY;   // otherwise no key of this row is visible yet
+        float pv[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          float x = live ? ex2(fmaf(__uint_as_float(sv[e]), p.sl2, nm)) : 0.f;
+          if (need_mask && !visible(p, qi, k0 + e)) x = 0.f;
+          pv[e] = x;
+          l += x;
+        }
+        const uint32_t prow = sP0 + (j & 1) * P_BYTES + r * 128;
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          const int chunk = half * 4 + q8;
+          const uint32_t addr = prow + ((chunk ^ (r & 7)) << 4);
+          const uint32_t w0 = pack_bf16x2(pv[q8 * 8 + 0], pv[q8 * 8 + 1]);
+          const uint32_t w1 = pack_bf16x2(pv[q8 * 8 + 2], pv[q8 * 8 + 3]);
+          const uint32_t w2 = pack_bf16x2(pv[q8 * 8 + 4], pv[q8 * 8 + 5]);
+          const uint32_t w3 = pack_bf16x2(pv[q8 * 8 + 6], pv[q8 * 8 + 7]);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w0), "r"(w1), "r"(w2), "r"(w3)
+                       : "memory");
+        }
+      }
+      fence_proxy_async();   // generic-proxy P stores -> visible to the tensor core
+      tc_fence_before();
+      mbar_arrive(smem_u32(&p_full[j & 1]));
+    }
+    // epilogue: O / l with l summed over the row's two halves
+    if (ok && nkt > 0)
+      ok = mbar_wait(smem_u32(&pv_done[(nkt - 1) & 1]), ((nkt - 1) >> 1) & 1, p.status, kErrTimeoutEpilogue,
+                     p.budget_ns);
+    const bool all_ok = __all_sync(0xffffffffu, ok) && nkt > 0;
+    float* xl = xmax + 4 * BQ;   // [2 half][BQ]
+    xl[half * BQ + r] = l;
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    l += xl[(half ^ 1) * BQ + r];
+    if (all_ok) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* og = p.out + ((long long)b * p.S + qi) * p.q_row + h * H + half * 32;
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(trow + O_COL + half * 32, v);
+      tmem_ld_wait();
+      if (qi < p.S) {
+        uint4* o4 = reinterpret_cast<uint4*>(og);
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          uint4 w;
+          w.x = pack_bf16x2(__uint_as_float(v[q8 * 8 + 0]) * inv, __uint_as_float(v[q8 * 8 + 1]) * inv);
+          w.y = pack_bf16x2(__uint_as_float(v[q8 * 8 + 2]) * inv, __uint_as_float(v[q8 * 8 + 3]) * inv);
+          w.z = pack_bf16x2(__uint_as_float(v[q8 * 8 + 4]) * inv, __uint_as_float(v[q8 * 8 + 5]) * inv);
+          w.w = pack_bf16x2(__uint_as_float(v[q8 * 8 + 6]) * inv, __uint_as_float(v[q8 * 8 + 7]) * inv);
+          o4[q8] = w;
+        }
+        if (half == 0) p.lse[((long long)b * p.Nq + h) * p.S + qi] = l > 0.f ? m_used + log2f(l) : INFINITY;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+}  // namespace fatc
+
+// q [B,S,Nq,64], k/v [B,S,Nkv,64] bf16 contiguous; out like q; lse [B,Nq,S] fp32.
+void flash_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
+                  int64_t window) {
+  const int B = q.size(0), S = q.size(1), Nq = q.size(2), Nkv = k.size(2);
+  HB_CHECK(q.size(3) == fatc::H, "flash_fwd_tc: head dim 64");
+  const c10::cuda::CUDAGuard guard(q.device());
+  fatc::TcParams p{};
+  p.B = B;
+  p.S = S;
+  p.Nq = Nq;
+  p.Nkv = Nkv;
+  p.window = (int)window;
+  p.sl2 = (1.f / std::sqrt((float)fatc::H)) * fatc::LOG2E;
+  p.q_row = (long long)Nq * fatc::H;
+  p.out = (__nv_bfloat16*)out.data_ptr();
+  p.lse = lse.data_ptr<float>();
+  p.status = status_ptr();
+  p.budget_ns = wait_budget_ns();
+  const uint64_t rows = (uint64_t)B * S;
+  CUtensorMap tq = tmap_bf16_2d(q.data_ptr(), rows, (uint64_t)Nq * fatc::H, (uint64_t)Nq * fatc::H, 64, fatc::BQ);
+  CUtensorMap tk = tmap_bf16_2d(k.data_ptr(), rows, (uint64_t)Nkv * fatc::H, (uint64_t)Nkv * fatc::H, 64, fatc::BK);
+  CUtensorMap tv = tmap_bf16_2d(v.data_ptr(), rows, (uint64_t)Nkv * fatc::H, (uint64_t)Nkv * fatc::H, 64, fatc::BK);
+  static bool configured = false;
+  if (!configured) {
+    HB_CUDA_CHECK(cudaFuncSetAttribute(fatc::fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fatc::SMEM));
+    configured = true;
+  }
+  dim3 grid((S + fatc::BQ - 1) / fatc::BQ, Nq, B);
+  fatc::fwd_tc_kernel<<<grid, fatc::THREADS, fatc::SMEM, cur_stream()>>>(tq, tk, tv, p);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace hb
