@@ -57,7 +57,7 @@ def generate_from_model(model: Transformer, config: Config, tokenizer, prompt: s
 
 def load_for_generate(config: Config, prompt: str, max_tokens: int = 100,
                       temperature: float = 1.0, top_k: int = 0, seed: int = 0,
-                      device: str = None):
+                      device: str = None, cached: bool = False):
     """Latest checkpoint of ``config`` -> text (generate.py:20-68)."""
     path = latest_checkpoint(config)
     if path is None:
@@ -75,5 +75,8 @@ def load_for_generate(config: Config, prompt: str, max_tokens: int = 100,
     if dev != "cpu":
         from .engine import Engine
         Engine(model, config, torch.device(dev))   # attaches compute-dtype working copies
+    if cached:
+        from .decode import generate_cached
+        return generate_cached(model, get_tokenizer(config), prompt, max_tokens, temperature, top_k, seed)
     return generate_from_model(model, config, get_tokenizer(config), prompt, max_tokens,
                                temperature, top_k, seed)

@@ -56,7 +56,7 @@ def cmd_generate(args):
     if args.yarn_factor is not None:
         config.yarn_factor = args.yarn_factor
     text, ids = load_for_generate(config, args.prompt, args.max_tokens, args.temperature,
-                                  args.top_k, args.seed)
+                                  args.top_k, args.seed, cached=args.cache)
     print("=== Generated ===")
     print(text)
     print("=== Token ids ===")
@@ -120,6 +120,8 @@ def build_parser():
     g.add_argument("--top_k", type=int, default=0)
     g.add_argument("--seed", type=int, default=0)
     g.add_argument("--yarn_factor", type=float, default=None)
+    g.add_argument("--cache", action="store_true",
+                   help="incremental decoding with KV / KDA-state caches (same tokens, no recompute)")
     g.set_defaults(func=cmd_generate)
     c = sub.add_parser("count", help="Print param counts")
     c.add_argument("--config", default="full_g4", choices=list(PRESETS))

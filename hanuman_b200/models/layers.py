@@ -123,11 +123,24 @@ class KDA(nn.Module):
         self.wo = nn.Parameter(_normal((H * V, D), std, gen))
         self.o_norm = nn.Parameter(torch.ones(V))
 
+    def _conv_with_history(self, state, name, x):
+        """Causal conv of ``x [B, S, C]`` continuing the rows kept in ``state``;
+        returns (conv output [B, S, C], ) and stores the new history."""
+        w = getattr(self, f"{name}_conv").weight
+        taps = w.shape[-1]
+        hist = state.get(f"conv_{name}")
+        if hist is None:
+            hist = torch.zeros(x.shape[0], taps - 1, x.shape[2], dtype=x.dtype, device=x.device)
+        full = torch.cat([hist.to(x.dtype), x], dim=1)
+        out = ref.short_conv(full, w)[:, taps - 1:]
+        state[f"conv_{name}"] = full[:, -(taps - 1):].detach()
+        return (out,)
+
     def forward(self, h, dtype, state=None):
         B, S, D = h.shape
         H, K = self.n_heads, self.head_dim
         V = K
-        if h.is_cuda:
+        if h.is_cuda and state is None:
             from ..ops.kda import kda_layer_cuda
             return kda_layer_cuda(self, h, dtype)
         x = h.reshape(B * S, D)
@@ -137,9 +150,18 @@ class KDA(nn.Module):
         qr = (xf @ self.wq.float()).to(dtype).view(B, S, H * K)
         kr = (xf @ self.wk.float()).to(dtype).view(B, S, H * K)
         vr = (xf @ self.wv.float()).to(dtype).view(B, S, H * V)
-        q = F.silu(ref.short_conv(qr, self.q_conv.weight).float()).view(B, S, H, K)
-        k = F.silu(ref.short_conv(kr, self.k_conv.weight).float()).view(B, S, H, K)
-        v = F.silu(ref.short_conv(vr, self.v_conv.weight).float()).view(B, S, H, V)
+        if state is not None:
+            # incremental decoding: the conv sees the last (taps - 1) projected
+            # rows of earlier calls (ShortConv1D.step of the reference, model/kda.py:138-146)
+            qr, kr, vr = (self._conv_with_history(state, name, x_)
+                          for name, x_ in (("q", qr), ("k", kr), ("v", vr)))
+            q = F.silu(qr[0].float()).view(B, S, H, K)
+            k = F.silu(kr[0].float()).view(B, S, H, K)
+            v = F.silu(vr[0].float()).view(B, S, H, V)
+        else:
+            q = F.silu(ref.short_conv(qr, self.q_conv.weight).float()).view(B, S, H, K)
+            k = F.silu(ref.short_conv(kr, self.k_conv.weight).float()).view(B, S, H, K)
+            v = F.silu(ref.short_conv(vr, self.v_conv.weight).float()).view(B, S, H, V)
         q = ref.l2_norm(q, 1e-6)
         k = ref.l2_norm(k, 1e-6)
         f = ((xf @ self.f_proj0.float()) @ self.f_proj1.float()).view(B, S, H, K)

@@ -146,3 +146,23 @@ def test_cli_count_and_report(capsys):
     main(["report", "--config", "smoke"])
     out = capsys.readouterr().out
     assert "Total params" in out and "step FLOPs" in out
+
+
+@pytest.mark.parametrize("name", ["smoke", "smoke_kda"])
+def test_cached_decoding_matches_full_recompute(name):
+    """KV / KDA-state caches: greedy tokens equal the reference's padded
+    full-recompute decoding (attention with a window in `smoke`, KDA + full
+    attention in `smoke_kda`)."""
+    from hanuman_b200.data import get_tokenizer
+    from hanuman_b200.decode import generate_cached
+    from hanuman_b200.generate import generate_from_model
+    c = get_config(name).replace(dtype="fp32")
+    tr = Trainer(c, device="cpu")
+    for s in range(3):
+        tr.step(_tokens(c, s))
+    model = tr.model
+    tok = get_tokenizer(c)
+    _, ref_ids = generate_from_model(model, c, tok, "hello world", max_tokens=12, temperature=0.0,
+                                     seq_len=64)
+    _, ids = generate_cached(model, tok, "hello world", max_tokens=12, temperature=0.0)
+    assert ids == ref_ids
