@@ -608,8 +608,11 @@ static void check_qkv(const torch::Tensor& q, const torch::Tensor& k, const torc
 // q [B,S,Nq,H], k/v [B,S,Nkv,H] -> out [B,S,Nq,H], lse [B,Nq,S] (log2 units)
 void flash_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                   int64_t window);
+void flash_bwd_kv_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor dout, torch::Tensor lse,
+                     torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, int64_t window);
 
-// Head dim 64 runs on the tcgen05 forward (flash_tc.cu) unless HB_FA_TC=0.
+// Head dim 64 runs on the tcgen05 kernels (flash_tc.cu: forward, and dK / dV
+// of the backward) unless HB_FA_TC=0.
 static bool use_fwd_tc(int H) {
   static const bool on = [] {
     const char* e = std::getenv("HB_FA_TC");
@@ -693,7 +696,11 @@ void flash_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor 
       fa::set_smem<64>((const void*)fa::bwd_dq_kernel<64>, smem_q);
       c = true;
     }
-    fa::bwd_dkdv_kernel<64><<<gkv, fa::NT, smem_kv, cur_stream()>>>(p);
+    if (use_fwd_tc(64)) {   // dK / dV on tcgen05 (flash_tc.cu), dQ below
+      flash_bwd_kv_tc(q, k, v, dout, lse, delta, dk, dv, window);
+    } else {
+      fa::bwd_dkdv_kernel<64><<<gkv, fa::NT, smem_kv, cur_stream()>>>(p);
+    }
     fa::bwd_dq_kernel<64><<<gq, fa::NT, smem_q, cur_stream()>>>(p);
   } else {
     static bool c = false;

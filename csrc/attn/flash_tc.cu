@@ -309,6 +309,252 @@ __global__ void __launch_bounds__(THREADS, 2)
   if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
 }
 
+
+// ============================================================== backward dK / dV
+// CTA = 128 keys of one KV head; loops over every query head of the GQA group
+// and every query tile of 64 that sees these keys.  Per query tile i:
+//   S^T  = K Q_i^T,  dP^T = V dO_i^T          (M 128 keys x N 64 queries, TMEM)
+//   P^T  = exp2(S^T * scale * log2e - lse),  dS^T = P^T (dP^T - delta)
+//          (two threads per key row, 32 queries each; bf16 into swizzled A tiles)
+//   dV  += P^T dO_i,  dK += dS^T Q_i           (M 128 x N 64 x K 64, TMEM)
+// then dK * scale and dV -> bf16.  The producer warp stages lse / delta of the
+// tile into shared memory (bounds-checked loads) beside the TMA loads of Q_i and
+// dO_i.  dQ is produced by the Q-major kernel in flash_attn.cu.
+constexpr int KBT = 128;    // keys per CTA
+constexpr int QBT = 64;     // queries per tile
+constexpr int BWD_THREADS = 320;
+constexpr int QT_BYTES = QBT * H * 2;     // 8 KB
+constexpr int KT_BYTES = KBT * H * 2;     // 16 KB
+constexpr int PT_BYTES = KBT * QBT * 2;   // 16 KB
+constexpr int BWD_SMEM = 2 * KT_BYTES + 2 * 2 * QT_BYTES + 2 * PT_BYTES + 2 * 2 * QBT * 4 + 1024 + 256;
+constexpr int BWD_TMEM = 256;
+constexpr int ST_COL = 0, DPT_COL = 64, DV_COL = 128, DK_COL = 192;
+
+struct BwdParams {
+  int B, S, Nq, Nkv, window;
+  float scale, sl2;
+  const float *lse, *delta;
+  __nv_bfloat16 *dk, *dv;
+  long long kv_row;
+  int* status;
+  unsigned long long budget_ns;
+};
+
+HB_DEVICE bool visible_b(const BwdParams& p, int qi, int kj) {
+  return kj <= qi && (p.window <= 0 || qi - kj < p.window) && kj < p.S && qi < p.S;
+}
+
+__global__ void __launch_bounds__(BWD_THREADS, 2)
+    bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmD,
+                     const BwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sK = smem_u32(smem);
+  const uint32_t sV = sK + KT_BYTES;
+  const uint32_t sQ0 = sV + KT_BYTES;                // 2 stages
+  const uint32_t sD0 = sQ0 + 2 * QT_BYTES;           // 2 stages (dO)
+  const uint32_t sPt = sD0 + 2 * QT_BYTES;           // P^T tile
+  const uint32_t sSt = sPt + PT_BYTES;               // dS^T tile
+  float* sLse = reinterpret_cast<float*>(smem + 2 * KT_BYTES + 4 * QT_BYTES + 2 * PT_BYTES);  // [2][QBT]
+  float* sDel = sLse + 2 * QBT;                                                               // [2][QBT]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDel + 2 * QBT);
+  uint64_t* kv_full = bars;
+  uint64_t* qd_full = bars + 1;    // [2]
+  uint64_t* qd_empty = bars + 3;   // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* pv_done = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int kb = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int k0 = kb * KBT;
+  const int rep = p.Nq / p.Nkv;
+  const int qlo = k0;
+  const int qhi = p.window > 0 ? min(p.S, k0 + KBT - 1 + p.window) : p.S;
+  const int ib0 = qlo / QBT, ib1 = (qhi + QBT - 1) / QBT;
+  const int nq = max(0, ib1 - ib0);
+  const int total = nq * rep;
+  const int row0 = b * p.S;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(kv_full), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&qd_full[s]), 32);
+      mbar_init(smem_u32(&qd_empty[s]), 1);
+    }
+    mbar_init(smem_u32(s_full), 1);
+    mbar_init(smem_u32(p_full), 256);
+    mbar_init(smem_u32(pv_done), 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), BWD_TMEM);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (whole warp)
+    if (lane == 0) {
+      mbar_expect_tx(smem_u32(kv_full), 2 * KT_BYTES);
+      tma_load_2d(sK, &tmK, smem_u32(kv_full), hk * H, row0 + k0);
+      tma_load_2d(sV, &tmV, smem_u32(kv_full), hk * H, row0 + k0);
+    }
+    for (int it = 0; it < total; ++it) {
+      const int st = it & 1;
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(smem_u32(&qd_empty[st]), ((it >> 1) & 1) ^ 1, p.status, kErrTimeoutProducer, p.budget_ns);
+      if (!__all_sync(0xffffffffu, __shfl_sync(0xffffffffu, ok, 0))) break;
+      const int hq = hk * rep + it / nq;
+      const int q0 = (ib0 + it % nq) * QBT;
+      for (int i = lane; i < QBT; i += 32) {
+        const bool in = q0 + i < p.S;
+        const long long idx = ((long long)b * p.Nq + hq) * p.S + q0 + i;
+        sLse[st * QBT + i] = in ? p.lse[idx] : INFINITY;
+        sDel[st * QBT + i] = in ? p.delta[idx] : 0.f;
+      }
+      const uint32_t fb = smem_u32(&qd_full[st]);
+      if (lane == 0) {
+        mbar_expect_tx(fb, 2 * QT_BYTES);
+        tma_load_2d(sQ0 + st * QT_BYTES, &tmQ, fb, hq * H, row0 + q0);
+        tma_load_2d(sD0 + st * QT_BYTES, &tmD, fb, hq * H, row0 + q0);
+      } else {
+        mbar_arrive(fb);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(KBT, QBT, false, false);   // K-major A and B
+      constexpr uint32_t idesc_a = make_idesc_bf16(KBT, H, false, true);      // B MN-major
+      bool ok = mbar_wait(smem_u32(kv_full), 0, p.status, kErrTimeoutMma, p.budget_ns);
+      auto issue_s = [&](int it) -> bool {
+        const int st = it & 1;
+        if (!mbar_wait(smem_u32(&qd_full[st]), (it >> 1) & 1, p.status, kErrTimeoutMma, p.budget_ns)) return false;
+        tc_fence_after();
+        const uint32_t sq = sQ0 + st * QT_BYTES, sd = sD0 + st * QT_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < H / 16; ++kk) {
+          umma_f16(tmem + ST_COL, make_smem_desc(sK + kk * 32, 16, 1024), make_smem_desc(sq + kk * 32, 16, 1024),
+                   idesc_s, kk != 0 ? 1u : 0u);
+          umma_f16(tmem + DPT_COL, make_smem_desc(sV + kk * 32, 16, 1024), make_smem_desc(sd + kk * 32, 16, 1024),
+                   idesc_s, kk != 0 ? 1u : 0u);
+        }
+        umma_commit(smem_u32(s_full));
+        return true;
+      };
+      if (ok && total > 0) ok = issue_s(0);
+      for (int it = 0; ok && it < total; ++it) {
+        if (!mbar_wait(smem_u32(p_full), it & 1, p.status, kErrTimeoutMma, p.budget_ns)) break;
+        tc_fence_after();
+        const int st = it & 1;
+        const uint32_t sq = sQ0 + st * QT_BYTES, sd = sD0 + st * QT_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < QBT / 16; ++kk) {
+          umma_f16(tmem + DV_COL, make_smem_desc(sPt + kk * 32, 16, 1024), make_smem_desc(sd + kk * 2048, 8192, 1024),
+                   idesc_a, (it | kk) != 0 ? 1u : 0u);
+          umma_f16(tmem + DK_COL, make_smem_desc(sSt + kk * 32, 16, 1024), make_smem_desc(sq + kk * 2048, 8192, 1024),
+                   idesc_a, (it | kk) != 0 ? 1u : 0u);
+        }
+        umma_commit(smem_u32(pv_done));
+        umma_commit(smem_u32(&qd_empty[st]));
+        if (it + 1 < total) ok = issue_s(it + 1);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ P^T / dS^T, epilogue
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int r = quad * 32 + lane;        // key row of the tile == TMEM lane
+    const int kj = k0 + r;
+    const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
+    bool ok = true;
+    for (int it = 0; it < total; ++it) {
+      if (ok) ok = mbar_wait(smem_u32(s_full), it & 1, p.status, kErrTimeoutEpilogue, p.budget_ns);
+      ok = __all_sync(0xffffffffu, ok);
+      tc_fence_after();
+      const int st = it & 1;
+      const int q0 = (ib0 + it % nq) * QBT + half * 32;   // this thread's 32 queries
+      const bool need_mask = q0 < k0 + KBT || p.window > 0 || q0 + 32 > p.S;
+      uint32_t sv[32], dv[32];
+      tmem_ld_32x32b_x32(trow + ST_COL + half * 32, sv);
+      tmem_ld_32x32b_x32(trow + DPT_COL + half * 32, dv);
+      tmem_ld_wait();
+      // the P^T / dS^T tiles are free once the previous tile's dV / dK MMAs are done
+      if (it > 0) {
+        if (ok) ok = mbar_wait(smem_u32(pv_done), (it - 1) & 1, p.status, kErrTimeoutEpilogue, p.budget_ns);
+        ok = __all_sync(0xffffffffu, ok);
+      }
+      const float* lse = sLse + st * QBT + half * 32;
+      const float* del = sDel + st * QBT + half * 32;
+      float pt[32], ds[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        float pv = ex2(fmaf(__uint_as_float(sv[e]), p.sl2, -lse[e]));
+        if (need_mask && !visible_b(p, q0 + e, kj)) pv = 0.f;
+        pt[e] = pv;
+        ds[e] = pv * (__uint_as_float(dv[e]) - del[e]);
+      }
+      const uint32_t off = r * 128;
+#pragma unroll
+      for (int q8 = 0; q8 < 4; ++q8) {
+        const int chunk = half * 4 + q8;
+        const uint32_t sw = off + ((chunk ^ (r & 7)) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sPt + sw),
+                     "r"(pack_bf16x2(pt[q8 * 8 + 0], pt[q8 * 8 + 1])), "r"(pack_bf16x2(pt[q8 * 8 + 2], pt[q8 * 8 + 3])),
+                     "r"(pack_bf16x2(pt[q8 * 8 + 4], pt[q8 * 8 + 5])), "r"(pack_bf16x2(pt[q8 * 8 + 6], pt[q8 * 8 + 7]))
+                     : "memory");
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sSt + sw),
+                     "r"(pack_bf16x2(ds[q8 * 8 + 0], ds[q8 * 8 + 1])), "r"(pack_bf16x2(ds[q8 * 8 + 2], ds[q8 * 8 + 3])),
+                     "r"(pack_bf16x2(ds[q8 * 8 + 4], ds[q8 * 8 + 5])), "r"(pack_bf16x2(ds[q8 * 8 + 6], ds[q8 * 8 + 7]))
+                     : "memory");
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      mbar_arrive(smem_u32(p_full));
+    }
+    if (ok && total > 0) ok = mbar_wait(smem_u32(pv_done), (total - 1) & 1, p.status, kErrTimeoutEpilogue, p.budget_ns);
+    if (__all_sync(0xffffffffu, ok)) {
+      tc_fence_after();
+      uint32_t vv[32], kv[32];
+      tmem_ld_32x32b_x32(trow + DV_COL + half * 32, vv);
+      tmem_ld_32x32b_x32(trow + DK_COL + half * 32, kv);
+      tmem_ld_wait();
+      if (kj < p.S) {
+        const long long o = ((long long)b * p.S + kj) * p.kv_row + hk * H + half * 32;
+        uint4* dv4 = reinterpret_cast<uint4*>(p.dv + o);
+        uint4* dk4 = reinterpret_cast<uint4*>(p.dk + o);
+        const bool any = total > 0;
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          uint4 w, u;
+          const float* fv = reinterpret_cast<const float*>(vv) + q8 * 8;
+          const float* fk = reinterpret_cast<const float*>(kv) + q8 * 8;
+          w.x = pack_bf16x2(any ? fv[0] : 0.f, any ? fv[1] : 0.f);
+          w.y = pack_bf16x2(any ? fv[2] : 0.f, any ? fv[3] : 0.f);
+          w.z = pack_bf16x2(any ? fv[4] : 0.f, any ? fv[5] : 0.f);
+          w.w = pack_bf16x2(any ? fv[6] : 0.f, any ? fv[7] : 0.f);
+          u.x = pack_bf16x2(any ? fk[0] * p.scale : 0.f, any ? fk[1] * p.scale : 0.f);
+          u.y = pack_bf16x2(any ? fk[2] * p.scale : 0.f, any ? fk[3] * p.scale : 0.f);
+          u.z = pack_bf16x2(any ? fk[4] * p.scale : 0.f, any ? fk[5] * p.scale : 0.f);
+          u.w = pack_bf16x2(any ? fk[6] * p.scale : 0.f, any ? fk[7] * p.scale : 0.f);
+          dv4[q8] = w;
+          dk4[q8] = u;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, BWD_TMEM);
+}
+
 }  // namespace fatc
 
 // q [B,S,Nq,64], k/v [B,S,Nkv,64] bf16 contiguous; out like q; lse [B,Nq,S] fp32.
@@ -340,6 +586,45 @@ void flash_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tens
   }
   dim3 grid((S + fatc::BQ - 1) / fatc::BQ, Nq, B);
   fatc::fwd_tc_kernel<<<grid, fatc::THREADS, fatc::SMEM, cur_stream()>>>(tq, tk, tv, p);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+
+// dK, dV of the attention backward on tcgen05 (head dim 64); lse / delta as
+// produced by the forward and the delta kernel.
+void flash_bwd_kv_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor dout, torch::Tensor lse,
+                     torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, int64_t window) {
+  const int B = q.size(0), S = q.size(1), Nq = q.size(2), Nkv = k.size(2);
+  HB_CHECK(q.size(3) == fatc::H, "flash_bwd_kv_tc: head dim 64");
+  const c10::cuda::CUDAGuard guard(q.device());
+  fatc::BwdParams p{};
+  p.B = B;
+  p.S = S;
+  p.Nq = Nq;
+  p.Nkv = Nkv;
+  p.window = (int)window;
+  p.scale = 1.f / std::sqrt((float)fatc::H);
+  p.sl2 = p.scale * fatc::LOG2E;
+  p.lse = lse.data_ptr<float>();
+  p.delta = delta.data_ptr<float>();
+  p.dk = (__nv_bfloat16*)dk.data_ptr();
+  p.dv = (__nv_bfloat16*)dv.data_ptr();
+  p.kv_row = (long long)Nkv * fatc::H;
+  p.status = status_ptr();
+  p.budget_ns = wait_budget_ns();
+  const uint64_t rows = (uint64_t)B * S;
+  CUtensorMap tk = tmap_bf16_2d(k.data_ptr(), rows, (uint64_t)Nkv * fatc::H, (uint64_t)Nkv * fatc::H, 64, fatc::KBT);
+  CUtensorMap tv = tmap_bf16_2d(v.data_ptr(), rows, (uint64_t)Nkv * fatc::H, (uint64_t)Nkv * fatc::H, 64, fatc::KBT);
+  CUtensorMap tq = tmap_bf16_2d(q.data_ptr(), rows, (uint64_t)Nq * fatc::H, (uint64_t)Nq * fatc::H, 64, fatc::QBT);
+  CUtensorMap td = tmap_bf16_2d(dout.data_ptr(), rows, (uint64_t)Nq * fatc::H, (uint64_t)Nq * fatc::H, 64, fatc::QBT);
+  static bool configured = false;
+  if (!configured) {
+    HB_CUDA_CHECK(cudaFuncSetAttribute(fatc::bwd_kv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       fatc::BWD_SMEM));
+    configured = true;
+  }
+  dim3 grid((S + fatc::KBT - 1) / fatc::KBT, Nkv, B);
+  fatc::bwd_kv_tc_kernel<<<grid, fatc::BWD_THREADS, fatc::BWD_SMEM, cur_stream()>>>(tk, tv, tq, td, p);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
