@@ -610,6 +610,8 @@ void flash_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tens
                   int64_t window);
 void flash_bwd_kv_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor dout, torch::Tensor lse,
                      torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, int64_t window);
+void flash_bwd_q_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor dout, torch::Tensor lse,
+                    torch::Tensor delta, torch::Tensor dq, int64_t window);
 
 // Head dim 64 runs on the tcgen05 kernels (flash_tc.cu: forward, and dK / dV
 // of the backward) unless HB_FA_TC=0.
@@ -696,12 +698,13 @@ void flash_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor 
       fa::set_smem<64>((const void*)fa::bwd_dq_kernel<64>, smem_q);
       c = true;
     }
-    if (use_fwd_tc(64)) {   // dK / dV on tcgen05 (flash_tc.cu), dQ below
+    if (use_fwd_tc(64)) {   // dK / dV and dQ on tcgen05 (flash_tc.cu)
       flash_bwd_kv_tc(q, k, v, dout, lse, delta, dk, dv, window);
+      flash_bwd_q_tc(q, k, v, dout, lse, delta, dq, window);
     } else {
       fa::bwd_dkdv_kernel<64><<<gkv, fa::NT, smem_kv, cur_stream()>>>(p);
+      fa::bwd_dq_kernel<64><<<gq, fa::NT, smem_q, cur_stream()>>>(p);
     }
-    fa::bwd_dq_kernel<64><<<gq, fa::NT, smem_q, cur_stream()>>>(p);
   } else {
     static bool c = false;
     if (!c) {

@@ -555,6 +555,209 @@ __global__ void __launch_bounds__(BWD_THREADS, 2)
   if (warp == 1) tmem_dealloc(tmem, BWD_TMEM);
 }
 
+
+// ============================================================== backward dQ
+// CTA = 128 queries of one head; loops over the key tiles of 64 they see:
+//   S = Q K_j^T,  dP = dO V_j^T                  (M 128 x N 64, TMEM)
+//   dS = P (dP - delta),  P = exp2(S * scale * log2e - lse)  (two threads per row)
+//   dQ += dS K_j                                 (M 128 x N 64 x K 64, TMEM)
+// then dQ * scale -> bf16.
+constexpr int DQ_THREADS = 320;
+constexpr int DQ_KB = 64;
+constexpr int DQ_KT = DQ_KB * H * 2;          // 8 KB
+constexpr int DQ_SMEM = 2 * Q_BYTES + 2 * 2 * DQ_KT + BQ * DQ_KB * 2 + 1024 + 256;
+constexpr int DQ_TMEM = 256;
+constexpr int DQ_S = 0, DQ_DP = 64, DQ_ACC = 128;
+
+struct DqParams {
+  int B, S, Nq, Nkv, window;
+  float scale, sl2;
+  const float *lse, *delta;
+  __nv_bfloat16* dq;
+  long long q_row;
+  int* status;
+  unsigned long long budget_ns;
+};
+
+HB_DEVICE bool visible_q(const DqParams& p, int qi, int kj) {
+  return kj <= qi && (p.window <= 0 || qi - kj < p.window) && kj < p.S && qi < p.S;
+}
+
+__global__ void __launch_bounds__(DQ_THREADS, 2)
+    bwd_q_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmD,
+                    const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                    const DqParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sQ = smem_u32(smem);
+  const uint32_t sD = sQ + Q_BYTES;
+  const uint32_t sK0 = sD + Q_BYTES;           // 2 stages of K then of V
+  const uint32_t sV0 = sK0 + 2 * DQ_KT;
+  const uint32_t sS = sV0 + 2 * DQ_KT;         // dS tile
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * Q_BYTES + 4 * DQ_KT + BQ * DQ_KB * 2);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;    // [2]
+  uint64_t* kv_empty = bars + 3;   // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* pv_done = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nqt = (p.S + BQ - 1) / BQ;
+  const int qt = nqt - 1 - blockIdx.x;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (p.Nq / p.Nkv);
+  const int q0 = qt * BQ;
+  const int hi = min(p.S, q0 + BQ);
+  const int lo = p.window > 0 ? max(0, q0 - p.window + 1) : 0;
+  const int jb0 = lo / DQ_KB, jb1 = (hi + DQ_KB - 1) / DQ_KB;
+  const int nkt = jb1 - jb0;
+  const int row0 = b * p.S;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(q_full), 1);
+    for (int st = 0; st < 2; ++st) {
+      mbar_init(smem_u32(&kv_full[st]), 1);
+      mbar_init(smem_u32(&kv_empty[st]), 1);
+    }
+    mbar_init(smem_u32(s_full), 1);
+    mbar_init(smem_u32(p_full), 256);
+    mbar_init(smem_u32(pv_done), 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), DQ_TMEM);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_expect_tx(smem_u32(q_full), 2 * Q_BYTES);
+      tma_load_2d(sQ, &tmQ, smem_u32(q_full), h * H, row0 + q0);
+      tma_load_2d(sD, &tmD, smem_u32(q_full), h * H, row0 + q0);
+      for (int j = 0; j < nkt; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(smem_u32(&kv_empty[st]), ((j >> 1) & 1) ^ 1, p.status, kErrTimeoutProducer, p.budget_ns))
+          break;
+        const uint32_t fb = smem_u32(&kv_full[st]);
+        mbar_expect_tx(fb, 2 * DQ_KT);
+        const int k0 = (jb0 + j) * DQ_KB;
+        tma_load_2d(sK0 + st * DQ_KT, &tmK, fb, hk * H, row0 + k0);
+        tma_load_2d(sV0 + st * DQ_KT, &tmV, fb, hk * H, row0 + k0);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(BQ, DQ_KB, false, false);
+      constexpr uint32_t idesc_q = make_idesc_bf16(BQ, H, false, true);
+      bool ok = mbar_wait(smem_u32(q_full), 0, p.status, kErrTimeoutMma, p.budget_ns);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!mbar_wait(smem_u32(&kv_full[st]), (j >> 1) & 1, p.status, kErrTimeoutMma, p.budget_ns)) return false;
+        tc_fence_after();
+        const uint32_t sk = sK0 + st * DQ_KT, sv = sV0 + st * DQ_KT;
+#pragma unroll
+        for (int kk = 0; kk < H / 16; ++kk) {
+          umma_f16(tmem + DQ_S, make_smem_desc(sQ + kk * 32, 16, 1024), make_smem_desc(sk + kk * 32, 16, 1024),
+                   idesc_s, kk != 0 ? 1u : 0u);
+          umma_f16(tmem + DQ_DP, make_smem_desc(sD + kk * 32, 16, 1024), make_smem_desc(sv + kk * 32, 16, 1024),
+                   idesc_s, kk != 0 ? 1u : 0u);
+        }
+        umma_commit(smem_u32(s_full));
+        return true;
+      };
+      if (ok && nkt > 0) ok = issue_s(0);
+      for (int j = 0; ok && j < nkt; ++j) {
+        if (!mbar_wait(smem_u32(p_full), j & 1, p.status, kErrTimeoutMma, p.budget_ns)) break;
+        tc_fence_after();
+        const uint32_t sk = sK0 + (j & 1) * DQ_KT;
+#pragma unroll
+        for (int kk = 0; kk < DQ_KB / 16; ++kk)
+          umma_f16(tmem + DQ_ACC, make_smem_desc(sS + kk * 32, 16, 1024), make_smem_desc(sk + kk * 2048, 8192, 1024),
+                   idesc_q, (j | kk) != 0 ? 1u : 0u);
+        umma_commit(smem_u32(pv_done));
+        umma_commit(smem_u32(&kv_empty[j & 1]));
+        if (j + 1 < nkt) ok = issue_s(j + 1);
+      }
+    }
+  } else {
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int r = quad * 32 + lane;
+    const int qi = q0 + r;
+    const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
+    const bool qin = qi < p.S;
+    const long long li = ((long long)b * p.Nq + h) * p.S + (qin ? qi : 0);
+    const float lse = qin ? p.lse[li] : INFINITY;
+    const float del = qin ? p.delta[li] : 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkt; ++j) {
+      // after a timeout the loop keeps going without waiting (no early exit)
+      if (ok) ok = mbar_wait(smem_u32(s_full), j & 1, p.status, kErrTimeoutEpilogue, p.budget_ns);
+      ok = __all_sync(0xffffffffu, ok);
+      tc_fence_after();
+      const int k0 = (jb0 + j) * DQ_KB + half * 32;
+      const bool need_mask = (k0 + 32 > q0) || p.window > 0 || (k0 + 32 > p.S);
+      uint32_t sv[32], dv[32];
+      tmem_ld_32x32b_x32(trow + DQ_S + half * 32, sv);
+      tmem_ld_32x32b_x32(trow + DQ_DP + half * 32, dv);
+      tmem_ld_wait();
+      if (j > 0) {   // the dS tile is free once the previous dQ MMA is done
+        if (ok) ok = mbar_wait(smem_u32(pv_done), (j - 1) & 1, p.status, kErrTimeoutEpilogue, p.budget_ns);
+        ok = __all_sync(0xffffffffu, ok);
+      }
+      float ds[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        float pv = ex2(fmaf(__uint_as_float(sv[e]), p.sl2, -lse));
+        if (need_mask && !visible_q(p, qi, k0 + e)) pv = 0.f;
+        ds[e] = pv * (__uint_as_float(dv[e]) - del);
+      }
+      const uint32_t off = r * 128;
+#pragma unroll
+      for (int q8 = 0; q8 < 4; ++q8) {
+        const int chunk = half * 4 + q8;
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sS + off + ((chunk ^ (r & 7)) << 4)),
+                     "r"(pack_bf16x2(ds[q8 * 8 + 0], ds[q8 * 8 + 1])), "r"(pack_bf16x2(ds[q8 * 8 + 2], ds[q8 * 8 + 3])),
+                     "r"(pack_bf16x2(ds[q8 * 8 + 4], ds[q8 * 8 + 5])), "r"(pack_bf16x2(ds[q8 * 8 + 6], ds[q8 * 8 + 7]))
+                     : "memory");
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      mbar_arrive(smem_u32(p_full));
+    }
+    if (ok && nkt > 0) ok = mbar_wait(smem_u32(pv_done), (nkt - 1) & 1, p.status, kErrTimeoutEpilogue, p.budget_ns);
+    if (__all_sync(0xffffffffu, ok) && nkt > 0) {
+      tc_fence_after();
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(trow + DQ_ACC + half * 32, v);
+      tmem_ld_wait();
+      if (qin) {
+        uint4* o4 = reinterpret_cast<uint4*>(p.dq + ((long long)b * p.S + qi) * p.q_row + h * H + half * 32);
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          const float* f = reinterpret_cast<const float*>(v) + q8 * 8;
+          uint4 w;
+          w.x = pack_bf16x2(f[0] * p.scale, f[1] * p.scale);
+          w.y = pack_bf16x2(f[2] * p.scale, f[3] * p.scale);
+          w.z = pack_bf16x2(f[4] * p.scale, f[5] * p.scale);
+          w.w = pack_bf16x2(f[6] * p.scale, f[7] * p.scale);
+          o4[q8] = w;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, DQ_TMEM);
+}
+
 }  // namespace fatc
 
 // q [B,S,Nq,64], k/v [B,S,Nkv,64] bf16 contiguous; out like q; lse [B,Nq,S] fp32.
@@ -625,6 +828,43 @@ void flash_bwd_kv_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::T
   }
   dim3 grid((S + fatc::KBT - 1) / fatc::KBT, Nkv, B);
   fatc::bwd_kv_tc_kernel<<<grid, fatc::BWD_THREADS, fatc::BWD_SMEM, cur_stream()>>>(tk, tv, tq, td, p);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+
+// dQ of the attention backward on tcgen05 (head dim 64).
+void flash_bwd_q_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor dout, torch::Tensor lse,
+                    torch::Tensor delta, torch::Tensor dq, int64_t window) {
+  const int B = q.size(0), S = q.size(1), Nq = q.size(2), Nkv = k.size(2);
+  HB_CHECK(q.size(3) == fatc::H, "flash_bwd_q_tc: head dim 64");
+  const c10::cuda::CUDAGuard guard(q.device());
+  fatc::DqParams p{};
+  p.B = B;
+  p.S = S;
+  p.Nq = Nq;
+  p.Nkv = Nkv;
+  p.window = (int)window;
+  p.scale = 1.f / std::sqrt((float)fatc::H);
+  p.sl2 = p.scale * fatc::LOG2E;
+  p.lse = lse.data_ptr<float>();
+  p.delta = delta.data_ptr<float>();
+  p.dq = (__nv_bfloat16*)dq.data_ptr();
+  p.q_row = (long long)Nq * fatc::H;
+  p.status = status_ptr();
+  p.budget_ns = wait_budget_ns();
+  const uint64_t rows = (uint64_t)B * S;
+  CUtensorMap tq = tmap_bf16_2d(q.data_ptr(), rows, (uint64_t)Nq * fatc::H, (uint64_t)Nq * fatc::H, 64, fatc::BQ);
+  CUtensorMap td = tmap_bf16_2d(dout.data_ptr(), rows, (uint64_t)Nq * fatc::H, (uint64_t)Nq * fatc::H, 64, fatc::BQ);
+  CUtensorMap tk = tmap_bf16_2d(k.data_ptr(), rows, (uint64_t)Nkv * fatc::H, (uint64_t)Nkv * fatc::H, 64, fatc::DQ_KB);
+  CUtensorMap tv = tmap_bf16_2d(v.data_ptr(), rows, (uint64_t)Nkv * fatc::H, (uint64_t)Nkv * fatc::H, 64, fatc::DQ_KB);
+  static bool configured = false;
+  if (!configured) {
+    HB_CUDA_CHECK(cudaFuncSetAttribute(fatc::bwd_q_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       fatc::DQ_SMEM));
+    configured = true;
+  }
+  dim3 grid((S + fatc::BQ - 1) / fatc::BQ, Nq, B);
+  fatc::bwd_q_tc_kernel<<<grid, fatc::DQ_THREADS, fatc::DQ_SMEM, cur_stream()>>>(tq, td, tk, tv, p);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
