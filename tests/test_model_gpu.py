@@ -60,3 +60,33 @@ def test_status_word_clean_after_training():
     from hanuman_b200.ops._ext import ext
     torch.cuda.synchronize()
     assert ext().read_status() == 0
+
+
+def test_cached_decoding_on_gpu_matches_recompute():
+    """KV / KDA-state caches on the device: teacher-forced step logits equal the
+    full recomputation's logits at every position (bf16 projections: 5e-2)."""
+    from hanuman_b200.decode import DecodeCache, step
+    # A top-k router is discontinuous: two nearly tied experts can swap under
+    # bf16-level input differences between the two paths.  Fixed, well
+    # separated biases pin the routing so the comparison measures the caches.
+    c = _tiny().replace(dtype="bf16", router_type="sigmoid_bias")
+    tr = Trainer(c, device="cuda")
+    tr.step(_tokens(c))
+    model = tr.model
+    for m in model.moe_layers():
+        b = torch.zeros_like(m.bias)
+        b[1], b[5] = 20.0, 19.0
+        m.bias.data.copy_(b)
+    g = torch.Generator().manual_seed(3)
+    seq = torch.randint(0, c.vocab_size, (1, 40), generator=g).cuda()
+    with torch.no_grad():
+        h, _ = model(seq)
+        full = model.logits(h[0]).float()
+        cache = DecodeCache(model)
+        got = [step(model, seq[:, :8], cache).float()]
+        for t in range(8, 40):
+            got.append(step(model, seq[:, t:t + 1], cache).float())
+    ref = torch.stack([full[7]] + [full[t] for t in range(8, 40)])
+    got = torch.cat(got)
+    err = ((got - ref).norm(dim=-1) / ref.norm(dim=-1)).max().item()
+    assert err < 5e-2, err
