@@ -164,6 +164,47 @@ void grouped_gemm_m(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Te
   gemm_dispatch_grouped(GROUPED_M, BN, false, !trans_b, epi, ta, tb, args, grid);
 }
 
+// Grouped over M with the SwiGLU backward in the epilogue (MoE backward):
+//   dh[rows of g] = a[rows of g] @ b[g]^T   (a [R, D] = dY, b [G, F, D] = W_down)
+//   dgu = [dh * u * silu'(g) | dh * silu(g)]   from gu = [g | u] ([R, 2F] bf16)
+// dh never reaches memory; pad rows of each expert segment get zeros.
+void grouped_gemm_m_swiglu_bwd(torch::Tensor a, torch::Tensor b, torch::Tensor gu, torch::Tensor dgu,
+                               torch::Tensor grp_start, torch::Tensor grp_count, torch::Tensor grp_tile_start) {
+  check_bf16(a, "a");
+  check_bf16(b, "b");
+  check_bf16(gu, "gu");
+  check_bf16(dgu, "dgu");
+  HB_CHECK(b.dim() == 3 && b.is_contiguous(), "b must be contiguous [G, F, D]");
+  const int G = b.size(0);
+  const int R = a.size(0), K = a.size(1);
+  const int F = b.size(1);
+  HB_CHECK(b.size(2) == K, "grouped_gemm_m_swiglu_bwd: inner dims differ");
+  HB_CHECK(gu.is_contiguous() && dgu.is_contiguous() && gu.size(0) == R && gu.size(1) == 2 * F &&
+               dgu.size(0) == R && dgu.size(1) == 2 * F,
+           "grouped_gemm_m_swiglu_bwd: gu / dgu must be contiguous [R, 2F]");
+  HB_CHECK(grp_start.numel() == G && grp_count.numel() == G && grp_tile_start.numel() == G + 1,
+           "grouped_gemm_m_swiglu_bwd: bad group arrays");
+  if (R == 0) return;
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int BN = pick_bn(F);
+  CUtensorMap ta = tmap_bf16_2d(a.data_ptr(), R, K, a.stride(0), 64, GEMM_BM);
+  CUtensorMap tb = tmap_bf16_3d(b.data_ptr(), G, F, K, K, (uint64_t)F * K, 64, BN);
+  GemmArgs args = base_args(dgu, 1.0);
+  args.ldc = 2LL * F;
+  args.aux = gu.data_ptr();
+  args.M = R;
+  args.N = F;
+  args.K = K;
+  args.tiles_n = (F + BN - 1) / BN;
+  args.num_groups = G;
+  args.grp_start = grp_start.data_ptr<int>();
+  args.grp_count = grp_count.data_ptr<int>();
+  args.grp_tile_start = grp_tile_start.data_ptr<int>();
+  const int max_tiles = ((R + GEMM_BM - 1) / GEMM_BM) * args.tiles_n;
+  const int grid = std::max(1, std::min(max_tiles, num_sms()));
+  gemm_dispatch_grouped(GROUPED_M, BN, false, false, EPI_SWIGLU_BWD, ta, tb, args, grid);
+}
+
 // Grouped over K (MoE weight gradients):  c[g] (+)= a_g^T @ b_g
 // a: [R, M] bf16 rows of group g at [start, start+count);  b: [R, N] bf16;
 // c: [G, M, N] fp32 (or bf16 without accumulate); counts multiples of 64.

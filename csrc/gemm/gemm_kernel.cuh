@@ -36,7 +36,11 @@ constexpr int GEMM_BK = 64;
 constexpr int GEMM_THREADS = 192;
 
 enum GemmMode { DENSE = 0, GROUPED_M = 1, GROUPED_K = 2 };
-enum GemmEpi { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACC = 2 };
+// EPI_SWIGLU_BWD (grouped-over-M only): the accumulator is dh = dY W_down^T
+// for the rows of a SwiGLU; the epilogue reads g, u from args.aux ([R, 2F]
+// bf16, the forward's gate | up) and writes dgu = [dh u silu'(g) | dh silu(g)]
+// (bf16, ldc = 2F); the pad rows of each expert's 128-row segment get zeros.
+enum GemmEpi { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACC = 2, EPI_SWIGLU_BWD = 3 };
 
 struct GemmArgs {
   int M, N, K;
@@ -52,6 +56,7 @@ struct GemmArgs {
   long long c_group_stride;     // GROUPED_K: elements between C[g] and C[g+1]
   float alpha;
   const float* alpha_ptr;       // optional device scalar; overrides alpha
+  const void* aux;              // EPI_SWIGLU_BWD: gate | up of the forward
   int* status;
   unsigned long long budget_ns;
 };
@@ -433,6 +438,77 @@ __global__ void __launch_bounds__(GATHER ? GEMM_THREADS + GATHER_COPY_THREADS : 
         tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c * 32, r);
         tmem_ld_wait();
         const int n = ti.n0 + c * 32;
+        if (EPI == EPI_SWIGLU_BWD) {
+          if (n >= args.N) continue;
+          const int F = args.N;
+          __nv_bfloat16* dg = reinterpret_cast<__nv_bfloat16*>(cbase) + (long long)m * args.ldc + n;
+          __nv_bfloat16* du = dg + F;
+          const int cnt = min(32, F - n);
+          const bool vec = cnt == 32 && (F % 8) == 0;
+          if (!row_ok) {   // pad row of the expert segment
+            if (vec) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                reinterpret_cast<uint4*>(dg)[q] = make_uint4(0u, 0u, 0u, 0u);
+                reinterpret_cast<uint4*>(du)[q] = make_uint4(0u, 0u, 0u, 0u);
+              }
+            } else {
+              for (int j = 0; j < cnt; ++j) dg[j] = du[j] = __float2bfloat16_rn(0.f);
+            }
+            continue;
+          }
+          const __nv_bfloat16* gp = reinterpret_cast<const __nv_bfloat16*>(args.aux) + (long long)m * args.ldc + n;
+          const __nv_bfloat16* up = gp + F;
+          __nv_bfloat16 gv[32], uv[32];
+          if (vec) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              reinterpret_cast<uint4*>(gv)[q] = reinterpret_cast<const uint4*>(gp)[q];
+              reinterpret_cast<uint4*>(uv)[q] = reinterpret_cast<const uint4*>(up)[q];
+            }
+          } else {
+            for (int j = 0; j < 32; ++j) {
+              gv[j] = j < cnt ? gp[j] : __float2bfloat16_rn(0.f);
+              uv[j] = j < cnt ? up[j] : __float2bfloat16_rn(0.f);
+            }
+          }
+          float og[32], ou[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            // dh is rounded to bf16 first, as when it is stored between kernels
+            const float d = __bfloat162float(__float2bfloat16_rn(has_k ? __uint_as_float(r[j]) * alpha : 0.f));
+            const float g = __bfloat162float(gv[j]), u = __bfloat162float(uv[j]);
+            const float sg = 1.f / (1.f + __expf(-g));
+            const float silu = g * sg;
+            const float dsilu = sg * (1.f + g * (1.f - sg));
+            og[j] = d * u * dsilu;
+            ou[j] = d * silu;
+          }
+          if (vec) {
+            uint4* g4 = reinterpret_cast<uint4*>(dg);
+            uint4* u4 = reinterpret_cast<uint4*>(du);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 w, x;
+              w.x = pack_bf16x2(og[q * 8 + 0], og[q * 8 + 1]);
+              w.y = pack_bf16x2(og[q * 8 + 2], og[q * 8 + 3]);
+              w.z = pack_bf16x2(og[q * 8 + 4], og[q * 8 + 5]);
+              w.w = pack_bf16x2(og[q * 8 + 6], og[q * 8 + 7]);
+              x.x = pack_bf16x2(ou[q * 8 + 0], ou[q * 8 + 1]);
+              x.y = pack_bf16x2(ou[q * 8 + 2], ou[q * 8 + 3]);
+              x.z = pack_bf16x2(ou[q * 8 + 4], ou[q * 8 + 5]);
+              x.w = pack_bf16x2(ou[q * 8 + 6], ou[q * 8 + 7]);
+              g4[q] = w;
+              u4[q] = x;
+            }
+          } else {
+            for (int j = 0; j < cnt; ++j) {
+              dg[j] = __float2bfloat16_rn(og[j]);
+              du[j] = __float2bfloat16_rn(ou[j]);
+            }
+          }
+          continue;
+        }
         if (!row_ok || n >= args.N) continue;
         float v[32];
 #pragma unroll

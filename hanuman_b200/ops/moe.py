@@ -19,11 +19,18 @@ counts from device memory.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from ._ext import ext
 from .dense import _bf16, _work, main_grad
 from .norm import SwiGLUFn
+
+# The expert backward runs dh = dY W_down^T with the SwiGLU backward in the
+# GEMM's epilogue (one kernel, dh never stored); HB_MOE_FUSED_SWIGLU=0 selects
+# the grouped GEMM followed by the standalone SwiGLU backward kernel.
+FUSED_SWIGLU_BWD = os.environ.get("HB_MOE_FUSED_SWIGLU", "1") != "0"
 
 
 def _bn(n: int) -> int:
@@ -204,11 +211,15 @@ class MoEFn(torch.autograd.Function):
         dtopw = torch.empty(T, K, dtype=torch.float32, device=dev)
         ext().moe_combine_bwd(dout, y, pos, topw, row_src, dy, dtopw)
         wg, wu, wd = ctx.expert_w
-        dhh = torch.empty(R, F, dtype=torch.bfloat16, device=dev)
-        ext().grouped_gemm_m(dy, wd, dhh, starts, counts, tprefix_f, True)
-        ext().grouped_gemm_k(hh, dy, main_grad(mod.expert_w_down), starts, padded, True)
         dgu = torch.empty_like(gu)
-        ext().swiglu_bwd(dhh, gu, dgu, row_src)  # pad rows -> 0 for the grouped-K GEMMs
+        if FUSED_SWIGLU_BWD:
+            # dh = dy W_down^T stays in TMEM; the epilogue writes dgu (pad rows 0)
+            ext().grouped_gemm_m_swiglu_bwd(dy, wd, gu, dgu, starts, counts, tprefix_f)
+        else:
+            dhh = torch.empty(R, F, dtype=torch.bfloat16, device=dev)
+            ext().grouped_gemm_m(dy, wd, dhh, starts, counts, tprefix_f, True)
+            ext().swiglu_bwd(dhh, gu, dgu, row_src)  # pad rows -> 0 for the grouped-K GEMMs
+        ext().grouped_gemm_k(hh, dy, main_grad(mod.expert_w_down), starts, padded, True)
         dxp = torch.empty(R, D, dtype=torch.float32, device=dev)
         tn_d = (D + _bn(D) - 1) // _bn(D)
         tn_f = (F + _bn(F) - 1) // _bn(F)

@@ -199,3 +199,39 @@ def test_pair_gemm_forced():
     r = subprocess.run([sys.executable, "-c", _PAIR_SCRIPT], env=env, capture_output=True, text=True,
                        timeout=600)
     assert "PAIR_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]
+
+
+def test_grouped_m_swiglu_bwd_matches_separate_kernels():
+    """dh = dy W_down^T with the SwiGLU backward in the epilogue equals the
+    grouped GEMM followed by the standalone SwiGLU backward (pad rows zero)."""
+    torch.manual_seed(4)
+    dev = "cuda"
+    G, D, F = 5, 512, 384
+    counts = [130, 0, 7, 256, 300]
+    starts, R = _groups(counts)
+    dy = torch.randn(R, D, device=dev).bfloat16()
+    wd = torch.randn(G, F, D, device=dev).bfloat16() * 0.05
+    gu = torch.randn(R, 2 * F, device=dev).bfloat16()
+    row_src = torch.full((R,), -1, dtype=torch.int32, device=dev)
+    for s, n in zip(starts, counts):
+        row_src[s:s + n] = 0
+    BN = 256 if F >= 256 else 128
+    tiles_n = (F + BN - 1) // BN
+    tstart = [0]
+    for cnt in counts:
+        tstart.append(tstart[-1] + (cnt + 127) // 128 * tiles_n)
+    gs = torch.tensor(starts, dtype=torch.int32, device=dev)
+    gc = torch.tensor(counts, dtype=torch.int32, device=dev)
+    gt = torch.tensor(tstart, dtype=torch.int32, device=dev)
+    dh = torch.zeros(R, F, device=dev).bfloat16()
+    _ext().grouped_gemm_m(dy, wd, dh, gs, gc, gt, True)
+    ref = torch.empty_like(gu)
+    _ext().swiglu_bwd(dh, gu, ref, row_src)
+    got = torch.full_like(gu, float("nan"))
+    _ext().grouped_gemm_m_swiglu_bwd(dy, wd, gu, got, gs, gc, gt)
+    torch.cuda.synchronize()
+    for s, n in zip(starts, counts):
+        if n == 0:
+            continue
+        seg = slice(s, s + (n + 127) // 128 * 128)
+        assert torch.equal(got[seg], ref[seg]), s
