@@ -68,7 +68,10 @@ class LinearMulti(torch.autograd.Function):
         xb, *ws = ctx.saved_tensors
         dx = None
         if ctx.needs_input_grad[0]:
-            dx = torch.empty(xb.shape, dtype=torch.float32, device=xb.device)
+            # one projection of a bf16 input: the GEMM writes the bf16 gradient itself
+            direct = ctx.x_dtype == torch.bfloat16 and len(ws) == 1
+            dx = torch.empty(xb.shape, dtype=torch.bfloat16 if direct else torch.float32,
+                             device=xb.device)
         first = True
         for dy, w, p in zip(douts, ws, ctx.params):
             if dy is None:
@@ -80,7 +83,7 @@ class LinearMulti(torch.autograd.Function):
             ext().gemm(xb, dyb, main_grad(p), True, False, True, 1.0)
         if dx is not None and first:
             dx.zero_()
-        if dx is not None and ctx.x_dtype != torch.float32:
+        if dx is not None and dx.dtype != ctx.x_dtype:
             dx = dx.to(ctx.x_dtype)
         return (dx, None, None) + (None,) * len(ws)
 
@@ -166,8 +169,9 @@ class LinearFused(torch.autograd.Function):
     def backward(ctx, dy):
         xb, *ws = ctx.saved_tensors
         dyb = _bf16(dy)
-        dx = torch.empty(xb.shape, dtype=torch.float32, device=xb.device) \
-            if ctx.needs_input_grad[0] else None
+        direct = ctx.x_dtype == torch.bfloat16 and len(ws) == 1
+        dx = torch.empty(xb.shape, dtype=torch.bfloat16 if direct else torch.float32,
+                         device=xb.device) if ctx.needs_input_grad[0] else None
         off = 0
         for i, (w, p) in enumerate(zip(ws, ctx.params)):
             sl = dyb[:, off:off + w.shape[1]]
@@ -175,7 +179,7 @@ class LinearFused(torch.autograd.Function):
                 _gemm_or_narrow(sl, w, dx, False, True, i > 0)
             _gemm_or_narrow(xb, sl, main_grad(p), True, False, True)
             off += w.shape[1]
-        if dx is not None and ctx.x_dtype != torch.float32:
+        if dx is not None and dx.dtype != ctx.x_dtype:
             dx = dx.to(ctx.x_dtype)
         return (dx, None) + (None,) * len(ws)
 

@@ -1,8 +1,9 @@
 """KDA layer on the native kernels (model/kda.py:240-376 semantics).
 
-    [q|k|v|f0|g0] = h @ [wq|wk|wv|f_proj0|g_proj0]     one fused bf16 GEMM
+    [q|k|v|f0|g0] = h @ [wq|wk|wv|f_proj0|g_proj0]     one bf16 buffer
     braw = h @ wb;  f = f0 @ f_proj1;  gl = g0 @ g_proj1  (fp32 outputs)
     q, k, v, g, beta = prep(...)   conv4 + SiLU (+ L2 norm for q, k), decay, sigmoid
+      (the projections and the prep are one autograd node, KdaFrontFn)
     o = chunked gated delta rule (fp32)
     y = RMSNorm_V(o) * o_norm * sigmoid(gl + bias) @ wo   (norm and gate in one kernel)
 """
@@ -13,7 +14,7 @@ import math
 import torch
 
 from ._ext import ext
-from .dense import linear_fused
+from .dense import _bf16, _gemm_or_narrow, _work, linear_fused, main_grad
 
 
 def chunk_size(dk: int) -> int:
@@ -61,31 +62,63 @@ def kda_chunked_cuda(q, k, v, g, beta, scale, chunk=None):
     return KdaCoreFn.apply(q, k, v, g, beta, scale)
 
 
-class KdaPrepFn(torch.autograd.Function):
-    """ShortConv4 + SiLU (+ L2 norm) for q/k/v, decay gate and beta."""
+class KdaFrontFn(torch.autograd.Function):
+    """Everything between the block's normed input and the delta rule, as ONE
+    autograd node (model/kda.py:248-284):
+
+        [q|k|v|f0|g0] = x @ [wq|wk|wv|f_proj0|g_proj0]   (one bf16 buffer)
+        braw = x @ wb;  f = f0 @ f_proj1;  gl = g0 @ g_proj1   (fp32)
+        q, k, v, g, beta = ShortConv4 + SiLU (+ L2 norm), decay gate, sigmoid
+
+    Returns q, k, v, g, beta and gl (the output gate's logits).  The backward
+    writes d[q|k|v|f0|g0] into one buffer (the prep kernel fills the q|k|v
+    columns, the low-rank GEMMs the f0|g0 columns) and accumulates a single
+    fp32 input gradient, so autograd never zero-fills, slices or sums
+    per-consumer gradients of x or of the projection buffer."""
 
     @staticmethod
-    def forward(ctx, raw, f, braw, wq, wk, wv, a_log, dt_bias, gate_mode, S, H, K):
-        T = raw.shape[0]
-        dev = raw.device
-        q = torch.empty(T, H, K, dtype=torch.float32, device=dev)
-        k, v, g = torch.empty_like(q), torch.empty_like(q), torch.empty_like(q)
-        beta = torch.empty(T, H, dtype=torch.float32, device=dev)
-        args = (raw, wq.float().contiguous(), wk.float().contiguous(), wv.float().contiguous(),
-                f.float().contiguous(), a_log.float().contiguous(), dt_bias.float().contiguous())
-        ext().kda_prep_fwd(*args, braw.float().contiguous(), gate_mode, S, q, k, v, g, beta)
-        ctx.save_for_backward(raw, f, wq, wk, wv, a_log, dt_bias, beta)
-        ctx.meta = (gate_mode, S, H, K)
-        return q, k, v, g, beta
-
-    @staticmethod
-    def backward(ctx, dq, dk, dv, dg, dbeta):
-        raw, f, wq, wk, wv, a_log, dt_bias, beta = ctx.saved_tensors
-        gate_mode, S, H, K = ctx.meta
-        T = raw.shape[0]
+    def forward(ctx, x, wq, wk, wv, f0, g0, wb, f1, g1, cq, ck, cv, a_log, dt_bias,
+                gate_mode, S, H, K):
+        xb = _bf16(x)
+        T = xb.shape[0]
         HK = H * K
-        dev = raw.device
-        z = lambda t: torch.zeros_like(t) if t is None else t.float().contiguous()
+        dev = xb.device
+        pw = [_work(w) for w in (wq, wk, wv, f0, g0)]
+        wbw, f1w, g1w = _work(wb), _work(f1), _work(g1)
+        W = 3 * HK + 2 * K
+        big = torch.empty(T, W, dtype=torch.bfloat16, device=dev)
+        off = 0
+        for w in pw:
+            _gemm_or_narrow(xb, w, big[:, off:off + w.shape[1]], False, False, False)
+            off += w.shape[1]
+        f32 = dict(dtype=torch.float32, device=dev)
+        braw = torch.empty(T, H, **f32)
+        _gemm_or_narrow(xb, wbw, braw, False, False, False)
+        f = torch.empty(T, HK, **f32)
+        _gemm_or_narrow(big[:, 3 * HK:3 * HK + K], f1w, f, False, False, False)
+        gl = torch.empty(T, HK, **f32)
+        _gemm_or_narrow(big[:, 3 * HK + K:], g1w, gl, False, False, False)
+        q = torch.empty(T, H, K, **f32)
+        k, v, g = torch.empty_like(q), torch.empty_like(q), torch.empty_like(q)
+        beta = torch.empty(T, H, **f32)
+        conv = [c.float().contiguous() for c in (cq, ck, cv)]
+        al, dtb = a_log.float().contiguous(), dt_bias.float().contiguous()
+        ext().kda_prep_fwd(big[:, :3 * HK], *conv, f, al, dtb, braw, gate_mode, S, q, k, v, g, beta)
+        ctx.save_for_backward(xb, big, f, beta, *pw, wbw, f1w, g1w, *conv, al, dtb)
+        ctx.params = (wq, wk, wv, f0, g0, wb, f1, g1)
+        ctx.meta = (gate_mode, S, H, K, x.dtype)
+        return q, k, v, g, beta, gl
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv, dg, dbeta, dgl):
+        (xb, big, f, beta, wq, wk, wv, wf0, wg0, wbw, f1w, g1w,
+         cq, ck, cv, al, dtb) = ctx.saved_tensors
+        gate_mode, S, H, K, x_dtype = ctx.meta
+        T = xb.shape[0]
+        HK = H * K
+        W = big.shape[1]
+        dev = xb.device
+        z = lambda t: torch.zeros_like(f) if t is None else t.float().contiguous()
         dq, dk, dv, dg = z(dq), z(dk), z(dv), z(dg)
         dbeta = torch.zeros(T, H, device=dev) if dbeta is None else dbeta.float().contiguous()
         dconv = torch.empty(T, 3 * HK, dtype=torch.float32, device=dev)
@@ -93,17 +126,41 @@ class KdaPrepFn(torch.autograd.Function):
         dbraw = torch.empty(T, H, dtype=torch.float32, device=dev)
         d_alog = torch.zeros(H, dtype=torch.float32, device=dev)
         d_dtb = torch.zeros(HK, dtype=torch.float32, device=dev)
-        ld = raw.stride(0)
-        draw_full = torch.empty(T, ld, dtype=torch.bfloat16, device=dev)
-        draw = draw_full[:, :3 * HK]
-        dwq = torch.zeros(HK, 1, 4, dtype=torch.float32, device=dev)
-        dwk, dwv = torch.zeros_like(dwq), torch.zeros_like(dwq)
-        ext().kda_prep_bwd(raw, wq.float().contiguous(), wk.float().contiguous(),
-                           wv.float().contiguous(), f.float().contiguous(),
-                           a_log.float().contiguous(), dt_bias.float().contiguous(), beta,
-                           gate_mode, S, dq, dk, dv, dg, dbeta, dconv, df, dbraw, d_alog, d_dtb,
-                           draw, dwq, dwk, dwv)
-        return (draw, df, dbraw, dwq, dwk, dwv, d_alog, d_dtb, None, None, None, None)
+        dbig = torch.empty(T, W, dtype=torch.bfloat16, device=dev)
+        dcq = torch.zeros(HK, 1, 4, dtype=torch.float32, device=dev)
+        dck, dcv = torch.zeros_like(dcq), torch.zeros_like(dcq)
+        ext().kda_prep_bwd(big[:, :3 * HK], cq, ck, cv, f, al, dtb, beta, gate_mode, S,
+                           dq, dk, dv, dg, dbeta, dconv, df, dbraw, d_alog, d_dtb,
+                           dbig[:, :3 * HK], dcq, dck, dcv)
+        p_wq, p_wk, p_wv, p_f0, p_g0, p_wb, p_f1, p_g1 = ctx.params
+        # low-rank second stage: d f0 / d g0 straight into their dbig columns
+        f0s, g0s = big[:, 3 * HK:3 * HK + K], big[:, 3 * HK + K:]
+        dfb = df.to(torch.bfloat16)
+        _gemm_or_narrow(dfb, f1w, dbig[:, 3 * HK:3 * HK + K], False, True, False)
+        _gemm_or_narrow(f0s, dfb, main_grad(p_f1), True, False, True)
+        if dgl is None:
+            dbig[:, 3 * HK + K:].zero_()
+        else:
+            dglb = dgl.to(torch.bfloat16)
+            _gemm_or_narrow(dglb, g1w, dbig[:, 3 * HK + K:], False, True, False)
+            _gemm_or_narrow(g0s, dglb, main_grad(p_g1), True, False, True)
+        # first stage: one fp32 input gradient over all six projections
+        dx = torch.empty(xb.shape, dtype=torch.float32, device=dev) \
+            if ctx.needs_input_grad[0] else None
+        off = 0
+        for i, (w, p) in enumerate(zip((wq, wk, wv, wf0, wg0), (p_wq, p_wk, p_wv, p_f0, p_g0))):
+            sl = dbig[:, off:off + w.shape[1]]
+            if dx is not None:
+                _gemm_or_narrow(sl, w, dx, False, True, i > 0)
+            _gemm_or_narrow(xb, sl, main_grad(p), True, False, True)
+            off += w.shape[1]
+        dbb = dbraw.to(torch.bfloat16)
+        if dx is not None:
+            _gemm_or_narrow(dbb, wbw, dx, False, True, True)
+        _gemm_or_narrow(xb, dbb, main_grad(p_wb), True, False, True)
+        if dx is not None and x_dtype != torch.float32:
+            dx = dx.to(x_dtype)
+        return (dx,) + (None,) * 8 + (dcq, dck, dcv, d_alog, d_dtb, None, None, None, None)
 
 
 class KdaOutGateFn(torch.autograd.Function):
@@ -140,14 +197,11 @@ def kda_layer_cuda(mod, h, dtype):
     H, K = mod.n_heads, mod.head_dim
     HK = H * K
     x2 = h.reshape(T, D)
-    big = linear_fused(x2, [mod.wq, mod.wk, mod.wv, mod.f_proj0, mod.g_proj0], torch.bfloat16)
-    braw = linear_fused(x2, [mod.wb], torch.float32)
-    raw = big[:, :3 * HK]
-    f = linear_fused(big[:, 3 * HK:3 * HK + K], [mod.f_proj1], torch.float32)
-    gl = linear_fused(big[:, 3 * HK + K:3 * HK + 2 * K], [mod.g_proj1], torch.float32)
     gate_mode = 0 if mod.gate == "kimi" else 1
-    q, k, v, g, beta = KdaPrepFn.apply(raw, f, braw, mod.q_conv.weight, mod.k_conv.weight,
-                                       mod.v_conv.weight, mod.a_log, mod.dt_bias, gate_mode, S, H, K)
+    q, k, v, g, beta, gl = KdaFrontFn.apply(
+        x2, mod.wq, mod.wk, mod.wv, mod.f_proj0, mod.g_proj0, mod.wb, mod.f_proj1, mod.g_proj1,
+        mod.q_conv.weight, mod.k_conv.weight, mod.v_conv.weight, mod.a_log, mod.dt_bias,
+        gate_mode, S, H, K)
     o = KdaCoreFn.apply(q.view(B, S, H, K), k.view(B, S, H, K), v.view(B, S, H, K),
                         g.view(B, S, H, K), beta.view(B, S, H), 1.0 / math.sqrt(K))
     if K in (32, 64, 128):

@@ -191,8 +191,9 @@ def test_kda_layer_grads_match_cpu():
     # small (fp32) parameters receive autograd grads; matrices accumulate main_grad
     for name in ("a_log", "dt_bias", "o_norm", "g_proj1_bias"):
         assert rel(getattr(mg, name).grad.cpu(), getattr(m, name).grad) < 5e-2, name
-    assert rel(mg.q_conv.weight.grad.cpu(), m.q_conv.weight.grad) < 5e-2
-    for name in ("wq", "wv", "wo", "f_proj1", "wb"):
+    for conv in ("q_conv", "k_conv", "v_conv"):
+        assert rel(getattr(mg, conv).weight.grad.cpu(), getattr(m, conv).weight.grad) < 5e-2, conv
+    for name in ("wq", "wk", "wv", "wo", "f_proj0", "f_proj1", "g_proj0", "g_proj1", "wb"):
         assert rel(getattr(mg, name).main_grad.cpu(), getattr(m, name).grad) < 5e-2, name
 
 
