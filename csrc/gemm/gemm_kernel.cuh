@@ -33,7 +33,11 @@ namespace hb {
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
-constexpr int GEMM_THREADS = 192;
+// warp 0: TMA producer, warp 1: MMA issuer, warps 2..9: epilogue.  Two
+// epilogue warps share each TMEM lane quadrant (alternate 32-column chunks),
+// so twice the loads and stores are in flight per SM as with one warp each.
+constexpr int GEMM_EPI_WARPS = 8;
+constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;
 
 enum GemmMode { DENSE = 0, GROUPED_M = 1, GROUPED_K = 2 };
 // EPI_SWIGLU_BWD (grouped-over-M only): the accumulator is dh = dY W_down^T
@@ -235,7 +239,7 @@ __global__ void __launch_bounds__(GATHER ? GEMM_THREADS + GATHER_COPY_THREADS : 
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&tfull_bar[i]), 1);
-      mbar_init(smem_u32(&tempty_bar[i]), 128);
+      mbar_init(smem_u32(&tempty_bar[i]), 32 * GEMM_EPI_WARPS);
     }
     fence_barrier_init();
   }
@@ -416,6 +420,7 @@ __global__ void __launch_bounds__(GATHER ? GEMM_THREADS + GATHER_COPY_THREADS : 
   } else {
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;  // TMEM lane quadrant accessible to this warp
+    const int half = (warp - 2) >> 2;  // which of the two warps of this quadrant
     const float alpha = args.alpha_ptr ? *args.alpha_ptr : args.alpha;
     const int row_in_tile = quad * 32 + lane;
     int acc = 0;
@@ -433,7 +438,7 @@ __global__ void __launch_bounds__(GATHER ? GEMM_THREADS + GATHER_COPY_THREADS : 
       char* cbase = reinterpret_cast<char*>(args.C);
       if (MODE == GROUPED_K) cbase += (long long)ti.group * args.c_group_stride * (EPI == EPI_BF16 ? 2 : 4);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half; c < BN / 32; c += 2) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c * 32, r);
         tmem_ld_wait();

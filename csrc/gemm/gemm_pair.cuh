@@ -24,6 +24,8 @@
 
 namespace hb {
 
+// warp 0: TMA producer, warp 1: MMA issuer (leader CTA), warps 2..5: epilogue
+constexpr int PAIR_THREADS = 192;
 constexpr int PAIR_BM = 256;   // rows per pair tile (128 per CTA)
 constexpr int PAIR_BN = 256;   // columns per pair tile (B: 128 per CTA)
 constexpr int PAIR_A_BYTES = 128 * GEMM_BK * 2;
@@ -67,7 +69,7 @@ __device__ __forceinline__ bool get_pair_tile(const GemmArgs& a, int t, TileInfo
 }
 
 template <bool A_MN, bool B_MN, int MODE, int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const GemmArgs args) {
   static_assert(MODE == DENSE || MODE == GROUPED_K, "pair kernel: dense or grouped-K");
@@ -302,7 +304,7 @@ void gemm_pair_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmAr
     HB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM));
     configured = true;
   }
-  kern<<<grid, GEMM_THREADS, PAIR_SMEM, cur_stream()>>>(ta, tb, args);
+  kern<<<grid, PAIR_THREADS, PAIR_SMEM, cur_stream()>>>(ta, tb, args);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
