@@ -24,8 +24,9 @@
 
 namespace hb {
 
-// warp 0: TMA producer, warp 1: MMA issuer (leader CTA), warps 2..5: epilogue
-constexpr int PAIR_THREADS = 192;
+// warp 0: TMA producer, warp 1: MMA issuer (leader CTA), warps 2..9: epilogue
+// (two warps per TMEM lane quadrant, alternate 32-column chunks)
+constexpr int PAIR_THREADS = 64 + 32 * GEMM_EPI_WARPS;
 constexpr int PAIR_BM = 256;   // rows per pair tile (128 per CTA)
 constexpr int PAIR_BN = 256;   // columns per pair tile (B: 128 per CTA)
 constexpr int PAIR_A_BYTES = 128 * GEMM_BK * 2;
@@ -95,7 +96,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&tfull_bar[i]), 1);
-      mbar_init(smem_u32(&tempty_bar[i]), 256);
+      mbar_init(smem_u32(&tempty_bar[i]), 2 * 32 * GEMM_EPI_WARPS);  // both CTAs' epilogue threads
     }
     fence_barrier_init();
   }
@@ -207,6 +208,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const float alpha = args.alpha_ptr ? *args.alpha_ptr : args.alpha;
     const int row_in_tile = quad * 32 + lane;
     int acc = 0;
@@ -223,7 +225,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
       char* cbase = reinterpret_cast<char*>(args.C);
       if (MODE == GROUPED_K) cbase += (long long)ti.group * args.c_group_stride * (EPI == EPI_BF16 ? 2 : 4);
 #pragma unroll 1
-      for (int c = 0; c < PAIR_BN / 32; ++c) {
+      for (int c = half; c < PAIR_BN / 32; c += 2) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * PAIR_BN + c * 32, r);
         tmem_ld_wait();
