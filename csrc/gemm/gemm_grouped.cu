@@ -4,10 +4,10 @@
 namespace hb {
 
 void gemm_dispatch_grouped(int mode, int bn, bool a_mn, bool b_mn, int epi, const CUtensorMap& ta,
-                           const CUtensorMap& tb, const GemmArgs& args, int grid) {
+                           const CUtensorMap& tb, const GemmArgs& args, int grid, const GatherMaps* gm) {
 #define HB_G(MD, BNV, AM, BMN, E)                                      \
   if (mode == MD && bn == BNV && a_mn == AM && b_mn == BMN && epi == E) { \
-    gemm_launch<BNV, AM, BMN, MD, E>(ta, tb, args, grid);              \
+    gemm_launch<BNV, AM, BMN, MD, E>(ta, tb, args, grid, gm);           \
     return;                                                            \
   }
   HB_G(GROUPED_M, 256, false, true, EPI_BF16) HB_G(GROUPED_M, 256, false, true, EPI_F32)

@@ -205,6 +205,47 @@ void grouped_gemm_m_swiglu_bwd(torch::Tensor a, torch::Tensor b, torch::Tensor g
   gemm_dispatch_grouped(GROUPED_M, BN, false, false, EPI_SWIGLU_BWD, ta, tb, args, grid);
 }
 
+// Grouped over M with two K-major B operands concatenated along K (MoE
+// input gradient through the SwiGLU's gate and up projections, one GEMM):
+//   c[rows of g] = a[rows of g, :K1] @ b1[g]^T + a[rows of g, K1:] @ b2[g]^T
+// a [R, 2 K1] (dg | du), b1 / b2 [G, N, K1] (W_gate, W_up), c [R, N] bf16 or fp32
+// (written once, no second accumulating pass).
+void grouped_gemm_m_cat2(torch::Tensor a, torch::Tensor b1, torch::Tensor b2, torch::Tensor c,
+                         torch::Tensor grp_start, torch::Tensor grp_count, torch::Tensor grp_tile_start) {
+  check_bf16(a, "a");
+  check_bf16(b1, "b1");
+  check_bf16(b2, "b2");
+  HB_CHECK(b1.dim() == 3 && b1.is_contiguous() && b2.is_contiguous() && b1.sizes() == b2.sizes(),
+           "grouped_gemm_m_cat2: b1 / b2 must be contiguous [G, N, K1] of one shape");
+  const int G = b1.size(0), N = b1.size(1), K1 = b1.size(2);
+  const int R = a.size(0);
+  HB_CHECK(a.size(1) == 2 * K1 && a.stride(1) == 1, "grouped_gemm_m_cat2: a must be [R, 2 K1]");
+  HB_CHECK(K1 % GEMM_BK == 0, "grouped_gemm_m_cat2: K1 must be a multiple of 64");
+  HB_CHECK(c.size(0) == R && c.size(1) == N && c.stride(1) == 1, "grouped_gemm_m_cat2: bad output");
+  HB_CHECK(grp_start.numel() == G && grp_count.numel() == G && grp_tile_start.numel() == G + 1,
+           "grouped_gemm_m_cat2: bad group arrays");
+  if (R == 0) return;
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int BN = pick_bn(N);
+  CUtensorMap ta = tmap_bf16_2d(a.data_ptr(), R, 2 * K1, a.stride(0), 64, GEMM_BM);
+  CUtensorMap tb = tmap_bf16_3d(b1.data_ptr(), G, N, K1, K1, (uint64_t)N * K1, 64, BN);
+  GatherMaps gm{};
+  gm.b_hi = tmap_bf16_3d(b2.data_ptr(), G, N, K1, K1, (uint64_t)N * K1, 64, BN);
+  GemmArgs args = base_args(c, 1.0);
+  args.M = R;
+  args.N = N;
+  args.K = 2 * K1;
+  args.k_split_b = K1;
+  args.tiles_n = (N + BN - 1) / BN;
+  args.num_groups = G;
+  args.grp_start = grp_start.data_ptr<int>();
+  args.grp_count = grp_count.data_ptr<int>();
+  args.grp_tile_start = grp_tile_start.data_ptr<int>();
+  const int max_tiles = ((R + GEMM_BM - 1) / GEMM_BM) * args.tiles_n;
+  const int grid = std::max(1, std::min(max_tiles, num_sms()));
+  gemm_dispatch_grouped(GROUPED_M, BN, false, false, epi_of(c, false), ta, tb, args, grid, &gm);
+}
+
 // Grouped over K (MoE weight gradients):  c[g] (+)= a_g^T @ b_g
 // a: [R, M] bf16 rows of group g at [start, start+count);  b: [R, N] bf16;
 // c: [G, M, N] fp32 (or bf16 without accumulate); counts multiples of 64.

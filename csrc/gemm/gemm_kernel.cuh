@@ -61,6 +61,8 @@ struct GemmArgs {
   float alpha;
   const float* alpha_ptr;       // optional device scalar; overrides alpha
   const void* aux;              // EPI_SWIGLU_BWD: gate | up of the forward
+  int k_split_b;                // GROUPED_M, K-major B: K at or past this comes from
+                                // GatherMaps::b_hi (at k - k_split_b); 0 = one B
   int* status;
   unsigned long long budget_ns;
 };
@@ -82,10 +84,13 @@ struct alignas(64) GatherMaps {
   __nv_bfloat16* dst;                  // the gathered copy
   int* flags;                          // [G][tiles_n][k_blocks]
   int rank, world, groups_per_rank;
+  // Not part of the gather: the second K-major B of a K-concatenated grouped
+  // GEMM, C = A[:, :Ks] B[g]^T + A[:, Ks:] B_hi[g]^T (GemmArgs::k_split_b = Ks).
+  CUtensorMap b_hi;
 };
 
-// Copy-ahead of the gathered B tiles by two extra warps (warps 6-7 of the
-// gathered variant), concurrent with the producer, MMA and epilogue.  CTA i takes tiles
+// Copy-ahead of the gathered B tiles by two extra warps (the last two warps
+// of the gathered variant), concurrent with the producer, MMA and epilogue.  CTA i takes tiles
 // i, i + grid, ... in the order the tile schedule needs them, claims each with
 // the same flag protocol as the producer (so a tile is copied exactly once)
 // and moves it with 16-byte peer loads / local stores.  Groups without rows
@@ -341,7 +346,10 @@ __global__ void __launch_bounds__(GATHER ? GEMM_THREADS + GATHER_COPY_THREADS : 
             }
           } else if (MODE == GROUPED_M) {
             if (!B_MN) {
-              tma_load_3d(sb, &tmB, fb, kc, ti.n0, ti.group);
+              if (args.k_split_b > 0 && kc >= args.k_split_b)
+                tma_load_3d(sb, &gm.b_hi, fb, kc - args.k_split_b, ti.n0, ti.group);
+              else
+                tma_load_3d(sb, &tmB, fb, kc, ti.n0, ti.group);
             } else {
 #pragma unroll
               for (int i = 0; i < BN / 64; ++i) tma_load_3d(sb + i * 8192, &tmB, fb, ti.n0 + 64 * i, kc, ti.group);
@@ -603,7 +611,8 @@ void gemm_dispatch_dense_ak(int bn, bool b_mn, int epi, const CUtensorMap& ta, c
 void gemm_dispatch_dense_amn(int bn, bool b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
                              const GemmArgs& args, int grid);
 void gemm_dispatch_grouped(int mode, int bn, bool a_mn, bool b_mn, int epi, const CUtensorMap& ta,
-                           const CUtensorMap& tb, const GemmArgs& args, int grid);
+                           const CUtensorMap& tb, const GemmArgs& args, int grid,
+                           const GatherMaps* gm = nullptr);
 void gemm_dispatch_gather(int bn, const CUtensorMap& ta, const GemmArgs& args, const GatherMaps& gm, int grid);
 
 }  // namespace hb

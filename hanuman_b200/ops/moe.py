@@ -220,12 +220,18 @@ class MoEFn(torch.autograd.Function):
             ext().grouped_gemm_m(dy, wd, dhh, starts, counts, tprefix_f, True)
             ext().swiglu_bwd(dhh, gu, dgu, row_src)  # pad rows -> 0 for the grouped-K GEMMs
         ext().grouped_gemm_k(hh, dy, main_grad(mod.expert_w_down), starts, padded, True)
-        dxp = torch.empty(R, D, dtype=torch.float32, device=dev)
         tn_d = (D + _bn(D) - 1) // _bn(D)
         tn_f = (F + _bn(F) - 1) // _bn(F)
         tprefix_dx = (tprefix_f // tn_f * tn_d).to(torch.int32)
-        ext().grouped_gemm_m(dgu[:, :F], wg, dxp, starts, counts, tprefix_dx, True, False)
-        ext().grouped_gemm_m(dgu[:, F:], wu, dxp, starts, counts, tprefix_dx, True, True)
+        if F % 64 == 0:
+            # one GEMM over K = 2F: [dg | du] @ [W_gate | W_up]^T, rows in bf16
+            # (the reference's ragged_dot input cotangent is bf16 as well)
+            dxp = torch.empty(R, D, dtype=torch.bfloat16, device=dev)
+            ext().grouped_gemm_m_cat2(dgu, wg, wu, dxp, starts, counts, tprefix_dx)
+        else:
+            dxp = torch.empty(R, D, dtype=torch.float32, device=dev)
+            ext().grouped_gemm_m(dgu[:, :F], wg, dxp, starts, counts, tprefix_dx, True, False)
+            ext().grouped_gemm_m(dgu[:, F:], wu, dxp, starts, counts, tprefix_dx, True, True)
         ext().grouped_gemm_k(xp, dgu[:, :F], main_grad(mod.expert_w_gate), starts, padded, True)
         ext().grouped_gemm_k(xp, dgu[:, F:], main_grad(mod.expert_w_up), starts, padded, True)
         ext().moe_scatter_add(dxp, pos, dx)

@@ -235,3 +235,34 @@ def test_grouped_m_swiglu_bwd_matches_separate_kernels():
             continue
         seg = slice(s, s + (n + 127) // 128 * 128)
         assert torch.equal(got[seg], ref[seg]), s
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_grouped_m_cat2_matches_fp32_reference(out_dtype):
+    """c = a[:, :K1] b1[g]^T + a[:, K1:] b2[g]^T in one GEMM (second B operand
+    for the K blocks past K1), against an fp32 PyTorch reference."""
+    torch.manual_seed(5)
+    dev = "cuda"
+    G, N, K1 = 4, 384, 192
+    counts = [70, 0, 129, 256]
+    starts, R = _groups(counts)
+    a = torch.randn(R, 2 * K1, device=dev).bfloat16()
+    b1 = (torch.randn(G, N, K1, device=dev) * 0.1).bfloat16()
+    b2 = (torch.randn(G, N, K1, device=dev) * 0.1).bfloat16()
+    BN = 256 if N >= 256 else 128
+    tiles_n = (N + BN - 1) // BN
+    tstart = [0]
+    for cnt in counts:
+        tstart.append(tstart[-1] + (cnt + 127) // 128 * tiles_n)
+    gs = torch.tensor(starts, dtype=torch.int32, device=dev)
+    gc = torch.tensor(counts, dtype=torch.int32, device=dev)
+    gt = torch.tensor(tstart, dtype=torch.int32, device=dev)
+    c = torch.zeros(R, N, device=dev, dtype=out_dtype)
+    _ext().grouped_gemm_m_cat2(a, b1, b2, c, gs, gc, gt)
+    torch.cuda.synchronize()
+    for g, (s, n) in enumerate(zip(starts, counts)):
+        if n == 0:
+            continue
+        ref = a[s:s + n, :K1].float() @ b1[g].float().t() + a[s:s + n, K1:].float() @ b2[g].float().t()
+        got = c[s:s + n].float()
+        assert (got - ref).norm() / ref.norm() < (1e-5 if out_dtype == torch.float32 else 1e-2), g
