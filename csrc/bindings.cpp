@@ -15,6 +15,9 @@ void grouped_gemm_k(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Te
                     torch::Tensor grp_count, bool accumulate);
 void grouped_gemm_m_swiglu_bwd(torch::Tensor a, torch::Tensor b, torch::Tensor gu, torch::Tensor dgu,
                                torch::Tensor grp_start, torch::Tensor grp_count, torch::Tensor grp_tile_start);
+void grouped_gemm_m_swiglu_fwd(torch::Tensor a, torch::Tensor b1, torch::Tensor b2, torch::Tensor h,
+                               torch::Tensor gu, torch::Tensor grp_start, torch::Tensor grp_count,
+                               torch::Tensor grp_tile_start);
 void grouped_gemm_m_cat2(torch::Tensor a, torch::Tensor b1, torch::Tensor b2, torch::Tensor c,
                          torch::Tensor grp_start, torch::Tensor grp_count, torch::Tensor grp_tile_start);
 void grouped_gemm_m_gather(torch::Tensor a, std::vector<int64_t> peer_ptrs, int64_t rank,
@@ -133,6 +136,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grouped_gemm_m_gather", &hb::grouped_gemm_m_gather);
   m.def("grouped_gemm_m_swiglu_bwd", &hb::grouped_gemm_m_swiglu_bwd);
   m.def("grouped_gemm_m_cat2", &hb::grouped_gemm_m_cat2);
+  m.def("grouped_gemm_m_swiglu_fwd", &hb::grouped_gemm_m_swiglu_fwd);
   m.def("rmsnorm_fwd", &hb::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &hb::rmsnorm_bwd);
   m.def("rope_apply", &hb::rope_apply);

@@ -15,6 +15,7 @@ void gemm_dispatch_grouped(int mode, int bn, bool a_mn, bool b_mn, int epi, cons
   HB_G(GROUPED_M, 256, false, false, EPI_BF16) HB_G(GROUPED_M, 256, false, false, EPI_F32)
   HB_G(GROUPED_M, 128, false, true, EPI_BF16) HB_G(GROUPED_M, 128, false, true, EPI_F32)
   HB_G(GROUPED_M, 128, false, false, EPI_BF16) HB_G(GROUPED_M, 128, false, false, EPI_F32)
+  HB_G(GROUPED_M, 256, false, true, EPI_SWIGLU_FWD)
   HB_G(GROUPED_M, 256, false, false, EPI_SWIGLU_BWD) HB_G(GROUPED_M, 128, false, false, EPI_SWIGLU_BWD)
   HB_G(GROUPED_K, 256, true, true, EPI_F32) HB_G(GROUPED_K, 256, true, true, EPI_F32_ACC)
   HB_G(GROUPED_K, 256, true, true, EPI_BF16)

@@ -205,6 +205,52 @@ void grouped_gemm_m_swiglu_bwd(torch::Tensor a, torch::Tensor b, torch::Tensor g
   gemm_dispatch_grouped(GROUPED_M, BN, false, false, EPI_SWIGLU_BWD, ta, tb, args, grid);
 }
 
+// Grouped over M with the SwiGLU in the epilogue (MoE expert forward):
+//   g = a @ b1[g], u = a @ b2[g]  (a [R, K], b1 / b2 [G, K, F] MN-major)
+//   gu = [g | u] (bf16, kept for the backward), h = bf16(silu(g)) * u
+// grp_tile_start counts tiles of the virtual width 2F in 256-column tiles.
+void grouped_gemm_m_swiglu_fwd(torch::Tensor a, torch::Tensor b1, torch::Tensor b2, torch::Tensor h,
+                               torch::Tensor gu, torch::Tensor grp_start, torch::Tensor grp_count,
+                               torch::Tensor grp_tile_start) {
+  check_bf16(a, "a");
+  check_bf16(b1, "b1");
+  check_bf16(b2, "b2");
+  check_bf16(h, "h");
+  check_bf16(gu, "gu");
+  HB_CHECK(b1.dim() == 3 && b1.is_contiguous() && b2.is_contiguous() && b1.sizes() == b2.sizes(),
+           "grouped_gemm_m_swiglu_fwd: b1 / b2 must be contiguous [G, K, F] of one shape");
+  const int G = b1.size(0), K = b1.size(1), F = b1.size(2);
+  const int R = a.size(0);
+  HB_CHECK(a.size(1) == K && a.stride(1) == 1, "grouped_gemm_m_swiglu_fwd: a must be [R, K]");
+  HB_CHECK(F % 128 == 0, "grouped_gemm_m_swiglu_fwd: F must be a multiple of 128");
+  HB_CHECK(h.is_contiguous() && h.size(0) == R && h.size(1) == F, "grouped_gemm_m_swiglu_fwd: h must be [R, F]");
+  HB_CHECK(gu.is_contiguous() && gu.size(0) == R && gu.size(1) == 2 * F,
+           "grouped_gemm_m_swiglu_fwd: gu must be [R, 2F]");
+  HB_CHECK(grp_start.numel() == G && grp_count.numel() == G && grp_tile_start.numel() == G + 1,
+           "grouped_gemm_m_swiglu_fwd: bad group arrays");
+  if (R == 0) return;
+  const c10::cuda::CUDAGuard guard(a.device());
+  constexpr int BN = 256;
+  CUtensorMap ta = tmap_bf16_2d(a.data_ptr(), R, K, a.stride(0), 64, GEMM_BM);
+  CUtensorMap tb = tmap_bf16_3d(b1.data_ptr(), G, K, F, F, (uint64_t)K * F, 64, 64);
+  GatherMaps gm{};
+  gm.b_hi = tmap_bf16_3d(b2.data_ptr(), G, K, F, F, (uint64_t)K * F, 64, 64);
+  GemmArgs args = base_args(h, 1.0);
+  args.c2 = gu.data_ptr();
+  args.ldc2 = 2LL * F;
+  args.M = R;
+  args.N = 2 * F;
+  args.K = K;
+  args.tiles_n = 2 * F / BN;
+  args.num_groups = G;
+  args.grp_start = grp_start.data_ptr<int>();
+  args.grp_count = grp_count.data_ptr<int>();
+  args.grp_tile_start = grp_tile_start.data_ptr<int>();
+  const int max_tiles = ((R + GEMM_BM - 1) / GEMM_BM) * args.tiles_n;
+  const int grid = std::max(1, std::min(max_tiles, num_sms()));
+  gemm_dispatch_grouped(GROUPED_M, BN, false, true, EPI_SWIGLU_FWD, ta, tb, args, grid, &gm);
+}
+
 // Grouped over M with two K-major B operands concatenated along K (MoE
 // input gradient through the SwiGLU's gate and up projections, one GEMM):
 //   c[rows of g] = a[rows of g, :K1] @ b1[g]^T + a[rows of g, K1:] @ b2[g]^T

@@ -44,7 +44,12 @@ enum GemmMode { DENSE = 0, GROUPED_M = 1, GROUPED_K = 2 };
 // for the rows of a SwiGLU; the epilogue reads g, u from args.aux ([R, 2F]
 // bf16, the forward's gate | up) and writes dgu = [dh u silu'(g) | dh silu(g)]
 // (bf16, ldc = 2F); the pad rows of each expert's 128-row segment get zeros.
-enum GemmEpi { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACC = 2, EPI_SWIGLU_BWD = 3 };
+// EPI_SWIGLU_FWD (grouped-over-M, MN-major B, BN 256 only): virtual N = 2F;
+// tile j loads columns [128 j, 128 j + 128) of W_gate (tmB) and of W_up
+// (GatherMaps::b_hi), so TMEM holds g and u of the same 128 columns; the
+// epilogue writes h = bf16(silu(g)) * u to C ([R, F]) and g | u (bf16) to
+// args.c2 ([R, 2F]); pad rows of each expert segment get h = 0.
+enum GemmEpi { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACC = 2, EPI_SWIGLU_BWD = 3, EPI_SWIGLU_FWD = 4 };
 
 struct GemmArgs {
   int M, N, K;
@@ -61,6 +66,8 @@ struct GemmArgs {
   float alpha;
   const float* alpha_ptr;       // optional device scalar; overrides alpha
   const void* aux;              // EPI_SWIGLU_BWD: gate | up of the forward
+  void* c2;                     // EPI_SWIGLU_FWD: g | u output
+  long long ldc2;
   int k_split_b;                // GROUPED_M, K-major B: K at or past this comes from
                                 // GatherMaps::b_hi (at k - k_split_b); 0 = one B
   int* status;
@@ -218,6 +225,48 @@ __device__ __forceinline__ bool get_tile(const GemmArgs& a, int t, TileInfo& ti)
   }
 }
 
+// EPI_SWIGLU_FWD: one row, 32 columns (n .. n+31, F a multiple of 128).  g and u
+// are rounded to bf16 as stored, silu(g) is rounded to bf16, then h = silu * u
+// (the rounding of the standalone SwiGLU kernel).
+HB_DEVICE void swiglu_fwd_store(const GemmArgs& args, int m, int n, bool row_ok, bool has_k, float alpha,
+                                const uint32_t (&rg)[32], const uint32_t (&ru)[32]) {
+  const int F = args.N / 2;
+  uint4* h4 = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.C) + (long long)m * args.ldc + n);
+  if (!row_ok) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) h4[q] = make_uint4(0u, 0u, 0u, 0u);
+    return;
+  }
+  __nv_bfloat16* gp = reinterpret_cast<__nv_bfloat16*>(args.c2) + (long long)m * args.ldc2 + n;
+  uint4* g4 = reinterpret_cast<uint4*>(gp);
+  uint4* u4 = reinterpret_cast<uint4*>(gp + F);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 wh, wg, wu;
+    uint32_t* ph = reinterpret_cast<uint32_t*>(&wh);
+    uint32_t* pg = reinterpret_cast<uint32_t*>(&wg);
+    uint32_t* pu = reinterpret_cast<uint32_t*>(&wu);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int j = q * 8 + 2 * e;
+      const float g0 = has_k ? __uint_as_float(rg[j]) * alpha : 0.f;
+      const float g1 = has_k ? __uint_as_float(rg[j + 1]) * alpha : 0.f;
+      const float u0 = has_k ? __uint_as_float(ru[j]) * alpha : 0.f;
+      const float u1 = has_k ? __uint_as_float(ru[j + 1]) * alpha : 0.f;
+      pg[e] = pack_bf16x2(g0, g1);
+      pu[e] = pack_bf16x2(u0, u1);
+      const float gr0 = __uint_as_float(pg[e] << 16), gr1 = __uint_as_float(pg[e] & 0xffff0000u);
+      const float ur0 = __uint_as_float(pu[e] << 16), ur1 = __uint_as_float(pu[e] & 0xffff0000u);
+      const float s0 = __bfloat162float(__float2bfloat16_rn(gr0 / (1.f + __expf(-gr0))));
+      const float s1 = __bfloat162float(__float2bfloat16_rn(gr1 / (1.f + __expf(-gr1))));
+      ph[e] = pack_bf16x2(s0 * ur0, s1 * ur1);
+    }
+    h4[q] = wh;
+    g4[q] = wg;
+    u4[q] = wu;
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN, int MODE, int EPI, bool GATHER = false>
 __global__ void __launch_bounds__(GATHER ? GEMM_THREADS + GATHER_COPY_THREADS : GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -350,6 +399,12 @@ __global__ void __launch_bounds__(GATHER ? GEMM_THREADS + GATHER_COPY_THREADS : 
                 tma_load_3d(sb, &gm.b_hi, fb, kc - args.k_split_b, ti.n0, ti.group);
               else
                 tma_load_3d(sb, &tmB, fb, kc, ti.n0, ti.group);
+            } else if (EPI == EPI_SWIGLU_FWD) {
+              // first half of the tile from W_gate, second half from W_up
+#pragma unroll
+              for (int i = 0; i < BN / 64; ++i)
+                tma_load_3d(sb + i * 8192, i < BN / 128 ? &tmB : &gm.b_hi, fb,
+                            ti.n0 / 2 + 64 * (i % (BN / 128)), kc, ti.group);
             } else {
 #pragma unroll
               for (int i = 0; i < BN / 64; ++i) tma_load_3d(sb + i * 8192, &tmB, fb, ti.n0 + 64 * i, kc, ti.group);
@@ -445,8 +500,21 @@ __global__ void __launch_bounds__(GATHER ? GEMM_THREADS + GATHER_COPY_THREADS : 
       const bool has_k = ti.k_iters > 0;
       char* cbase = reinterpret_cast<char*>(args.C);
       if (MODE == GROUPED_K) cbase += (long long)ti.group * args.c_group_stride * (EPI == EPI_BF16 ? 2 : 4);
+      if constexpr (EPI == EPI_SWIGLU_FWD) {
+        const int F = args.N / 2;
 #pragma unroll 1
-      for (int c = half; c < BN / 32; c += 2) {
+        for (int c = half; c < BN / 64; c += 2) {
+          uint32_t rg[32], ru[32];
+          const uint32_t tb = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
+          tmem_ld_32x32b_x32(tb + c * 32, rg);
+          tmem_ld_32x32b_x32(tb + BN / 2 + c * 32, ru);
+          tmem_ld_wait();
+          const int n = ti.n0 / 2 + c * 32;
+          if (n < F) swiglu_fwd_store(args, m, n, row_ok, has_k, alpha, rg, ru);
+        }
+      }
+#pragma unroll 1
+      for (int c = half; c < (EPI == EPI_SWIGLU_FWD ? 0 : BN / 32); c += 2) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c * 32, r);
         tmem_ld_wait();

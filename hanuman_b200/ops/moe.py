@@ -147,11 +147,17 @@ class MoEFn(torch.autograd.Function):
             wg, wu, wd = (gat.bufs[k] for k in ("expert_w_gate", "expert_w_up", "expert_w_down"))
             gat.gemm(xp, "expert_w_gate", gu[:, :F], starts, counts, tprefix_f)
             gat.gemm(xp, "expert_w_up", gu[:, F:], starts, counts, tprefix_f)
-        else:
-            ext().grouped_gemm_m(xp, wg, gu[:, :F], starts, counts, tprefix_f, False)
-            ext().grouped_gemm_m(xp, wu, gu[:, F:], starts, counts, tprefix_f, False)
         hh = torch.empty(R, F, dtype=torch.bfloat16, device=dev)
-        ext().swiglu_fwd(gu, hh, row_src)  # pad rows -> 0 (grouped-K reads them)
+        if gat is None and F % 128 == 0:
+            # gate and up in one GEMM (tile j: 128 columns of each), the SwiGLU
+            # in its epilogue; pad rows of h -> 0 (grouped-K reads them)
+            tprefix_v = (tprefix_f // tn_f * (2 * F // 256)).to(torch.int32)
+            ext().grouped_gemm_m_swiglu_fwd(xp, wg, wu, hh, gu, starts, counts, tprefix_v)
+        else:
+            if gat is None:
+                ext().grouped_gemm_m(xp, wg, gu[:, :F], starts, counts, tprefix_f, False)
+                ext().grouped_gemm_m(xp, wu, gu[:, F:], starts, counts, tprefix_f, False)
+            ext().swiglu_fwd(gu, hh, row_src)  # pad rows -> 0 (grouped-K reads them)
         y = torch.empty(R, D, dtype=torch.bfloat16, device=dev)
         if gat is not None:
             gat.gemm(hh, "expert_w_down", y, starts, counts, tprefix_d)

@@ -266,3 +266,45 @@ def test_grouped_m_cat2_matches_fp32_reference(out_dtype):
         ref = a[s:s + n, :K1].float() @ b1[g].float().t() + a[s:s + n, K1:].float() @ b2[g].float().t()
         got = c[s:s + n].float()
         assert (got - ref).norm() / ref.norm() < (1e-5 if out_dtype == torch.float32 else 1e-2), g
+
+
+def test_grouped_m_swiglu_fwd_matches_separate_kernels():
+    """Gate and up in one GEMM with the SwiGLU in the epilogue equals two
+    grouped GEMMs followed by the standalone SwiGLU kernel, bit for bit
+    (g | u and h; pad rows of h zero)."""
+    torch.manual_seed(6)
+    dev = "cuda"
+    G, D, F = 5, 512, 384
+    counts = [130, 0, 7, 256, 300]
+    starts, R = _groups(counts)
+    x = torch.randn(R, D, device=dev).bfloat16()
+    wg = (torch.randn(G, D, F, device=dev) * 0.05).bfloat16()
+    wu = (torch.randn(G, D, F, device=dev) * 0.05).bfloat16()
+    row_src = torch.full((R,), -1, dtype=torch.int32, device=dev)
+    for s, n in zip(starts, counts):
+        row_src[s:s + n] = 0
+
+    def prefix(tiles_n):
+        t = [0]
+        for cnt in counts:
+            t.append(t[-1] + (cnt + 127) // 128 * tiles_n)
+        return torch.tensor(t, dtype=torch.int32, device=dev)
+
+    gs = torch.tensor(starts, dtype=torch.int32, device=dev)
+    gc = torch.tensor(counts, dtype=torch.int32, device=dev)
+    BN = 256 if F >= 256 else 128
+    gu_ref = torch.zeros(R, 2 * F, device=dev).bfloat16()
+    _ext().grouped_gemm_m(x, wg, gu_ref[:, :F], gs, gc, prefix((F + BN - 1) // BN), False)
+    _ext().grouped_gemm_m(x, wu, gu_ref[:, F:], gs, gc, prefix((F + BN - 1) // BN), False)
+    h_ref = torch.empty(R, F, device=dev).bfloat16()
+    _ext().swiglu_fwd(gu_ref, h_ref, row_src)
+    gu = torch.zeros(R, 2 * F, device=dev).bfloat16()
+    h = torch.full((R, F), float("nan"), device=dev).bfloat16()
+    _ext().grouped_gemm_m_swiglu_fwd(x, wg, wu, h, gu, gs, gc, prefix(2 * F // 256))
+    torch.cuda.synchronize()
+    for s, n in zip(starts, counts):
+        if n == 0:
+            continue
+        assert torch.equal(gu[s:s + n], gu_ref[s:s + n]), s
+        seg = slice(s, s + (n + 127) // 128 * 128)
+        assert torch.equal(h[seg], h_ref[seg]), s
