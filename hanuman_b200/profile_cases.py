@@ -6,7 +6,7 @@ Each case builds inputs on the current GPU (a few GB at most; operands larger
 than the 126 MB L2 where the kernel is memory-bound), runs the kernel a few
 times and exits.  With ``--time`` it prints the CUDA-event time of one launch
 and the achieved TFLOP/s or GB/s.  Cases: gemm_fwd, gemm_dw, grouped_fwd,
-gather_gemm_emulated, kda_layer, kda_fwd, kda_bwd, kda128_fwd, kda128_bwd, flash_fwd, flash_bwd, router_fwd, p2p_rs_emulated.
+grouped_swiglu_fwd, grouped_swiglu_bwd, grouped_cat2, gather_gemm_emulated, kda_layer, kda_fwd, kda_bwd, kda128_fwd, kda128_bwd, flash_fwd, flash_bwd, router_fwd, p2p_rs_emulated.
 """
 from __future__ import annotations
 
@@ -60,6 +60,56 @@ def case_grouped_fwd():
     i32 = lambda v: torch.tensor(v, dtype=torch.int32, device="cuda")
     gs, gc, gt = i32(starts), i32(counts), i32(tp)
     return (lambda: ext().grouped_gemm_m(xp, w, y, gs, gc, gt, False)), 2 * T * K * D * F, "flop"
+
+
+def _expert_plan(tiles_n, T=32768, K=4, N=32):
+    """Balanced expert segments of the flagship MoE (T tokens x top-K over N
+    experts, 128-row aligned) and the grouped GEMM tile prefix."""
+    counts = [T * K // N] * N
+    starts = [i * ((T * K // N + 127) // 128 * 128) for i in range(N)]
+    R = starts[-1] + counts[-1]
+    tp = [0]
+    for c in counts:
+        tp.append(tp[-1] + (c + 127) // 128 * tiles_n)
+    i32 = lambda v: torch.tensor(v, dtype=torch.int32, device="cuda")
+    return R, i32(starts), i32(counts), i32(tp)
+
+
+def case_grouped_swiglu_fwd():
+    """Expert gate + up GEMMs with the SwiGLU in the epilogue (one launch)."""
+    T, K, N, D, F = 32768, 4, 32, 1024, 768
+    R, gs, gc, gt = _expert_plan(2 * F // 256)
+    xp = torch.randn(R, D, device="cuda").bfloat16()
+    wg = (torch.randn(N, D, F, device="cuda") * 0.03).bfloat16()
+    wu = (torch.randn(N, D, F, device="cuda") * 0.03).bfloat16()
+    h = torch.empty(R, F, device="cuda", dtype=torch.bfloat16)
+    gu = torch.empty(R, 2 * F, device="cuda", dtype=torch.bfloat16)
+    return (lambda: ext().grouped_gemm_m_swiglu_fwd(xp, wg, wu, h, gu, gs, gc, gt)), \
+        2 * 2 * T * K * D * F, "flop"
+
+
+def case_grouped_swiglu_bwd():
+    """dh = dY W_down^T with the SwiGLU backward in the epilogue (one launch)."""
+    T, K, N, D, F = 32768, 4, 32, 1024, 768
+    R, gs, gc, gt = _expert_plan((F + 255) // 256)
+    dy = torch.randn(R, D, device="cuda").bfloat16()
+    wd = (torch.randn(N, F, D, device="cuda") * 0.03).bfloat16()
+    gu = torch.randn(R, 2 * F, device="cuda").bfloat16()
+    dgu = torch.empty(R, 2 * F, device="cuda", dtype=torch.bfloat16)
+    return (lambda: ext().grouped_gemm_m_swiglu_bwd(dy, wd, gu, dgu, gs, gc, gt)), \
+        2 * T * K * D * F, "flop"
+
+
+def case_grouped_cat2():
+    """Expert input gradient [dg | du] @ [W_gate | W_up]^T in one launch (K = 2F)."""
+    T, K, N, D, F = 32768, 4, 32, 1024, 768
+    R, gs, gc, gt = _expert_plan((D + 255) // 256)
+    dgu = torch.randn(R, 2 * F, device="cuda").bfloat16()
+    wg = (torch.randn(N, D, F, device="cuda") * 0.03).bfloat16()
+    wu = (torch.randn(N, D, F, device="cuda") * 0.03).bfloat16()
+    dxp = torch.empty(R, D, device="cuda", dtype=torch.bfloat16)
+    return (lambda: ext().grouped_gemm_m_cat2(dgu, wg, wu, dxp, gs, gc, gt)), \
+        2 * T * K * 2 * F * D, "flop"
 
 
 def case_gather_gemm_emulated():
