@@ -859,11 +859,12 @@ __global__ void prep_fwd_kernel(const __nv_bfloat16* __restrict__ raw, long long
   }
 }
 
-// Backward part 1 (warp per token, all heads): gradients at the conv outputs of
-// q/k/v (fp32, [T, 3*HK]), df [T, HK], dbraw [T, H]; d a_log and d dt_bias are
-// block partials in shared memory, flushed with one atomic per element.
+// Backward part 1 (block per head, warp per token): gradients at the conv
+// outputs of q/k/v (fp32, [T, 3*HK]), df [T, HK], dbraw [T, H]; d dt_bias and
+// d a_log of the block's head are summed in each lane's registers over its
+// tokens, then reduced through shared memory with one global atomic each.
 template <int DK>
-__global__ void prep_bwd1_kernel(const __nv_bfloat16* __restrict__ raw, long long ld_raw,
+__global__ void __launch_bounds__(256, DK >= 128 ? 2 : 3) prep_bwd1_kernel(const __nv_bfloat16* __restrict__ raw, long long ld_raw,
                                  const float* __restrict__ wq, const float* __restrict__ wk,
                                  const float* __restrict__ wv, const float* __restrict__ f,
                                  const float* __restrict__ a_log, const float* __restrict__ dt_bias,
@@ -874,19 +875,22 @@ __global__ void prep_bwd1_kernel(const __nv_bfloat16* __restrict__ raw, long lon
                                  float* __restrict__ df, float* __restrict__ dbraw,
                                  float* __restrict__ d_alog, float* __restrict__ d_dtb) {
   constexpr int NP = (DK + 63) / 64;
-  extern __shared__ float s_acc[];
+  __shared__ float s_dtb[DK + 1];  // this block's head: d dt_bias, then d a_log
   const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
   const int HK = H * DK;
-  float* s_dtb = s_acc;
-  float* s_al = s_acc + HK;
-  for (int i = threadIdx.x; i < HK + H; i += blockDim.x) s_acc[i] = 0.f;
+  const int h = blockIdx.y;        // one head per block: the bias gradients sum in registers
+  float2 acc_dtb[NP];
+#pragma unroll
+  for (int j = 0; j < NP; ++j) acc_dtb[j] = make_float2(0.f, 0.f);
+  float acc_al = 0.f;
+  for (int i = threadIdx.x; i < DK + 1; i += blockDim.x) s_dtb[i] = 0.f;
   __syncthreads();
   for (long long t = blockIdx.x * (long long)warps + (threadIdx.x >> 5); t < T; t += (long long)gridDim.x * warps) {
     const int pos = t % S;
     const __nv_bfloat16* rows[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) rows[i] = pos - (3 - i) >= 0 ? raw + (t - (3 - i)) * ld_raw : nullptr;
-    for (int h = 0; h < H; ++h) {
+    {
       float2 cq[NP], ck[NP], sq[NP], sk[NP], gq[NP], gk[NP];
       float ssq = 0.f, ssk = 0.f, dotq = 0.f, dotk = 0.f, dal = 0.f;
 #pragma unroll
@@ -928,8 +932,8 @@ __global__ void prep_bwd1_kernel(const __nv_bfloat16* __restrict__ raw, long lon
           }
         }
         *reinterpret_cast<float2*>(df + o) = make_float2(dz[0], dz[1]);
-        atomicAdd(s_dtb + ch, dz[0]);
-        atomicAdd(s_dtb + ch + 1, dz[1]);
+        acc_dtb[j].x += dz[0];
+        acc_dtb[j].y += dz[1];
       }
       ssq = warp_sum(ssq);
       ssk = warp_sum(ssk);
@@ -950,18 +954,26 @@ __global__ void prep_bwd1_kernel(const __nv_bfloat16* __restrict__ raw, long lon
         *reinterpret_cast<float2*>(dconv + co) = make_float2(dq0 * dsilu_f(cq[j].x), dq1 * dsilu_f(cq[j].y));
         *reinterpret_cast<float2*>(dconv + co + HK) = make_float2(dk0 * dsilu_f(ck[j].x), dk1 * dsilu_f(ck[j].y));
       }
+      acc_al += dal;
       if (lane == 0) {
-        if (gate_mode == 0) atomicAdd(s_al + h, dal);
         const float bt = beta[t * H + h];
         dbraw[t * H + h] = dbeta[t * H + h] * bt * (1.f - bt);
       }
     }
   }
+#pragma unroll
+  for (int j = 0; j < NP; ++j) {
+    const int c = 2 * lane + 64 * j;
+    if (c < DK) {
+      atomicAdd(s_dtb + c, acc_dtb[j].x);
+      atomicAdd(s_dtb + c + 1, acc_dtb[j].y);
+    }
+  }
+  if (lane == 0 && gate_mode == 0) atomicAdd(s_dtb + DK, acc_al);
   __syncthreads();
-  for (int i = threadIdx.x; i < HK; i += blockDim.x)
-    if (s_dtb[i] != 0.f) atomicAdd(d_dtb + i, s_dtb[i]);
-  for (int i = threadIdx.x; i < H; i += blockDim.x)
-    if (s_al[i] != 0.f) atomicAdd(d_alog + i, s_al[i]);
+  for (int i = threadIdx.x; i < DK; i += blockDim.x)
+    if (s_dtb[i] != 0.f) atomicAdd(d_dtb + h * DK + i, s_dtb[i]);
+  if (threadIdx.x == 0 && s_dtb[DK] != 0.f) atomicAdd(d_alog + h, s_dtb[DK]);
 }
 
 // Backward part 2 (thread per channel of the 3*HK conv inputs, a run of tokens):
@@ -1179,12 +1191,13 @@ void kda_prep_bwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::
                   torch::Tensor dwk, torch::Tensor dwv) {
   const int T = dq.size(0), H = dq.size(1), DKV = dq.size(2);
   HB_CHECK(raw.stride(0) % 2 == 0 && DKV % 2 == 0, "kda_prep: even row stride and head dim");
-  const int grid = (int)std::min<long long>(((long long)T + 7) / 8, num_sms() * 8);
-  const size_t acc_smem = (size_t)(H * DKV + H) * 4;
-  HB_CHECK(acc_smem <= 48 * 1024, "kda_prep_bwd: too many channels");
+  // blocks: (token runs) x (heads); about 8 resident blocks per SM in all
+  const int gx = (int)std::max<long long>(
+      1, std::min<long long>(((long long)T + 7) / 8, ((long long)num_sms() * 8 + H - 1) / H));
+  const dim3 grid(gx, H);
   auto launch = [&](auto dkc) {
     constexpr int DK = decltype(dkc)::value;
-    kda::prep_bwd1_kernel<DK><<<grid, 256, acc_smem, cur_stream()>>>(
+    kda::prep_bwd1_kernel<DK><<<grid, 256, 0, cur_stream()>>>(
         (const __nv_bfloat16*)raw.data_ptr(), raw.stride(0), wq.data_ptr<float>(), wk.data_ptr<float>(),
         wv.data_ptr<float>(), f.data_ptr<float>(), a_log.data_ptr<float>(), dt_bias.data_ptr<float>(),
         beta.data_ptr<float>(), (int)gate_mode, T, (int)S, H, dq.data_ptr<float>(), dk.data_ptr<float>(),
