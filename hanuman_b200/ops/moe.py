@@ -100,6 +100,27 @@ class ExpertGather:
                                     self.flags, c, starts, counts, tprefix)
 
 
+_ONE_GROUP: dict = {}
+
+
+def _one_group(T: int, tiles_n: int, dev) -> tuple:
+    """Group arrays of a grouped GEMM over ONE group of T rows (the shared
+    expert on the expert kernels), cached per shape: start 0, count T, tile
+    prefix [0, T / 128 * tiles_n]."""
+    key = (T, tiles_n, str(dev))
+    if key not in _ONE_GROUP:
+        i32 = dict(dtype=torch.int32, device=dev)
+        _ONE_GROUP[key] = (torch.zeros(1, **i32), torch.full((1,), T, **i32),
+                           torch.tensor([0, T // 128 * tiles_n], **i32))
+    return _ONE_GROUP[key]
+
+
+def _shared_fused(T: int, Fs: int) -> bool:
+    """The fused SwiGLU kernels write whole 128-row tiles (pad rows zeroed), so
+    the shared expert uses them when T fills whole tiles."""
+    return T % 128 == 0 and Fs % 128 == 0
+
+
 class MoEFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, h, mod, B, S):
@@ -169,10 +190,16 @@ class MoEFn(torch.autograd.Function):
         sg, su, sd = _work(mod.shared_w_gate), _work(mod.shared_w_up), _work(mod.shared_w_down)
         Fs = sg.shape[1]
         sgu = torch.empty(T, 2 * Fs, dtype=torch.bfloat16, device=dev)
-        ext().gemm(xb, sg, sgu[:, :Fs], False, False, False, 1.0)
-        ext().gemm(xb, su, sgu[:, Fs:], False, False, False, 1.0)
         shh = torch.empty(T, Fs, dtype=torch.bfloat16, device=dev)
-        ext().swiglu_fwd(sgu, shh)
+        if _shared_fused(T, Fs):
+            # the fused expert kernels with one group of T rows
+            gs1, gc1, gt1 = _one_group(T, 2 * Fs // 256, dev)
+            ext().grouped_gemm_m_swiglu_fwd(xb, sg.unsqueeze(0), su.unsqueeze(0), shh, sgu,
+                                            gs1, gc1, gt1)
+        else:
+            ext().gemm(xb, sg, sgu[:, :Fs], False, False, False, 1.0)
+            ext().gemm(xb, su, sgu[:, Fs:], False, False, False, 1.0)
+            ext().swiglu_fwd(sgu, shh)
         out = torch.empty(T, D, **f32)
         ext().gemm(shh, sd, out, False, False, False, 1.0)
         ext().moe_combine(y, pos, topw, out)
@@ -202,14 +229,20 @@ class MoEFn(torch.autograd.Function):
         db = dout.to(torch.bfloat16)
         # shared expert
         sg, su, sd = _work(mod.shared_w_gate), _work(mod.shared_w_up), _work(mod.shared_w_down)
-        dsh = torch.empty_like(shh)
-        ext().gemm(db, sd, dsh, False, True, False, 1.0)
-        ext().gemm(shh, db, main_grad(mod.shared_w_down), True, False, True, 1.0)
         dsgu = torch.empty_like(sgu)
-        ext().swiglu_bwd(dsh, sgu, dsgu)
         dx = torch.empty(T, D, dtype=torch.float32, device=dev)
-        ext().gemm(dsgu[:, :Fs], sg, dx, False, True, False, 1.0)
-        ext().gemm(dsgu[:, Fs:], su, dx, False, True, True, 1.0)
+        if _shared_fused(T, Fs):
+            gs1, gc1, gtf = _one_group(T, (Fs + _bn(Fs) - 1) // _bn(Fs), dev)
+            ext().grouped_gemm_m_swiglu_bwd(db, sd.unsqueeze(0), sgu, dsgu, gs1, gc1, gtf)
+            gtd = _one_group(T, (D + _bn(D) - 1) // _bn(D), dev)[2]
+            ext().grouped_gemm_m_cat2(dsgu, sg.unsqueeze(0), su.unsqueeze(0), dx, gs1, gc1, gtd)
+        else:
+            dsh = torch.empty_like(shh)
+            ext().gemm(db, sd, dsh, False, True, False, 1.0)
+            ext().swiglu_bwd(dsh, sgu, dsgu)
+            ext().gemm(dsgu[:, :Fs], sg, dx, False, True, False, 1.0)
+            ext().gemm(dsgu[:, Fs:], su, dx, False, True, True, 1.0)
+        ext().gemm(shh, db, main_grad(mod.shared_w_down), True, False, True, 1.0)
         ext().gemm(xb, dsgu[:, :Fs], main_grad(mod.shared_w_gate), True, False, True, 1.0)
         ext().gemm(xb, dsgu[:, Fs:], main_grad(mod.shared_w_up), True, False, True, 1.0)
         # combine backward

@@ -197,15 +197,16 @@ def test_kda_layer_grads_match_cpu():
         assert rel(getattr(mg, name).main_grad.cpu(), getattr(m, name).grad) < 5e-2, name
 
 
+@pytest.mark.parametrize("S", [96, 128])   # 128: whole-tile shared expert (fused kernels)
 @pytest.mark.parametrize("router_type", ["sigmoid_bias", "softmax"])
-def test_moe_layer_fwd_bwd(router_type):
+def test_moe_layer_fwd_bwd(router_type, S):
     from hanuman_b200.models.layers import MoE
     torch.manual_seed(8)
     D, Fh, N, K = 256, 128, 8, 2
     m = MoE(D, Fh, N, K, 1, 0.5, 2.5, torch.Generator().manual_seed(2), router_type=router_type)
     with torch.no_grad():
         m.bias.copy_(torch.randn(N) * 0.1)
-    B, S = 2, 96
+    B = 2
     h = torch.randn(B, S, D).bfloat16()
     hc = h.float().requires_grad_()
     yc, auxc = m(hc, torch.float32)
@@ -225,7 +226,7 @@ def test_moe_layer_fwd_bwd(router_type):
     loss_g.backward()
     assert rel(hg.grad.cpu(), hc.grad) < 5e-2
     for name in ("expert_w_gate", "expert_w_up", "expert_w_down", "shared_w_gate",
-                 "shared_w_down", "router"):
+                 "shared_w_up", "shared_w_down", "router"):
         assert rel(getattr(mg, name).main_grad.cpu(), getattr(m, name).grad) < 5e-2, name
 
 
