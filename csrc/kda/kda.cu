@@ -860,7 +860,8 @@ __global__ void prep_fwd_kernel(const __nv_bfloat16* __restrict__ raw, long long
 }
 
 // Backward part 1 (block per head, warp per token): gradients at the conv
-// outputs of q/k/v (fp32, [T, 3*HK]), df [T, HK], dbraw [T, H]; d dt_bias and
+// outputs of q/k/v (fp32, [T, 3*HK]), df [T, HK] (bf16: it only feeds the
+// f_proj GEMMs), dbraw [T, H]; d dt_bias and
 // d a_log of the block's head are summed in each lane's registers over its
 // tokens, then reduced through shared memory with one global atomic each.
 template <int DK>
@@ -872,7 +873,7 @@ __global__ void __launch_bounds__(256, DK >= 128 ? 2 : 3) prep_bwd1_kernel(const
                                  const float* __restrict__ dq, const float* __restrict__ dk,
                                  const float* __restrict__ dv, const float* __restrict__ dg,
                                  const float* __restrict__ dbeta, float* __restrict__ dconv,
-                                 float* __restrict__ df, float* __restrict__ dbraw,
+                                 __nv_bfloat16* __restrict__ df, float* __restrict__ dbraw,
                                  float* __restrict__ d_alog, float* __restrict__ d_dtb) {
   constexpr int NP = (DK + 63) / 64;
   __shared__ float s_dtb[DK + 1];  // this block's head: d dt_bias, then d a_log
@@ -931,7 +932,7 @@ __global__ void __launch_bounds__(256, DK >= 128 ? 2 : 3) prep_bwd1_kernel(const
             dz[e] = dgv[e] * (1.f - sig);
           }
         }
-        *reinterpret_cast<float2*>(df + o) = make_float2(dz[0], dz[1]);
+        *reinterpret_cast<__nv_bfloat162*>(df + o) = __floats2bfloat162_rn(dz[0], dz[1]);
         acc_dtb[j].x += dz[0];
         acc_dtb[j].y += dz[1];
       }
@@ -1191,6 +1192,7 @@ void kda_prep_bwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::
                   torch::Tensor dwk, torch::Tensor dwv) {
   const int T = dq.size(0), H = dq.size(1), DKV = dq.size(2);
   HB_CHECK(raw.stride(0) % 2 == 0 && DKV % 2 == 0, "kda_prep: even row stride and head dim");
+  HB_CHECK(df.scalar_type() == at::kBFloat16 && df.is_contiguous(), "kda_prep_bwd: df must be contiguous bf16");
   // blocks: (token runs) x (heads); about 8 resident blocks per SM in all
   const int gx = (int)std::max<long long>(
       1, std::min<long long>(((long long)T + 7) / 8, ((long long)num_sms() * 8 + H - 1) / H));
@@ -1202,7 +1204,7 @@ void kda_prep_bwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::
         wv.data_ptr<float>(), f.data_ptr<float>(), a_log.data_ptr<float>(), dt_bias.data_ptr<float>(),
         beta.data_ptr<float>(), (int)gate_mode, T, (int)S, H, dq.data_ptr<float>(), dk.data_ptr<float>(),
         dv.data_ptr<float>(), dg.data_ptr<float>(), dbeta.data_ptr<float>(), dconv.data_ptr<float>(),
-        df.data_ptr<float>(), dbraw.data_ptr<float>(), d_alog.data_ptr<float>(), d_dtb.data_ptr<float>());
+        (__nv_bfloat16*)df.data_ptr(), dbraw.data_ptr<float>(), d_alog.data_ptr<float>(), d_dtb.data_ptr<float>());
   };
   if (DKV == 16) launch(std::integral_constant<int, 16>{});
   else if (DKV == 32) launch(std::integral_constant<int, 32>{});

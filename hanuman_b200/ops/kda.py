@@ -122,7 +122,7 @@ class KdaFrontFn(torch.autograd.Function):
         dq, dk, dv, dg = z(dq), z(dk), z(dv), z(dg)
         dbeta = torch.zeros(T, H, device=dev) if dbeta is None else dbeta.float().contiguous()
         dconv = torch.empty(T, 3 * HK, dtype=torch.float32, device=dev)
-        df = torch.empty(T, HK, dtype=torch.float32, device=dev)
+        df = torch.empty(T, HK, dtype=torch.bfloat16, device=dev)
         dbraw = torch.empty(T, H, dtype=torch.float32, device=dev)
         d_alog = torch.zeros(H, dtype=torch.float32, device=dev)
         d_dtb = torch.zeros(HK, dtype=torch.float32, device=dev)
@@ -135,7 +135,7 @@ class KdaFrontFn(torch.autograd.Function):
         p_wq, p_wk, p_wv, p_f0, p_g0, p_wb, p_f1, p_g1 = ctx.params
         # low-rank second stage: d f0 / d g0 straight into their dbig columns
         f0s, g0s = big[:, 3 * HK:3 * HK + K], big[:, 3 * HK + K:]
-        dfb = df.to(torch.bfloat16)
+        dfb = df
         _gemm_or_narrow(dfb, f1w, dbig[:, 3 * HK:3 * HK + K], False, True, False)
         _gemm_or_narrow(f0s, dfb, main_grad(p_f1), True, False, True)
         if dgl is None:
