@@ -15,6 +15,7 @@ void grouped_gemm_k(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Te
                     torch::Tensor grp_count, bool accumulate);
 void grouped_gemm_m_swiglu_bwd(torch::Tensor a, torch::Tensor b, torch::Tensor gu, torch::Tensor dgu,
                                torch::Tensor grp_start, torch::Tensor grp_count, torch::Tensor grp_tile_start);
+void gemm_kseg(torch::Tensor a, std::vector<torch::Tensor> bs, torch::Tensor c, bool accumulate);
 void grouped_gemm_m_swiglu_fwd(torch::Tensor a, torch::Tensor b1, torch::Tensor b2, torch::Tensor h,
                                torch::Tensor gu, torch::Tensor grp_start, torch::Tensor grp_count,
                                torch::Tensor grp_tile_start);
@@ -136,6 +137,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grouped_gemm_m_gather", &hb::grouped_gemm_m_gather);
   m.def("grouped_gemm_m_swiglu_bwd", &hb::grouped_gemm_m_swiglu_bwd);
   m.def("grouped_gemm_m_cat2", &hb::grouped_gemm_m_cat2);
+  m.def("gemm_kseg", &hb::gemm_kseg);
   m.def("grouped_gemm_m_swiglu_fwd", &hb::grouped_gemm_m_swiglu_fwd);
   m.def("rmsnorm_fwd", &hb::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &hb::rmsnorm_bwd);

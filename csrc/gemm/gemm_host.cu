@@ -2,6 +2,7 @@
 // tile counts, and dispatch to the instantiation units.
 #include <cstdlib>
 #include <string>
+#include <vector>
 
 #include "gemm_kernel.cuh"
 #include "gemm_pair.cuh"
@@ -123,6 +124,58 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool trans_a, bool 
     gemm_dispatch_dense_amn(BN, !trans_b, epi, ta, tb, args, grid);
   else
     gemm_dispatch_dense_ak(BN, !trans_b, epi, ta, tb, args, grid);
+}
+
+// c (+)= sum_s a[:, k_s : k_s + K_s] @ b_s^T for K-major b_s [N, K_s]: the
+// input gradient of several projections whose output gradients sit side by
+// side in a.  One CTA-pair launch (a K-segmented B) where the pair path
+// applies, else one accumulating GEMM per segment.
+void gemm_kseg(torch::Tensor a, std::vector<torch::Tensor> bs, torch::Tensor c, bool accumulate) {
+  check_bf16(a, "a");
+  HB_CHECK(!bs.empty() && (int)bs.size() <= KSEG_MAX, "gemm_kseg: 1..6 segments");
+  HB_CHECK(a.dim() == 2 && a.stride(1) == 1 && c.dim() == 2 && c.stride(1) == 1, "gemm_kseg: 2-D, unit column stride");
+  const int M = a.size(0), N = c.size(1);
+  int K = 0;
+  bool aligned = true;
+  for (auto& b : bs) {
+    check_bf16(b, "b");
+    HB_CHECK(b.dim() == 2 && b.stride(1) == 1 && b.size(0) == N, "gemm_kseg: each b must be [N, K_s]");
+    aligned = aligned && b.size(1) % GEMM_BK == 0;
+    K += b.size(1);
+  }
+  HB_CHECK(a.size(1) == K && c.size(0) == M, "gemm_kseg: shapes differ");
+  if (M == 0 || N == 0) return;
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int epi = epi_of(c, accumulate);
+  const long long ptiles = (long long)((M + PAIR_BM - 1) / PAIR_BM) * ((N + PAIR_BN - 1) / PAIR_BN);
+  if (aligned && M >= 128 && N >= 256 && use_pair(ptiles)) {
+    KSegMaps ks{};
+    int k0 = 0;
+    for (size_t i = 0; i < bs.size(); ++i) {
+      ks.seg[i] = tmap_bf16_2d(bs[i].data_ptr(), N, bs[i].size(1), bs[i].stride(0), 64, 128);
+      ks.seg_k[i] = k0;
+      k0 += bs[i].size(1);
+    }
+    ks.seg_k[bs.size()] = k0;
+    ks.nseg = (int)bs.size();
+    CUtensorMap ta = tmap_bf16_2d(a.data_ptr(), M, K, a.stride(0), 64, GEMM_BM);
+    GemmArgs pa = base_args(c, 1.0);
+    pa.M = M;
+    pa.N = N;
+    pa.K = K;
+    pa.tiles_m = (M + PAIR_BM - 1) / PAIR_BM;
+    pa.tiles_n = (N + PAIR_BN - 1) / PAIR_BN;
+    pa.num_tiles = pa.tiles_m * pa.tiles_n;
+    const int grid = 2 * std::min(pa.num_tiles, num_sms() / 2);
+    gemm_dispatch_pair(DENSE, false, false, epi, ta, ks.seg[0], pa, grid, &ks);
+    return;
+  }
+  int k0 = 0;
+  for (size_t i = 0; i < bs.size(); ++i) {
+    const int ks_ = bs[i].size(1);
+    gemm(a.narrow(1, k0, ks_), bs[i], c, false, true, accumulate || i > 0, 1.0, c10::nullopt);
+    k0 += ks_;
+  }
 }
 
 // Grouped over M (MoE forward / input-gradient):

@@ -27,6 +27,15 @@ namespace hb {
 // warp 0: TMA producer, warp 1: MMA issuer (leader CTA), warps 2..9: epilogue
 // (two warps per TMEM lane quadrant, alternate 32-column chunks)
 constexpr int PAIR_THREADS = 64 + 32 * GEMM_EPI_WARPS;
+// K split into segments, each with its own K-major B (DENSE, !B_MN only):
+// C = sum_s A[:, k_s .. k_s+1) B_s^T, one write of C.  nseg 0 = one B (tmB).
+constexpr int KSEG_MAX = 6;
+struct alignas(64) KSegMaps {
+  CUtensorMap seg[KSEG_MAX];
+  int seg_k[KSEG_MAX + 1];   // K start of each segment (multiples of 64), then K
+  int nseg;
+};
+
 constexpr int PAIR_BM = 256;   // rows per pair tile (128 per CTA)
 constexpr int PAIR_BN = 256;   // columns per pair tile (B: 128 per CTA)
 constexpr int PAIR_A_BYTES = 128 * GEMM_BK * 2;
@@ -72,7 +81,7 @@ __device__ __forceinline__ bool get_pair_tile(const GemmArgs& a, int t, TileInfo
 template <bool A_MN, bool B_MN, int MODE, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const GemmArgs args) {
+                     const GemmArgs args, const __grid_constant__ KSegMaps ks) {
   static_assert(MODE == DENSE || MODE == GROUPED_K, "pair kernel: dense or grouped-K");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -144,7 +153,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
             tma_load_2d_pair(sa + 8192, &tmA, fb, mr + 64, kc);
           }
           if (!B_MN) {
-            tma_load_2d_pair(sb, &tmB, fb, kc, nr);
+            if (ks.nseg > 0) {
+              int sg = 0;
+              while (sg + 1 < ks.nseg && kc >= ks.seg_k[sg + 1]) ++sg;
+              tma_load_2d_pair(sb, &ks.seg[sg], fb, kc - ks.seg_k[sg], nr);
+            } else {
+              tma_load_2d_pair(sb, &tmB, fb, kc, nr);
+            }
           } else {
             tma_load_2d_pair(sb, &tmB, fb, nr, kc);
             tma_load_2d_pair(sb + 8192, &tmB, fb, nr + 64, kc);
@@ -299,18 +314,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
 }
 
 template <bool A_MN, bool B_MN, int MODE, int EPI>
-void gemm_pair_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid) {
+void gemm_pair_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
+                      const KSegMaps* ks = nullptr) {
   auto kern = gemm_pair_kernel<A_MN, B_MN, MODE, EPI>;
   static bool configured = false;
   if (!configured) {
     HB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM));
     configured = true;
   }
-  kern<<<grid, PAIR_THREADS, PAIR_SMEM, cur_stream()>>>(ta, tb, args);
+  static const KSegMaps none{};
+  kern<<<grid, PAIR_THREADS, PAIR_SMEM, cur_stream()>>>(ta, tb, args, ks ? *ks : none);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
 void gemm_dispatch_pair(int mode, bool a_mn, bool b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
-                        const GemmArgs& args, int grid);
+                        const GemmArgs& args, int grid, const KSegMaps* ks = nullptr);
 
 }  // namespace hb

@@ -147,10 +147,15 @@ class KdaFrontFn(torch.autograd.Function):
         # first stage: one fp32 input gradient over all six projections
         dx = torch.empty(xb.shape, dtype=torch.float32, device=dev) \
             if ctx.needs_input_grad[0] else None
+        first = (wq, wk, wv, wf0, wg0)
+        kseg = dx is not None and all(w.shape[1] % 64 == 0 for w in first)
+        if kseg:
+            # dx = dbig @ [wq|wk|wv|f_proj0|g_proj0]^T: one GEMM, K split by weight
+            ext().gemm_kseg(dbig, list(first), dx, False)
         off = 0
-        for i, (w, p) in enumerate(zip((wq, wk, wv, wf0, wg0), (p_wq, p_wk, p_wv, p_f0, p_g0))):
+        for i, (w, p) in enumerate(zip(first, (p_wq, p_wk, p_wv, p_f0, p_g0))):
             sl = dbig[:, off:off + w.shape[1]]
-            if dx is not None:
+            if dx is not None and not kseg:
                 _gemm_or_narrow(sl, w, dx, False, True, i > 0)
             _gemm_or_narrow(xb, sl, main_grad(p), True, False, True)
             off += w.shape[1]

@@ -308,3 +308,22 @@ def test_grouped_m_swiglu_fwd_matches_separate_kernels():
         assert torch.equal(gu[s:s + n], gu_ref[s:s + n]), s
         seg = slice(s, s + (n + 127) // 128 * 128)
         assert torch.equal(h[seg], h_ref[seg]), s
+
+
+@pytest.mark.parametrize("M", [32768, 200])   # pair path (>= 74 pair tiles) / per-segment fallback
+def test_gemm_kseg_matches_fp32_reference(M):
+    """c = sum_s a[:, k_s:k_s+K_s] @ b_s^T (K-segmented B) against fp32 PyTorch."""
+    torch.manual_seed(10)
+    dev = "cuda"
+    N = 512
+    ks = [256, 128, 64, 64]
+    a = torch.randn(M, sum(ks), device=dev).bfloat16()
+    bs = [(torch.randn(N, k, device=dev) * 0.1).bfloat16() for k in ks]
+    c = torch.full((M, N), float("nan"), device=dev)
+    _ext().gemm_kseg(a, bs, c, False)
+    ref = a.float() @ torch.cat([b.float() for b in bs], 1).t()
+    torch.cuda.synchronize()
+    assert (c - ref).norm() / ref.norm() < 1e-5
+    c2 = torch.ones(M, N, device=dev)
+    _ext().gemm_kseg(a, bs, c2, True)
+    assert (c2 - 1.0 - ref).norm() / ref.norm() < 1e-5
