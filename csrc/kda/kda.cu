@@ -157,6 +157,16 @@ HB_DEVICE void load_rows(const Ptrs& p, const float* x, int b, int h, int n, flo
   }
 }
 
+// In shared memory the cumulative decays are kept as G' = G log2(e), so every
+// e^{G_t - G_s} of the chunk kernels is one 2^{G'_t - G'_s} on the MUFU unit
+// (PTX ex2.approx), without a separate multiply by log2(e).
+constexpr float kLog2e = 1.4426950408889634f;
+HB_DEVICE float exp2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // q, k, v, g and beta of one chunk; g is cumulated in place into G
 // (registers per column, so the 32 loads of a column are independent).
 template <int DK, int C>
@@ -179,7 +189,7 @@ HB_DEVICE void load_chunk(const Ptrs& p, int b, int h, int n, float* q, float* k
 #pragma unroll
     for (int r = 1; r < C; ++r) x[r] += x[r - 1];
 #pragma unroll
-    for (int r = 0; r < C; ++r) G[r * L + c] = x[r];
+    for (int r = 0; r < C; ++r) G[r * L + c] = x[r] * kLog2e;  // base-2 log decays
   }
   __syncthreads();
 }
@@ -209,8 +219,8 @@ HB_DEVICE void pair_products(const float* q, const float* k, const float* G, con
         const int s = s0 + j * nw;
         if (s >= C) break;
         const float4 ks = ld4(k + s * L + c), gs = ld4(G + s * L + c);
-        const float e0 = __expf(gt.x - gs.x) * ks.x, e1 = __expf(gt.y - gs.y) * ks.y;
-        const float e2 = __expf(gt.z - gs.z) * ks.z, e3 = __expf(gt.w - gs.w) * ks.w;
+        const float e0 = exp2_fast(gt.x - gs.x) * ks.x, e1 = exp2_fast(gt.y - gs.y) * ks.y;
+        const float e2 = exp2_fast(gt.z - gs.z) * ks.z, e3 = exp2_fast(gt.w - gs.w) * ks.w;
         a[j] += kt.x * e0 + kt.y * e1 + kt.z * e2 + kt.w * e3;
         pp[j] += qt.x * e0 + qt.y * e1 + qt.z * e2 + qt.w * e3;
       }
@@ -286,7 +296,7 @@ __global__ void __launch_bounds__(256) intra_fwd_kernel(Ptrs p) {
       2 * DK, N,
       [&](int t, int col) {
         return col < DK ? bet[t] * v[t * L + col]
-                        : bet[t] * bet[t] * k[t * L + col - DK] * __expf(G[t * L + col - DK]);
+                        : bet[t] * bet[t] * k[t * L + col - DK] * exp2_fast(G[t * L + col - DK]);
       },
       [&](int t, int col, float x) {
         if (col < DK) v[t * L + col] = x;
@@ -301,18 +311,18 @@ __global__ void __launch_bounds__(256) intra_fwd_kernel(Ptrs p) {
     const float4 kk = ld4(k + si), gg = ld4(G + si), qq = ld4(q + si), gc = ld4(GC + c);
     st4(p.Ut + co + r * DK + c, ld4(v + si));
     st4(p.Wt + co + r * DK + c, ld4(Wt + si));
-    st4(p.Kh + co + r * DK + c, make_float4(kk.x * __expf(gc.x - gg.x), kk.y * __expf(gc.y - gg.y),
-                                            kk.z * __expf(gc.z - gg.z), kk.w * __expf(gc.w - gg.w)));
+    st4(p.Kh + co + r * DK + c, make_float4(kk.x * exp2_fast(gc.x - gg.x), kk.y * exp2_fast(gc.y - gg.y),
+                                            kk.z * exp2_fast(gc.z - gg.z), kk.w * exp2_fast(gc.w - gg.w)));
     const float sc = p.scale;
-    st4(p.Qg + co + r * DK + c, make_float4(sc * qq.x * __expf(gg.x), sc * qq.y * __expf(gg.y),
-                                            sc * qq.z * __expf(gg.z), sc * qq.w * __expf(gg.w)));
+    st4(p.Qg + co + r * DK + c, make_float4(sc * qq.x * exp2_fast(gg.x), sc * qq.y * exp2_fast(gg.y),
+                                            sc * qq.z * exp2_fast(gg.z), sc * qq.w * exp2_fast(gg.w)));
   }
   const long long po = chunk_off(p, b, h, n, C * C);
   for (int i = threadIdx.x; i < C * C / 4; i += blockDim.x) {
     const int r = i / (C / 4), c = (i % (C / 4)) * 4;
     st4(p.Pm + po + r * C + c, ld4(P + r * LC + c));
   }
-  for (int c = threadIdx.x; c < DK; c += blockDim.x) p.gC[chunk_off(p, b, h, n, DK) + c] = __expf(GC[c]);
+  for (int c = threadIdx.x; c < DK; c += blockDim.x) p.gC[chunk_off(p, b, h, n, DK) + c] = exp2_fast(GC[c]);
 }
 
 // ------------------------------------------------------------------ state fwd
@@ -552,7 +562,7 @@ __global__ void __launch_bounds__(NTB<DK>(), DK >= 128 ? 1 : 2) intra_bwd_kernel
       2 * DK, N,
       [&](int t, int col) {
         return col < DK ? bet[t] * v[t * L + col]
-                        : bet[t] * bet[t] * k[t * L + col - DK] * __expf(G[t * L + col - DK]);
+                        : bet[t] * bet[t] * k[t * L + col - DK] * exp2_fast(G[t * L + col - DK]);
       },
       [&](int t, int col, float x) {
         if (col < DK) U[t * L + col] = x;
@@ -560,7 +570,7 @@ __global__ void __launch_bounds__(NTB<DK>(), DK >= 128 ? 1 : 2) intra_bwd_kernel
       });
   for (int e = threadIdx.x; e < C * DK; e += blockDim.x) {
     const int t = e / DK, c = e % DK;
-    T1[t * L + c] = k[t * L + c] * __expf(GC[c] - G[t * L + c]);
+    T1[t * L + c] = k[t * L + c] * exp2_fast(GC[c] - G[t * L + c]);
   }
   __syncthreads();
   // dU = P^T dO
@@ -620,7 +630,7 @@ __global__ void __launch_bounds__(NTB<DK>(), DK >= 128 ? 1 : 2) intra_bwd_kernel
   for (int c = threadIdx.x; c < DK; c += blockDim.x) {
     float s = 0.f;
 #pragma unroll 8
-    for (int t = 0; t < C; ++t) s += T1[t * L + c] * k[t * L + c] * __expf(GC[c] - G[t * L + c]);
+    for (int t = 0; t < C; ++t) s += T1[t * L + c] * k[t * L + c] * exp2_fast(GC[c] - G[t * L + c]);
     red[c] = s;
   }
   __syncthreads();
@@ -629,7 +639,7 @@ __global__ void __launch_bounds__(NTB<DK>(), DK >= 128 ? 1 : 2) intra_bwd_kernel
     const int t = e / DK, c = e % DK;
     const int si = t * L + c;
     const float dkh = T1[si], dqg = T2[si];
-    const float ed = __expf(GC[c] - G[si]), eg = __expf(G[si]);
+    const float ed = exp2_fast(GC[c] - G[si]), eg = exp2_fast(G[si]);
     T1[si] = dkh * ed;
     U[si] = -dkh * k[si] * ed + dqg * scale * q[si] * eg;
     T2[si] = dqg * scale * eg;
@@ -652,7 +662,7 @@ __global__ void __launch_bounds__(NTB<DK>(), DK >= 128 ? 1 : 2) intra_bwd_kernel
   mm<C, C, DK, false, true>(dA, LC, X, L, dU, L, -1.f, false);
   __syncthreads();
   solve_cols<C, false>(
-      DK, N, [&](int t, int c) { return bet[t] * bet[t] * k[t * L + c] * __expf(G[t * L + c]); },
+      DK, N, [&](int t, int c) { return bet[t] * bet[t] * k[t * L + c] * exp2_fast(G[t * L + c]); },
       [&](int t, int c, float x) { dU[t * L + c] = x; });
   __syncthreads();
   mm<C, C, DK, false, true>(dA, LC, Y, L, dU, L, -1.f, true);
@@ -668,7 +678,7 @@ __global__ void __launch_bounds__(NTB<DK>(), DK >= 128 ? 1 : 2) intra_bwd_kernel
     for (int s = lane; s < t; s += 32) s1 += A[t * LC + s] * dA[t * LC + s];
     for (int c = lane; c < DK; c += 32) {
       const int si = t * L + c;
-      s2 += k[si] * __expf(G[si]) * Y[si];
+      s2 += k[si] * exp2_fast(G[si]) * Y[si];
       s3 += v[si] * X[si];
     }
     s1 = warp_sum(s1);
@@ -685,7 +695,7 @@ __global__ void __launch_bounds__(NTB<DK>(), DK >= 128 ? 1 : 2) intra_bwd_kernel
   for (int e = threadIdx.x; e < C * DK; e += blockDim.x) {
     const int t = e / DK, c = e % DK;
     const int si = t * L + c;
-    const float eg = __expf(G[si]);
+    const float eg = exp2_fast(G[si]);
     const float dkg = bet[t] * bet[t] * Y[si];
     T1[si] += dkg * eg;
     U[si] += dkg * k[si] * eg;
@@ -699,7 +709,7 @@ __global__ void __launch_bounds__(NTB<DK>(), DK >= 128 ? 1 : 2) intra_bwd_kernel
     const float gt = G[si];
     float sp = 0.f, sa = 0.f;
     for (int s = 0; s <= t; ++s) {
-      const float ks = k[s * L + c] * __expf(gt - G[s * L + c]);
+      const float ks = k[s * L + c] * exp2_fast(gt - G[s * L + c]);
       sp += P[t * LC + s] * ks;
       sa += dA[t * LC + s] * ks;
     }
@@ -716,7 +726,7 @@ __global__ void __launch_bounds__(NTB<DK>(), DK >= 128 ? 1 : 2) intra_bwd_kernel
     const float gs = G[si];
     float acc = 0.f;
     for (int t = s; t < C; ++t) {
-      const float ee = __expf(G[t * L + c] - gs);
+      const float ee = exp2_fast(G[t * L + c] - gs);
       acc += (scale * P[t * LC + s] * q[t * L + c] + dA[t * LC + s] * k[t * L + c]) * ee;
     }
     T1[si] += acc;
@@ -728,7 +738,7 @@ __global__ void __launch_bounds__(NTB<DK>(), DK >= 128 ? 1 : 2) intra_bwd_kernel
     float x[C];
 #pragma unroll
     for (int r = 0; r < C; ++r) x[r] = U[r * L + c];
-    x[C - 1] += red[c] + dgc[c] * __expf(GC[c]);
+    x[C - 1] += red[c] + dgc[c] * exp2_fast(GC[c]);
 #pragma unroll
     for (int r = C - 2; r >= 0; --r) x[r] += x[r + 1];
 #pragma unroll
