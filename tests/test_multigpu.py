@@ -20,6 +20,18 @@ def _port():
     return p
 
 
+def _losses_match(la, lb):
+    """Step 1 sees identical weights and the same forward kernels, so its loss
+    agrees to rounding.  Later steps inherit the run-to-run differences of the
+    atomically summed gradients (embedding, decay biases); AdamW's first
+    updates are sign-like, so a near-zero gradient element can move by 2 lr
+    either way and the loss drifts (a 1.1e-3 relative gap at step 3 was seen
+    once, 1e-5 on a rerun of the same build)."""
+    assert abs(la[0] - lb[0]) < 1e-4 * abs(la[0]), (la, lb)
+    for a, b in zip(la[1:], lb[1:]):
+        assert abs(a - b) < 3e-3 * abs(a), (la, lb)
+
+
 def _worker(rank, world, port, out_path):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
@@ -71,14 +83,12 @@ def test_p2p_transport_matches_nccl(tmp_path):
     # the fused expert-weight gather (P1) computes exactly what the replicated
     # weights compute: same tiles, same kernels, only the source of B differs
     (lg, sg), (lp, sp) = res["gather"], res[True]
-    for a, b in zip(lg, lp):
-        assert abs(a - b) < 1e-3 * abs(a), (lg, lp)
+    _losses_match(lg, lp)
     for k in sp:
         diff = (sg[k] - sp[k]).abs()
         assert diff.max().item() <= 6 * 3e-4 + 1e-5, (k, diff.max().item())
     (l0, s0), (l1, s1) = res[False], res[True]
-    for a, b in zip(l0, l1):
-        assert abs(a - b) < 1e-3 * abs(a), (l0, l1)
+    _losses_match(l0, l1)
     # The embedding gradient is summed with atomics, so the two runs differ in the
     # last bits; AdamW's first steps are sign-like (|update| ~ lr per step), so an
     # element can move by up to 2 * lr per step between runs (lr = 3e-4, 3 steps).
