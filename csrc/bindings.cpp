@@ -83,6 +83,18 @@ void kda_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
              double scale, torch::Tensor dout, torch::Tensor Wt, torch::Tensor Kh, torch::Tensor Qg,
              torch::Tensor Pm, torch::Tensor gC, torch::Tensor states, torch::Tensor dstates,
              torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor dg, torch::Tensor dbeta);
+void kda_fwd64(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
+               double scale, torch::Tensor o, torch::Tensor Wt, torch::Tensor Ut, torch::Tensor Kh,
+               torch::Tensor Qg, torch::Tensor Pm, torch::Tensor gC, torch::Tensor states,
+               torch::Tensor Linv, torch::Tensor Am, torch::Tensor U);
+void kda_bwd64(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
+               double scale, torch::Tensor dout, torch::Tensor Wt, torch::Tensor Ut, torch::Tensor Kh,
+               torch::Tensor Qg, torch::Tensor Pm, torch::Tensor gC, torch::Tensor states,
+               torch::Tensor Linv, torch::Tensor Am, torch::Tensor U, torch::Tensor dstates,
+               torch::Tensor dU, torch::Tensor dUp, torch::Tensor dSq, torch::Tensor dQg,
+               torch::Tensor dKh, torch::Tensor dWt, torch::Tensor dP, torch::Tensor dgC,
+               torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor dg, torch::Tensor dbeta);
+void kda64_set_profile(c10::optional<torch::Tensor> counters);
 void kda_prep_fwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::Tensor wv, torch::Tensor f,
                   torch::Tensor a_log, torch::Tensor dt_bias, torch::Tensor braw, int64_t gate_mode,
                   int64_t S, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
@@ -121,11 +133,21 @@ static int64_t read_status() {
 }
 static void clear_status() { HB_CUDA_CHECK(cudaMemset(hb::status_ptr(), 0, sizeof(int))); }
 
+// The status word of the current device as a one-element int32 CUDA tensor
+// (a view: it lives as long as the process), for asynchronous copies.
+static torch::Tensor status_view() {
+  int dev = 0;
+  HB_CUDA_CHECK(cudaGetDevice(&dev));
+  return torch::from_blob(hb::status_ptr(), {1},
+                          torch::TensorOptions().dtype(torch::kInt32).device(torch::kCUDA, dev));
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "hanuman_b200 sm_100a kernels";
   m.def("num_sms", &hb::num_sms);
   m.def("read_status", &read_status, "read the device status word (0 = ok)");
   m.def("clear_status", &clear_status);
+  m.def("status_view", &status_view, "the device status word as an int32 tensor view");
   m.def("set_wait_budget_ns", &hb::set_wait_budget_ns);
   m.def("gemm", &hb::gemm, "c (+)= op(a) @ op(b) on tcgen05", py::arg("a"), py::arg("b"),
         py::arg("c"), py::arg("trans_a"), py::arg("trans_b"), py::arg("accumulate"),
@@ -167,6 +189,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kda_chunk_size", &hb::kda_chunk_size);
   m.def("kda_fwd", &hb::kda_fwd);
   m.def("kda_bwd", &hb::kda_bwd);
+  m.def("kda_fwd64", &hb::kda_fwd64);
+  m.def("kda_bwd64", &hb::kda_bwd64);
+  m.def("kda64_set_profile", &hb::kda64_set_profile);
   m.def("kda_prep_fwd", &hb::kda_prep_fwd);
   m.def("kda_prep_bwd", &hb::kda_prep_bwd);
   m.def("p2p_barrier", &hb::p2p_barrier);

@@ -11,7 +11,10 @@
 //                        stored into the working copy of EVERY rank (peer
 //                        stores), which replaces the parameter all-gather
 // Plain ld/st to peer addresses only: no TMA, no multicast.  A wait that runs
-// out of budget records kErrTimeoutPeer in the status word and returns.
+// out of budget records kErrTimeoutPeer in the status word and returns; the
+// reduce-scatter and update kernels read the status word first and do nothing
+// (no peer load or store) once any earlier kernel recorded an error, so a rank
+// whose peers stopped never reads gradients that may not be final.
 #include <torch/extension.h>
 
 #include "../common/host.h"
@@ -66,7 +69,8 @@ __device__ __forceinline__ float block_sum(float v) {
 // out[i] = scale * sum_r peers[r][off + i]  (float4 vectorised); sumsq += out^2
 __global__ void reduce_scatter_kernel(const long long* __restrict__ peers, int world, long long off,
                                       long long n, float* __restrict__ out, float scale,
-                                      float* __restrict__ sumsq) {
+                                      float* __restrict__ sumsq, const int* __restrict__ status) {
+  if (*reinterpret_cast<const volatile int*>(status) != 0) return;
   float ss = 0.f;
   const long long n4 = n / 4;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
@@ -104,7 +108,9 @@ __global__ void update_bcast_kernel(float* __restrict__ p, const float* __restri
                                     float* __restrict__ v, const float* __restrict__ decay,
                                     const long long* __restrict__ work_peers, int world, long long off,
                                     long long n, int mode, float lr, float wd, float b1, float b2,
-                                    float eps, float bc1, float bc2, const float* __restrict__ coef_ptr) {
+                                    float eps, float bc1, float bc2, const float* __restrict__ coef_ptr,
+                                    const int* __restrict__ status) {
+  if (*reinterpret_cast<const volatile int*>(status) != 0) return;
   const float coef = *coef_ptr;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x) {
@@ -152,7 +158,7 @@ void p2p_reduce_scatter(torch::Tensor peers, int64_t world, int64_t off, int64_t
   if (n == 0) return;
   reduce_scatter_kernel<<<grid_for(n / 4 + 1, 256), 256, 0, cur_stream()>>>(
       reinterpret_cast<const long long*>(peers.data_ptr<int64_t>()), (int)world, off, n,
-      out.data_ptr<float>(), (float)scale, sumsq.data_ptr<float>());
+      out.data_ptr<float>(), (float)scale, sumsq.data_ptr<float>(), status_ptr());
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -173,7 +179,7 @@ void p2p_update_bcast(torch::Tensor p, torch::Tensor g, torch::Tensor m, c10::op
     update_bcast_kernel<W, M><<<grid, 256, 0, cur_stream()>>>(
         p.data_ptr<float>(), g.data_ptr<float>(), mptr, vp, decay.data_ptr<float>(), wp, (int)world, off,
         n, (int)mode, (float)lr, (float)wd, (float)b1, (float)b2, (float)eps, bc1, bc2,
-        coef.data_ptr<float>());
+        coef.data_ptr<float>(), status_ptr());
   };
   const bool mb = m.scalar_type() == at::kBFloat16;
   if (work_bf16 && mb) launch(__nv_bfloat16(), (__nv_bfloat16*)m.data_ptr());

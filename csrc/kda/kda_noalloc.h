@@ -10,6 +10,8 @@
 //
 // The caller passes device pointers to the inputs and the output and a stream;
 // q, k, v, g and o must be 16-byte aligned (HB_NOALLOC_BAD_SHAPE otherwise).
+// Head dims 16, 32 and 64 are accepted; any other DK (the allocating entry
+// point also takes 128) returns HB_NOALLOC_BAD_HEAD_DIM.
 // The chunk intermediates live in a file-scope __device__ array of 64 MiB
 // (16 Mi floats) that every GPU which loads the library holds until the
 // process exits; inputs needing more (B * H * ceil(S / 32) * (4*32*DK + 32*32 +
@@ -17,8 +19,11 @@
 // launched.  No cudaMalloc, cudaFree or allocating library routine is called.
 //
 // The first call on a device looks the array's device address up with
-// cudaGetSymbolAddress (with that device current) and caches it; make that
-// first call before any stream capture begins.  All calls share the one array:
+// cudaGetSymbolAddress (with that device current) and caches it together with
+// the device's current CUDA context; make that first call before any stream
+// capture begins.  A later call that finds a different current context (after
+// cudaDeviceReset, for instance) looks the address up again, so that call too
+// must come before any capture.  All calls share the one array:
 // calls whose kernels overlap on the GPU (different streams, or concurrent host
 // threads) race on it and must be serialised by the caller.  Every scratch
 // region is fully written before it is read, so no clearing is needed between

@@ -117,6 +117,8 @@ class Config:
 
     # ---- Logging ----
     log_every: int = 1
+    # path of a JSON-lines metrics sink (one record per logged step; "" = off)
+    metrics_jsonl: str = ""
 
     # ================= B200 additions =================
     # Optimizer: "lion" (reference parity, optimizer.py:126-155) or "adamw".

@@ -26,7 +26,7 @@ def _apply_overrides(config, args):
         "optimizer": "optimizer", "router_type": "router_type",
         "capacity_factor": "capacity_factor", "micro_batch": "micro_batch",
         "checkpoint_every": "checkpoint_every", "fused_comm": "fused_comm",
-        "expert_weights": "expert_weights",
+        "expert_weights": "expert_weights", "metrics_jsonl": "metrics_jsonl",
     }
     for a, f in mapping.items():
         v = getattr(args, a, None)
@@ -98,7 +98,7 @@ def build_parser():
                       ("swa_window", int), ("swa_period", int), ("gen_every", int),
                       ("gen_prompt", str), ("gen_max_tokens", int), ("kda_period", int),
                       ("capacity_factor", float), ("micro_batch", int),
-                      ("checkpoint_every", int)]:
+                      ("checkpoint_every", int), ("metrics_jsonl", str)]:
         t.add_argument(f"--{name}", type=typ, default=None)
     t.add_argument("--remat_policy", default=None,
                    choices=["full", "dots", "dots_no_batch", "experts", "none"])

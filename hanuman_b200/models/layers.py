@@ -172,7 +172,8 @@ class KDA(nn.Module):
             o, new_state = ref.kda_recurrent(q, k, v, g, beta, scale, state.get("S"))
             state["S"] = new_state
         else:
-            o = ops.kda_core(q, k, v, g, beta, scale, self.chunk)
+            o = ops.kda_core(q, k, v, g, beta, scale, self.chunk,
+                             getattr(self, "recompute_core", False))
         o = o.float()
         var = (o * o).mean(-1, keepdim=True)
         o = o * torch.rsqrt(var + 1e-5) * self.o_norm

@@ -10,10 +10,12 @@ from __future__ import annotations
 
 import torch
 import torch.nn as nn
+from torch.utils.checkpoint import checkpoint
 
 from .. import ops
 from ..config import Config
 from ..ops import reference as ref
+from ..utils.nvtx import rng
 from .layers import KDA, Attention, DenseFFN, MoE, RMSNorm
 
 
@@ -51,15 +53,27 @@ class Block(nn.Module):
             return self.ffn(h, dtype)
         return self.ffn(h, dtype), {}
 
-    def forward(self, x, cos, sin, dtype, positions=None, cache=None):
-        rs = self.residual_scale.float()
+    def _mixer_half(self, x, cos, sin, dtype, positions=None, cache=None):
         h = self.norm1(x, dtype)
         a = self.mix(h, cos, sin, dtype, positions, cache)
-        x = x + rs * a
+        return x + self.residual_scale.float() * a
+
+    def _ffn_half(self, x, dtype):
         h = self.norm2(x, dtype)
         f, aux = self.feed_forward(h, dtype)
-        x = x + rs * f
-        return x, aux
+        return x + self.residual_scale.float() * f, aux
+
+    def _whole(self, x, cos, sin, dtype, positions=None):
+        return self._ffn_half(self._mixer_half(x, cos, sin, dtype, positions), dtype)
+
+    def forward(self, x, cos, sin, dtype, positions=None, cache=None, remat="none"):
+        if remat == "full" and cache is None and torch.is_grad_enabled():
+            return checkpoint(self._whole, x, cos, sin, dtype, positions, use_reentrant=False)
+        if remat == "experts" and cache is None and torch.is_grad_enabled():
+            x = checkpoint(self._mixer_half, x, cos, sin, dtype, positions, use_reentrant=False)
+        else:
+            x = self._mixer_half(x, cos, sin, dtype, positions, cache)
+        return self._ffn_half(x, dtype)
 
 
 class Transformer(nn.Module):
@@ -95,6 +109,23 @@ class Transformer(nn.Module):
             return embedding_cuda(tokens, self.wte)
         return self.wte[tokens].float()
 
+    def remat_policy(self) -> str:
+        """Activation recompute of the training forward (model/transformer.py:100-181):
+        ``full`` recomputes each block in its backward (only the block input is
+        kept); ``experts`` recomputes the token mixer and keeps the MoE / FFN
+        activations (the reference keeps the expert matmul outputs);
+        ``dots`` / ``dots_no_batch`` keep every projection output and recompute
+        the KDA chunk intermediates, the model's largest activations; ``none``
+        keeps everything.  ``remat=False`` is ``none``."""
+        c = self.cfg
+        return c.remat_policy if c.remat else "none"
+
+    def _apply_core_recompute(self):
+        core = self.remat_policy() in ("dots", "dots_no_batch")
+        for b in self.blocks:
+            if b.attention_type == "kda":
+                b.attn.recompute_core = core
+
     def _fused_residual_ok(self, x, cache) -> bool:
         D = self.cfg.d_model
         return (x.is_cuda and cache is None and self.dtype == torch.bfloat16 and D % 4 == 0
@@ -103,29 +134,53 @@ class Transformer(nn.Module):
     def _forward_fused(self, x, positions):
         """CUDA path: every residual add is fused with the RMSNorm that follows
         it (norm2 of the same block, norm1 of the next block, or norm_f)."""
-        from ..ops.norm import add_rms_norm_cuda
         dtype = self.dtype
         aux_list = []
         h = self.blocks[0].norm1(x, dtype)
-        nb = len(self.blocks)
+        remat = self.remat_policy() if torch.is_grad_enabled() else "none"
         for i, blk in enumerate(self.blocks):
-            a = blk.mix(h, self.rope_cos, self.rope_sin, dtype, positions)
-            x, h = add_rms_norm_cuda(x, a, blk.residual_scale, blk.norm2.weight, blk.norm2.eps)
-            f, aux = blk.feed_forward(h, dtype)
+            if remat == "full":
+                x, h, aux = checkpoint(self._fused_block, i, x, h, positions, use_reentrant=False)
+            else:
+                if remat == "experts":
+                    x, h = checkpoint(self._fused_mixer, i, x, h, positions, use_reentrant=False)
+                else:
+                    x, h = self._fused_mixer(i, x, h, positions)
+                x, h, aux = self._fused_ffn(i, x, h)
             if aux:
                 aux_list.append(aux)
-            nxt = self.blocks[i + 1].norm1 if i + 1 < nb else self.norm_f
-            x, h = add_rms_norm_cuda(x, f, blk.residual_scale, nxt.weight, nxt.eps)
         return h, merge_aux(aux_list, self.cfg.n_experts, self.n_moe, x.device)
+
+    def _fused_mixer(self, i, x, h, positions):
+        from ..ops.norm import add_rms_norm_cuda
+        blk = self.blocks[i]
+        with rng(f"layer{i}/{blk.attention_type}"):
+            a = blk.mix(h, self.rope_cos, self.rope_sin, self.dtype, positions)
+            return add_rms_norm_cuda(x, a, blk.residual_scale, blk.norm2.weight, blk.norm2.eps)
+
+    def _fused_ffn(self, i, x, h):
+        from ..ops.norm import add_rms_norm_cuda
+        blk = self.blocks[i]
+        with rng(f"layer{i}/{'moe' if blk.use_moe else 'ffn'}"):
+            f, aux = blk.feed_forward(h, self.dtype)
+            nxt = self.blocks[i + 1].norm1 if i + 1 < len(self.blocks) else self.norm_f
+            x, h = add_rms_norm_cuda(x, f, blk.residual_scale, nxt.weight, nxt.eps)
+        return x, h, aux
+
+    def _fused_block(self, i, x, h, positions):
+        x, h = self._fused_mixer(i, x, h, positions)
+        return self._fused_ffn(i, x, h)
 
     def forward(self, tokens, positions=None, cache=None):
         dtype = self.dtype
+        self._apply_core_recompute()
         x = self.embed(tokens)
         if self._fused_residual_ok(x, cache):
             return self._forward_fused(x, positions)
         aux_list = []
+        remat = self.remat_policy() if torch.is_grad_enabled() else "none"
         for blk in self.blocks:
-            x, aux = blk(x, self.rope_cos, self.rope_sin, dtype, positions, cache)
+            x, aux = blk(x, self.rope_cos, self.rope_sin, dtype, positions, cache, remat=remat)
             if aux:
                 aux_list.append(aux)
         h = self.norm_f(x, dtype)
@@ -143,7 +198,8 @@ class Transformer(nn.Module):
         B, S, D = h.shape
         hs = h[:, :-1].reshape(B * (S - 1), D)
         tgt = tokens[:, 1:].reshape(-1)
-        ce = ops.head_cross_entropy(hs, self.wte, tgt, compute_dtype=self.dtype)
+        with rng("head_ce"):
+            ce = ops.head_cross_entropy(hs, self.wte, tgt, compute_dtype=self.dtype)
         z = cfg.z_loss_weight * aux["router_z_loss"]
         bal = cfg.balance_loss_weight * aux["balance_loss"]
         total = ce + z + bal

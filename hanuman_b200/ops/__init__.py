@@ -89,11 +89,16 @@ def swiglu_act(gu: torch.Tensor) -> torch.Tensor:
 
 
 # ------------------------------------------------------------------ KDA
-def kda_core(q, k, v, g, beta, scale: float, chunk: int):
-    """Gated delta rule over the sequence; fp32 in/out."""
+def kda_core(q, k, v, g, beta, scale: float, chunk: int, recompute: bool = False):
+    """Gated delta rule over the sequence; fp32 in/out.  ``recompute`` keeps
+    only the inputs for the backward (the chunk intermediates are recomputed)."""
     if on_gpu(q):
-        from .kda import kda_chunked_cuda
-        return kda_chunked_cuda(q, k, v, g, beta, scale, chunk)
+        from .kda import KdaCoreFn
+        return KdaCoreFn.apply(q, k, v, g, beta, scale, recompute)
+    if recompute and torch.is_grad_enabled():
+        from torch.utils.checkpoint import checkpoint
+        return checkpoint(lambda *a: ref.kda_chunked(*a, scale, chunk)[0], q, k, v, g, beta,
+                          use_reentrant=False)
     o, _ = ref.kda_chunked(q, k, v, g, beta, scale, chunk)
     return o
 

@@ -56,3 +56,64 @@ def check_status():
     if s != 0:
         ext().clear_status()
         raise RuntimeError(f"hanuman_b200 kernel reported error status {s}")
+
+
+_STATUS_NAMES = {1: "TMA producer wait timed out", 2: "MMA wait timed out",
+                 3: "epilogue wait timed out", 4: "peer wait timed out",
+                 5: "index out of bounds", 6: "expert capacity exceeded"}
+
+
+class KernelStatusError(RuntimeError):
+    """A kernel recorded an error in the device status word (a bounded wait
+    that ran out of budget, a bounds check); the step that saw it is not valid."""
+
+    def __init__(self, code: int):
+        self.code = int(code)
+        super().__init__(f"hanuman_b200 kernel error status {code} "
+                         f"({_STATUS_NAMES.get(int(code), 'unknown')})")
+
+
+class StatusMonitor:
+    """Checks the device status word once per training step without stalling
+    the device.
+
+    ``poll()`` enqueues an asynchronous copy of the status word into pinned
+    host memory (after the step's kernels, on the current stream) and checks
+    the copy enqueued by the previous ``poll()``, waiting for that copy's
+    event: the host then runs at most one step ahead of the device, and an
+    error is raised at the end of the step after the one that recorded it.
+    ``flush()`` waits for and checks the latest copy."""
+
+    def __init__(self):
+        self._view = ext().status_view()
+        self._bufs = [torch_empty_pinned_int() for _ in range(2)]
+        self._events = [None, None]
+        self._i = 0
+
+    def _check(self, j):
+        ev = self._events[j]
+        if ev is None:
+            return
+        ev.synchronize()
+        self._events[j] = None
+        code = int(self._bufs[j][0])
+        if code != 0:
+            raise KernelStatusError(code)
+
+    def poll(self):
+        import torch
+        i = self._i
+        self._bufs[i].copy_(self._view, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._events[i] = ev
+        self._i = i ^ 1
+        self._check(i ^ 1)
+
+    def flush(self):
+        self._check(self._i ^ 1)
+
+
+def torch_empty_pinned_int():
+    import torch
+    return torch.zeros(1, dtype=torch.int32, pin_memory=True)

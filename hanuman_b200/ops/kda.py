@@ -10,6 +10,7 @@
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
@@ -21,41 +22,76 @@ def chunk_size(dk: int) -> int:
     return int(ext().kda_chunk_size(dk))
 
 
+def use_chunk64(dk: int) -> bool:
+    """Head dim 64 runs the chunk-64 sub-block kernels (csrc/kda/kda64.cu);
+    HB_KDA_CHUNK64=0 selects the chunk-32 kernels (csrc/kda/kda.cu) instead."""
+    return dk == 64 and os.environ.get("HB_KDA_CHUNK64", "1") != "0"
+
+
 class KdaCoreFn(torch.autograd.Function):
-    """Chunk-parallel gated delta rule; q,k,v,g ``[B,S,H,K]`` fp32, beta ``[B,S,H]``."""
+    """Chunk-parallel gated delta rule; q,k,v,g ``[B,S,H,K]`` fp32, beta ``[B,S,H]``.
+
+    With ``recompute`` the forward keeps only its inputs and the backward
+    re-runs the forward kernels for the chunk intermediates (Wt, Ut, Kh, Qg,
+    P, states, ...: about 9 fp32 values per token, head and channel), which
+    are the largest activations of the model (the ``dots`` remat policies)."""
 
     @staticmethod
-    def forward(ctx, q, k, v, g, beta, scale):
-        q, k, v, g, beta = (t.float().contiguous() for t in (q, k, v, g, beta))
+    def _run_fwd(q, k, v, g, beta, scale):
         B, S, H, K = q.shape
-        C = chunk_size(K)
+        c64 = use_chunk64(K)
+        C = 64 if c64 else chunk_size(K)
         NC = (S + C - 1) // C
-        dev = q.device
+        f32 = dict(dtype=torch.float32, device=q.device)
         o = torch.empty_like(v)
-        f32 = dict(dtype=torch.float32, device=dev)
-        Wt = torch.empty(B, H, NC, C, K, **f32)
-        Ut = torch.empty(B, H, NC, C, K, **f32)
-        Kh = torch.empty(B, H, NC, C, K, **f32)
-        Qg = torch.empty(B, H, NC, C, K, **f32)
+        Wt, Ut, Kh, Qg = (torch.empty(B, H, NC, C, K, **f32) for _ in range(4))
         Pm = torch.empty(B, H, NC, C, C, **f32)
         gC = torch.empty(B, H, NC, K, **f32)
         states = torch.empty(B, H, NC, K, K, **f32)
+        if c64:
+            Linv = torch.empty(B, H, NC, C, C, **f32)
+            Am = torch.empty(B, H, NC, C, C, **f32)
+            U = torch.empty(B, H, NC, C, K, **f32)
+            ext().kda_fwd64(q, k, v, g, beta, float(scale), o, Wt, Ut, Kh, Qg, Pm, gC, states, Linv, Am, U)
+            return o, (Wt, Ut, Kh, Qg, Pm, gC, states, Linv, Am, U)
         ext().kda_fwd(q, k, v, g, beta, float(scale), o, Wt, Ut, Kh, Qg, Pm, gC, states, None, None)
-        del Ut
-        ctx.save_for_backward(q, k, v, g, beta, Wt, Kh, Qg, Pm, gC, states)
+        return o, (Wt, Kh, Qg, Pm, gC, states)
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, scale, recompute=False):
+        q, k, v, g, beta = (t.float().contiguous() for t in (q, k, v, g, beta))
         ctx.scale = float(scale)
+        ctx.c64 = use_chunk64(q.shape[-1])
+        ctx.recompute = bool(recompute)
+        o, inter = KdaCoreFn._run_fwd(q, k, v, g, beta, scale)
+        if recompute:
+            del inter
+            ctx.save_for_backward(q, k, v, g, beta)
+        else:
+            ctx.save_for_backward(q, k, v, g, beta, *inter)
         return o
 
     @staticmethod
     def backward(ctx, do):
-        q, k, v, g, beta, Wt, Kh, Qg, Pm, gC, states = ctx.saved_tensors
         do = do.float().contiguous()
-        dstates = torch.empty_like(states)
+        q, k, v, g, beta = ctx.saved_tensors[:5]
+        inter = ctx.saved_tensors[5:] if not ctx.recompute else \
+            KdaCoreFn._run_fwd(q, k, v, g, beta, ctx.scale)[1]
         dq, dk, dv, dg = (torch.empty_like(q) for _ in range(4))
         dbeta = torch.empty_like(beta)
+        if ctx.c64:
+            Wt, Ut, Kh, Qg, Pm, gC, states, Linv, Am, U = inter
+            dstates, dSq = torch.empty_like(states), torch.empty_like(states)
+            dU, dUp, dQg, dKh, dWt, dP = (torch.empty_like(Wt) for _ in range(6))
+            dgC = torch.empty_like(gC)
+            ext().kda_bwd64(q, k, v, g, beta, ctx.scale, do, Wt, Ut, Kh, Qg, Pm, gC, states, Linv, Am, U,
+                            dstates, dU, dUp, dSq, dQg, dKh, dWt, dP, dgC, dq, dk, dv, dg, dbeta)
+            return dq, dk, dv, dg, dbeta, None, None
+        Wt, Kh, Qg, Pm, gC, states = inter
+        dstates = torch.empty_like(states)
         ext().kda_bwd(q, k, v, g, beta, ctx.scale, do, Wt, Kh, Qg, Pm, gC, states, dstates,
                       dq, dk, dv, dg, dbeta)
-        return dq, dk, dv, dg, dbeta, None
+        return dq, dk, dv, dg, dbeta, None, None
 
 
 def kda_chunked_cuda(q, k, v, g, beta, scale, chunk=None):
@@ -208,7 +244,8 @@ def kda_layer_cuda(mod, h, dtype):
         mod.q_conv.weight, mod.k_conv.weight, mod.v_conv.weight, mod.a_log, mod.dt_bias,
         gate_mode, S, H, K)
     o = KdaCoreFn.apply(q.view(B, S, H, K), k.view(B, S, H, K), v.view(B, S, H, K),
-                        g.view(B, S, H, K), beta.view(B, S, H), 1.0 / math.sqrt(K))
+                        g.view(B, S, H, K), beta.view(B, S, H), 1.0 / math.sqrt(K),
+                        getattr(mod, "recompute_core", False))
     if K in (32, 64, 128):
         y = KdaOutGateFn.apply(o.view(T, H, K), gl, mod.o_norm, mod.g_proj1_bias)
     else:

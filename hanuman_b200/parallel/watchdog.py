@@ -25,6 +25,7 @@ class Watchdog:
         self.timeout_s, self.interval_s, self.prefix = timeout_s, interval_s, prefix
         self.step = 0
         self.dead: list[int] = []
+        self._t0 = time.time()   # a peer with no heartbeat yet counts from here
         self._stop = threading.Event()
         self._t = threading.Thread(target=self._loop, daemon=True)
         self._beat()
@@ -45,16 +46,25 @@ class Watchdog:
                 for r in range(self.world):
                     if r == self.rank:
                         continue
-                    try:
-                        v = self.store.get(self._key(r)).decode()
-                        ts = float(v.split(":")[1])
-                    except Exception:
-                        ts = 0.0
+                    ts = self._peer_time(r)
                     if now - ts > self.timeout_s:
                         dead.append(r)
                 self.dead = dead
             except Exception:
                 pass
+
+    def _peer_time(self, r) -> float:
+        """Wall time of peer r's last heartbeat.  ``store.check`` does not
+        block, so a peer that never wrote one (it died before its first beat)
+        costs no store timeout: it counts from this watchdog's start and is
+        reported once ``timeout_s`` has passed."""
+        key = self._key(r)
+        try:
+            if not self.store.check([key]):
+                return self._t0
+            return float(self.store.get(key).decode().split(":")[1])
+        except Exception:
+            return self._t0
 
     def tick(self, step: int):
         self.step = step

@@ -253,6 +253,38 @@ def case_p2p_rs_emulated():
 
 CASES = {k[5:]: v for k, v in globals().items() if k.startswith("case_")}
 
+# phase slots of the chunk-64 KDA intra kernels (csrc/kda/kda64.cu PhaseClock marks)
+KDA64_PHASES = {
+    0: "fwd load", 1: "fwd cumsum", 2: "fwd Kh/Qg + off-diagonal A,P", 3: "fwd diagonal pairs",
+    4: "fwd store P,A / N", 5: "fwd block inverse", 6: "fwd Linv store, bV, b2Ke^G",
+    7: "fwd Ut/Wt products",
+    10: "bwd load", 11: "bwd X,Y", 12: "bwd dN", 13: "bwd dbeta,dv", 14: "bwd init accumulators",
+    15: "bwd j0 staging", 16: "bwd j0 products", 17: "bwd j0 epilogue",
+    18: "bwd j1 staging", 19: "bwd j1 products", 20: "bwd j1 epilogue",
+    21: "bwd j2 staging", 22: "bwd j2 products", 23: "bwd j2 epilogue",
+    24: "bwd diagonal pairs", 25: "bwd cumsum", 26: "bwd stores"}
+
+
+def kda64_phases(fn):
+    """Run ``fn`` once with the chunk-64 KDA phase counters on; print each
+    phase's share of its kernel's summed CTA cycles."""
+    import torch
+    cnt = torch.zeros(64, dtype=torch.int64, device="cuda")
+    ext().kda64_set_profile(cnt)
+    try:
+        fn()
+        torch.cuda.synchronize()
+    finally:
+        ext().kda64_set_profile(None)
+    c = cnt.cpu().tolist()
+    for lo, hi, name in ((0, 8, "intra_fwd64"), (10, 27, "intra_bwd64")):
+        tot = sum(c[lo:hi])
+        if tot == 0:
+            continue
+        print(f"{name}: {tot / 1e9:.3f} G CTA-cycles")
+        for i in range(lo, hi):
+            print(f"  {KDA64_PHASES[i]:34s} {100 * c[i] / tot:5.1f} %")
+
 
 def main(argv=None):
     argv = sys.argv[1:] if argv is None else argv
@@ -263,6 +295,8 @@ def main(argv=None):
         rate = work / (ms / 1e3)
         print(f"{name}: {ms:.3f} ms  " + (f"{rate/1e12:.1f} TFLOP/s" if unit == "flop"
                                           else f"{rate/1e9:.0f} GB/s"))
+    if "--phases" in argv:
+        kda64_phases(fn)
     assert ext().read_status() == 0
 
 

@@ -9,6 +9,7 @@ returns the loss as a device tensor (``float(loss)`` reads it back).
 """
 from __future__ import annotations
 
+import json
 import os
 import time
 from typing import Optional
@@ -19,6 +20,7 @@ from . import flops as fl
 from .config import Config
 from .engine import Engine
 from .models.transformer import Transformer
+from .utils.nvtx import rng
 
 
 class Trainer:
@@ -55,6 +57,12 @@ class Trainer:
         else:
             self.engine = Engine(self.model, cfg, self.device, world=1, rank=0)
         self.last_metrics = {}
+        # device status word (bounded waits that ran out, bounds checks):
+        # checked every step, raised as KernelStatusError one step later
+        self._status = None
+        if self.device.type == "cuda":
+            from .ops._ext import StatusMonitor
+            self._status = StatusMonitor()
 
     # ------------------------------------------------------------------
     def _micro_batches(self, tokens: torch.Tensor):
@@ -75,8 +83,10 @@ class Trainer:
         for i, mb in enumerate(mbs):
             if hasattr(eng, "before_forward"):
                 eng.before_forward(i, n)
-            loss, metrics = self.model.loss(mb)
-            (loss / n).backward()
+            with rng(f"micro{i}/forward"):
+                loss, metrics = self.model.loss(mb)
+            with rng(f"micro{i}/backward"):
+                (loss / n).backward()
             if hasattr(eng, "after_backward"):
                 eng.after_backward(i, n)
             tot = loss.detach() / n if tot is None else tot + loss.detach() / n
@@ -96,20 +106,30 @@ class Trainer:
         loss, metrics = self.forward_backward(tokens)
         counts = metrics["expert_counts"]
         eng.finish_step_reduce = getattr(eng, "reduce_grads", None)
-        if eng.finish_step_reduce is not None:
-            loss, counts = eng.reduce_grads(loss, counts)
-        sq = eng.grad_sq_sum()
-        if hasattr(eng, "allreduce_scalar"):
-            sq = eng.allreduce_scalar(sq)
-        from .optimizer import clip_coef
-        coef = clip_coef(sq, self.cfg.grad_clip)
-        lr = eng.apply_update(coef)
-        eng.update_router_bias(counts)
+        with rng("optimizer"):
+            if eng.finish_step_reduce is not None:
+                loss, counts = eng.reduce_grads(loss, counts)
+            sq = eng.grad_sq_sum()
+            if hasattr(eng, "allreduce_scalar"):
+                sq = eng.allreduce_scalar(sq)
+            from .optimizer import clip_coef
+            coef = clip_coef(sq, self.cfg.grad_clip)
+            lr = eng.apply_update(coef)
+            eng.update_router_bias(counts)
         metrics["expert_counts"] = counts
         metrics["grad_norm"] = torch.sqrt(sq)
         metrics["lr"] = lr
         self.last_metrics = metrics
+        if self._status is not None:
+            self._status.poll()
         return loss
+
+    def check_device_status(self):
+        """Wait for the last step and raise KernelStatusError if any kernel of
+        it (or before it) recorded an error."""
+        if self._status is not None:
+            self._status.poll()
+            self._status.flush()
 
     # ------------------------------------------------------------------
     def state_dict(self):
@@ -176,6 +196,8 @@ def train(config: Config, use_random_data: bool = True, save: bool = True, dist_
             log(f"[train] compile-free first step done in {time.time()-t_init:.1f}s "
                 f"(loss {losses[-1]:.4f})")
             if trainer.device.type == "cuda":
+                log(hbm_report(trainer.device))
+            if trainer.device.type == "cuda":
                 ev0 = torch.cuda.Event(enable_timing=True)
                 ev0.record()
             t_win, steps_win = time.time(), 0
@@ -202,6 +224,19 @@ def train(config: Config, use_random_data: bool = True, save: bool = True, dist_
                 f"| ent {float(m['mean_entropy']):.3f} "
                 f"| experts {float(m['eff_experts']):.1f}/{config.n_experts} "
                 f"| lr {m['lr']:.2e} | {sec*1e3:.0f} ms/step | tok/s {tps:,.0f}{mfu}")
+            if config.metrics_jsonl and is_main:
+                rec = {"step": step, "loss": lv, "ce": float(m["ce"]), "z_loss": float(m["z_loss"]),
+                       "bal_loss": float(m["bal_loss"]), "mean_entropy": float(m["mean_entropy"]),
+                       "eff_experts": float(m["eff_experts"]), "grad_norm": float(m["grad_norm"]),
+                       "lr": float(m["lr"]), "ms_per_step": sec * 1e3, "tokens_per_s": tps,
+                       "time": time.time()}
+                if peak:
+                    rec["mfu"] = model_fl / sec / peak
+                    rec["hw_mfu"] = hw_fl / sec / peak
+                if trainer.device.type == "cuda":
+                    rec.update(hbm_stats(trainer.device))
+                with open(config.metrics_jsonl, "a") as f:
+                    f.write(json.dumps(rec) + "\n")
             if trainer.device.type == "cuda":
                 ev0 = torch.cuda.Event(enable_timing=True)
                 ev0.record()
@@ -220,9 +255,31 @@ def train(config: Config, use_random_data: bool = True, save: bool = True, dist_
                         extra={"loader": loader.state_dict()})
     if wd is not None:
         wd.close()
+    if trainer.device.type == "cuda":
+        trainer.check_device_status()
+        log(hbm_report(trainer.device))
     if losses:
         log(f"[train] Done. First loss={losses[0]:.4f}, last loss={losses[-1]:.4f}")
     return trainer, losses
+
+
+def hbm_stats(device) -> dict:
+    """Device-memory figures of this process (the reference's hbm_report,
+    train.py:337-346, reads the same from the accelerator's memory stats)."""
+    st = torch.cuda.memory_stats(device)
+    free, total = torch.cuda.mem_get_info(device)
+    gb = 1e9
+    return {"hbm_in_use_gb": st.get("allocated_bytes.all.current", 0) / gb,
+            "hbm_peak_gb": st.get("allocated_bytes.all.peak", 0) / gb,
+            "hbm_reserved_gb": st.get("reserved_bytes.all.current", 0) / gb,
+            "hbm_total_gb": total / gb, "hbm_free_gb": free / gb}
+
+
+def hbm_report(device) -> str:
+    h = hbm_stats(device)
+    return (f"[hbm] {device}: in use {h['hbm_in_use_gb']:.2f} GB, peak {h['hbm_peak_gb']:.2f} GB, "
+            f"reserved {h['hbm_reserved_gb']:.2f} GB of {h['hbm_total_gb']:.1f} GB "
+            f"({h['hbm_free_gb']:.1f} GB free)")
 
 
 def memory_report(config: Config) -> str:
@@ -240,15 +297,18 @@ def memory_report(config: Config) -> str:
         mb = n * 4 / 1e6
         small = n < (1 << 16)
         pmb = mb if small else mb / world
-        rows.append((mb, pmb, name, shape, "replicated" if small else f"shard/{world}"))
+        rows.append((mb, pmb, name, shape, "replicated" if small else f"state shard/{world}"))
         total += mb
         per_dev += pmb
-    out = [f"{'tensor':46s} {'shape':24s} {'layout':14s} {'fp32 MB':>9s} {'per-dev':>9s}",
-           "-" * 106]
+    out = [f"layout: fp32 master + optimizer state of tensors >= 65536 elements are sharded over "
+           f"the {world} data ranks; the bf16 working copy and the fp32 gradient buffers are "
+           f"full on every rank",
+           f"{'tensor':46s} {'shape':24s} {'layout':18s} {'fp32 MB':>9s} {'master/dev':>10s}",
+           "-" * 111]
     for mb, pmb, name, shape, lay in sorted(rows, reverse=True):
-        out.append(f"{name[:46]:46s} {str(tuple(shape))[:24]:24s} {lay:14s} {mb:9.1f} {pmb:9.1f}")
-    out.append("-" * 106)
-    out.append(f"{'TOTAL':46s} {'':24s} {'':14s} {total:9.1f} {per_dev:9.1f}")
+        out.append(f"{name[:46]:46s} {str(tuple(shape))[:24]:24s} {lay:18s} {mb:9.1f} {pmb:10.1f}")
+    out.append("-" * 111)
+    out.append(f"{'TOTAL':46s} {'':24s} {'':18s} {total:9.1f} {per_dev:10.1f}")
     opt_mult = 2 if config.optimizer == "adamw" else (0.5 if config.opt_state_dtype == "bf16" else 1)
     out.append(f"per device: master {per_dev/1e3:.2f} GB + optimizer {per_dev*opt_mult/1e3:.2f} GB "
                f"({config.optimizer}) + bf16 working copy {total/2/1e3:.2f} GB + fp32 grads "

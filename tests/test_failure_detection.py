@@ -117,3 +117,54 @@ def test_device_barrier_times_out_with_error_status():
     # the context is still usable
     x = torch.randn(64, 64, device="cuda")
     assert torch.isfinite((x @ x).sum())
+
+
+@pytest.mark.gpu
+def test_trainer_step_raises_after_device_wait_timeout():
+    """A bounded device wait that runs out (a peer flag nothing sets, 0.2 s)
+    makes the next Trainer steps raise KernelStatusError instead of training on."""
+    from hanuman_b200.config import get_config
+    from hanuman_b200.ops._ext import KernelStatusError, ext
+    from hanuman_b200.train import Trainer
+    e = ext()
+    e.clear_status()
+    cfg = get_config("tiny_hybrid").replace(seq_len=128, batch_size=2, micro_batch=0)
+    tr = Trainer(cfg, device="cuda:0")
+    toks = torch.randint(0, cfg.vocab_size, (2, 128), generator=torch.Generator().manual_seed(0))
+    tr.step(toks)
+    tr.check_device_status()                    # a clean step raises nothing
+    pad = torch.zeros(32, dtype=torch.int32, device="cuda")
+    pads = torch.tensor([pad.data_ptr(), pad.data_ptr()], dtype=torch.int64, device="cuda")
+    e.set_wait_budget_ns(200_000_000)
+    try:
+        e.p2p_barrier(pads, 0, 2, 1)            # slot 1 is never signalled
+        with pytest.raises(KernelStatusError) as ei:
+            for _ in range(3):
+                tr.step(toks)
+        assert ei.value.code == 4
+    finally:
+        torch.cuda.synchronize()
+        e.set_wait_budget_ns(4_000_000_000)
+        e.clear_status()
+    x = torch.randn(64, 64, device="cuda")
+    assert torch.isfinite((x @ x).sum())
+
+
+def test_watchdog_peer_without_any_heartbeat_is_reported_after_timeout():
+    """A peer that dies before its first heartbeat is reported after timeout_s
+    (counted from the watchdog's start), neither at once nor after the store's
+    own blocking timeout."""
+    import torch.distributed as dist
+    from hanuman_b200.parallel.watchdog import Watchdog
+    store = dist.HashStore()
+    wd = Watchdog(store, 0, 2, timeout_s=1.0, interval_s=0.1)
+    try:
+        time.sleep(0.4)
+        assert wd.dead == []
+        t0 = time.time()
+        while not wd.dead and time.time() - t0 < 5:
+            time.sleep(0.05)
+        assert wd.dead == [1]
+        assert time.time() - t0 < 3
+    finally:
+        wd.close()

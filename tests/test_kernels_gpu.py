@@ -106,6 +106,37 @@ def test_head_cross_entropy_fwd_bwd():
     assert rel(w.main_grad, wf.grad) < 2e-2
 
 
+def test_head_ce_full_vocab_against_fp32_head_and_memory():
+    """The tied head at the flagship shape (D 1024, V 32768) with bf16 operands
+    against an fp32 head over the fp32 master weights (the reference's
+    ``x @ wte.T``), and no [T, V] buffer: peak extra memory stays under half of
+    one bf16 [T, V] array."""
+    from hanuman_b200.ops.ce import head_ce_cuda
+    torch.manual_seed(21)
+    T, D, V = 65536, 1024, 32768
+    x = torch.randn(T, D, device=DEV).bfloat16().requires_grad_()
+    w32 = torch.randn(V, D, device=DEV) * D ** -0.5
+    w = w32.bfloat16()
+    w.main_grad = torch.zeros(V, D, device=DEV)
+    tgt = torch.randint(0, V, (T,), device=DEV)
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats()
+    base = torch.cuda.memory_allocated()
+    loss = head_ce_cuda(x, w.requires_grad_(), tgt)
+    loss.backward()
+    torch.cuda.synchronize()
+    peak = torch.cuda.max_memory_allocated() - base
+    assert peak < 0.5 * T * V * 2, peak
+    xf = x.detach().float().requires_grad_()
+    wf = w32.clone().requires_grad_()
+    torch.backends.cuda.matmul.allow_tf32 = False
+    lr_ = F.cross_entropy(xf @ wf.t(), tgt)
+    lr_.backward()
+    assert abs(loss.item() - lr_.item()) / lr_.item() < 1e-4
+    assert rel(x.grad, xf.grad) < 1e-2
+    assert rel(w.main_grad, wf.grad) < 1e-2
+
+
 @pytest.mark.parametrize("H,window,S,Nq,Nkv", [(64, 0, 256, 4, 2), (64, 0, 200, 4, 4),
                                                (32, 0, 128, 2, 1), (32, 64, 128, 2, 1),
                                                (64, 96, 300, 4, 1), (128, 0, 192, 2, 2),

@@ -166,3 +166,69 @@ def test_cached_decoding_matches_full_recompute(name):
                                      seq_len=64)
     _, ids = generate_cached(model, tok, "hello world", max_tokens=12, temperature=0.0)
     assert ids == ref_ids
+
+
+def test_train_loop_writes_jsonl_metrics(tmp_path, monkeypatch):
+    """The training loop's metrics sink: one JSON record per logged step with
+    the log line's fields."""
+    import json
+    from hanuman_b200.train import train
+    monkeypatch.chdir(tmp_path)
+    c = get_config("smoke").replace(train_steps=4, log_every=1, batch_size=2, seq_len=32,
+                                    metrics_jsonl=str(tmp_path / "m.jsonl"))
+    _, losses = train(c, save=False, log=lambda *a, **k: None)
+    recs = [json.loads(line) for line in open(tmp_path / "m.jsonl")]
+    assert [r["step"] for r in recs] == [1, 2, 3]
+    for r in recs:
+        for key in ("loss", "ce", "z_loss", "bal_loss", "lr", "ms_per_step", "tokens_per_s", "grad_norm"):
+            assert math.isfinite(r[key]), key
+    assert recs[-1]["loss"] == pytest.approx(losses[-1])
+
+
+def test_memory_report_labels_the_replicated_working_copy():
+    from hanuman_b200.train import memory_report
+    rep = memory_report(get_config("hybrid_1p3b"))
+    assert "bf16 working copy and the fp32 gradient buffers are full on every rank" in rep
+    assert "state shard/8" in rep
+
+
+@pytest.mark.parametrize("policy", ["full", "experts", "dots"])
+def test_remat_recomputes_and_gradients_are_bitwise_equal(policy, monkeypatch):
+    """Activation recompute re-runs the forward in the backward and gives the
+    same gradients, bit for bit, as keeping every activation."""
+    from hanuman_b200 import ops
+    from hanuman_b200.models.layers import KDA
+
+    def grads(pol):
+        c = get_config("smoke_kda").replace(remat=pol != "none", remat_policy=pol)
+        tr = Trainer(c, device="cpu")
+        toks = torch.randint(0, c.vocab_size, (c.batch_size, c.seq_len),
+                             generator=torch.Generator().manual_seed(1))
+        calls = {"kda": 0, "core": 0}
+        f0, c0 = KDA.forward, ops.kda_core
+
+        def kda_fwd(self, *a, **k):
+            calls["kda"] += 1
+            return f0(self, *a, **k)
+
+        def core(*a, **k):
+            calls["core"] += 1
+            return c0(*a, **k)
+        monkeypatch.setattr(KDA, "forward", kda_fwd)
+        monkeypatch.setattr(ops, "kda_core", core)
+        tr.engine.zero_grad()
+        loss, _ = tr.forward_backward(toks)
+        monkeypatch.setattr(KDA, "forward", f0)
+        monkeypatch.setattr(ops, "kda_core", c0)
+        g = [p.grad.clone() for p in tr.model.parameters() if p.grad is not None]
+        return float(loss), g, calls
+
+    l0, g0, c_none = grads("none")
+    l1, g1, c_pol = grads(policy)
+    assert l0 == l1
+    assert len(g0) == len(g1) and all(torch.equal(a, b) for a, b in zip(g0, g1))
+    n_kda = c_none["kda"]
+    if policy in ("full", "experts"):
+        assert c_pol["kda"] == 2 * n_kda          # every KDA layer ran again in the backward
+    else:
+        assert c_pol["kda"] == n_kda

@@ -51,9 +51,11 @@ def _rel(a, b):
     return ((a - b).norm() / b.norm().clamp_min(1e-12)).item()
 
 
-def test_noalloc_matches_allocating_entry_point_twice():
+@pytest.mark.parametrize("K", [16, 32, 64])
+@pytest.mark.parametrize("S", [200, 256])   # 256: a whole number of 32-token chunks
+def test_noalloc_matches_allocating_entry_point_twice(K, S):
     fn = _lib()
-    B, S, H, K = 2, 200, 4, 64
+    B, H = 2, 4
     scale = 1.0 / math.sqrt(K)
     stream = torch.cuda.current_stream().cuda_stream
     for seed in (0, 1):  # two calls in a row share the static scratch
