@@ -42,6 +42,11 @@ def parse():
     ap.add_argument("--seq_len", type=int, default=SEQ_LEN)
     ap.add_argument("--micro_batch", type=int, default=8)
     ap.add_argument("--no_e2e", action="store_true")
+    ap.add_argument("--expert_weights", default=None, choices=["replicated", "fused_gather"],
+                    help="override the preset (fused_gather: FSDP expert shards gathered inside "
+                         "the grouped GEMMs)")
+    ap.add_argument("--no_shard", action="store_true",
+                    help="data parallelism with a replicated working copy instead of FSDP")
     return ap.parse_args()
 
 
@@ -158,6 +163,10 @@ def main():
     cfg.micro_batch = args.micro_batch
     cfg.train_steps = 10 ** 6   # constant-lr region of the schedule
     cfg.warmup_steps = 0
+    if args.expert_weights:
+        cfg.expert_weights = args.expert_weights
+    if args.no_shard:
+        cfg.shard_params = False
     trainer = Trainer(cfg, device=f"cuda:{local}", dist_ctx=ctx)
     B = args.per_gpu_seqs
     gen = torch.Generator().manual_seed(0 + rank)
@@ -226,7 +235,10 @@ def main():
             "dtype": "bf16", "data": "synthetic (seed-0 uniform random tokens, random-init weights)",
             "config": {"model": cfg.name, "global_batch": cfg.batch_size, "seq_len": cfg.seq_len,
                        "per_gpu_batch": B, "micro_batch": cfg.micro_batch,
-                       "parallelism": f"dp{world}" if world > 1 else "single",
+                       "parallelism": (f"fsdp{world}" if getattr(trainer.engine, "sharded_units", None)
+                                       else f"dp{world}") if world > 1 else "single",
+                       "expert_weights": cfg.expert_weights if world > 1 else "local",
+                       "overlap_reduce": bool(cfg.overlap_reduce) if world > 1 else False,
                        "optimizer": cfg.optimizer,
                        "grad_transport": getattr(trainer.engine, "transport", "local"),
                        "l2": "working set per step is tens of GB (> 126 MB L2); no flush needed"},
@@ -236,6 +248,7 @@ def main():
             "gpu_launches": native * args.steps,
             "gpu_launches_per_step": {"native": native, "other": other},
             "kernel_status": status,
+            "hbm_peak_gb": torch.cuda.max_memory_allocated() / 1e9,
         }
         print(json.dumps(out))
     if ctx:

@@ -109,6 +109,7 @@ void kda_prep_bwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::
 void p2p_barrier(torch::Tensor pads, int64_t rank, int64_t world, int64_t epoch);
 void p2p_reduce_scatter(torch::Tensor peers, int64_t world, int64_t off, int64_t n, torch::Tensor out,
                         double scale, torch::Tensor sumsq);
+void p2p_gather(torch::Tensor peers, int64_t world, int64_t shard_bytes, torch::Tensor out);
 void p2p_update_bcast(torch::Tensor p, torch::Tensor g, torch::Tensor m, c10::optional<torch::Tensor> v,
                       torch::Tensor decay, torch::Tensor work_peers, int64_t world, int64_t off,
                       bool work_bf16, int64_t mode, double lr, double wd, double b1, double b2, double eps,
@@ -196,6 +197,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kda_prep_bwd", &hb::kda_prep_bwd);
   m.def("p2p_barrier", &hb::p2p_barrier);
   m.def("p2p_reduce_scatter", &hb::p2p_reduce_scatter);
+  m.def("p2p_gather", &hb::p2p_gather);
   m.def("p2p_update_bcast", &hb::p2p_update_bcast);
   m.def("ep_scatter", &hb::ep_scatter);
   m.def("ep_zero_pads", &hb::ep_zero_pads);

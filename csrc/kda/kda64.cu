@@ -564,36 +564,52 @@ __global__ void __launch_bounds__(NT, 1) intra_bwd64_kernel(Ptrs p) {
   const float scale = p.scale;
   PhaseClock pc(p.prof);
   const long long co = chunk_off(p, b, h, n, C * D), po = chunk_off(p, b, h, n, C * C);
-  cp_token_rows(p, p.q, b, h, n, q);
-  cp_token_rows(p, p.k, b, h, n, k);
-  cp_token_rows(p, p.g, b, h, n, G);
+  // three load groups, consumed in order: (Linv, dU, dWt) for X and Y,
+  // (Ut, Wt) for dN, then (q, k, g, dP, A)
   cp_chunk_tile(Li, p.Linv + po);
   cp_chunk_tile(dU, p.dU + co);
   cp_chunk_tile(dWt, p.dWt + co);
+  cp_async_commit();
   cp_chunk_tile(Ut, p.Ut + co);
   cp_chunk_tile(Wt, p.Wt + co);
+  cp_async_commit();
+  cp_token_rows(p, p.q, b, h, n, q);
+  cp_token_rows(p, p.k, b, h, n, k);
+  cp_token_rows(p, p.g, b, h, n, G);
   cp_chunk_tile(dP, p.dP + po);
   cp_chunk_tile(Am, p.Am + po);
   cp_async_commit();
   load_beta(p, b, h, n, bet);
   if (threadIdx.x < D) red[threadIdx.x] = 0.f;
-  cp_async_wait_all();
+  cp_async_wait<2>();
   __syncthreads();
   pc.mark(10);
-  cumsum_log2(G);
-  for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
-    const int t = i / C, s = i % C;
-    if (s > t) dP[t * L + s] = 0.f;
-  }
   // X = Linv^T dU,  Y = Linv^T dWt
   mm<C, D, C, true, false>(X, L, Li, L, dU, L, 1.f, false);
   mm<C, D, C, true, false>(Y, L, Li, L, dWt, L, 1.f, false);
+  cp_async_wait<1>();
   __syncthreads();
   pc.mark(11);
   // dN = -(X Ut^T + Y Wt^T)   (same warp tiles in both calls: no barrier needed)
   float* dN = dA;
   mm<C, C, D, false, true>(dN, L, X, L, Ut, L, -1.f, false);
   mm<C, C, D, false, true>(dN, L, Y, L, Wt, L, -1.f, true);
+  cp_async_wait<0>();
+  __syncthreads();
+  // v, dKh and dQg land in the freed dWt / Ut / Wt tiles while dbeta starts
+  float* vs = T5;
+  float* dKh = T8;
+  float* dQg = T9;
+  cp_token_rows(p, p.v, b, h, n, vs);
+  cp_chunk_tile(dKh, p.dKh + co);
+  cp_chunk_tile(dQg, p.dQg + co);
+  cp_async_commit();
+  cumsum_log2(G);
+  for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
+    const int t = i / C, s = i % C;
+    if (s > t) dP[t * L + s] = 0.f;
+  }
+  cp_async_wait<0>();
   __syncthreads();
   pc.mark(12);
   // dbeta_t = v_t.X_t + 2 b_t (sum_c K e^G Y + sum_{s<t} dN_ts A_ts);  dv = b X
@@ -606,11 +622,8 @@ __global__ void __launch_bounds__(NT, 1) intra_bwd64_kernel(Ptrs p) {
       const int c = lane + 32 * cc;
       const int si = t * L + c;
       const float x = X[si];
-      if (ok) {
-        const long long o = tok_off(p, b, tg, h, D) + c;
-        s3 += p.v[o] * x;
-        p.dv[o] = bet[t] * x;
-      }
+      s3 += vs[si] * x;   // zero past S
+      if (ok) p.dv[tok_off(p, b, tg, h, D) + c] = bet[t] * x;
       s2 += k[si] * exp2_fast(G[si]) * Y[si];
       if (c < t) s1 += dN[si] * Am[si];
     }
@@ -637,7 +650,7 @@ __global__ void __launch_bounds__(NT, 1) intra_bwd64_kernel(Ptrs p) {
       const float4 gt = ld4(G + si);
       const float4 eg = exp2_4(gt, f4(0.f)), eh = exp2_4(gc, gt);
       const float4 y = ld4(Y + si), kk = ld4(k + si), qq = ld4(q + si);
-      const float4 dkh = ld4(p.dKh + co + t * D + c), dqg = ld4(p.dQg + co + t * D + c);
+      const float4 dkh = ld4(dKh + si), dqg = ld4(dQg + si);
       const float4 w = mul4(mul4(dkh, kk), eh);
       racc = add4(racc, w);
       const float4 yb = scl4(b2, mul4(y, eg));

@@ -236,6 +236,9 @@ HB_DEVICE void cp_async16(float* smem, const float* gmem, bool valid = true) {
 }
 HB_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 HB_DEVICE void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+// waits until at most N of this thread's committed cp.async groups are pending
+template <int N>
+HB_DEVICE void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // rows x cols fp32 (cols % 4 == 0) from global (row stride gs) to smem (row stride ls)
 template <int ROWS, int COLS>

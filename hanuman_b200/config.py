@@ -142,6 +142,14 @@ class Config:
     micro_batch: int = 0
     # Use the hand-written fused compute+collective paths when world > 1.
     fused_comm: bool = True
+    # data parallelism: reduce-scatter each block's gradients during the last
+    # micro-batch's backward, as soon as they are final (False: after the backward)
+    overlap_reduce: bool = True
+    # FSDP (ZeRO-3): with data parallelism the compute-dtype working copy of every
+    # block's and the embedding's matrices is sharded over the ranks and gathered
+    # for each use (forward, then again for the backward) into a buffer that is
+    # freed afterwards (model/sharding.py:67-113); False keeps it replicated
+    shard_params: bool = True
     # MoE expert weights under data parallelism (no expert axis): "replicated"
     # keeps the full bf16 working copy on every rank (the optimizer stores each
     # updated shard into every peer); "fused_gather" keeps only the rank's own

@@ -67,6 +67,9 @@ class FlatGroup:
     local: bool = False             # expert-parallel slice owned by this rank only
     gathered: bool = False          # one expert-weight tensor, shards = whole experts,
                                     # gathered by the consuming grouped GEMM
+    matrices: bool = False          # the unit's GEMM-weight group
+    sharded: bool = False           # FSDP: only `shard` persists; `work` is gathered for use
+    shard: torch.Tensor = None      # this rank's slice [lo, hi) of the working copy
 
 
 def _build_group(named, dtype, device, world, rank, master_init) -> Optional[FlatGroup]:
@@ -123,7 +126,9 @@ class Engine:
         model.to(self.device)
         self.units = self._units(model)
         self.groups: list[FlatGroup] = []
+        self.unit_groups: list[list[int]] = []   # group indices of each unit
         for unit in self.units:
+            first = len(self.groups)
             local = [(n, p) for n, p in unit if getattr(p, "_ep_local", False)]
             rest = [(n, p) for n, p in unit if not getattr(p, "_ep_local", False)]
             gath = [(n, p) for n, p in rest if getattr(p, "_fsdp_gather", False)]
@@ -140,7 +145,9 @@ class Engine:
                                  master_init)
                 if g is not None:
                     g.local = loc
+                    g.matrices = named is mats
                     self.groups.append(g)
+            self.unit_groups.append(list(range(first, len(self.groups))))
         mdt = torch.bfloat16 if (cfg.optimizer == "lion" and cfg.opt_state_dtype == "bf16") \
             else torch.float32
         for g in self.groups:
@@ -205,7 +212,7 @@ class Engine:
                 optim.adamw_update_(g.master, gs, g.m, g.v, g.decay, lr, cfg.weight_decay,
                                     cfg.adam_b1, cfg.adam_b2, cfg.adam_eps, self.step_count,
                                     coef)
-            g.work[g.lo:g.hi].copy_(g.master.to(g.work.dtype))
+            (g.shard if g.sharded else g.work[g.lo:g.hi]).copy_(g.master.to(g.work.dtype))
         return lr
 
     @torch.no_grad()
@@ -266,7 +273,10 @@ class Engine:
                     v = v[self.rank * nl:(self.rank + 1) * nl]
                 full[o:o + p.numel()] = v.reshape(-1).to(self.device, torch.float32)
             g.master.copy_(full[g.lo:g.hi])
-            g.work.copy_(full.to(g.work.dtype))
+            if g.sharded:
+                g.shard.copy_(full[g.lo:g.hi].to(g.shard.dtype))
+            else:
+                g.work.copy_(full.to(g.work.dtype))
 
     def optimizer_state(self) -> dict:
         return {f"group{i}": {"m": g.m, **({"v": g.v} if g.v is not None else {})}

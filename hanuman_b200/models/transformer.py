@@ -19,6 +19,32 @@ from ..utils.nvtx import rng
 from .layers import KDA, Attention, DenseFFN, MoE, RMSNorm
 
 
+class _UnitBoundary(torch.autograd.Function):
+    """Identity on the tensors that cross a unit (block) boundary.  Its
+    backward runs ``cb``: placed at a block's input it fires once every
+    gradient of that block is final; at a block's output, just before the
+    block's backward starts.  The engine uses the first to launch the block's
+    gradient reduce-scatter while the backward of earlier blocks continues."""
+
+    @staticmethod
+    def forward(ctx, cb, *xs):
+        ctx.cb = cb
+        return xs
+
+    @staticmethod
+    def backward(ctx, *gs):
+        ctx.cb()
+        return (None,) + gs
+
+
+def unit_boundary(hooks, event: str, unit: int, *xs):
+    """Route ``xs`` through a boundary whose backward calls
+    ``hooks.<event>(unit)``; a no-op without hooks or outside autograd."""
+    if hooks is None or not torch.is_grad_enabled() or not any(x.requires_grad for x in xs):
+        return xs
+    return _UnitBoundary.apply(lambda: getattr(hooks, event)(unit), *xs)
+
+
 class Block(nn.Module):
     def __init__(self, cfg: Config, layer: int, gen: torch.Generator):
         super().__init__()
@@ -98,6 +124,9 @@ class Transformer(nn.Module):
         self.register_buffer("rope_cos", cos.to(dt), persistent=False)
         self.register_buffer("rope_sin", sin.to(dt), persistent=False)
         self.n_moe = sum(1 for b in self.blocks if b.use_moe)
+        # set by a data-parallel engine: post_backward(unit) / pre_backward(unit)
+        # callbacks; unit i + 1 is block i (unit 0 is the embedding)
+        self.unit_hooks = None
 
     @property
     def dtype(self):
@@ -138,7 +167,11 @@ class Transformer(nn.Module):
         aux_list = []
         h = self.blocks[0].norm1(x, dtype)
         remat = self.remat_policy() if torch.is_grad_enabled() else "none"
+        hooks = self.unit_hooks
         for i, blk in enumerate(self.blocks):
+            if hooks is not None:
+                hooks.pre_forward(i + 1)
+            x, h = unit_boundary(hooks, "post_backward", i + 1, x, h)
             if remat == "full":
                 x, h, aux = checkpoint(self._fused_block, i, x, h, positions, use_reentrant=False)
             else:
@@ -147,6 +180,9 @@ class Transformer(nn.Module):
                 else:
                     x, h = self._fused_mixer(i, x, h, positions)
                 x, h, aux = self._fused_ffn(i, x, h)
+            x, h = unit_boundary(hooks, "pre_backward", i + 1, x, h)
+            if hooks is not None:
+                hooks.post_forward(i + 1)
             if aux:
                 aux_list.append(aux)
         return h, merge_aux(aux_list, self.cfg.n_experts, self.n_moe, x.device)
@@ -174,13 +210,22 @@ class Transformer(nn.Module):
     def forward(self, tokens, positions=None, cache=None):
         dtype = self.dtype
         self._apply_core_recompute()
+        if self.unit_hooks is not None:
+            self.unit_hooks.pre_forward(0)   # the embedding (also the tied head)
         x = self.embed(tokens)
         if self._fused_residual_ok(x, cache):
             return self._forward_fused(x, positions)
         aux_list = []
         remat = self.remat_policy() if torch.is_grad_enabled() else "none"
-        for blk in self.blocks:
+        hooks = self.unit_hooks if cache is None else None
+        for i, blk in enumerate(self.blocks):
+            if self.unit_hooks is not None:
+                self.unit_hooks.pre_forward(i + 1)
+            (x,) = unit_boundary(hooks, "post_backward", i + 1, x)
             x, aux = blk(x, self.rope_cos, self.rope_sin, dtype, positions, cache, remat=remat)
+            (x,) = unit_boundary(hooks, "pre_backward", i + 1, x)
+            if self.unit_hooks is not None:
+                self.unit_hooks.post_forward(i + 1)
             if aux:
                 aux_list.append(aux)
         h = self.norm_f(x, dtype)

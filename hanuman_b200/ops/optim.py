@@ -18,7 +18,7 @@ def fused_update_cuda(g, cfg, lr, step, coef):
     mode = 0 if cfg.optimizer == "adamw" else 1
     b1 = cfg.adam_b1 if mode == 0 else cfg.lion_b1
     b2 = cfg.adam_b2 if mode == 0 else cfg.lion_b2
-    work = g.work[g.lo:g.hi]
+    work = g.shard if g.sharded else g.work[g.lo:g.hi]
     ext().fused_update(g.master, g.grad[g.lo:g.hi], g.m, g.v, g.decay, work, mode, float(lr),
                        float(cfg.weight_decay), float(b1), float(b2), float(cfg.adam_eps),
                        int(step), coef.reshape(1).float().contiguous())

@@ -27,8 +27,28 @@ Two transports implement the two collectives:
   grouped GEMMs pull the other experts' tiles from the owners' memory
   (model/moe.py:202-245 gathers them with ``all_gather(tiled)`` instead).
 
-With 180 GB per GPU the full working copy stays resident (no re-gather in the
-backward), which is what makes the all-gather a once-per-step operation.
+FSDP (``cfg.shard_params``, the default with more than one rank): the
+compute-dtype working copy of each unit's matrices is sharded too.  Only the
+rank's slice (``shard``, in symmetric memory on the fused transport) persists;
+the model calls ``pre_forward`` / ``post_forward`` around each block and the
+block-boundary autograd nodes call ``pre_backward`` / ``post_backward``, and the
+engine gathers the unit's full weights into the storage of its ``work`` tensor
+before each use (``p2p_gather``: peer loads from every rank's shard; or NCCL
+``all_gather_into_tensor``) and releases that storage afterwards.  The
+parameters and the weight views saved for the backward keep pointing at the
+same storage object, which is re-filled before the unit's backward.  The
+optimizer writes only the local shard; the embedding stays gathered from the
+first forward to the end of the backward (the tied head reads it).
+
+Overlap (``cfg.overlap_reduce``): during the last micro-batch's backward the
+model calls ``post_backward(unit)`` as soon as a block's gradients are final
+(an identity autograd node at the block's input, models/transformer.py), and
+that block's reduce-scatter starts while the backward of the earlier blocks
+runs: NCCL ``reduce_scatter_tensor(async_op=True)``, or on the fused transport
+a comm stream that waits for the block's gradients, runs the device barrier and
+the peer-reading reduce-scatter kernel.  ``reduce_grads`` reduces the units not
+reduced yet (the embedding, whose last gradient is the embedding backward, and
+the final norm) and joins the outstanding work.
 """
 from __future__ import annotations
 
@@ -39,10 +59,17 @@ from ..config import Config
 from ..engine import Engine
 
 
+def ext_gather(peers, world, shard_bytes, out):
+    from ..ops._ext import ext
+    ext().p2p_gather(peers, world, shard_bytes, out)
+
+
 class FSDPEngine(Engine):
     def __init__(self, model, cfg: Config, device, ctx):
         self.ctx = ctx
         super().__init__(model, cfg, device, world=ctx.world, rank=ctx.rank)
+        self._gathered_units: set[int] = set()
+        self._shard_units()
         self.transport = "nccl"
         self.p2p = None
         if cfg.fused_comm and self.device.type == "cuda":
@@ -55,6 +82,125 @@ class FSDPEngine(Engine):
                     print(f"[fsdp] fused peer-memory transport unavailable ({e}); using NCCL")
                 self.p2p = None
         self._attach_expert_gather()
+        self._last_micro = False
+        self._reduced: set[int] = set()
+        self._pending = []          # NCCL work handles of this step
+        self._comm_stream = None
+        if cfg.overlap_reduce or self.sharded_units:
+            model.unit_hooks = self
+        if cfg.overlap_reduce and self.p2p is not None:
+            self._comm_stream = torch.cuda.Stream(device=self.device)
+
+    # ------------------------------------------------------------------
+    # FSDP: sharded working weights
+    def _shard_units(self):
+        """Keep only this rank's slice of every unit's matrix group; the full
+        ``work`` tensor (which the parameters view) gets its storage only while
+        the unit is in use."""
+        self.sharded_units: dict[int, list] = {}
+        if not self.cfg.shard_params or self.world <= 1:
+            return
+        for u, idx in enumerate(self.unit_groups):
+            for i in idx:
+                g = self.groups[i]
+                if g.local or g.gathered or not g.matrices:
+                    continue
+                g.sharded = True
+                g.shard = g.work[g.lo:g.hi].clone()
+                g.full_bytes = g.numel * g.work.element_size()
+                g.work.untyped_storage().resize_(0)
+                self.sharded_units.setdefault(u, []).append(g)
+
+    def gather_unit(self, unit: int):
+        """Full working weights of ``unit`` from every rank's shard (no-op if
+        the unit holds none or is gathered already)."""
+        groups = self.sharded_units.get(unit)
+        if not groups or unit in self._gathered_units:
+            return
+        self._gathered_units.add(unit)
+        for g in groups:
+            st = g.work.untyped_storage()
+            st.resize_(g.full_bytes)
+            if self.p2p is not None:
+                ext_gather(self.p2p.shard_ptrs[id(g)], self.world,
+                           (g.hi - g.lo) * g.work.element_size(), g.work)
+            else:
+                # the collective bumps its output's version counter, which
+                # autograd checks on the weight views saved for the backward:
+                # gather into a temporary and copy at the storage level
+                tmp = torch.empty(g.numel, dtype=g.work.dtype, device=g.work.device)
+                dist.all_gather_into_tensor(tmp, g.shard)
+                st.copy_(tmp.untyped_storage())
+
+    def free_unit(self, unit: int):
+        if unit not in self._gathered_units:
+            return
+        self._gathered_units.discard(unit)
+        for g in self.sharded_units.get(unit, ()):
+            g.work.untyped_storage().resize_(0)
+
+    def gathered_all(self):
+        """Context manager: every unit's weights gathered (evaluation, sampling)."""
+        import contextlib
+
+        @contextlib.contextmanager
+        def cm():
+            for u in self.sharded_units:
+                self.gather_unit(u)
+            try:
+                yield
+            finally:
+                for u in list(self.sharded_units):
+                    self.free_unit(u)
+        return cm()
+
+    def pre_forward(self, unit: int):
+        self.gather_unit(unit)
+
+    def post_forward(self, unit: int):
+        # the embedding stays gathered through the tied head (freed after the
+        # backward); a block is re-gathered for its backward
+        if unit != 0:
+            self.free_unit(unit)
+
+    # ------------------------------------------------------------------
+    # unit hooks (called from the model's backward)
+    def before_forward(self, i, n):
+        self._last_micro = i == n - 1
+
+    def pre_backward(self, unit: int):
+        self.gather_unit(unit)
+
+    def post_backward(self, unit: int):
+        """All gradients of ``unit`` are final for this micro-batch; free its
+        gathered weights and, on the last one, start its reduce-scatter."""
+        self.free_unit(unit)
+        if self.cfg.overlap_reduce and self._last_micro and unit not in self._reduced:
+            self._reduce_unit(unit)
+
+    def _reduce_unit(self, unit: int):
+        first = not self._reduced
+        self._reduced.add(unit)
+        if first and self.p2p is not None:
+            self.p2p.begin_step()   # zeroed sum of squares, on the compute stream
+        groups = [self.groups[i] for i in self.unit_groups[unit] if not self.groups[i].local]
+        if not groups:
+            return
+        if self.p2p is not None:
+            ev = torch.cuda.Event()
+            ev.record()
+            with torch.cuda.stream(self._comm_stream or torch.cuda.current_stream()):
+                if self._comm_stream is not None:
+                    self._comm_stream.wait_event(ev)
+                self.p2p.reduce_scatter_groups(groups)
+            return
+        for g in groups:
+            shard = g.grad[g.lo:g.hi]
+            if self.ctx.backend == "nccl":
+                h = dist.reduce_scatter_tensor(shard, g.grad, op=dist.ReduceOp.SUM, async_op=True)
+            else:  # gloo (CPU ranks): all-reduce, keep the owned slice
+                h = dist.all_reduce(g.grad, op=dist.ReduceOp.SUM, async_op=True)
+            self._pending.append((h, g))
 
     def _attach_expert_gather(self):
         """Hand each MoE layer the shard addresses of its gathered expert tensors."""
@@ -84,10 +230,26 @@ class FSDPEngine(Engine):
     def reduce_grads(self, loss, counts):
         """Mean gradient over ranks into each group's shard; global counts/loss."""
         w = self.world
+        for u in list(self._gathered_units):   # the embedding (kept for the tied head)
+            self.free_unit(u)
         for g in self.groups:
             if g.local:  # expert-parallel slice: the owner saw every token; mean over ranks
                 g.grad.mul_(1.0 / w)
-        if self.p2p is not None:
+        if self.cfg.overlap_reduce:
+            for u in range(len(self.unit_groups)):   # units the backward did not reduce
+                if u not in self._reduced:
+                    self._reduce_unit(u)
+            if self.p2p is not None:
+                with torch.cuda.stream(self._comm_stream or torch.cuda.current_stream()):
+                    self.p2p.end_reduce()
+                if self._comm_stream is not None:
+                    torch.cuda.current_stream().wait_stream(self._comm_stream)
+            for h, g in self._pending:
+                h.wait()
+                g.grad[g.lo:g.hi].mul_(1.0 / w)
+            self._pending = []
+            self._reduced = set()
+        elif self.p2p is not None:
             self.p2p.reduce_scatter_grads()
         else:
             for g in self.groups:
@@ -136,7 +298,7 @@ class FSDPEngine(Engine):
 
     def gather_work(self):
         for g in self.groups:
-            if g.local:
+            if g.local or g.sharded:   # sharded units are gathered at their next use
                 continue
             dist.all_gather_into_tensor(g.work, g.work[g.lo:g.hi].clone()
                                         if self.device.type == "cpu" else g.work[g.lo:g.hi])

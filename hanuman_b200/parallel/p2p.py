@@ -43,7 +43,7 @@ class P2PComm:
         kinds = {}
         for g in groups:
             kinds.setdefault(g.work.dtype, 0)
-            kinds[g.work.dtype] += g.numel
+            kinds[g.work.dtype] += (g.hi - g.lo) if g.sharded else g.numel
         self.wbuf, self.whdl = {}, {}
         for dt, n in kinds.items():
             t = symm.empty(n, dtype=dt, device=dev)
@@ -58,15 +58,23 @@ class P2PComm:
         goff, woff = 0, {dt: 0 for dt in kinds}
         self.layout = []
         self.gather_ptrs = {}   # gathered tensor name -> every rank's shard address
+        self.shard_ptrs = {}    # id(sharded group) -> every rank's shard address (device tensor)
         for g in groups:
             dt = g.work.dtype
+            nw = (g.hi - g.lo) if g.sharded else g.numel
             new_grad = self.gbuf[goff:goff + g.numel]
-            new_work = self.wbuf[dt][woff[dt]:woff[dt] + g.numel]
+            new_work = self.wbuf[dt][woff[dt]:woff[dt] + nw]
             new_grad.copy_(g.grad)
-            new_work.copy_(g.work)
-            g.grad, g.work = new_grad, new_work
+            g.grad = new_grad
+            if g.sharded:   # FSDP: the shard is symmetric; the full buffer stays local
+                new_work.copy_(g.shard)
+                g.shard = new_work
+            else:
+                new_work.copy_(g.work)
+                g.work = new_work
             for n, o, p in zip(g.names, g.offsets, g.params):
-                p.data = g.work[o:o + p.numel()].view(p.shape)
+                if not g.sharded:
+                    p.data = g.work[o:o + p.numel()].view(p.shape)
                 gv = g.grad[o:o + p.numel()].view(p.shape)
                 p.main_grad = gv
                 if p.requires_grad and dt == torch.float32:
@@ -75,7 +83,12 @@ class P2PComm:
             gp = torch.tensor([int(self.ghdl.buffer_ptrs[r]) + goff * 4 for r in range(self.world)],
                               dtype=torch.int64, device=dev)
             bases = [int(self.whdl[dt].buffer_ptrs[r]) + woff[dt] * esz_w for r in range(self.world)]
-            if g.gathered:
+            if g.sharded:
+                # the update writes this rank's shard (its element lo + i sits at
+                # shard + i); peers read the shards to gather the unit
+                wp = torch.tensor([bases[self.rank] - g.lo * esz_w], dtype=torch.int64, device=dev)
+                self.shard_ptrs[id(g)] = torch.tensor(bases, dtype=torch.int64, device=dev)
+            elif g.gathered:
                 # the update stays local; peers pull this shard in their forward
                 wp = torch.tensor([bases[self.rank]], dtype=torch.int64, device=dev)
                 shard = g.numel // self.world
@@ -84,7 +97,7 @@ class P2PComm:
                 wp = torch.tensor(bases, dtype=torch.int64, device=dev)
             self.layout.append((gp, wp))
             goff += g.numel
-            woff[dt] += g.numel
+            woff[dt] += nw
         self.pads = torch.tensor([int(p) for p in self.fhdl.buffer_ptrs], dtype=torch.int64, device=dev)
         self.epoch = 0
         self.sumsq = None
@@ -103,6 +116,23 @@ class P2PComm:
                                      1.0 / self.world, self.sumsq)
         self.barrier()                      # nobody reads a peer's gradients any more
 
+    # per-unit reduce-scatter (overlapped with the backward, on the caller's stream)
+    def begin_step(self):
+        self.sumsq = torch.zeros(1, dtype=torch.float32, device=self.eng.device)
+
+    def reduce_scatter_groups(self, groups):
+        """Barrier (every rank's gradients of these groups are final), then the
+        peer-reading reduce-scatter of each group into its shard."""
+        self.barrier()
+        index = {id(g): i for i, g in enumerate(self.groups)}
+        for g in groups:
+            gp, _ = self.layout[index[id(g)]]
+            ext().p2p_reduce_scatter(gp, self.world, g.lo, g.hi - g.lo, g.grad[g.lo:g.hi],
+                                     1.0 / self.world, self.sumsq)
+
+    def end_reduce(self):
+        self.barrier()                      # nobody reads a peer's gradients any more
+
     def update_and_broadcast(self, cfg, lr, step, coef):
         mode = 0 if cfg.optimizer == "adamw" else 1
         b1 = cfg.adam_b1 if mode == 0 else cfg.lion_b1
@@ -110,7 +140,7 @@ class P2PComm:
         c = coef.reshape(1).float().contiguous()
         for g, (_, wp) in zip(self.groups, self.layout):
             ext().p2p_update_bcast(g.master, g.grad[g.lo:g.hi], g.m, g.v, g.decay, wp,
-                                   1 if g.gathered else self.world,
+                                   1 if (g.gathered or g.sharded) else self.world,
                                    g.lo, g.work.dtype == torch.bfloat16, mode, float(lr),
                                    float(cfg.weight_decay), float(b1), float(b2),
                                    float(cfg.adam_eps), int(step), c)

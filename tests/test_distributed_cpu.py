@@ -48,6 +48,14 @@ def _worker(rank, world, port, out_path):
         for step in range(3):
             toks = _tokens(c, step)[rank * per:(rank + 1) * per]
             losses.append(float(tr.step(toks)))
+        eng = tr.engine
+        # FSDP: every block's and the embedding's matrix group keeps only its
+        # shard between steps (no storage behind the full working tensor)
+        assert len(eng.sharded_units) == len(tr.model.blocks) + 1
+        for gs in eng.sharded_units.values():
+            for g in gs:
+                assert g.work.untyped_storage().nbytes() == 0
+                assert g.shard.numel() * world == g.numel
         st = tr.engine.master_state()
         if rank == 0:
             torch.save((losses, {k: v.clone() for k, v in st.items()},
@@ -78,3 +86,39 @@ def test_fsdp_gloo_matches_single_process(tmp_path):
         assert torch.allclose(state[k], v, atol=2e-5, rtol=1e-4), k
     for b, m in zip(biases, single.model.moe_layers()):
         assert torch.allclose(b, m.bias.detach())
+
+
+def test_unit_hooks_fire_in_backward_order():
+    """The block-boundary autograd nodes call pre_backward(i) before block i's
+    backward and post_backward(i) once its gradients are final, last block first:
+    the order in which the engine starts the per-block gradient reduce-scatter."""
+    from hanuman_b200.models.transformer import Transformer
+    c = _cfg()
+    m = Transformer(c)
+    events = []
+
+    class Rec:
+        def pre_forward(self, u):
+            events.append(("fwd", u))
+
+        def post_forward(self, u):
+            events.append(("fwd_done", u))
+
+        def pre_backward(self, u):
+            events.append(("pre", u))
+
+        def post_backward(self, u):
+            grads_final = all(p.grad is not None for p in m.blocks[u - 1].parameters() if p.requires_grad
+                              and p is not m.blocks[u - 1].ffn.bias if hasattr(m.blocks[u - 1].ffn, "bias"))
+            events.append(("post", u, grads_final))
+
+    m.unit_hooks = Rec()
+    loss, _ = m.loss(_tokens(c, 0))
+    loss.backward()
+    L = len(m.blocks)
+    want = [("fwd", 0)]
+    for u in range(1, L + 1):
+        want += [("fwd", u), ("fwd_done", u)]
+    for u in range(L, 0, -1):
+        want += [("pre", u), ("post", u, True)]
+    assert events == want, events
