@@ -69,6 +69,8 @@ class FSDPEngine(Engine):
         self.ctx = ctx
         super().__init__(model, cfg, device, world=ctx.world, rank=ctx.rank)
         self._gathered_units: set[int] = set()
+        self._prefetch_ev: dict[int, object] = {}
+        self._pf_stream = None
         self._shard_units()
         self.transport = "nccl"
         self.p2p = None
@@ -113,14 +115,43 @@ class FSDPEngine(Engine):
 
     def gather_unit(self, unit: int):
         """Full working weights of ``unit`` from every rank's shard (no-op if
-        the unit holds none or is gathered already)."""
+        the unit holds none or is gathered already; a prefetched unit makes the
+        current stream wait for its gather)."""
         groups = self.sharded_units.get(unit)
-        if not groups or unit in self._gathered_units:
+        if not groups:
+            return
+        if unit in self._gathered_units:
+            ev = self._prefetch_ev.pop(unit, None)
+            if ev is not None:
+                torch.cuda.current_stream().wait_event(ev)
             return
         self._gathered_units.add(unit)
+        self._fill(groups)
+
+    def prefetch_unit(self, unit: int):
+        """Start gathering ``unit`` on the prefetch stream, behind everything the
+        compute stream has enqueued so far, so that it overlaps the compute of
+        the unit in progress."""
+        groups = self.sharded_units.get(unit)
+        if not groups or unit in self._gathered_units or self.device.type != "cuda":
+            return
+        self._gathered_units.add(unit)
+        main = torch.cuda.current_stream()
+        if self._pf_stream is None:
+            self._pf_stream = torch.cuda.Stream(device=self.device)
+        self._pf_stream.wait_stream(main)
+        with torch.cuda.stream(self._pf_stream):
+            self._fill(groups, record=main)
+            ev = torch.cuda.Event()
+            ev.record()
+        self._prefetch_ev[unit] = ev
+
+    def _fill(self, groups, record=None):
         for g in groups:
             st = g.work.untyped_storage()
             st.resize_(g.full_bytes)
+            if record is not None:   # allocated on the prefetch stream, used on `record`
+                g.work.record_stream(record)
             if self.p2p is not None:
                 ext_gather(self.p2p.shard_ptrs[id(g)], self.world,
                            (g.hi - g.lo) * g.work.element_size(), g.work)
@@ -135,6 +166,9 @@ class FSDPEngine(Engine):
     def free_unit(self, unit: int):
         if unit not in self._gathered_units:
             return
+        ev = self._prefetch_ev.pop(unit, None)
+        if ev is not None:          # never used: still order the release after its gather
+            torch.cuda.current_stream().wait_event(ev)
         self._gathered_units.discard(unit)
         for g in self.sharded_units.get(unit, ()):
             g.work.untyped_storage().resize_(0)
@@ -156,6 +190,7 @@ class FSDPEngine(Engine):
 
     def pre_forward(self, unit: int):
         self.gather_unit(unit)
+        self.prefetch_unit(unit + 1)
 
     def post_forward(self, unit: int):
         # the embedding stays gathered through the tied head (freed after the
@@ -170,6 +205,8 @@ class FSDPEngine(Engine):
 
     def pre_backward(self, unit: int):
         self.gather_unit(unit)
+        if unit > 1:
+            self.prefetch_unit(unit - 1)
 
     def post_backward(self, unit: int):
         """All gradients of ``unit`` are final for this micro-batch; free its
