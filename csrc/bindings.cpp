@@ -95,6 +95,10 @@ void kda_bwd64(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor 
                torch::Tensor dKh, torch::Tensor dWt, torch::Tensor dP, torch::Tensor dgC,
                torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor dg, torch::Tensor dbeta);
 void kda64_set_profile(c10::optional<torch::Tensor> counters);
+void kda64_tc_products(torch::Tensor Pm, torch::Tensor Qg, torch::Tensor dout, torch::Tensor dU,
+                       torch::Tensor states, torch::Tensor dstates, torch::Tensor U, torch::Tensor dUp,
+                       torch::Tensor dSq, torch::Tensor dWt, torch::Tensor dQg, torch::Tensor dP,
+                       torch::Tensor dKh, torch::Tensor dgC);
 void kda_prep_fwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::Tensor wv, torch::Tensor f,
                   torch::Tensor a_log, torch::Tensor dt_bias, torch::Tensor braw, int64_t gate_mode,
                   int64_t S, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
@@ -193,6 +197,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kda_fwd64", &hb::kda_fwd64);
   m.def("kda_bwd64", &hb::kda_bwd64);
   m.def("kda64_set_profile", &hb::kda64_set_profile);
+  m.def("kda64_tc_products", &hb::kda64_tc_products);
   m.def("kda_prep_fwd", &hb::kda_prep_fwd);
   m.def("kda_prep_bwd", &hb::kda_prep_bwd);
   m.def("p2p_barrier", &hb::p2p_barrier);

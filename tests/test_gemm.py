@@ -327,3 +327,69 @@ def test_gemm_kseg_matches_fp32_reference(M):
     c2 = torch.ones(M, N, device=dev)
     _ext().gemm_kseg(a, bs, c2, True)
     assert (c2 - 1.0 - ref).norm() / ref.norm() < 1e-5
+
+
+def _swiglu_case(seed, G=5, D=512, F=384, counts=(130, 0, 7, 256, 300)):
+    torch.manual_seed(seed)
+    dev = "cuda"
+    starts, R = _groups(list(counts))
+    BN = 256 if F >= 256 else 128
+
+    def prefix(tiles_n):
+        t = [0]
+        for cnt in counts:
+            t.append(t[-1] + (cnt + 127) // 128 * tiles_n)
+        return torch.tensor(t, dtype=torch.int32, device=dev)
+
+    gs = torch.tensor(starts, dtype=torch.int32, device=dev)
+    gc = torch.tensor(list(counts), dtype=torch.int32, device=dev)
+    return dev, starts, R, BN, prefix, gs, gc
+
+
+def test_grouped_m_swiglu_fwd_matches_fp32_product():
+    """The fused gate|up GEMM with the SwiGLU epilogue against an fp32 PyTorch
+    product of the same bf16 operands: g | u and h = silu(g) u per expert."""
+    import torch.nn.functional as F_
+    G, D, F = 5, 512, 384
+    dev, starts, R, BN, prefix, gs, gc = _swiglu_case(16, G, D, F)
+    counts = (130, 0, 7, 256, 300)
+    x = torch.randn(R, D, device=dev).bfloat16()
+    wg = (torch.randn(G, D, F, device=dev) * 0.05).bfloat16()
+    wu = (torch.randn(G, D, F, device=dev) * 0.05).bfloat16()
+    gu = torch.zeros(R, 2 * F, device=dev).bfloat16()
+    h = torch.zeros(R, F, device=dev).bfloat16()
+    _ext().grouped_gemm_m_swiglu_fwd(x, wg, wu, h, gu, gs, gc, prefix(2 * F // 256))
+    torch.cuda.synchronize()
+    for g, (s, n) in enumerate(zip(starts, counts)):
+        if n == 0:
+            continue
+        xf = x[s:s + n].float()
+        gr, ur = xf @ wg[g].float(), xf @ wu[g].float()
+        hr = F_.silu(gr) * ur
+        assert _rel_err(gu[s:s + n, :F].float(), gr) < 5e-3, g
+        assert _rel_err(gu[s:s + n, F:].float(), ur) < 5e-3, g
+        assert _rel_err(h[s:s + n].float(), hr) < 1e-2, g
+
+
+def test_grouped_m_swiglu_bwd_matches_fp32_product():
+    """dh = dy W_down^T with the SwiGLU backward in the epilogue against fp32
+    PyTorch: dg = dh u silu'(g), du = dh silu(g)."""
+    G, D, F = 5, 512, 384
+    dev, starts, R, BN, prefix, gs, gc = _swiglu_case(17, G, D, F)
+    counts = (130, 0, 7, 256, 300)
+    dy = torch.randn(R, D, device=dev).bfloat16()
+    wd = (torch.randn(G, F, D, device=dev) * 0.05).bfloat16()
+    gu = torch.randn(R, 2 * F, device=dev).bfloat16()
+    got = torch.zeros_like(gu)
+    _ext().grouped_gemm_m_swiglu_bwd(dy, wd, gu, got, gs, gc, prefix((F + BN - 1) // BN))
+    torch.cuda.synchronize()
+    for g, (s, n) in enumerate(zip(starts, counts)):
+        if n == 0:
+            continue
+        dh = dy[s:s + n].float() @ wd[g].float().t()
+        gg, uu = gu[s:s + n, :F].float(), gu[s:s + n, F:].float()
+        sg = torch.sigmoid(gg)
+        dg = dh * uu * sg * (1 + gg * (1 - sg))
+        du = dh * gg * sg
+        assert _rel_err(got[s:s + n, :F].float(), dg) < 1e-2, g
+        assert _rel_err(got[s:s + n, F:].float(), du) < 1e-2, g

@@ -90,3 +90,20 @@ def test_cached_decoding_on_gpu_matches_recompute():
     got = torch.cat(got)
     err = ((got - ref).norm(dim=-1) / ref.norm(dim=-1)).max().item()
     assert err < 5e-2, err
+
+
+def test_tiny_hybrid_gpu_tracks_cpu_oracle_for_ten_steps():
+    """Config 1 trained 10 steps on the GPU (bf16 kernels) and on the CPU fp32
+    oracle from the same weights and tokens: every step's loss within the
+    bf16-versus-fp32 gap, and both descend."""
+    c = _tiny()
+    cpu = Trainer(c, device="cpu")
+    gpu = Trainer(c.replace(dtype="bf16"), device="cuda")
+    lc, lg = [], []
+    for step in range(10):
+        toks = _tokens(c, seed=step % 3)
+        lc.append(float(cpu.step(toks)))
+        lg.append(float(gpu.step(toks)))
+    for a, b in zip(lg, lc):
+        assert abs(a - b) < 3e-2 * b, (lg, lc)
+    assert lg[-1] < lg[0] - 0.2 and lc[-1] < lc[0] - 0.2, (lg, lc)
