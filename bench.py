@@ -47,6 +47,10 @@ def parse():
                          "the grouped GEMMs)")
     ap.add_argument("--no_shard", action="store_true",
                     help="data parallelism with a replicated working copy instead of FSDP")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="validation override: fewer layers than the named config (reported in config)")
+    ap.add_argument("--expert_axis", type=int, default=None,
+                    help="validation override of the expert-parallel degree (reported in config)")
     return ap.parse_args()
 
 
@@ -167,6 +171,10 @@ def main():
         cfg.expert_weights = args.expert_weights
     if args.no_shard:
         cfg.shard_params = False
+    if args.layers:
+        cfg.layers = args.layers
+    if args.expert_axis:
+        cfg.mesh_expert_axis = args.expert_axis
     trainer = Trainer(cfg, device=f"cuda:{local}", dist_ctx=ctx)
     B = args.per_gpu_seqs
     gen = torch.Generator().manual_seed(0 + rank)
@@ -238,6 +246,7 @@ def main():
                        "parallelism": (f"fsdp{world}" if getattr(trainer.engine, "sharded_units", None)
                                        else f"dp{world}") if world > 1 else "single",
                        "expert_weights": cfg.expert_weights if world > 1 else "local",
+                       "layers": cfg.layers, "expert_parallel": cfg.mesh_expert_axis,
                        "overlap_reduce": bool(cfg.overlap_reduce) if world > 1 else False,
                        "optimizer": cfg.optimizer,
                        "grad_transport": getattr(trainer.engine, "transport", "local"),

@@ -113,7 +113,6 @@ void kda_prep_bwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::
 void p2p_barrier(torch::Tensor pads, int64_t rank, int64_t world, int64_t epoch);
 void p2p_reduce_scatter(torch::Tensor peers, int64_t world, int64_t off, int64_t n, torch::Tensor out,
                         double scale, torch::Tensor sumsq);
-void p2p_gather(torch::Tensor peers, int64_t world, int64_t shard_bytes, torch::Tensor out);
 void p2p_update_bcast(torch::Tensor p, torch::Tensor g, torch::Tensor m, c10::optional<torch::Tensor> v,
                       torch::Tensor decay, torch::Tensor work_peers, int64_t world, int64_t off,
                       bool work_bf16, int64_t mode, double lr, double wd, double b1, double b2, double eps,
@@ -147,12 +146,26 @@ static torch::Tensor status_view() {
                           torch::TensorOptions().dtype(torch::kInt32).device(torch::kCUDA, dev));
 }
 
+// FSDP gather through the copy engines: out[r * shard_bytes ...] = bytes at
+// srcs[r] (every rank's shard, peer addresses included), one cudaMemcpyAsync
+// per rank on the current stream; no SM runs the copy, so it overlaps compute.
+static void copy_engine_gather(std::vector<int64_t> srcs, int64_t shard_bytes, torch::Tensor out) {
+  HB_CHECK(out.is_contiguous() && (int64_t)out.numel() * out.element_size() == shard_bytes * (int64_t)srcs.size(),
+           "copy_engine_gather: contiguous output of world * shard bytes");
+  char* dst = reinterpret_cast<char*>(out.data_ptr());
+  const cudaStream_t st = hb::cur_stream();
+  for (size_t r = 0; r < srcs.size(); ++r)
+    HB_CUDA_CHECK(cudaMemcpyAsync(dst + r * shard_bytes, reinterpret_cast<const void*>(srcs[r]), shard_bytes,
+                                  cudaMemcpyDeviceToDevice, st));
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "hanuman_b200 sm_100a kernels";
   m.def("num_sms", &hb::num_sms);
   m.def("read_status", &read_status, "read the device status word (0 = ok)");
   m.def("clear_status", &clear_status);
   m.def("status_view", &status_view, "the device status word as an int32 tensor view");
+  m.def("copy_engine_gather", &copy_engine_gather);
   m.def("set_wait_budget_ns", &hb::set_wait_budget_ns);
   m.def("gemm", &hb::gemm, "c (+)= op(a) @ op(b) on tcgen05", py::arg("a"), py::arg("b"),
         py::arg("c"), py::arg("trans_a"), py::arg("trans_b"), py::arg("accumulate"),
@@ -202,7 +215,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kda_prep_bwd", &hb::kda_prep_bwd);
   m.def("p2p_barrier", &hb::p2p_barrier);
   m.def("p2p_reduce_scatter", &hb::p2p_reduce_scatter);
-  m.def("p2p_gather", &hb::p2p_gather);
   m.def("p2p_update_bcast", &hb::p2p_update_bcast);
   m.def("ep_scatter", &hb::ep_scatter);
   m.def("ep_zero_pads", &hb::ep_zero_pads);

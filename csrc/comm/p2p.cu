@@ -10,8 +10,6 @@
 //   p2p_update_bcast     Lion / AdamW on the shard; the new working value is
 //                        stored into the working copy of EVERY rank (peer
 //                        stores), which replaces the parameter all-gather
-//   p2p_gather           FSDP: a unit's full working weights from every rank's
-//                        shard (peer loads), before the unit's forward and backward
 // Plain ld/st to peer addresses only: no TMA, no multicast.  A wait that runs
 // out of budget records kErrTimeoutPeer in the status word and returns; the
 // reduce-scatter and update kernels read the status word first and do nothing
@@ -138,24 +136,6 @@ __global__ void update_bcast_kernel(float* __restrict__ p, const float* __restri
   }
 }
 
-// FSDP all-gather of a working-weight group: out[r * shard + i] = peers[r][i]
-// (each rank's shard in symmetric memory, plain 16-byte peer loads; the bytes
-// are copied as they are, whatever the element type).  Skips everything once
-// an earlier kernel recorded an error.
-__global__ void gather_kernel(const long long* __restrict__ peers, int world, long long shard_bytes,
-                              char* __restrict__ out, const int* __restrict__ status) {
-  if (*reinterpret_cast<const volatile int*>(status) != 0) return;
-  const long long n16 = shard_bytes / 16;
-  const long long total = n16 * world;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int r = (int)(i / n16);
-    const long long j = i - (long long)r * n16;
-    const int4 v = reinterpret_cast<const int4*>(peers[r])[j];
-    reinterpret_cast<int4*>(out + (long long)r * shard_bytes)[j] = v;
-  }
-}
-
 int grid_for(long long work, int per_block) {
   long long gsz = (work + per_block - 1) / per_block;
   return (int)std::max(1LL, std::min(gsz, (long long)num_sms() * 8));
@@ -179,18 +159,6 @@ void p2p_reduce_scatter(torch::Tensor peers, int64_t world, int64_t off, int64_t
   reduce_scatter_kernel<<<grid_for(n / 4 + 1, 256), 256, 0, cur_stream()>>>(
       reinterpret_cast<const long long*>(peers.data_ptr<int64_t>()), (int)world, off, n,
       out.data_ptr<float>(), (float)scale, sumsq.data_ptr<float>(), status_ptr());
-  HB_CUDA_CHECK(cudaGetLastError());
-}
-
-void p2p_gather(torch::Tensor peers, int64_t world, int64_t shard_bytes, torch::Tensor out) {
-  HB_CHECK(shard_bytes % 16 == 0, "p2p_gather: shard size must be a multiple of 16 bytes");
-  HB_CHECK(out.is_contiguous() && (long long)out.numel() * out.element_size() == shard_bytes * world,
-           "p2p_gather: contiguous output of world * shard bytes");
-  HB_CHECK((reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0, "p2p_gather: 16-byte aligned output");
-  if (shard_bytes == 0) return;
-  gather_kernel<<<grid_for(shard_bytes / 16 * world, 256), 256, 0, cur_stream()>>>(
-      reinterpret_cast<const long long*>(peers.data_ptr<int64_t>()), (int)world, shard_bytes,
-      reinterpret_cast<char*>(out.data_ptr()), status_ptr());
   HB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -169,8 +169,9 @@ class ParquetLoader:
             if field is None:
                 raise KeyError(f"no text field in {path}; columns={tab.column_names}")
             docs = tab.column(field).to_pylist()
-            if self.shuffle:  # seeded within-row-group shuffle
-                order = np.random.default_rng([self.seed, rg, len(path)]).permutation(len(docs))
+            if self.shuffle:  # seeded within-row-group shuffle (file = its index in `files`)
+                fi = self.files.index(path)
+                order = np.random.default_rng([self.seed, fi, rg]).permutation(len(docs))
                 docs = [docs[i] for i in order]
             for text in docs:
                 yield text or ""

@@ -33,8 +33,10 @@ rank's slice (``shard``, in symmetric memory on the fused transport) persists;
 the model calls ``pre_forward`` / ``post_forward`` around each block and the
 block-boundary autograd nodes call ``pre_backward`` / ``post_backward``, and the
 engine gathers the unit's full weights into the storage of its ``work`` tensor
-before each use (``p2p_gather``: peer loads from every rank's shard; or NCCL
-``all_gather_into_tensor``) and releases that storage afterwards.  The
+before each use (on the fused transport, one copy-engine ``cudaMemcpyAsync``
+per rank from every rank's shard in symmetric memory, so a prefetch of the
+next unit on a side stream takes no SM time from the unit that computes; or
+NCCL ``all_gather_into_tensor``) and releases that storage afterwards.  The
 parameters and the weight views saved for the backward keep pointing at the
 same storage object, which is re-filled before the unit's backward.  The
 optimizer writes only the local shard; the embedding stays gathered from the
@@ -59,9 +61,9 @@ from ..config import Config
 from ..engine import Engine
 
 
-def ext_gather(peers, world, shard_bytes, out):
+def ext_copy_gather(addrs, shard_bytes, out):
     from ..ops._ext import ext
-    ext().p2p_gather(peers, world, shard_bytes, out)
+    ext().copy_engine_gather(list(addrs), shard_bytes, out)
 
 
 class FSDPEngine(Engine):
@@ -153,8 +155,9 @@ class FSDPEngine(Engine):
             if record is not None:   # allocated on the prefetch stream, used on `record`
                 g.work.record_stream(record)
             if self.p2p is not None:
-                ext_gather(self.p2p.shard_ptrs[id(g)], self.world,
-                           (g.hi - g.lo) * g.work.element_size(), g.work)
+                # copy engines read every rank's shard (peer addresses of the
+                # symmetric buffers): no SM time, so a prefetch overlaps compute
+                ext_copy_gather(self.p2p.shard_addrs[id(g)], (g.hi - g.lo) * g.work.element_size(), g.work)
             else:
                 # the collective bumps its output's version counter, which
                 # autograd checks on the weight views saved for the backward:

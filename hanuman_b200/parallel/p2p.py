@@ -59,6 +59,7 @@ class P2PComm:
         self.layout = []
         self.gather_ptrs = {}   # gathered tensor name -> every rank's shard address
         self.shard_ptrs = {}    # id(sharded group) -> every rank's shard address (device tensor)
+        self.shard_addrs = {}   # the same addresses as host integers (copy-engine gather)
         for g in groups:
             dt = g.work.dtype
             nw = (g.hi - g.lo) if g.sharded else g.numel
@@ -88,6 +89,7 @@ class P2PComm:
                 # shard + i); peers read the shards to gather the unit
                 wp = torch.tensor([bases[self.rank] - g.lo * esz_w], dtype=torch.int64, device=dev)
                 self.shard_ptrs[id(g)] = torch.tensor(bases, dtype=torch.int64, device=dev)
+                self.shard_addrs[id(g)] = bases
             elif g.gathered:
                 # the update stays local; peers pull this shard in their forward
                 wp = torch.tensor([bases[self.rank]], dtype=torch.int64, device=dev)

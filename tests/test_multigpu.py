@@ -20,20 +20,19 @@ def _port():
     return p
 
 
-def _losses_match(la, lb, spread=None):
+def _losses_match(la, lb):
     """Step 1 sees identical weights and the same forward kernels, so its loss
-    agrees to rounding.  Later steps inherit the run-to-run differences of the
-    atomically summed gradients (embedding, decay biases); AdamW's first
-    updates are sign-like, so a near-zero gradient element can move by 2 lr
-    either way and the loss drifts (a 1.1e-3 relative gap at step 3 was seen
-    once, 1e-5 on a rerun of the same build)."""
+    agrees to rounding.  Later steps inherit run-to-run differences of the
+    gradients that are summed with atomics (the split-K weight-gradient GEMMs,
+    the embedding scatter-add, the decay-bias sums); AdamW's first updates are
+    sign-like, so a near-zero gradient element can move by 2 lr either way and
+    the loss drifts by up to about 1e-3 relative between any two runs, the NCCL
+    arm against itself included (measured: 2.3e-4 and 2.5e-4 at steps 2 and 3
+    of two identical NCCL runs).  The transports themselves are checked
+    exactly by test_p2p_transport_kernels_are_exact_and_replayable."""
     assert abs(la[0] - lb[0]) < 1e-4 * abs(la[0]), (la, lb)
-    for i, (a, b) in enumerate(zip(la[1:], lb[1:]), start=1):
-        bound = 3e-3 * abs(a)
-        if spread is not None:
-            # no looser than three times what the same arm shows against itself
-            bound = min(bound, max(3.0 * spread[i], 1e-4 * abs(a)))
-        assert abs(a - b) < bound, (i, la, lb, spread)
+    for a, b in zip(la[1:], lb[1:]):
+        assert abs(a - b) < 3e-3 * abs(a), (la, lb)
 
 
 def _worker(rank, world, port, out_path):
@@ -46,7 +45,7 @@ def _worker(rank, world, port, out_path):
     ctx = init_distributed(timeout_s=120)
     try:
         res = {}
-        for fused in (False, "nccl_again", True, "gather"):
+        for fused in (False, True, "gather"):
             c = get_config("tiny_hybrid").replace(dtype="bf16", batch_size=4, seq_len=128,
                                                   fused_comm=fused in (True, "gather"))
             if fused == "gather":
@@ -84,19 +83,16 @@ def test_p2p_transport_matches_nccl(tmp_path):
         p.join(timeout=600)
         assert p.exitcode == 0
     res = torch.load(out)
-    # run-to-run spread of one arm (the NCCL baseline run twice): the atomically
-    # summed gradients make later steps differ in the last bits
-    spread = [abs(a - b) for a, b in zip(res[False][0], res["nccl_again"][0])]
     # the fused expert-weight gather (P1) computes what the replicated weights
     # compute: the same products (the replicated arm's SwiGLU-epilogue GEMM
     # matches the separate GEMMs + SwiGLU bit for bit), only the source of B differs
     (lg, sg), (lp, sp) = res["gather"], res[True]
-    _losses_match(lg, lp, spread)
+    _losses_match(lg, lp)
     for k in sp:
         diff = (sg[k] - sp[k]).abs()
         assert diff.max().item() <= 6 * 3e-4 + 1e-5, (k, diff.max().item())
     (l0, s0), (l1, s1) = res[False], res[True]
-    _losses_match(l0, l1, spread)
+    _losses_match(l0, l1)
     # The embedding gradient is summed with atomics, so the two runs differ in the
     # last bits; AdamW's first steps are sign-like (|update| ~ lr per step), so an
     # element can move by up to 2 * lr per step between runs (lr = 3e-4, 3 steps).
@@ -164,7 +160,8 @@ def test_expert_parallel_matches_data_parallel(tmp_path):
 def _replay_worker(rank, world, port, out_path):
     """The peer-memory reduce-scatter run twice on the same symmetric buffers:
     bitwise-equal outputs, the NCCL all-reduce's values, and every signal-pad
-    slot at the last barrier epoch."""
+    slot at the last barrier epoch; the FSDP copy-engine gather of every rank's
+    symmetric shard equals NCCL's all-gather bit for bit."""
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     import torch.distributed as dist
@@ -203,7 +200,19 @@ def _replay_worker(rank, world, port, out_path):
         ref = buf.clone()
         dist.all_reduce(ref)
         ref = ref[lo:lo + cnt] * 0.5
+        # FSDP gather: copy engines from the peers' symmetric shards vs NCCL
+        shard = symm.empty(4096, dtype=torch.bfloat16, device=dev)
+        shard.copy_(torch.randn(4096, generator=g, device=dev).bfloat16())
+        sh = symm.rendezvous(shard, dist.group.WORLD)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        full = torch.empty(4096 * world, dtype=torch.bfloat16, device=dev)
+        ext().copy_engine_gather([int(sh.buffer_ptrs[r]) for r in range(world)], 4096 * 2, full)
+        ref_full = torch.empty_like(full)
+        dist.all_gather_into_tensor(ref_full, shard)
+        torch.cuda.synchronize(dev)
         res = {"bitwise": torch.equal(outs[0][0], outs[1][0]),
+               "gather_exact": torch.equal(full, ref_full),
                "err": ((outs[0][0] - ref).abs().max() / ref.abs().max()).item(),
                "ss_rel": abs(outs[0][1].item() - (ref * ref).sum().item()) / (ref * ref).sum().item(),
                "flags": flags[:world].cpu().tolist(), "epoch": epoch,
@@ -215,7 +224,7 @@ def _replay_worker(rank, world, port, out_path):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_p2p_reduce_scatter_deterministic_replay(tmp_path):
+def test_p2p_transport_kernels_are_exact_and_replayable(tmp_path):
     ctx = mp.get_context("spawn")
     port = _port()
     out = str(tmp_path / "replay.pt")
@@ -228,6 +237,7 @@ def test_p2p_reduce_scatter_deterministic_replay(tmp_path):
     for r in range(2):
         res = torch.load(f"{out}.{r}")
         assert res["bitwise"], res
+        assert res["gather_exact"], res
         assert res["err"] < 1e-6, res
         assert res["ss_rel"] < 1e-5, res
         assert res["flags"] == [res["epoch"]] * 2, res
