@@ -95,10 +95,9 @@ void kda_bwd64(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor 
                torch::Tensor dKh, torch::Tensor dWt, torch::Tensor dP, torch::Tensor dgC,
                torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor dg, torch::Tensor dbeta);
 void kda64_set_profile(c10::optional<torch::Tensor> counters);
-void kda64_tc_products(torch::Tensor Pm, torch::Tensor Qg, torch::Tensor dout, torch::Tensor dU,
-                       torch::Tensor states, torch::Tensor dstates, torch::Tensor U, torch::Tensor dUp,
-                       torch::Tensor dSq, torch::Tensor dWt, torch::Tensor dQg, torch::Tensor dP,
-                       torch::Tensor dKh, torch::Tensor dgC);
+void kda64_tc_products(torch::Tensor dout, torch::Tensor dU, torch::Tensor states, torch::Tensor dstates,
+                       torch::Tensor U, torch::Tensor dWt, torch::Tensor dQg, torch::Tensor dP, torch::Tensor dKh,
+                       torch::Tensor dgC);
 void kda_prep_fwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::Tensor wv, torch::Tensor f,
                   torch::Tensor a_log, torch::Tensor dt_bias, torch::Tensor braw, int64_t gate_mode,
                   int64_t S, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,

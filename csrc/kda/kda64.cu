@@ -30,8 +30,7 @@
 //   bwd_pre64_kernel          P^T dO and Qg^T dO
 //   state_bwd64_kernel        grid (64 / VS, H, B): dS per chunk (dstates) and dU
 //   state_products64_kernel   dQg, dKh, dWt, dP, dgC (the S0 / dS products)
-// The chunk-parallel backward products (P^T dO, Qg^T dO and the S0 / dS
-// products) also have a tcgen05 version (kda64_tc.cu, HB_KDA64_TC=1).
+// The S0 / dS state products also have a tcgen05 version (kda64_tc.cu).
 //   intra_bwd64_kernel        X, Y, dN, dbeta, dv and the decay contractions
 // All products are 3xTF32 warp-tile matmuls (fp32-level accuracy).
 #include <torch/extension.h>
@@ -782,9 +781,7 @@ __global__ void __launch_bounds__(NT, 1) intra_bwd64_kernel(Ptrs p) {
 
 static bool al16_64(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-// tcgen05 versions of the chunk-parallel backward products (kda64_tc.cu)
-void kda64_bwd_pre_tc(const float* Pm, const float* Qg, const float* dout, float* dUp, float* dSq, int B,
-                      int S, int H, int NC);
+// tcgen05 version of the chunk-parallel backward state products (kda64_tc.cu)
 void kda64_products_tc(const float* dU, const float* dout, const float* states, const float* dstates,
                        const float* U, float* dWt, float* dQg, float* dP, float* dKh, float* dgC, int B, int S,
                        int H, int NC);
@@ -940,12 +937,8 @@ void kda_bwd64(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor 
   }
   const dim3 chunks(p.NC, p.H, p.B);
   const bool tc = kda64_use_tc();
-  if (tc) {
-    kda64_bwd_pre_tc(p.Pm, p.Qg, p.dout, p.dUp, p.dSq, p.B, p.S, p.H, p.NC);
-  } else {
-    bwd_pre64_kernel<<<chunks, 256, s0, cur_stream()>>>(p);
-    HB_CUDA_CHECK(cudaGetLastError());
-  }
+  bwd_pre64_kernel<<<chunks, 256, s0, cur_stream()>>>(p);
+  HB_CUDA_CHECK(cudaGetLastError());
   state_bwd64_kernel<<<dim3(D / VS, p.H, p.B), 256, s1, cur_stream()>>>(p);
   HB_CUDA_CHECK(cudaGetLastError());
   if (tc) {

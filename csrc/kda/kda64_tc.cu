@@ -1,17 +1,19 @@
 // Chunk-parallel products of the chunk-64 KDA backward on the 5th-generation
 // tensor cores (tcgen05 + TMEM), fp32 accurate.
 //
-// Each CTA handles one chunk (64 tokens of one head) and computes two 64x64
-// products that share their B operand, as ONE M = 128 MMA:
+// Per chunk (64 tokens of one head) two 64x64 products that share their B
+// operand run as ONE M = 128 MMA:
 //
 //     [C_top; C_bot] (128 x 64) = [A_top; A_bot] (128 x 64) . B (64 x 64)
 //
-//   bwd_pre      A = [P^T ; Qg^T] (MN-major), B = dO  (MN-major)
-//                -> dUp = P^T dO,  dSq = Qg^T dO
-//   products_u   A = [dU ; dO]    (K-major),  B = S0^T (K-major)
-//                -> dWt = -dU S0^T, dQg = dO S0^T
-//   products_s   A = [dO ; dS]    (K-major),  B = U^T  (K-major)
-//                -> dP = dO U^T,   dKh = (dS U^T)^T;  and dgC = rowsum(dS * S0)
+//   products_u   A = [dU ; dO],  B = S0^T  -> dWt = -dU S0^T, dQg = dO S0^T
+//   products_s   A = [dO ; dS],  B = U^T   -> dP = dO U^T,   dKh = (dS U^T)^T;
+//                                             and dgC = rowsum(dS * S0)
+//
+// Both contract over the value index, the contiguous one of every tile, so
+// all operands are K-major.  (Products over the row index, like P^T dO, would
+// need MN-major fp32 operands, which tcgen05 reads only in the 128-byte swizzle
+// with 32-byte atoms; those stay on the warp-level kernels.)
 //
 // Operands are fp32 [64 x 64] tiles loaded by TMA (two 32-column boxes with
 // 128-byte swizzle, the canonical tcgen05 tile layout; rows past the sequence
@@ -36,7 +38,7 @@ constexpr int ATOM = 8192;                 // one 32-column x 64-row fp32 box (1
 constexpr int A_BYTES = 4 * ATOM;          // 128 x 64 fp32
 constexpr int B_BYTES = 2 * ATOM;          // 64 x 64 fp32
 constexpr int SMEM = 2 * (A_BYTES + B_BYTES) + 1024 + 64;  // hi + lo regions, align, barriers
-constexpr int TMEM_COLS = 64;
+constexpr int TMEM_COLS = 128;   // two 64-column accumulators
 
 // Instruction descriptor, kind::tf32: D fp32, A / B tf32, M = 128, N = 64.
 __host__ __device__ constexpr uint32_t idesc_tf32(bool a_mn, bool b_mn) {
@@ -81,14 +83,15 @@ HB_DEVICE void load_box(uint32_t dst, const CUtensorMap* m, uint32_t bar, int ki
 HB_DEVICE uint64_t desc_kmajor(uint32_t base, int rows, int kk) {
   return make_smem_desc(base + (kk >> 2) * rows * 128 + (kk & 3) * 32, 16, 1024);
 }
-// MN-major: 32-element MN atoms of [64 K rows x 128 B] (8 KB apart); a K step
-// of 8 rows advances 1024 B.
-HB_DEVICE uint64_t desc_mnmajor(uint32_t base, int kk) { return make_smem_desc(base + kk * 1024, ATOM, 1024); }
 
-template <bool A_MN, bool B_MN>
+// Persistent: each CTA walks chunks c = blockIdx.x, blockIdx.x + gridDim.x, ...
+// The next chunk's TMA loads are issued as soon as the current chunk's MMAs
+// have retired (the operand tiles are free) and land while the current
+// accumulator is read back from TMEM and stored; the accumulator alternates
+// between two 64-column TMEM buffers.
 __global__ void __launch_bounds__(THREADS, 2)
     pair_product_kernel(const __grid_constant__ CUtensorMap tmTop, const __grid_constant__ CUtensorMap tmBot,
-                        const __grid_constant__ CUtensorMap tmB, const Args p) {
+                        const __grid_constant__ CUtensorMap tmB, const Args p, int chunks) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sA = smem_u32(smem);
@@ -101,8 +104,6 @@ __global__ void __launch_bounds__(THREADS, 2)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
   volatile int* go_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int c = blockIdx.x;
-  const int n = c % p.NC, h = (c / p.NC) % p.H, b = c / (p.NC * p.H);
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(full), 1);
@@ -116,105 +117,120 @@ __global__ void __launch_bounds__(THREADS, 2)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem0 = *tmem_slot;
 
-  // ---- TMA: A_top, A_bot, B (two 32-column boxes each)
-  if (threadIdx.x == 0) {
+  auto issue_loads = [&](int c) {
+    const int n = c % p.NC, h = (c / p.NC) % p.H, b = c / (p.NC * p.H);
     mbar_expect_tx(smem_u32(full), A_BYTES + B_BYTES);
     for (int a = 0; a < 2; ++a) {
-      // K-major A: [k atom][128 rows]; MN-major A: [m atom][64 k rows]
-      const uint32_t top = A_MN ? sA + a * ATOM : sA + a * 2 * ATOM;
-      const uint32_t bot = A_MN ? sA + (2 + a) * ATOM : sA + a * 2 * ATOM + ATOM;
+      // K-major A: [k atom][128 rows] (top rows 0-63, bottom rows 64-127)
+      const uint32_t top = sA + a * 2 * ATOM;
+      const uint32_t bot = top + ATOM;
       load_box(top, &tmTop, smem_u32(full), p.kind_top, 32 * a, c, n, h, b);
       load_box(bot, &tmBot, smem_u32(full), p.kind_bot, 32 * a, c, n, h, b);
       load_box(sB + a * ATOM, &tmB, smem_u32(full), p.kind_b, 32 * a, c, n, h, b);
     }
-  }
-  bool ok = mbar_wait(smem_u32(full), 0, p.status, kErrTimeoutProducer, p.budget_ns);
-  if (!ok) mbar_wait(smem_u32(full), 0, nullptr, 0, p.budget_ns);  // copies still in flight
-  // ---- hi / lo split in place (elementwise: the swizzle does not matter)
-  if (ok) {
-    float4* hi = reinterpret_cast<float4*>(smem);
-    float4* lo = reinterpret_cast<float4*>(smem + A_BYTES + B_BYTES);
-    for (int i = threadIdx.x; i < (A_BYTES + B_BYTES) / 16; i += THREADS) {
-      float4 x = hi[i];
-      float4 hv, lv;
-      hv.x = __uint_as_float(__float_as_uint(x.x) & 0xffffe000u);
-      hv.y = __uint_as_float(__float_as_uint(x.y) & 0xffffe000u);
-      hv.z = __uint_as_float(__float_as_uint(x.z) & 0xffffe000u);
-      hv.w = __uint_as_float(__float_as_uint(x.w) & 0xffffe000u);
-      lv = make_float4(x.x - hv.x, x.y - hv.y, x.z - hv.z, x.w - hv.w);
-      hi[i] = hv;
-      lo[i] = lv;
+  };
+  if (threadIdx.x == 0 && blockIdx.x < chunks) issue_loads(blockIdx.x);
+  bool alive = true;
+  int it = 0;
+  for (int c = blockIdx.x; c < chunks && alive; c += gridDim.x, ++it) {
+    const uint32_t par = it & 1;
+    bool ok = mbar_wait(smem_u32(full), par, p.status, kErrTimeoutProducer, p.budget_ns);
+    if (!ok) mbar_wait(smem_u32(full), par, nullptr, 0, p.budget_ns);  // copies still in flight
+    // ---- hi / lo split in place (elementwise: the swizzle does not matter)
+    if (ok) {
+      float4* hi = reinterpret_cast<float4*>(smem);
+      float4* lo = reinterpret_cast<float4*>(smem + A_BYTES + B_BYTES);
+      for (int i = threadIdx.x; i < (A_BYTES + B_BYTES) / 16; i += THREADS) {
+        const float4 x = hi[i];
+        float4 hv;
+        hv.x = __uint_as_float(__float_as_uint(x.x) & 0xffffe000u);
+        hv.y = __uint_as_float(__float_as_uint(x.y) & 0xffffe000u);
+        hv.z = __uint_as_float(__float_as_uint(x.z) & 0xffffe000u);
+        hv.w = __uint_as_float(__float_as_uint(x.w) & 0xffffe000u);
+        hi[i] = hv;
+        lo[i] = make_float4(x.x - hv.x, x.y - hv.y, x.z - hv.z, x.w - hv.w);
+      }
+      fence_proxy_async();   // generic-proxy smem writes -> visible to the tensor core
     }
-    fence_proxy_async();   // generic-proxy smem writes -> visible to the tensor core
-  }
-  // one decision for the whole CTA: thread 0's view of its loads and the status
-  if (threadIdx.x == 0) *go_flag = (ok && *reinterpret_cast<volatile int*>(p.status) == 0) ? 1 : 0;
-  __syncthreads();
-  const bool go = *go_flag != 0;
-  // ---- MMAs: 8 K steps x (hi.hi + hi.lo + lo.hi)
-  if (go && threadIdx.x == 0) {
+    tc_fence_before();
+    // one decision for the whole CTA: thread 0's view of its loads and the status
+    if (threadIdx.x == 0) *go_flag = (ok && *reinterpret_cast<volatile int*>(p.status) == 0) ? 1 : 0;
+    __syncthreads();
+    const bool go = *go_flag != 0;
+    const uint32_t tmem = tmem0 + 64 * par;
+    // ---- MMAs: 8 K steps x (hi.hi + hi.lo + lo.hi), then the next chunk's loads
+    if (go && threadIdx.x == 0) {
+      tc_fence_after();
+      constexpr uint32_t idesc = idesc_tf32(false, false);
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint64_t ah = desc_kmajor(sA, 128, kk), al = desc_kmajor(sAlo, 128, kk);
+        const uint64_t bh = desc_kmajor(sB, 64, kk), bl = desc_kmajor(sBlo, 64, kk);
+        umma_tf32(tmem, ah, bh, idesc, kk > 0 ? 1u : 0u);
+        umma_tf32(tmem, ah, bl, idesc, 1u);
+        umma_tf32(tmem, al, bh, idesc, 1u);
+      }
+      umma_commit(smem_u32(done));
+    }
+    ok = go;
+    if (go) {
+      ok = mbar_wait(smem_u32(done), par, p.status, kErrTimeoutMma, p.budget_ns);
+      if (!ok) mbar_wait(smem_u32(done), par, nullptr, 0, p.budget_ns);  // MMAs still in flight
+    }
     tc_fence_after();
-    constexpr uint32_t idesc = idesc_tf32(A_MN, B_MN);
-    for (int kk = 0; kk < 8; ++kk) {
-      const uint64_t ah = A_MN ? desc_mnmajor(sA, kk) : desc_kmajor(sA, 128, kk);
-      const uint64_t al = A_MN ? desc_mnmajor(sAlo, kk) : desc_kmajor(sAlo, 128, kk);
-      const uint64_t bh = B_MN ? desc_mnmajor(sB, kk) : desc_kmajor(sB, 64, kk);
-      const uint64_t bl = B_MN ? desc_mnmajor(sBlo, kk) : desc_kmajor(sBlo, 64, kk);
-      umma_tf32(tmem, ah, bh, idesc, kk > 0 ? 1u : 0u);
-      umma_tf32(tmem, ah, bl, idesc, 1u);
-      umma_tf32(tmem, al, bh, idesc, 1u);
-    }
-    umma_commit(smem_u32(done));
-  }
-  ok = go;
-  if (go) {
-    ok = mbar_wait(smem_u32(done), 0, p.status, kErrTimeoutMma, p.budget_ns);
-    if (!ok) mbar_wait(smem_u32(done), 0, nullptr, 0, p.budget_ns);  // MMAs still in flight
-  }
-  tc_fence_after();
-  // ---- epilogue: row r = 32 warp + lane of the 128 x 64 accumulator
-  if (ok) {
-    const long long co = (long long)c * 64 * 64;
-    const int r = 32 * warp + lane;
-    const bool top = r < 64;
-    const int rr = top ? r : r - 64;
-    const float alpha = top ? p.alpha_top : p.alpha_bot;
+    if (!ok) alive = false;
+    // operands consumed: the next chunk's tiles land during this epilogue
+    if (ok && threadIdx.x == 0 && c + gridDim.x < chunks) issue_loads(c + gridDim.x);
+    // ---- epilogue: row r = 32 warp + lane of the 128 x 64 accumulator
+    if (ok) {
+      const long long co = (long long)c * 64 * 64;
+      const int r = 32 * warp + lane;
+      const bool top = r < 64;
+      const int rr = top ? r : r - 64;
+      const float alpha = top ? p.alpha_top : p.alpha_bot;
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * warp) << 16) + 32 * half, v);
-      tmem_ld_wait();
-      if (top || !p.bot_transposed) {
-        float* dst = (top ? p.out_top : p.out_bot) + co + rr * 64 + 32 * half;
+      for (int half = 0; half < 2; ++half) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * warp) << 16) + 32 * half, v);
+        tmem_ld_wait();
+        if (top || !p.bot_transposed) {
+          float* dst = (top ? p.out_top : p.out_bot) + co + rr * 64 + 32 * half;
 #pragma unroll
-        for (int j = 0; j < 32; j += 4)
-          *reinterpret_cast<float4*>(dst + j) =
-              make_float4(alpha * __uint_as_float(v[j]), alpha * __uint_as_float(v[j + 1]),
-                          alpha * __uint_as_float(v[j + 2]), alpha * __uint_as_float(v[j + 3]));
-      } else {
-        // transposed: element (rr, col) goes to [col][rr] (lanes write consecutive rr)
-        float* dst = p.out_bot + co + rr;
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(dst + j) =
+                make_float4(alpha * __uint_as_float(v[j]), alpha * __uint_as_float(v[j + 1]),
+                            alpha * __uint_as_float(v[j + 2]), alpha * __uint_as_float(v[j + 3]));
+        } else {
+          // transposed: element (rr, col) goes to [col][rr] (lanes write consecutive rr)
+          float* dst = p.out_bot + co + rr;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) dst[(32 * half + j) * 64] = alpha * __uint_as_float(v[j]);
+          for (int j = 0; j < 32; ++j) dst[(32 * half + j) * 64] = alpha * __uint_as_float(v[j]);
+        }
+      }
+      // optional dgC[k] = sum_v dS[k][v] S0[k][v]: 8 threads per row, float4 loads
+      if (p.dgC) {
+        for (int i = threadIdx.x; i < 64 * 8; i += THREADS) {
+          const int row = i >> 3, q8 = (i & 7) * 8;
+          const float4 a0 = *reinterpret_cast<const float4*>(p.dS + co + row * 64 + q8);
+          const float4 a1 = *reinterpret_cast<const float4*>(p.dS + co + row * 64 + q8 + 4);
+          const float4 b0 = *reinterpret_cast<const float4*>(p.S0 + co + row * 64 + q8);
+          const float4 b1 = *reinterpret_cast<const float4*>(p.S0 + co + row * 64 + q8 + 4);
+          float sv = a0.x * b0.x + a0.y * b0.y + a0.z * b0.z + a0.w * b0.w + a1.x * b1.x + a1.y * b1.y +
+                     a1.z * b1.z + a1.w * b1.w;
+          sv += __shfl_xor_sync(0xffffffffu, sv, 1);
+          sv += __shfl_xor_sync(0xffffffffu, sv, 2);
+          sv += __shfl_xor_sync(0xffffffffu, sv, 4);
+          if ((i & 7) == 0) p.dgC[(long long)c * 64 + row] = sv;
+        }
       }
     }
-  }
-  // optional dgC[k] = sum_v dS[k][v] S0[k][v] (one warp per row)
-  if (p.dgC) {
-    const long long co = (long long)c * 64 * 64;
-    for (int r = warp; r < 64; r += THREADS / 32) {
-      const float* ds = p.dS + co + r * 64;
-      const float* s0 = p.S0 + co + r * 64;
-      float sv = ds[lane] * s0[lane] + ds[lane + 32] * s0[lane + 32];
-      sv = warp_sum(sv);
-      if (lane == 0) p.dgC[(long long)c * 64 + r] = sv;
-    }
+    tc_fence_before();
+    __syncthreads();   // TMEM buffer and barrier phases are reused two iterations on
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
+  if (warp == 0) tmem_dealloc(tmem0, TMEM_COLS);
 }
 
 }  // namespace kda64tc
@@ -234,17 +250,17 @@ CUtensorMap token_map(const float* base, int B, int S, int H) {
   return make_tmap(base, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <bool A_MN, bool B_MN>
 void launch_pair(const CUtensorMap& top, const CUtensorMap& bot, const CUtensorMap& bm,
                  const kda64tc::Args& a, int chunks) {
-  auto kern = kda64tc::pair_product_kernel<A_MN, B_MN>;
+  auto kern = kda64tc::pair_product_kernel;
   static bool cfg = false;
   if (!cfg) {
     HB_CUDA_CHECK(cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        kda64tc::SMEM));
     cfg = true;
   }
-  kern<<<chunks, kda64tc::THREADS, kda64tc::SMEM, cur_stream()>>>(top, bot, bm, a);
+  const int grid = std::min(chunks, 2 * num_sms());
+  kern<<<grid, kda64tc::THREADS, kda64tc::SMEM, cur_stream()>>>(top, bot, bm, a, chunks);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -260,19 +276,6 @@ kda64tc::Args base_args(int S, int H, int NC) {
 }
 }  // namespace
 
-// dUp = P^T dO, dSq = Qg^T dO for every chunk (tcgen05).
-void kda64_bwd_pre_tc(const float* Pm, const float* Qg, const float* dout, float* dUp, float* dSq, int B,
-                      int S, int H, int NC) {
-  const long long chunks = (long long)B * H * NC;
-  auto a = base_args(S, H, NC);
-  a.out_top = dUp;
-  a.out_bot = dSq;
-  a.kind_top = a.kind_bot = kda64tc::kChunk;
-  a.kind_b = kda64tc::kToken;
-  launch_pair<true, true>(chunk_map(Pm, chunks), chunk_map(Qg, chunks), token_map(dout, B, S, H), a,
-                          (int)chunks);
-}
-
 // dWt = -dU S0^T, dQg = dO S0^T;  dP = dO U^T, dKh = (dS U^T)^T, dgC (tcgen05).
 void kda64_products_tc(const float* dU, const float* dout, const float* states, const float* dstates,
                        const float* U, float* dWt, float* dQg, float* dP, float* dKh, float* dgC, int B, int S,
@@ -286,7 +289,7 @@ void kda64_products_tc(const float* dU, const float* dout, const float* states, 
   a.kind_top = kda64tc::kChunk;
   a.kind_bot = kda64tc::kToken;
   a.kind_b = kda64tc::kChunk;
-  launch_pair<false, false>(chunk_map(dU, chunks), mdO, chunk_map(states, chunks), a, (int)chunks);
+  launch_pair(chunk_map(dU, chunks), mdO, chunk_map(states, chunks), a, (int)chunks);
   auto a2 = base_args(S, H, NC);
   a2.out_top = dP;
   a2.out_bot = dKh;
@@ -297,22 +300,19 @@ void kda64_products_tc(const float* dU, const float* dout, const float* states, 
   a2.dS = dstates;
   a2.S0 = states;
   a2.dgC = dgC;
-  launch_pair<false, false>(mdO, chunk_map(dstates, chunks), chunk_map(U, chunks), a2, (int)chunks);
+  launch_pair(mdO, chunk_map(dstates, chunks), chunk_map(U, chunks), a2, (int)chunks);
 }
 
 }  // namespace hb
 
 namespace hb {
-// Direct entry for tests: the three stacked products of one chunk-64 KDA
-// backward on tcgen05, from fp32 chunk-layout / token-layout tensors.
-void kda64_tc_products(torch::Tensor Pm, torch::Tensor Qg, torch::Tensor dout, torch::Tensor dU,
-                       torch::Tensor states, torch::Tensor dstates, torch::Tensor U, torch::Tensor dUp,
-                       torch::Tensor dSq, torch::Tensor dWt, torch::Tensor dQg, torch::Tensor dP,
-                       torch::Tensor dKh, torch::Tensor dgC) {
+// Direct entry for tests: the stacked products of the chunk-64 KDA backward on
+// tcgen05, from fp32 chunk-layout / token-layout tensors.
+void kda64_tc_products(torch::Tensor dout, torch::Tensor dU, torch::Tensor states, torch::Tensor dstates,
+                       torch::Tensor U, torch::Tensor dWt, torch::Tensor dQg, torch::Tensor dP, torch::Tensor dKh,
+                       torch::Tensor dgC) {
   const int B = dout.size(0), S = dout.size(1), H = dout.size(2);
   const int NC = (S + 63) / 64;
-  kda64_bwd_pre_tc(Pm.data_ptr<float>(), Qg.data_ptr<float>(), dout.data_ptr<float>(), dUp.data_ptr<float>(),
-                   dSq.data_ptr<float>(), B, S, H, NC);
   kda64_products_tc(dU.data_ptr<float>(), dout.data_ptr<float>(), states.data_ptr<float>(),
                     dstates.data_ptr<float>(), U.data_ptr<float>(), dWt.data_ptr<float>(), dQg.data_ptr<float>(),
                     dP.data_ptr<float>(), dKh.data_ptr<float>(), dgC.data_ptr<float>(), B, S, H, NC);
