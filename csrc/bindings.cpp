@@ -5,6 +5,7 @@
 
 namespace hb {
 void set_wait_budget_ns(uint64_t ns);
+void set_peer_wait_budget_ns(uint64_t ns);
 // gemm
 void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool trans_a, bool trans_b,
           bool accumulate, double alpha, c10::optional<torch::Tensor> alpha_t);
@@ -166,6 +167,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("status_view", &status_view, "the device status word as an int32 tensor view");
   m.def("copy_engine_gather", &copy_engine_gather);
   m.def("set_wait_budget_ns", &hb::set_wait_budget_ns);
+  m.def("set_peer_wait_budget_ns", &hb::set_peer_wait_budget_ns);
   m.def("gemm", &hb::gemm, "c (+)= op(a) @ op(b) on tcgen05", py::arg("a"), py::arg("b"),
         py::arg("c"), py::arg("trans_a"), py::arg("trans_b"), py::arg("accumulate"),
         py::arg("alpha") = 1.0, py::arg("alpha_t") = py::none());

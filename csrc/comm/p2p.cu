@@ -147,7 +147,7 @@ void p2p_barrier(torch::Tensor pads, int64_t rank, int64_t world, int64_t epoch)
   HB_CHECK(world <= 1024, "p2p_barrier: world too large");
   barrier_kernel<<<1, 1024 >= world ? (int)((world + 31) / 32 * 32) : 1024, 0, cur_stream()>>>(
       reinterpret_cast<const long long*>(pads.data_ptr<int64_t>()), (int)rank, (int)world,
-      (unsigned)epoch, status_ptr(), wait_budget_ns());
+      (unsigned)epoch, status_ptr(), peer_wait_budget_ns());
   HB_CUDA_CHECK(cudaGetLastError());
 }
 

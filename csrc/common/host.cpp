@@ -10,7 +10,8 @@ namespace {
 std::mutex g_mu;
 std::vector<int*> g_status;  // per device
 std::vector<int> g_sms;
-uint64_t g_budget_ns = 4000000000ull;  // 4 s per bounded wait
+uint64_t g_budget_ns = 4000000000ull;         // 4 s per bounded wait on this GPU
+uint64_t g_peer_budget_ns = 120000000000ull;  // 120 s for a wait on another rank
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -54,6 +55,8 @@ int* status_ptr() {
 
 uint64_t wait_budget_ns() { return g_budget_ns; }
 void set_wait_budget_ns(uint64_t ns) { g_budget_ns = ns; }
+uint64_t peer_wait_budget_ns() { return g_peer_budget_ns; }
+void set_peer_wait_budget_ns(uint64_t ns) { g_peer_budget_ns = ns; }
 
 CUtensorMap make_tmap(const void* base, CUtensorMapDataType dtype, int rank,
                       const uint64_t* dims, const uint64_t* strides_bytes,

@@ -33,7 +33,11 @@ inline cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().strea
 
 int num_sms();
 int* status_ptr();  // device status word of the current device (zeroed at creation)
-uint64_t wait_budget_ns();
+uint64_t wait_budget_ns();       // budget of a bounded wait on work of this GPU
+// Budget of a wait on another rank (device barrier on peer signal pads): ranks
+// can drift apart by seconds (first steps: lazy module loading, descriptor
+// creation), so it is much larger than the on-device budget.
+uint64_t peer_wait_budget_ns();
 
 // 2-D / 3-D bf16 (or other) tiled tensor maps with 128-byte swizzle.
 // dims/strides are innermost-first; strides in bytes for dims 1..rank-1.

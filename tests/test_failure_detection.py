@@ -104,7 +104,7 @@ def test_device_barrier_times_out_with_error_status():
     # two "ranks" whose signal pads are both this GPU's buffer: slot 1 is never set
     pad = torch.zeros(32, dtype=torch.int32, device="cuda")
     pads = torch.tensor([pad.data_ptr(), pad.data_ptr()], dtype=torch.int64, device="cuda")
-    e.set_wait_budget_ns(200_000_000)           # 0.2 s
+    e.set_peer_wait_budget_ns(200_000_000)      # 0.2 s
     try:
         t0 = time.time()
         e.p2p_barrier(pads, 0, 2, 1)
@@ -112,7 +112,7 @@ def test_device_barrier_times_out_with_error_status():
         assert time.time() - t0 < 10
         assert e.read_status() == 4             # kErrTimeoutPeer
     finally:
-        e.set_wait_budget_ns(4_000_000_000)
+        e.set_peer_wait_budget_ns(120_000_000_000)
         e.clear_status()
     # the context is still usable
     x = torch.randn(64, 64, device="cuda")
@@ -135,7 +135,7 @@ def test_trainer_step_raises_after_device_wait_timeout():
     tr.check_device_status()                    # a clean step raises nothing
     pad = torch.zeros(32, dtype=torch.int32, device="cuda")
     pads = torch.tensor([pad.data_ptr(), pad.data_ptr()], dtype=torch.int64, device="cuda")
-    e.set_wait_budget_ns(200_000_000)
+    e.set_peer_wait_budget_ns(200_000_000)
     try:
         e.p2p_barrier(pads, 0, 2, 1)            # slot 1 is never signalled
         with pytest.raises(KernelStatusError) as ei:
@@ -144,7 +144,7 @@ def test_trainer_step_raises_after_device_wait_timeout():
         assert ei.value.code == 4
     finally:
         torch.cuda.synchronize()
-        e.set_wait_budget_ns(4_000_000_000)
+        e.set_peer_wait_budget_ns(120_000_000_000)
         e.clear_status()
     x = torch.randn(64, 64, device="cuda")
     assert torch.isfinite((x @ x).sum())
