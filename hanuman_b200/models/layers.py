@@ -207,7 +207,7 @@ class MoE(nn.Module):
     """Routed SwiGLU experts + shared expert (model/moe.py:116-294)."""
 
     def __init__(self, d_model, d_ff, n_experts, n_active, n_shared, router_std,
-                 scaling, gen, d_ff_shared=None, router_type="sigmoid_bias"):
+                 scaling, gen, d_ff_shared=None, router_type="sigmoid_bias", ep=None):
         super().__init__()
         self.n_experts, self.n_active, self.n_shared = n_experts, n_active, n_shared
         self.scaling = scaling
@@ -218,6 +218,10 @@ class MoE(nn.Module):
         self.expert_w_gate = nn.Parameter(_normal((n_experts, d_model, d_ff), std, gen))
         self.expert_w_up = nn.Parameter(_normal((n_experts, d_model, d_ff), std, gen))
         self.expert_w_down = nn.Parameter(_normal((n_experts, d_ff, d_model), std, gen))
+        if ep is not None:
+            # expert parallelism: keep this rank's experts right away (the random
+            # stream is the full model's, so the weights equal the unsliced ones)
+            self.make_expert_parallel(*ep)
         dfs = d_ff if d_ff_shared is None else d_ff_shared
         if n_shared == 1:
             shp_in, shp_out = (d_model, dfs), (dfs, d_model)

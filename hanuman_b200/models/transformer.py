@@ -46,7 +46,7 @@ def unit_boundary(hooks, event: str, unit: int, *xs):
 
 
 class Block(nn.Module):
-    def __init__(self, cfg: Config, layer: int, gen: torch.Generator):
+    def __init__(self, cfg: Config, layer: int, gen: torch.Generator, ep=None):
         super().__init__()
         self.layer = layer
         self.attention_type = cfg.layer_types()[layer]
@@ -62,7 +62,7 @@ class Block(nn.Module):
         if self.use_moe:
             self.ffn = MoE(cfg.d_model, cfg.d_ff, cfg.n_experts, cfg.n_active,
                            cfg.n_shared_experts, cfg.router_init_std, cfg.routed_scaling_factor,
-                           gen, d_ff_shared=cfg.d_ff_shared, router_type=cfg.router_type)
+                           gen, d_ff_shared=cfg.d_ff_shared, router_type=cfg.router_type, ep=ep)
         else:
             self.ffn = DenseFFN(cfg.d_model, cfg.d_ff_shared, gen)
         self.residual_scale = nn.Parameter(torch.tensor(float(cfg.residual_scale_init)))
@@ -107,13 +107,16 @@ class Transformer(nn.Module):
     (compute dtype) and the merged aux dict; :meth:`logits` applies the tied
     head.  Training uses :meth:`loss`, which fuses the head with the CE."""
 
-    def __init__(self, cfg: Config, seed: int = 0):
+    def __init__(self, cfg: Config, seed: int = 0, ep=None):
+        """``ep = (rank, world)``: expert parallelism; each MoE layer keeps only
+        this rank's experts as it is built (host memory stays at one layer's
+        experts instead of the whole model's)."""
         super().__init__()
         self.cfg = cfg
         gen = torch.Generator().manual_seed(seed)
         std = cfg.d_model ** -0.5
         self.wte = nn.Parameter(torch.randn(cfg.vocab_size, cfg.d_model, generator=gen) * std)
-        self.blocks = nn.ModuleList([Block(cfg, i, gen) for i in range(cfg.layers)])
+        self.blocks = nn.ModuleList([Block(cfg, i, gen, ep=ep) for i in range(cfg.layers)])
         self.norm_f = RMSNorm(cfg.d_model, cfg.norm_eps)
         max_len = max(cfg.seq_len, cfg.infer_seq_len)
         cos, sin = ref.precompute_rope(cfg.head_dim, max_len, cfg.rope_base, cfg.yarn_factor,

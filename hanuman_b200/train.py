@@ -33,15 +33,17 @@ class Trainer:
         self.dist = dist_ctx
         world = dist_ctx.world if dist_ctx is not None else 1
         rank = dist_ctx.rank if dist_ctx is not None else 0
-        self.model = Transformer(cfg, seed=cfg.seed if seed is None else seed)
+        ep = None
         if dist_ctx is not None and world > 1 and cfg.mesh_expert_axis > 1:
             if cfg.mesh_expert_axis != world:
                 raise ValueError("expert parallelism spans all ranks: mesh_expert_axis must equal "
                                  f"the world size ({world})")
             if self.device.type != "cuda":
                 raise ValueError("expert parallelism runs on the GPU transport")
+            ep = (rank, world)
+        self.model = Transformer(cfg, seed=cfg.seed if seed is None else seed, ep=ep)
+        if ep is not None:
             for m in self.model.moe_layers():
-                m.make_expert_parallel(rank, world)
                 m.ep_dist = dist_ctx
                 m.capacity_factor = cfg.capacity_factor
         if (dist_ctx is not None and world > 1 and cfg.mesh_expert_axis <= 1

@@ -232,3 +232,26 @@ def test_remat_recomputes_and_gradients_are_bitwise_equal(policy, monkeypatch):
         assert c_pol["kda"] == 2 * n_kda          # every KDA layer ran again in the backward
     else:
         assert c_pol["kda"] == n_kda
+
+
+def test_expert_parallel_construction_slices_the_full_models_experts():
+    """Each rank of an expert-parallel model builds only its experts, and they
+    are exactly the rank's slice of the unsliced model (same random stream)."""
+    from hanuman_b200.models.transformer import Transformer
+    c = get_config("tiny_hybrid")
+    full = Transformer(c, seed=3)
+    world = 2
+    for rank in range(world):
+        part = Transformer(c, seed=3, ep=(rank, world))
+        fm, pm = full.moe_layers(), part.moe_layers()
+        assert len(fm) == len(pm) > 0
+        for a, b in zip(fm, pm):
+            nl = a.n_experts // world
+            for name in ("expert_w_gate", "expert_w_up", "expert_w_down"):
+                assert torch.equal(getattr(a, name)[rank * nl:(rank + 1) * nl],
+                                   getattr(b, name))
+            assert torch.equal(a.router, b.router)
+        for (na, pa), (nb, pb) in zip(full.named_parameters(), part.named_parameters()):
+            assert na == nb
+            if "expert_w" not in na:
+                assert torch.equal(pa, pb), na
