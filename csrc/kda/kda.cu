@@ -596,12 +596,16 @@ __global__ void __launch_bounds__(256, DK >= 128 ? 2 : 3) prep_bwd1_kernel(const
 
 // Backward part 2 (thread per channel of the 3*HK conv inputs, a run of tokens):
 //   draw[t] = sum_i w[i] dconv[t + 3 - i] (same sequence); dw[i] += dconv[t] raw[t-3+i]
-// dconv and raw are held in 4-deep register windows, so each element is loaded once.
+// dconv and raw are held in 4-deep register windows, so each element is loaded
+// once; the loads of U tokens are issued together ahead of their arithmetic
+// (a thread walks hundreds of tokens, so one load pair per step would leave
+// the kernel bound by memory latency).
 __global__ void prep_bwd2_kernel(const __nv_bfloat16* __restrict__ raw, long long ld_raw,
                                  const float* __restrict__ wq, const float* __restrict__ wk,
                                  const float* __restrict__ wv, const float* __restrict__ dconv,
                                  int T, int S, int HK, __nv_bfloat16* __restrict__ draw,
                                  float* __restrict__ dwq, float* __restrict__ dwk, float* __restrict__ dwv) {
+  constexpr int U = 8;
   const int C3 = 3 * HK;
   const int ch = blockIdx.x * blockDim.x + threadIdx.x;
   if (ch >= C3) return;
@@ -615,37 +619,266 @@ __global__ void prep_bwd2_kernel(const __nv_bfloat16* __restrict__ raw, long lon
   float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
   const float* dcol = dconv + ch;
   const __nv_bfloat16* rcol = raw + ch;
-  auto dc = [&](int t) { return t < T ? dcol[(long long)t * C3] : 0.f; };
-  auto rw = [&](int t) { return t >= 0 ? __bfloat162float(rcol[(long long)t * ld_raw]) : 0.f; };
+  auto dc = [&](int t) { return t < T ? __ldg(dcol + (long long)t * C3) : 0.f; };
+  auto rw = [&](int t) { return t >= 0 && t < T ? __bfloat162float(rcol[(long long)t * ld_raw]) : 0.f; };
   // windows: d0..d3 = dconv[t..t+3], r1..r3 = raw[t-1..t-3]
   float d0 = dc(tb), d1 = dc(tb + 1), d2 = dc(tb + 2), d3 = dc(tb + 3);
   float r1 = rw(tb - 1), r2 = rw(tb - 2), r3 = rw(tb - 3);
   int pos = tb % S;
-  for (int t = tb; t < te; ++t) {
-    const float r0 = rw(t);
-    const float dn = dc(t + 4);
-    float acc = wt.w * d0;
-    if (pos + 1 < S) acc += wt.z * d1;
-    if (pos + 2 < S) acc += wt.y * d2;
-    if (pos + 3 < S) acc += wt.x * d3;
-    draw[(long long)t * ld_raw + ch] = __float2bfloat16_rn(acc);
-    a3 += d0 * r0;
-    if (pos >= 1) a2 += d0 * r1;
-    if (pos >= 2) a1 += d0 * r2;
-    if (pos >= 3) a0 += d0 * r3;
-    d0 = d1;
-    d1 = d2;
-    d2 = d3;
-    d3 = dn;
-    r3 = r2;
-    r2 = r1;
-    r1 = r0;
-    if (++pos == S) pos = 0;
+  for (int t0 = tb; t0 < te; t0 += U) {
+    float dn[U], rn[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      dn[u] = dc(t0 + u + 4);
+      rn[u] = rw(t0 + u);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int t = t0 + u;
+      if (t < te) {
+        const float r0 = rn[u];
+        float acc = wt.w * d0;
+        if (pos + 1 < S) acc += wt.z * d1;
+        if (pos + 2 < S) acc += wt.y * d2;
+        if (pos + 3 < S) acc += wt.x * d3;
+        draw[(long long)t * ld_raw + ch] = __float2bfloat16_rn(acc);
+        a3 += d0 * r0;
+        if (pos >= 1) a2 += d0 * r1;
+        if (pos >= 2) a1 += d0 * r2;
+        if (pos >= 3) a0 += d0 * r3;
+        d0 = d1;
+        d1 = d2;
+        d2 = d3;
+        d3 = dn[u];
+        r3 = r2;
+        r2 = r1;
+        r1 = r0;
+        if (++pos == S) pos = 0;
+      }
+    }
   }
   atomicAdd(dw + cc * 4 + 0, a0);
   atomicAdd(dw + cc * 4 + 1, a1);
   atomicAdd(dw + cc * 4 + 2, a2);
   atomicAdd(dw + cc * 4 + 3, a3);
+}
+
+// Fused backward (block per head, persistent over token tiles of R rows):
+// the gradient at the conv outputs never leaves shared memory.
+//   stage 0: the raw projection rows t0-3 .. t0+R+2 of the block's head
+//            (q | k | v columns, bf16) into shared memory;
+//   stage 1: warp per row r in [0, R+3): conv + SiLU (+ L2 norm) recomputed from
+//            the staged taps, dconv of rows t0 .. t0+R+2 into shared memory (the
+//            last three rows are the next tile's, recomputed here); rows < R also
+//            write df, dbraw and sum the bias gradients;
+//   stage 2: draw[t] = sum_i w[i] dconv[t+3-i] (same sequence) for the R rows,
+//            dw[i] += dconv[t] raw[t-3+i] in per-thread registers across tiles.
+// One atomic per channel and tap per block at the end.
+template <int DK>
+struct PrepTile {
+  static constexpr int ROWS = 2048 / DK;       // dconv rows per tile: a multiple of the 8 warps
+  static constexpr int R = ROWS - 3;           // rows the tile owns (3 halo rows recomputed)
+  static constexpr int C3 = 3 * DK;            // channels per head
+  static constexpr int NC = (C3 + 255) / 256;                            // channels per thread (dw)
+  static constexpr int smem = (R + 3) * C3 * 4 + (R + 6) * C3 * 2;
+};
+
+template <int DK>
+__global__ void __launch_bounds__(256, 4) prep_bwd_fused_kernel(
+    const __nv_bfloat16* __restrict__ raw, long long ld_raw, const float* __restrict__ wq,
+    const float* __restrict__ wk, const float* __restrict__ wv, const float* __restrict__ f,
+    const float* __restrict__ a_log, const float* __restrict__ dt_bias, const float* __restrict__ beta,
+    int gate_mode, int T, int S, int H, const float* __restrict__ dq, const float* __restrict__ dk,
+    const float* __restrict__ dv, const float* __restrict__ dg, const float* __restrict__ dbeta,
+    __nv_bfloat16* __restrict__ df, float* __restrict__ dbraw, float* __restrict__ d_alog,
+    float* __restrict__ d_dtb, __nv_bfloat16* __restrict__ draw, float* __restrict__ dwq,
+    float* __restrict__ dwk, float* __restrict__ dwv) {
+  using P = PrepTile<DK>;
+  constexpr int R = P::R, C3 = P::C3, NP = (DK + 63) / 64;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* sdc = reinterpret_cast<float*>(smem_raw);                                  // [R+3][C3]
+  __nv_bfloat16* sraw = reinterpret_cast<__nv_bfloat16*>(smem_raw + (R + 3) * C3 * 4);  // [R+6][C3]
+  __shared__ float s_dtb[DK + 1];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, warps = blockDim.x >> 5;
+  const int HK = H * DK, h = blockIdx.y;
+  const float A = gate_mode == 0 ? __expf(a_log[h]) : 0.f;
+  float2 acc_dtb[NP];
+#pragma unroll
+  for (int j = 0; j < NP; ++j) acc_dtb[j] = make_float2(0.f, 0.f);
+  float acc_al = 0.f;
+  float dwacc[P::NC][4];
+#pragma unroll
+  for (int n = 0; n < P::NC; ++n)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dwacc[n][i] = 0.f;
+  for (int i = tid; i < DK + 1; i += blockDim.x) s_dtb[i] = 0.f;
+  const int ntiles = (T + R - 1) / R;
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const int t0 = tile * R;
+    // ---- stage 0: raw rows t0-3 .. t0+R+2 (16-byte vectors; zero outside [0, T))
+    {
+      constexpr int VPR = C3 * 2 / 16;  // vectors per row
+      for (int idx = tid; idx < (R + 6) * VPR; idx += blockDim.x) {
+        const int r = idx / VPR, v = idx % VPR;
+        const int c = v * 8, which = c / DK, cc = c % DK;
+        const int t = t0 - 3 + r;
+        uint4 val = make_uint4(0, 0, 0, 0);
+        if (t >= 0 && t < T)
+          val = *reinterpret_cast<const uint4*>(raw + (long long)t * ld_raw + which * HK + h * DK + cc);
+        *reinterpret_cast<uint4*>(sraw + r * C3 + c) = val;
+      }
+    }
+    __syncthreads();
+    // ---- stage 1: dconv rows (warp per row)
+    for (int r = warp; r < R + 3; r += warps) {
+      const int t = t0 + r;
+      float* drow = sdc + r * C3;
+      if (t >= T) {
+        for (int c = lane; c < C3; c += 32) drow[c] = 0.f;
+        continue;
+      }
+      const int pos = t % S;
+      const bool own = r < R;
+      float2 cq[NP], ck[NP], sq[NP], sk[NP], gq[NP], gk[NP];
+      float ssq = 0.f, ssk = 0.f, dotq = 0.f, dotk = 0.f, dal = 0.f;
+#pragma unroll
+      for (int j = 0; j < NP; ++j) {
+        const int c = 2 * lane + 64 * j;
+        cq[j] = ck[j] = sq[j] = sk[j] = gq[j] = gk[j] = make_float2(0.f, 0.f);
+        if (c >= DK) continue;
+        const int ch = h * DK + c;
+        const long long o = (long long)t * HK + ch;
+        float2 cv = make_float2(0.f, 0.f);
+        {
+          const float4 wa = *reinterpret_cast<const float4*>(wq + ch * 4);
+          const float4 wb = *reinterpret_cast<const float4*>(wq + ch * 4 + 4);
+          const float4 ka = *reinterpret_cast<const float4*>(wk + ch * 4);
+          const float4 kb = *reinterpret_cast<const float4*>(wk + ch * 4 + 4);
+          const float4 va = *reinterpret_cast<const float4*>(wv + ch * 4);
+          const float4 vb = *reinterpret_cast<const float4*>(wv + ch * 4 + 4);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            if (pos - 3 + i < 0) continue;
+            const __nv_bfloat16* row = sraw + (r + i) * C3;
+            const float2 xq = ld_bf2(row + c), xk = ld_bf2(row + DK + c), xv = ld_bf2(row + 2 * DK + c);
+            cq[j].x += tap(wa, i) * xq.x;  cq[j].y += tap(wb, i) * xq.y;
+            ck[j].x += tap(ka, i) * xk.x;  ck[j].y += tap(kb, i) * xk.y;
+            cv.x += tap(va, i) * xv.x;     cv.y += tap(vb, i) * xv.y;
+          }
+          cq[j] = make_float2(rbf(cq[j].x), rbf(cq[j].y));
+          ck[j] = make_float2(rbf(ck[j].x), rbf(ck[j].y));
+          cv = make_float2(rbf(cv.x), rbf(cv.y));
+        }
+        sq[j] = make_float2(silu_f(cq[j].x), silu_f(cq[j].y));
+        sk[j] = make_float2(silu_f(ck[j].x), silu_f(ck[j].y));
+        ssq += sq[j].x * sq[j].x + sq[j].y * sq[j].y;
+        ssk += sk[j].x * sk[j].x + sk[j].y * sk[j].y;
+        gq[j] = *reinterpret_cast<const float2*>(dq + o);
+        gk[j] = *reinterpret_cast<const float2*>(dk + o);
+        dotq += gq[j].x * sq[j].x + gq[j].y * sq[j].y;
+        dotk += gk[j].x * sk[j].x + gk[j].y * sk[j].y;
+        const float2 gv = *reinterpret_cast<const float2*>(dv + o);
+        *reinterpret_cast<float2*>(drow + 2 * DK + c) =
+            make_float2(gv.x * dsilu_f(cv.x), gv.y * dsilu_f(cv.y));
+        if (own) {
+          const float2 fz = *reinterpret_cast<const float2*>(f + o);
+          const float2 db = *reinterpret_cast<const float2*>(dt_bias + ch);
+          const float2 gg = *reinterpret_cast<const float2*>(dg + o);
+          const float z[2] = {fz.x + db.x, fz.y + db.y}, dgv[2] = {gg.x, gg.y};
+          float dz[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float sig = 1.f / (1.f + __expf(-z[e]));
+            if (gate_mode == 0) {
+              dz[e] = dgv[e] * (-A) * sig;
+              dal += dgv[e] * (-A * softplus_f(z[e]));
+            } else {
+              dz[e] = dgv[e] * (1.f - sig);
+            }
+          }
+          *reinterpret_cast<__nv_bfloat162*>(df + o) = __floats2bfloat162_rn(dz[0], dz[1]);
+          acc_dtb[j].x += dz[0];
+          acc_dtb[j].y += dz[1];
+        }
+      }
+      ssq = warp_sum(ssq);
+      ssk = warp_sum(ssk);
+      dotq = warp_sum(dotq);
+      dotk = warp_sum(dotk);
+      const float nq = sqrtf(ssq + 1e-6f), nk = sqrtf(ssk + 1e-6f);
+#pragma unroll
+      for (int j = 0; j < NP; ++j) {
+        const int c = 2 * lane + 64 * j;
+        if (c >= DK) continue;
+        // y = x / n, n = sqrt(|x|^2 + eps): dx = (dy - y (dy . y)) / n
+        const float dq0 = (gq[j].x - sq[j].x / nq * (dotq / nq)) / nq;
+        const float dq1 = (gq[j].y - sq[j].y / nq * (dotq / nq)) / nq;
+        const float dk0 = (gk[j].x - sk[j].x / nk * (dotk / nk)) / nk;
+        const float dk1 = (gk[j].y - sk[j].y / nk * (dotk / nk)) / nk;
+        *reinterpret_cast<float2*>(drow + c) = make_float2(dq0 * dsilu_f(cq[j].x), dq1 * dsilu_f(cq[j].y));
+        *reinterpret_cast<float2*>(drow + DK + c) = make_float2(dk0 * dsilu_f(ck[j].x), dk1 * dsilu_f(ck[j].y));
+      }
+      if (own) {
+        acc_al += warp_sum(dal);
+        if (lane == 0) {
+          const float bt = beta[(long long)t * H + h];
+          dbraw[(long long)t * H + h] = dbeta[(long long)t * H + h] * bt * (1.f - bt);
+        }
+      }
+    }
+    __syncthreads();
+    // ---- stage 2: draw rows and the conv weight gradient
+    for (int idx = tid; idx < R * C3; idx += blockDim.x) {
+      const int r = idx / C3, c = idx % C3;
+      const int t = t0 + r;
+      if (t >= T) break;
+      const int pos = t % S;
+      const int which = c / DK;
+      const float* w = which == 0 ? wq : (which == 1 ? wk : wv);
+      const float4 wt = *reinterpret_cast<const float4*>(w + (h * DK + c % DK) * 4);
+      float acc = wt.w * sdc[r * C3 + c];
+      if (pos + 1 < S) acc += wt.z * sdc[(r + 1) * C3 + c];
+      if (pos + 2 < S) acc += wt.y * sdc[(r + 2) * C3 + c];
+      if (pos + 3 < S) acc += wt.x * sdc[(r + 3) * C3 + c];
+      draw[(long long)t * ld_raw + which * HK + h * DK + c % DK] = __float2bfloat16_rn(acc);
+    }
+#pragma unroll
+    for (int n = 0; n < P::NC; ++n) {
+      const int c = tid + 256 * n;
+      if (c >= C3) continue;
+      for (int r = 0; r < R && t0 + r < T; ++r) {
+        const float d = sdc[r * C3 + c];
+        const int pos = (t0 + r) % S;
+        // raw row t-3+i sits at staged row r+i
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (pos - 3 + i >= 0) dwacc[n][i] += d * __bfloat162float(sraw[(r + i) * C3 + c]);
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int n = 0; n < P::NC; ++n) {
+    const int c = tid + 256 * n;
+    if (c >= C3) continue;
+    const int which = c / DK, cc = h * DK + c % DK;
+    float* dw = which == 0 ? dwq : (which == 1 ? dwk : dwv);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) atomicAdd(dw + cc * 4 + i, dwacc[n][i]);
+  }
+#pragma unroll
+  for (int j = 0; j < NP; ++j) {
+    const int c = 2 * lane + 64 * j;
+    if (c < DK) {
+      atomicAdd(s_dtb + c, acc_dtb[j].x);
+      atomicAdd(s_dtb + c + 1, acc_dtb[j].y);
+    }
+  }
+  if (lane == 0 && gate_mode == 0) atomicAdd(s_dtb + DK, acc_al);
+  __syncthreads();
+  for (int i = tid; i < DK; i += blockDim.x)
+    if (s_dtb[i] != 0.f) atomicAdd(d_dtb + h * DK + i, s_dtb[i]);
+  if (tid == 0 && s_dtb[DK] != 0.f) atomicAdd(d_alog + h, s_dtb[DK]);
 }
 
 }  // namespace kda
@@ -810,6 +1043,40 @@ void kda_prep_bwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::
   const int T = dq.size(0), H = dq.size(1), DKV = dq.size(2);
   HB_CHECK(raw.stride(0) % 2 == 0 && DKV % 2 == 0, "kda_prep: even row stride and head dim");
   HB_CHECK(df.scalar_type() == at::kBFloat16 && df.is_contiguous(), "kda_prep_bwd: df must be contiguous bf16");
+  if (dconv.numel() == 0) {
+    // fused: the conv-output gradient stays in shared memory
+    HB_CHECK(raw.stride(0) % 8 == 0 && al16(raw.data_ptr()) && draw.stride(0) == raw.stride(0),
+             "kda_prep_bwd: 16-byte aligned raw rows");
+    auto launch = [&](auto dkc) {
+      constexpr int DK = decltype(dkc)::value;
+      using PT = kda::PrepTile<DK>;
+      static bool cfg = false;
+      if (!cfg) {
+        set_smem((const void*)kda::prep_bwd_fused_kernel<DK>, PT::smem);
+        cfg = true;
+      }
+      int per_sm = 0;
+      HB_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+          &per_sm, kda::prep_bwd_fused_kernel<DK>, 256, PT::smem));
+      const int ntiles = (T + PT::R - 1) / PT::R;
+      const int gx = (int)std::max<long long>(
+          1, std::min<long long>(ntiles, ((long long)num_sms() * std::max(per_sm, 1) + H - 1) / H));
+      kda::prep_bwd_fused_kernel<DK><<<dim3(gx, H), 256, PT::smem, cur_stream()>>>(
+          (const __nv_bfloat16*)raw.data_ptr(), raw.stride(0), wq.data_ptr<float>(), wk.data_ptr<float>(),
+          wv.data_ptr<float>(), f.data_ptr<float>(), a_log.data_ptr<float>(), dt_bias.data_ptr<float>(),
+          beta.data_ptr<float>(), (int)gate_mode, T, (int)S, H, dq.data_ptr<float>(), dk.data_ptr<float>(),
+          dv.data_ptr<float>(), dg.data_ptr<float>(), dbeta.data_ptr<float>(), (__nv_bfloat16*)df.data_ptr(),
+          dbraw.data_ptr<float>(), d_alog.data_ptr<float>(), d_dtb.data_ptr<float>(),
+          (__nv_bfloat16*)draw.data_ptr(), dwq.data_ptr<float>(), dwk.data_ptr<float>(), dwv.data_ptr<float>());
+    };
+    if (DKV == 16) launch(std::integral_constant<int, 16>{});
+    else if (DKV == 32) launch(std::integral_constant<int, 32>{});
+    else if (DKV == 64) launch(std::integral_constant<int, 64>{});
+    else if (DKV == 128) launch(std::integral_constant<int, 128>{});
+    else HB_CHECK(false, "kda_prep: unsupported head dim");
+    HB_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   // blocks: (token runs) x (heads); about 8 resident blocks per SM in all
   const int gx = (int)std::max<long long>(
       1, std::min<long long>(((long long)T + 7) / 8, ((long long)num_sms() * 8 + H - 1) / H));

@@ -27,6 +27,18 @@ def _normal(shape, std, gen):
     return torch.randn(shape, generator=gen, dtype=torch.float32) * std
 
 
+def _expert_normal(n, lo, shape, std, base, which):
+    """Experts lo .. lo+n-1 of one expert weight: expert e's matrix comes from
+    a generator seeded ``base + 3 e + which`` (which: 0 gate, 1 up, 2 down)."""
+    if _META:
+        return torch.empty((n,) + tuple(shape), device="meta")
+    out = torch.empty((n,) + tuple(shape), dtype=torch.float32)
+    for i in range(n):
+        g = torch.Generator().manual_seed(base + 3 * (lo + i) + which)
+        out[i] = torch.randn(shape, generator=g, dtype=torch.float32) * std
+    return out
+
+
 class RMSNorm(nn.Module):
     def __init__(self, d: int, eps: float):
         super().__init__()
@@ -215,13 +227,20 @@ class MoE(nn.Module):
         std = d_model ** -0.5
         self.router = nn.Parameter(_normal((d_model, n_experts), router_std, gen))
         self.bias = nn.Parameter(torch.zeros(n_experts), requires_grad=False)
-        self.expert_w_gate = nn.Parameter(_normal((n_experts, d_model, d_ff), std, gen))
-        self.expert_w_up = nn.Parameter(_normal((n_experts, d_model, d_ff), std, gen))
-        self.expert_w_down = nn.Parameter(_normal((n_experts, d_ff, d_model), std, gen))
+        # Every expert matrix is drawn from its own generator, seeded from the
+        # layer's stream, so an expert-parallel rank draws only its own experts
+        # (1/world of the work) and still gets exactly the unsliced values.
+        base = 0 if _META else int(torch.randint(0, 2 ** 48, (1,), generator=gen))
+        if ep is not None and n_experts % ep[1]:
+            raise ValueError(f"{n_experts} experts do not split over {ep[1]} ranks")
+        nl = n_experts if ep is None else n_experts // ep[1]
+        lo = 0 if ep is None else ep[0] * nl
+        shapes = {"expert_w_gate": (d_model, d_ff), "expert_w_up": (d_model, d_ff),
+                  "expert_w_down": (d_ff, d_model)}
+        for which, (name, shp) in enumerate(shapes.items()):
+            setattr(self, name, nn.Parameter(_expert_normal(nl, lo, shp, std, base, which)))
         if ep is not None:
-            # expert parallelism: keep this rank's experts right away (the random
-            # stream is the full model's, so the weights equal the unsliced ones)
-            self.make_expert_parallel(*ep)
+            self._mark_expert_parallel(*ep)
         dfs = d_ff if d_ff_shared is None else d_ff_shared
         if n_shared == 1:
             shp_in, shp_out = (d_model, dfs), (dfs, d_model)
@@ -250,7 +269,11 @@ class MoE(nn.Module):
         for name in ("expert_w_gate", "expert_w_up", "expert_w_down"):
             p = getattr(self, name)
             p.data = p.data[rank * nl:(rank + 1) * nl].clone()
-            p._ep_local = True
+        self._mark_expert_parallel(rank, world)
+
+    def _mark_expert_parallel(self, rank: int, world: int):
+        for name in ("expert_w_gate", "expert_w_up", "expert_w_down"):
+            getattr(self, name)._ep_local = True
         self.ep_rank, self.ep_world = rank, world
         self.ep_ctx = None
 

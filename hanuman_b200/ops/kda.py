@@ -157,7 +157,9 @@ class KdaFrontFn(torch.autograd.Function):
         z = lambda t: torch.zeros_like(f) if t is None else t.float().contiguous()
         dq, dk, dv, dg = z(dq), z(dk), z(dv), z(dg)
         dbeta = torch.zeros(T, H, device=dev) if dbeta is None else dbeta.float().contiguous()
-        dconv = torch.empty(T, 3 * HK, dtype=torch.float32, device=dev)
+        # fused backward (empty dconv): the conv-output gradient stays on chip
+        fused = os.environ.get("HB_KDA_PREP_FUSED", "1") != "0"
+        dconv = torch.empty(0 if fused else T * 3 * HK, dtype=torch.float32, device=dev)
         df = torch.empty(T, HK, dtype=torch.bfloat16, device=dev)
         dbraw = torch.empty(T, H, dtype=torch.float32, device=dev)
         d_alog = torch.zeros(H, dtype=torch.float32, device=dev)
