@@ -415,8 +415,34 @@ HB_DEVICE float2 conv2(const __nv_bfloat16* const (&rows)[4], int off, const flo
   return make_float2(rbf(a0), rbf(a1));
 }
 
+// sigmoid by the hardware exponential and an approximate divide (2 ulp);
+// 1 / (1 + inf) = 0 gives the right limit for very negative x
+HB_DEVICE float sigm(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+
+// The conv taps of one head's channels (c, c+1) of projection `which`.
+struct Taps2 { float4 a, b; };
+HB_DEVICE Taps2 load_taps(const float* w, int ch) {
+  return {*reinterpret_cast<const float4*>(w + ch * 4), *reinterpret_cast<const float4*>(w + ch * 4 + 4)};
+}
+// Causal 4-tap conv of channels (c, c+1) at offset `off` of the token rows
+// rows[i] = row of token t - 3 + i (nullptr before the sequence start),
+// rounded to the compute dtype (model/kda.py:136, 257-259).
+HB_DEVICE float2 conv_taps(const __nv_bfloat16* const (&rows)[4], int off, const Taps2& w) {
+  float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (!rows[i]) continue;
+    const float2 x = ld_bf2(rows[i] + off);
+    a0 += tap(w.a, i) * x.x;
+    a1 += tap(w.b, i) * x.y;
+  }
+  return make_float2(rbf(a0), rbf(a1));
+}
+
+// Forward (block per head, warp per token row of that head): the head's conv
+// taps, dt_bias and A stay in registers across the block's rows.
 template <int DK>
-__global__ void prep_fwd_kernel(const __nv_bfloat16* __restrict__ raw, long long ld_raw,
+__global__ void __launch_bounds__(256) prep_fwd_kernel(const __nv_bfloat16* __restrict__ raw, long long ld_raw,
                                 const float* __restrict__ wq, const float* __restrict__ wk,
                                 const float* __restrict__ wv, const float* __restrict__ f,
                                 const float* __restrict__ a_log, const float* __restrict__ dt_bias,
@@ -425,54 +451,61 @@ __global__ void prep_fwd_kernel(const __nv_bfloat16* __restrict__ raw, long long
                                 float* __restrict__ g, float* __restrict__ beta) {
   constexpr int NP = (DK + 63) / 64;
   const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
-  const int HK = H * DK;
+  const int HK = H * DK, h = blockIdx.y;
+  const float A = gate_mode == 0 ? -__expf(a_log[h]) : 0.f;
+  Taps2 tq[NP], tk[NP], tv[NP];
+  float2 db[NP];
+#pragma unroll
+  for (int j = 0; j < NP; ++j) {
+    const int ch = h * DK + min(2 * lane + 64 * j, DK - 2);
+    tq[j] = load_taps(wq, ch);
+    tk[j] = load_taps(wk, ch);
+    tv[j] = load_taps(wv, ch);
+    db[j] = *reinterpret_cast<const float2*>(dt_bias + ch);
+  }
   for (long long t = blockIdx.x * (long long)warps + (threadIdx.x >> 5); t < T; t += (long long)gridDim.x * warps) {
     const int pos = t % S;
     const __nv_bfloat16* rows[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) rows[i] = pos - (3 - i) >= 0 ? raw + (t - (3 - i)) * ld_raw : nullptr;
-    for (int h = 0; h < H; ++h) {
-      float2 qv[NP], kv[NP];
-      float ssq = 0.f, ssk = 0.f;
+    float2 qv[NP], kv[NP];
+    float ssq = 0.f, ssk = 0.f;
 #pragma unroll
-      for (int j = 0; j < NP; ++j) {
-        const int c = 2 * lane + 64 * j;
-        qv[j] = kv[j] = make_float2(0.f, 0.f);
-        if (c >= DK) continue;
-        const int ch = h * DK + c;
-        const float2 cq = conv2(rows, ch, wq, ch), ck = conv2(rows, HK + ch, wk, ch),
-                     cv = conv2(rows, 2 * HK + ch, wv, ch);
-        qv[j] = make_float2(silu_f(cq.x), silu_f(cq.y));
-        kv[j] = make_float2(silu_f(ck.x), silu_f(ck.y));
-        ssq += qv[j].x * qv[j].x + qv[j].y * qv[j].y;
-        ssk += kv[j].x * kv[j].x + kv[j].y * kv[j].y;
-        const long long o = t * HK + ch;
-        *reinterpret_cast<float2*>(v + o) = make_float2(silu_f(cv.x), silu_f(cv.y));
-        const float2 fz = *reinterpret_cast<const float2*>(f + o);
-        const float2 db = *reinterpret_cast<const float2*>(dt_bias + ch);
-        const float z0 = fz.x + db.x, z1 = fz.y + db.y;
-        float2 gg;
-        if (gate_mode == 0) {
-          const float A = -__expf(a_log[h]);
-          gg = make_float2(A * softplus_f(z0), A * softplus_f(z1));
-        } else {
-          gg = make_float2(-softplus_f(-z0), -softplus_f(-z1));
-        }
-        *reinterpret_cast<float2*>(g + o) = gg;
+    for (int j = 0; j < NP; ++j) {
+      const int c = 2 * lane + 64 * j;
+      qv[j] = kv[j] = make_float2(0.f, 0.f);
+      if (c >= DK) continue;
+      const int ch = h * DK + c;
+      const float2 cq = conv_taps(rows, ch, tq[j]), ck = conv_taps(rows, HK + ch, tk[j]),
+                   cv = conv_taps(rows, 2 * HK + ch, tv[j]);
+      qv[j] = make_float2(cq.x * sigm(cq.x), cq.y * sigm(cq.y));
+      kv[j] = make_float2(ck.x * sigm(ck.x), ck.y * sigm(ck.y));
+      ssq += qv[j].x * qv[j].x + qv[j].y * qv[j].y;
+      ssk += kv[j].x * kv[j].x + kv[j].y * kv[j].y;
+      const long long o = t * HK + ch;
+      *reinterpret_cast<float2*>(v + o) = make_float2(cv.x * sigm(cv.x), cv.y * sigm(cv.y));
+      const float2 fz = *reinterpret_cast<const float2*>(f + o);
+      const float z0 = fz.x + db[j].x, z1 = fz.y + db[j].y;
+      float2 gg;
+      if (gate_mode == 0) {
+        gg = make_float2(A * softplus_f(z0), A * softplus_f(z1));
+      } else {
+        gg = make_float2(-softplus_f(-z0), -softplus_f(-z1));
       }
-      ssq = warp_sum(ssq);
-      ssk = warp_sum(ssk);
-      const float rq = rsqrtf(ssq + 1e-6f), rk = rsqrtf(ssk + 1e-6f);
-#pragma unroll
-      for (int j = 0; j < NP; ++j) {
-        const int c = 2 * lane + 64 * j;
-        if (c >= DK) continue;
-        const long long o = t * HK + h * DK + c;
-        *reinterpret_cast<float2*>(q + o) = make_float2(qv[j].x * rq, qv[j].y * rq);
-        *reinterpret_cast<float2*>(k + o) = make_float2(kv[j].x * rk, kv[j].y * rk);
-      }
-      if (lane == 0) beta[t * H + h] = 1.f / (1.f + __expf(-braw[t * H + h]));
+      *reinterpret_cast<float2*>(g + o) = gg;
     }
+    ssq = warp_sum(ssq);
+    ssk = warp_sum(ssk);
+    const float rq = rsqrtf(ssq + 1e-6f), rk = rsqrtf(ssk + 1e-6f);
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+      const int c = 2 * lane + 64 * j;
+      if (c >= DK) continue;
+      const long long o = t * HK + h * DK + c;
+      *reinterpret_cast<float2*>(q + o) = make_float2(qv[j].x * rq, qv[j].y * rq);
+      *reinterpret_cast<float2*>(k + o) = make_float2(kv[j].x * rk, kv[j].y * rk);
+    }
+    if (lane == 0) beta[t * H + h] = sigm(braw[t * H + h]);
   }
 }
 
@@ -671,16 +704,20 @@ __global__ void prep_bwd2_kernel(const __nv_bfloat16* __restrict__ raw, long lon
 //            the staged taps, dconv of rows t0 .. t0+R+2 into shared memory (the
 //            last three rows are the next tile's, recomputed here); rows < R also
 //            write df, dbraw and sum the bias gradients;
-//   stage 2: draw[t] = sum_i w[i] dconv[t+3-i] (same sequence) for the R rows,
-//            dw[i] += dconv[t] raw[t-3+i] in per-thread registers across tiles.
-// One atomic per channel and tap per block at the end.
+//   stage 2: thread per channel, sliding 4-row windows over dconv and raw:
+//            draw[t] = sum_i w[i] dconv[t+3-i] (same sequence) for the R rows,
+//            dw[i] += dconv[t] raw[t-3+i] in registers across tiles.
+// One atomic per channel and tap per block at the end.  The kernel is
+// instruction-bound, so sigmoids use the approximate divide, the L2-norm
+// backward one reciprocal square root per row, and the sequence position
+// is advanced instead of divided.
 template <int DK>
 struct PrepTile {
   static constexpr int ROWS = 2048 / DK;       // dconv rows per tile: a multiple of the 8 warps
   static constexpr int R = ROWS - 3;           // rows the tile owns (3 halo rows recomputed)
   static constexpr int C3 = 3 * DK;            // channels per head
-  static constexpr int NC = (C3 + 255) / 256;                            // channels per thread (dw)
-  static constexpr int smem = (R + 3) * C3 * 4 + (R + 6) * C3 * 2;
+  static constexpr int NC = (C3 + 255) / 256;  // channels per thread in stage 2
+  static constexpr int smem = (R + 3) * C3 * 4 + (R + 6) * C3 * 2 + C3 * 16;
 };
 
 template <int DK>
@@ -696,15 +733,24 @@ __global__ void __launch_bounds__(256, 4) prep_bwd_fused_kernel(
   using P = PrepTile<DK>;
   constexpr int R = P::R, C3 = P::C3, NP = (DK + 63) / 64;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  float* sdc = reinterpret_cast<float*>(smem_raw);                                  // [R+3][C3]
+  float* sdc = reinterpret_cast<float*>(smem_raw);                                      // [R+3][C3]
   __nv_bfloat16* sraw = reinterpret_cast<__nv_bfloat16*>(smem_raw + (R + 3) * C3 * 4);  // [R+6][C3]
+  float4* sw = reinterpret_cast<float4*>(smem_raw + (R + 3) * C3 * 4 + (R + 6) * C3 * 2);  // [C3] taps
   __shared__ float s_dtb[DK + 1];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, warps = blockDim.x >> 5;
   const int HK = H * DK, h = blockIdx.y;
   const float A = gate_mode == 0 ? __expf(a_log[h]) : 0.f;
-  float2 acc_dtb[NP];
+  for (int c = tid; c < C3; c += blockDim.x) {
+    const int which = c / DK;
+    const float* w = which == 0 ? wq : (which == 1 ? wk : wv);
+    sw[c] = *reinterpret_cast<const float4*>(w + (h * DK + c % DK) * 4);
+  }
+  float2 dtb[NP], acc_dtb[NP];
 #pragma unroll
-  for (int j = 0; j < NP; ++j) acc_dtb[j] = make_float2(0.f, 0.f);
+  for (int j = 0; j < NP; ++j) {
+    dtb[j] = *reinterpret_cast<const float2*>(dt_bias + h * DK + min(2 * lane + 64 * j, DK - 2));
+    acc_dtb[j] = make_float2(0.f, 0.f);
+  }
   float acc_al = 0.f;
   float dwacc[P::NC][4];
 #pragma unroll
@@ -715,6 +761,7 @@ __global__ void __launch_bounds__(256, 4) prep_bwd_fused_kernel(
   const int ntiles = (T + R - 1) / R;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const int t0 = tile * R;
+    const int pos0 = t0 % S;
     // ---- stage 0: raw rows t0-3 .. t0+R+2 (16-byte vectors; zero outside [0, T))
     {
       constexpr int VPR = C3 * 2 / 16;  // vectors per row
@@ -737,61 +784,69 @@ __global__ void __launch_bounds__(256, 4) prep_bwd_fused_kernel(
         for (int c = lane; c < C3; c += 32) drow[c] = 0.f;
         continue;
       }
-      const int pos = t % S;
+      int pos = pos0 + r;
+      if (pos >= S) pos %= S;
       const bool own = r < R;
-      float2 cq[NP], ck[NP], sq[NP], sk[NP], gq[NP], gk[NP];
-      float ssq = 0.f, ssk = 0.f, dotq = 0.f, dotk = 0.f, dal = 0.f;
+      const long long orow = (long long)t * HK + h * DK;
+      float2 sq[NP], sk[NP], dsq[NP], dsk[NP], gq[NP], gk[NP];
+      float ssq = 0.f, ssk = 0.f, dotq = 0.f, dotk = 0.f;
 #pragma unroll
       for (int j = 0; j < NP; ++j) {
         const int c = 2 * lane + 64 * j;
-        cq[j] = ck[j] = sq[j] = sk[j] = gq[j] = gk[j] = make_float2(0.f, 0.f);
+        sq[j] = sk[j] = dsq[j] = dsk[j] = gq[j] = gk[j] = make_float2(0.f, 0.f);
         if (c >= DK) continue;
-        const int ch = h * DK + c;
-        const long long o = (long long)t * HK + ch;
-        float2 cv = make_float2(0.f, 0.f);
+        const long long o = orow + c;
+        float2 cq = make_float2(0.f, 0.f), ck = cq, cv = cq;
         {
-          const float4 wa = *reinterpret_cast<const float4*>(wq + ch * 4);
-          const float4 wb = *reinterpret_cast<const float4*>(wq + ch * 4 + 4);
-          const float4 ka = *reinterpret_cast<const float4*>(wk + ch * 4);
-          const float4 kb = *reinterpret_cast<const float4*>(wk + ch * 4 + 4);
-          const float4 va = *reinterpret_cast<const float4*>(wv + ch * 4);
-          const float4 vb = *reinterpret_cast<const float4*>(wv + ch * 4 + 4);
+          const float4 wa = sw[c], wb = sw[c + 1], ka = sw[DK + c], kb = sw[DK + c + 1],
+                       va = sw[2 * DK + c], vb = sw[2 * DK + c + 1];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             if (pos - 3 + i < 0) continue;
             const __nv_bfloat16* row = sraw + (r + i) * C3;
             const float2 xq = ld_bf2(row + c), xk = ld_bf2(row + DK + c), xv = ld_bf2(row + 2 * DK + c);
-            cq[j].x += tap(wa, i) * xq.x;  cq[j].y += tap(wb, i) * xq.y;
-            ck[j].x += tap(ka, i) * xk.x;  ck[j].y += tap(kb, i) * xk.y;
-            cv.x += tap(va, i) * xv.x;     cv.y += tap(vb, i) * xv.y;
+            cq.x += tap(wa, i) * xq.x;  cq.y += tap(wb, i) * xq.y;
+            ck.x += tap(ka, i) * xk.x;  ck.y += tap(kb, i) * xk.y;
+            cv.x += tap(va, i) * xv.x;  cv.y += tap(vb, i) * xv.y;
           }
-          cq[j] = make_float2(rbf(cq[j].x), rbf(cq[j].y));
-          ck[j] = make_float2(rbf(ck[j].x), rbf(ck[j].y));
-          cv = make_float2(rbf(cv.x), rbf(cv.y));
         }
-        sq[j] = make_float2(silu_f(cq[j].x), silu_f(cq[j].y));
-        sk[j] = make_float2(silu_f(ck[j].x), silu_f(ck[j].y));
+        cq = make_float2(rbf(cq.x), rbf(cq.y));
+        ck = make_float2(rbf(ck.x), rbf(ck.y));
+        cv = make_float2(rbf(cv.x), rbf(cv.y));
+        // silu(x) = x s, silu'(x) = s (1 + x (1 - s)), s = sigmoid(x)
+        {
+          const float s0 = sigm(cq.x), s1 = sigm(cq.y);
+          sq[j] = make_float2(cq.x * s0, cq.y * s1);
+          dsq[j] = make_float2(s0 * (1.f + cq.x * (1.f - s0)), s1 * (1.f + cq.y * (1.f - s1)));
+        }
+        {
+          const float s0 = sigm(ck.x), s1 = sigm(ck.y);
+          sk[j] = make_float2(ck.x * s0, ck.y * s1);
+          dsk[j] = make_float2(s0 * (1.f + ck.x * (1.f - s0)), s1 * (1.f + ck.y * (1.f - s1)));
+        }
         ssq += sq[j].x * sq[j].x + sq[j].y * sq[j].y;
         ssk += sk[j].x * sk[j].x + sk[j].y * sk[j].y;
         gq[j] = *reinterpret_cast<const float2*>(dq + o);
         gk[j] = *reinterpret_cast<const float2*>(dk + o);
         dotq += gq[j].x * sq[j].x + gq[j].y * sq[j].y;
         dotk += gk[j].x * sk[j].x + gk[j].y * sk[j].y;
-        const float2 gv = *reinterpret_cast<const float2*>(dv + o);
-        *reinterpret_cast<float2*>(drow + 2 * DK + c) =
-            make_float2(gv.x * dsilu_f(cv.x), gv.y * dsilu_f(cv.y));
+        {
+          const float2 gv = *reinterpret_cast<const float2*>(dv + o);
+          const float s0 = sigm(cv.x), s1 = sigm(cv.y);
+          *reinterpret_cast<float2*>(drow + 2 * DK + c) =
+              make_float2(gv.x * s0 * (1.f + cv.x * (1.f - s0)), gv.y * s1 * (1.f + cv.y * (1.f - s1)));
+        }
         if (own) {
           const float2 fz = *reinterpret_cast<const float2*>(f + o);
-          const float2 db = *reinterpret_cast<const float2*>(dt_bias + ch);
           const float2 gg = *reinterpret_cast<const float2*>(dg + o);
-          const float z[2] = {fz.x + db.x, fz.y + db.y}, dgv[2] = {gg.x, gg.y};
+          const float z[2] = {fz.x + dtb[j].x, fz.y + dtb[j].y}, dgv[2] = {gg.x, gg.y};
           float dz[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const float sig = 1.f / (1.f + __expf(-z[e]));
+            const float sig = sigm(z[e]);
             if (gate_mode == 0) {
               dz[e] = dgv[e] * (-A) * sig;
-              dal += dgv[e] * (-A * softplus_f(z[e]));
+              acc_al += dgv[e] * (-A * softplus_f(z[e]));
             } else {
               dz[e] = dgv[e] * (1.f - sig);
             }
@@ -805,54 +860,52 @@ __global__ void __launch_bounds__(256, 4) prep_bwd_fused_kernel(
       ssk = warp_sum(ssk);
       dotq = warp_sum(dotq);
       dotk = warp_sum(dotk);
-      const float nq = sqrtf(ssq + 1e-6f), nk = sqrtf(ssk + 1e-6f);
+      // y = x / n, n = sqrt(|x|^2 + eps): dx = (dy - y (dy . y)) / n
+      const float iq = rsqrtf(ssq + 1e-6f), ik = rsqrtf(ssk + 1e-6f);
+      const float cqf = dotq * iq * iq, ckf = dotk * ik * ik;
 #pragma unroll
       for (int j = 0; j < NP; ++j) {
         const int c = 2 * lane + 64 * j;
         if (c >= DK) continue;
-        // y = x / n, n = sqrt(|x|^2 + eps): dx = (dy - y (dy . y)) / n
-        const float dq0 = (gq[j].x - sq[j].x / nq * (dotq / nq)) / nq;
-        const float dq1 = (gq[j].y - sq[j].y / nq * (dotq / nq)) / nq;
-        const float dk0 = (gk[j].x - sk[j].x / nk * (dotk / nk)) / nk;
-        const float dk1 = (gk[j].y - sk[j].y / nk * (dotk / nk)) / nk;
-        *reinterpret_cast<float2*>(drow + c) = make_float2(dq0 * dsilu_f(cq[j].x), dq1 * dsilu_f(cq[j].y));
-        *reinterpret_cast<float2*>(drow + DK + c) = make_float2(dk0 * dsilu_f(ck[j].x), dk1 * dsilu_f(ck[j].y));
+        *reinterpret_cast<float2*>(drow + c) =
+            make_float2((gq[j].x - sq[j].x * cqf) * iq * dsq[j].x, (gq[j].y - sq[j].y * cqf) * iq * dsq[j].y);
+        *reinterpret_cast<float2*>(drow + DK + c) =
+            make_float2((gk[j].x - sk[j].x * ckf) * ik * dsk[j].x, (gk[j].y - sk[j].y * ckf) * ik * dsk[j].y);
       }
-      if (own) {
-        acc_al += warp_sum(dal);
-        if (lane == 0) {
-          const float bt = beta[(long long)t * H + h];
-          dbraw[(long long)t * H + h] = dbeta[(long long)t * H + h] * bt * (1.f - bt);
-        }
+      if (own && lane == 0) {
+        const float bt = beta[(long long)t * H + h];
+        dbraw[(long long)t * H + h] = dbeta[(long long)t * H + h] * bt * (1.f - bt);
       }
     }
     __syncthreads();
-    // ---- stage 2: draw rows and the conv weight gradient
-    for (int idx = tid; idx < R * C3; idx += blockDim.x) {
-      const int r = idx / C3, c = idx % C3;
-      const int t = t0 + r;
-      if (t >= T) break;
-      const int pos = t % S;
-      const int which = c / DK;
-      const float* w = which == 0 ? wq : (which == 1 ? wk : wv);
-      const float4 wt = *reinterpret_cast<const float4*>(w + (h * DK + c % DK) * 4);
-      float acc = wt.w * sdc[r * C3 + c];
-      if (pos + 1 < S) acc += wt.z * sdc[(r + 1) * C3 + c];
-      if (pos + 2 < S) acc += wt.y * sdc[(r + 2) * C3 + c];
-      if (pos + 3 < S) acc += wt.x * sdc[(r + 3) * C3 + c];
-      draw[(long long)t * ld_raw + which * HK + h * DK + c % DK] = __float2bfloat16_rn(acc);
-    }
+    // ---- stage 2: thread per channel, sliding windows over the tile's rows
+    const int rn = min(R, T - t0);
 #pragma unroll
     for (int n = 0; n < P::NC; ++n) {
       const int c = tid + 256 * n;
       if (c >= C3) continue;
-      for (int r = 0; r < R && t0 + r < T; ++r) {
-        const float d = sdc[r * C3 + c];
-        const int pos = (t0 + r) % S;
-        // raw row t-3+i sits at staged row r+i
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          if (pos - 3 + i >= 0) dwacc[n][i] += d * __bfloat162float(sraw[(r + i) * C3 + c]);
+      const float4 wt = sw[c];
+      const long long col = (c / DK) * HK + h * DK + c % DK;
+      // d0..d3 = dconv rows r..r+3; x0..x3 = staged raw rows r..r+3 (tokens t-3..t)
+      float d0 = sdc[c], d1 = sdc[C3 + c], d2 = sdc[2 * C3 + c], d3;
+      float x0 = __bfloat162float(sraw[c]), x1 = __bfloat162float(sraw[C3 + c]),
+            x2 = __bfloat162float(sraw[2 * C3 + c]), x3;
+      int pos = pos0;
+      for (int r = 0; r < rn; ++r) {
+        d3 = sdc[(r + 3) * C3 + c];
+        x3 = __bfloat162float(sraw[(r + 3) * C3 + c]);
+        float acc = wt.w * d0;
+        if (pos + 1 < S) acc += wt.z * d1;
+        if (pos + 2 < S) acc += wt.y * d2;
+        if (pos + 3 < S) acc += wt.x * d3;
+        draw[(long long)(t0 + r) * ld_raw + col] = __float2bfloat16_rn(acc);
+        dwacc[n][3] += d0 * x3;
+        if (pos >= 1) dwacc[n][2] += d0 * x2;
+        if (pos >= 2) dwacc[n][1] += d0 * x1;
+        if (pos >= 3) dwacc[n][0] += d0 * x0;
+        d0 = d1; d1 = d2; d2 = d3;
+        x0 = x1; x1 = x2; x2 = x3;
+        if (++pos == S) pos = 0;
       }
     }
     __syncthreads();
@@ -874,7 +927,10 @@ __global__ void __launch_bounds__(256, 4) prep_bwd_fused_kernel(
       atomicAdd(s_dtb + c + 1, acc_dtb[j].y);
     }
   }
-  if (lane == 0 && gate_mode == 0) atomicAdd(s_dtb + DK, acc_al);
+  if (gate_mode == 0) {
+    acc_al = warp_sum(acc_al);
+    if (lane == 0) atomicAdd(s_dtb + DK, acc_al);
+  }
   __syncthreads();
   for (int i = tid; i < DK; i += blockDim.x)
     if (s_dtb[i] != 0.f) atomicAdd(d_dtb + h * DK + i, s_dtb[i]);
@@ -1017,7 +1073,10 @@ void kda_prep_fwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::
                   torch::Tensor beta) {
   const int T = q.size(0), H = q.size(1), DKV = q.size(2);
   HB_CHECK(raw.stride(0) % 2 == 0 && DKV % 2 == 0, "kda_prep: even row stride and head dim");
-  const int grid = (int)std::min<long long>(((long long)T + 7) / 8, num_sms() * 16);
+  // blocks: (token runs) x (heads), about 8 resident blocks per SM in all
+  const int gx = (int)std::max<long long>(
+      1, std::min<long long>(((long long)T + 7) / 8, ((long long)num_sms() * 8 + H - 1) / H));
+  const dim3 grid(gx, H);
   auto launch = [&](auto dk) {
     constexpr int DK = decltype(dk)::value;
     kda::prep_fwd_kernel<DK><<<grid, 256, 0, cur_stream()>>>(
