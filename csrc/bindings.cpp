@@ -106,7 +106,7 @@ void kda_prep_fwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::
 void kda_prep_bwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::Tensor wv, torch::Tensor f,
                   torch::Tensor a_log, torch::Tensor dt_bias, torch::Tensor beta, int64_t gate_mode,
                   int64_t S, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor dg,
-                  torch::Tensor dbeta, torch::Tensor dconv, torch::Tensor df, torch::Tensor dbraw,
+                  torch::Tensor dbeta, torch::Tensor df, torch::Tensor dbraw,
                   torch::Tensor d_alog, torch::Tensor d_dtb, torch::Tensor draw, torch::Tensor dwq,
                   torch::Tensor dwk, torch::Tensor dwv);
 // comm

@@ -381,8 +381,8 @@ constexpr int intra_bwd_smem() {
 }
 
 // ================================================================ front-end
-// One warp per token (all heads), two adjacent channels per lane: bf16x2 loads
-// of the projection taps, float4 loads of the conv taps, float2 stores.
+// Blocks per head, two adjacent channels per lane: bf16x2 loads of the
+// projection taps, float2 loads and stores of the fp32 rows.
 // raw: [T, 3*HK] bf16 rows (q | k | v projections, row stride ld_raw); conv
 // weights [HK, 4] fp32 each; outputs fp32 [T, H, K].
 HB_DEVICE float2 ld_bf2(const __nv_bfloat16* p) {
@@ -390,30 +390,8 @@ HB_DEVICE float2 ld_bf2(const __nv_bfloat16* p) {
 }
 HB_DEVICE float tap(const float4& w, int i) { return i == 0 ? w.x : i == 1 ? w.y : i == 2 ? w.z : w.w; }
 HB_DEVICE float rbf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
-HB_DEVICE float silu_f(float x) { return x / (1.f + __expf(-x)); }
-HB_DEVICE float dsilu_f(float x) {
-  const float s = 1.f / (1.f + __expf(-x));
-  return s * (1.f + x * (1.f - s));
-}
 // softplus(y) = max(y, 0) + log1p(exp(-|y|)) never overflows
 HB_DEVICE float softplus_f(float y) { return fmaxf(y, 0.f) + log1pf(__expf(-fabsf(y))); }
-
-// Causal 4-tap conv of channels (ch, ch+1) of projection `which` at token t;
-// rows[i] is the row of token t - 3 + i (nullptr before the sequence start).
-// The result is rounded to the compute dtype (model/kda.py:136, 257-259).
-HB_DEVICE float2 conv2(const __nv_bfloat16* const (&rows)[4], int off, const float* w, int ch) {
-  const float4 wa = *reinterpret_cast<const float4*>(w + ch * 4);
-  const float4 wb = *reinterpret_cast<const float4*>(w + ch * 4 + 4);
-  float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    if (!rows[i]) continue;
-    const float2 x = ld_bf2(rows[i] + off);
-    a0 += tap(wa, i) * x.x;
-    a1 += tap(wb, i) * x.y;
-  }
-  return make_float2(rbf(a0), rbf(a1));
-}
 
 // sigmoid by the hardware exponential and an approximate divide (2 ulp);
 // 1 / (1 + inf) = 0 gives the right limit for very negative x
@@ -507,193 +485,6 @@ __global__ void __launch_bounds__(256) prep_fwd_kernel(const __nv_bfloat16* __re
     }
     if (lane == 0) beta[t * H + h] = sigm(braw[t * H + h]);
   }
-}
-
-// Backward part 1 (block per head, warp per token): gradients at the conv
-// outputs of q/k/v (fp32, [T, 3*HK]), df [T, HK] (bf16: it only feeds the
-// f_proj GEMMs), dbraw [T, H]; d dt_bias and
-// d a_log of the block's head are summed in each lane's registers over its
-// tokens, then reduced through shared memory with one global atomic each.
-template <int DK>
-__global__ void __launch_bounds__(256, DK >= 128 ? 2 : 3) prep_bwd1_kernel(const __nv_bfloat16* __restrict__ raw, long long ld_raw,
-                                 const float* __restrict__ wq, const float* __restrict__ wk,
-                                 const float* __restrict__ wv, const float* __restrict__ f,
-                                 const float* __restrict__ a_log, const float* __restrict__ dt_bias,
-                                 const float* __restrict__ beta, int gate_mode, int T, int S, int H,
-                                 const float* __restrict__ dq, const float* __restrict__ dk,
-                                 const float* __restrict__ dv, const float* __restrict__ dg,
-                                 const float* __restrict__ dbeta, float* __restrict__ dconv,
-                                 __nv_bfloat16* __restrict__ df, float* __restrict__ dbraw,
-                                 float* __restrict__ d_alog, float* __restrict__ d_dtb) {
-  constexpr int NP = (DK + 63) / 64;
-  __shared__ float s_dtb[DK + 1];  // this block's head: d dt_bias, then d a_log
-  const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
-  const int HK = H * DK;
-  const int h = blockIdx.y;        // one head per block: the bias gradients sum in registers
-  float2 acc_dtb[NP];
-#pragma unroll
-  for (int j = 0; j < NP; ++j) acc_dtb[j] = make_float2(0.f, 0.f);
-  float acc_al = 0.f;
-  for (int i = threadIdx.x; i < DK + 1; i += blockDim.x) s_dtb[i] = 0.f;
-  __syncthreads();
-  for (long long t = blockIdx.x * (long long)warps + (threadIdx.x >> 5); t < T; t += (long long)gridDim.x * warps) {
-    const int pos = t % S;
-    const __nv_bfloat16* rows[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) rows[i] = pos - (3 - i) >= 0 ? raw + (t - (3 - i)) * ld_raw : nullptr;
-    {
-      float2 cq[NP], ck[NP], sq[NP], sk[NP], gq[NP], gk[NP];
-      float ssq = 0.f, ssk = 0.f, dotq = 0.f, dotk = 0.f, dal = 0.f;
-#pragma unroll
-      for (int j = 0; j < NP; ++j) {
-        const int c = 2 * lane + 64 * j;
-        cq[j] = ck[j] = sq[j] = sk[j] = gq[j] = gk[j] = make_float2(0.f, 0.f);
-        if (c >= DK) continue;
-        const int ch = h * DK + c;
-        const long long o = t * HK + ch;
-        cq[j] = conv2(rows, ch, wq, ch);
-        ck[j] = conv2(rows, HK + ch, wk, ch);
-        const float2 cv = conv2(rows, 2 * HK + ch, wv, ch);
-        sq[j] = make_float2(silu_f(cq[j].x), silu_f(cq[j].y));
-        sk[j] = make_float2(silu_f(ck[j].x), silu_f(ck[j].y));
-        ssq += sq[j].x * sq[j].x + sq[j].y * sq[j].y;
-        ssk += sk[j].x * sk[j].x + sk[j].y * sk[j].y;
-        gq[j] = *reinterpret_cast<const float2*>(dq + o);
-        gk[j] = *reinterpret_cast<const float2*>(dk + o);
-        dotq += gq[j].x * sq[j].x + gq[j].y * sq[j].y;
-        dotk += gk[j].x * sk[j].x + gk[j].y * sk[j].y;
-        const float2 gv = *reinterpret_cast<const float2*>(dv + o);
-        const long long co = t * 3 * HK + ch;
-        *reinterpret_cast<float2*>(dconv + co + 2 * HK) = make_float2(gv.x * dsilu_f(cv.x), gv.y * dsilu_f(cv.y));
-        // decay gate
-        const float2 fz = *reinterpret_cast<const float2*>(f + o);
-        const float2 db = *reinterpret_cast<const float2*>(dt_bias + ch);
-        const float2 gg = *reinterpret_cast<const float2*>(dg + o);
-        const float z[2] = {fz.x + db.x, fz.y + db.y}, dgv[2] = {gg.x, gg.y};
-        float dz[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const float sig = 1.f / (1.f + __expf(-z[e]));
-          if (gate_mode == 0) {
-            const float A = __expf(a_log[h]);
-            dz[e] = dgv[e] * (-A) * sig;
-            dal += dgv[e] * (-A * softplus_f(z[e]));
-          } else {
-            dz[e] = dgv[e] * (1.f - sig);
-          }
-        }
-        *reinterpret_cast<__nv_bfloat162*>(df + o) = __floats2bfloat162_rn(dz[0], dz[1]);
-        acc_dtb[j].x += dz[0];
-        acc_dtb[j].y += dz[1];
-      }
-      ssq = warp_sum(ssq);
-      ssk = warp_sum(ssk);
-      dotq = warp_sum(dotq);
-      dotk = warp_sum(dotk);
-      dal = warp_sum(dal);
-      const float nq = sqrtf(ssq + 1e-6f), nk = sqrtf(ssk + 1e-6f);
-#pragma unroll
-      for (int j = 0; j < NP; ++j) {
-        const int c = 2 * lane + 64 * j;
-        if (c >= DK) continue;
-        const long long co = t * 3 * HK + h * DK + c;
-        // y = x / n, n = sqrt(|x|^2 + eps): dx = (dy - y (dy . y)) / n
-        const float dq0 = (gq[j].x - sq[j].x / nq * (dotq / nq)) / nq;
-        const float dq1 = (gq[j].y - sq[j].y / nq * (dotq / nq)) / nq;
-        const float dk0 = (gk[j].x - sk[j].x / nk * (dotk / nk)) / nk;
-        const float dk1 = (gk[j].y - sk[j].y / nk * (dotk / nk)) / nk;
-        *reinterpret_cast<float2*>(dconv + co) = make_float2(dq0 * dsilu_f(cq[j].x), dq1 * dsilu_f(cq[j].y));
-        *reinterpret_cast<float2*>(dconv + co + HK) = make_float2(dk0 * dsilu_f(ck[j].x), dk1 * dsilu_f(ck[j].y));
-      }
-      acc_al += dal;
-      if (lane == 0) {
-        const float bt = beta[t * H + h];
-        dbraw[t * H + h] = dbeta[t * H + h] * bt * (1.f - bt);
-      }
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < NP; ++j) {
-    const int c = 2 * lane + 64 * j;
-    if (c < DK) {
-      atomicAdd(s_dtb + c, acc_dtb[j].x);
-      atomicAdd(s_dtb + c + 1, acc_dtb[j].y);
-    }
-  }
-  if (lane == 0 && gate_mode == 0) atomicAdd(s_dtb + DK, acc_al);
-  __syncthreads();
-  for (int i = threadIdx.x; i < DK; i += blockDim.x)
-    if (s_dtb[i] != 0.f) atomicAdd(d_dtb + h * DK + i, s_dtb[i]);
-  if (threadIdx.x == 0 && s_dtb[DK] != 0.f) atomicAdd(d_alog + h, s_dtb[DK]);
-}
-
-// Backward part 2 (thread per channel of the 3*HK conv inputs, a run of tokens):
-//   draw[t] = sum_i w[i] dconv[t + 3 - i] (same sequence); dw[i] += dconv[t] raw[t-3+i]
-// dconv and raw are held in 4-deep register windows, so each element is loaded
-// once; the loads of U tokens are issued together ahead of their arithmetic
-// (a thread walks hundreds of tokens, so one load pair per step would leave
-// the kernel bound by memory latency).
-__global__ void prep_bwd2_kernel(const __nv_bfloat16* __restrict__ raw, long long ld_raw,
-                                 const float* __restrict__ wq, const float* __restrict__ wk,
-                                 const float* __restrict__ wv, const float* __restrict__ dconv,
-                                 int T, int S, int HK, __nv_bfloat16* __restrict__ draw,
-                                 float* __restrict__ dwq, float* __restrict__ dwk, float* __restrict__ dwv) {
-  constexpr int U = 8;
-  const int C3 = 3 * HK;
-  const int ch = blockIdx.x * blockDim.x + threadIdx.x;
-  if (ch >= C3) return;
-  const int which = ch / HK, cc = ch % HK;
-  const float* w = which == 0 ? wq : (which == 1 ? wk : wv);
-  float* dw = which == 0 ? dwq : (which == 1 ? dwk : dwv);
-  const float4 wt = *reinterpret_cast<const float4*>(w + cc * 4);
-  const int tpb = (T + gridDim.y - 1) / gridDim.y;
-  const int tb = blockIdx.y * tpb, te = min(T, tb + tpb);
-  if (tb >= te) return;
-  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-  const float* dcol = dconv + ch;
-  const __nv_bfloat16* rcol = raw + ch;
-  auto dc = [&](int t) { return t < T ? __ldg(dcol + (long long)t * C3) : 0.f; };
-  auto rw = [&](int t) { return t >= 0 && t < T ? __bfloat162float(rcol[(long long)t * ld_raw]) : 0.f; };
-  // windows: d0..d3 = dconv[t..t+3], r1..r3 = raw[t-1..t-3]
-  float d0 = dc(tb), d1 = dc(tb + 1), d2 = dc(tb + 2), d3 = dc(tb + 3);
-  float r1 = rw(tb - 1), r2 = rw(tb - 2), r3 = rw(tb - 3);
-  int pos = tb % S;
-  for (int t0 = tb; t0 < te; t0 += U) {
-    float dn[U], rn[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      dn[u] = dc(t0 + u + 4);
-      rn[u] = rw(t0 + u);
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int t = t0 + u;
-      if (t < te) {
-        const float r0 = rn[u];
-        float acc = wt.w * d0;
-        if (pos + 1 < S) acc += wt.z * d1;
-        if (pos + 2 < S) acc += wt.y * d2;
-        if (pos + 3 < S) acc += wt.x * d3;
-        draw[(long long)t * ld_raw + ch] = __float2bfloat16_rn(acc);
-        a3 += d0 * r0;
-        if (pos >= 1) a2 += d0 * r1;
-        if (pos >= 2) a1 += d0 * r2;
-        if (pos >= 3) a0 += d0 * r3;
-        d0 = d1;
-        d1 = d2;
-        d2 = d3;
-        d3 = dn[u];
-        r3 = r2;
-        r2 = r1;
-        r1 = r0;
-        if (++pos == S) pos = 0;
-      }
-    }
-  }
-  atomicAdd(dw + cc * 4 + 0, a0);
-  atomicAdd(dw + cc * 4 + 1, a1);
-  atomicAdd(dw + cc * 4 + 2, a2);
-  atomicAdd(dw + cc * 4 + 3, a3);
 }
 
 // Fused backward (block per head, persistent over token tiles of R rows):
@@ -1096,14 +887,13 @@ void kda_prep_fwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::
 void kda_prep_bwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::Tensor wv, torch::Tensor f,
                   torch::Tensor a_log, torch::Tensor dt_bias, torch::Tensor beta, int64_t gate_mode,
                   int64_t S, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor dg,
-                  torch::Tensor dbeta, torch::Tensor dconv, torch::Tensor df, torch::Tensor dbraw,
+                  torch::Tensor dbeta, torch::Tensor df, torch::Tensor dbraw,
                   torch::Tensor d_alog, torch::Tensor d_dtb, torch::Tensor draw, torch::Tensor dwq,
                   torch::Tensor dwk, torch::Tensor dwv) {
   const int T = dq.size(0), H = dq.size(1), DKV = dq.size(2);
   HB_CHECK(raw.stride(0) % 2 == 0 && DKV % 2 == 0, "kda_prep: even row stride and head dim");
   HB_CHECK(df.scalar_type() == at::kBFloat16 && df.is_contiguous(), "kda_prep_bwd: df must be contiguous bf16");
-  if (dconv.numel() == 0) {
-    // fused: the conv-output gradient stays in shared memory
+  {
     HB_CHECK(raw.stride(0) % 8 == 0 && al16(raw.data_ptr()) && draw.stride(0) == raw.stride(0),
              "kda_prep_bwd: 16-byte aligned raw rows");
     auto launch = [&](auto dkc) {
@@ -1134,34 +924,7 @@ void kda_prep_bwd(torch::Tensor raw, torch::Tensor wq, torch::Tensor wk, torch::
     else if (DKV == 128) launch(std::integral_constant<int, 128>{});
     else HB_CHECK(false, "kda_prep: unsupported head dim");
     HB_CUDA_CHECK(cudaGetLastError());
-    return;
   }
-  // blocks: (token runs) x (heads); about 8 resident blocks per SM in all
-  const int gx = (int)std::max<long long>(
-      1, std::min<long long>(((long long)T + 7) / 8, ((long long)num_sms() * 8 + H - 1) / H));
-  const dim3 grid(gx, H);
-  auto launch = [&](auto dkc) {
-    constexpr int DK = decltype(dkc)::value;
-    kda::prep_bwd1_kernel<DK><<<grid, 256, 0, cur_stream()>>>(
-        (const __nv_bfloat16*)raw.data_ptr(), raw.stride(0), wq.data_ptr<float>(), wk.data_ptr<float>(),
-        wv.data_ptr<float>(), f.data_ptr<float>(), a_log.data_ptr<float>(), dt_bias.data_ptr<float>(),
-        beta.data_ptr<float>(), (int)gate_mode, T, (int)S, H, dq.data_ptr<float>(), dk.data_ptr<float>(),
-        dv.data_ptr<float>(), dg.data_ptr<float>(), dbeta.data_ptr<float>(), dconv.data_ptr<float>(),
-        (__nv_bfloat16*)df.data_ptr(), dbraw.data_ptr<float>(), d_alog.data_ptr<float>(), d_dtb.data_ptr<float>());
-  };
-  if (DKV == 16) launch(std::integral_constant<int, 16>{});
-  else if (DKV == 32) launch(std::integral_constant<int, 32>{});
-  else if (DKV == 64) launch(std::integral_constant<int, 64>{});
-  else if (DKV == 128) launch(std::integral_constant<int, 128>{});
-  else HB_CHECK(false, "kda_prep: unsupported head dim");
-  HB_CUDA_CHECK(cudaGetLastError());
-  const int HK = H * DKV;
-  dim3 g2((3 * HK + 255) / 256, std::max(1, std::min(64, T / 64)));
-  kda::prep_bwd2_kernel<<<g2, 256, 0, cur_stream()>>>(
-      (const __nv_bfloat16*)raw.data_ptr(), raw.stride(0), wq.data_ptr<float>(), wk.data_ptr<float>(),
-      wv.data_ptr<float>(), dconv.data_ptr<float>(), T, (int)S, HK, (__nv_bfloat16*)draw.data_ptr(),
-      dwq.data_ptr<float>(), dwk.data_ptr<float>(), dwv.data_ptr<float>());
-  HB_CUDA_CHECK(cudaGetLastError());
 }
 
 }  // namespace hb

@@ -786,12 +786,12 @@ void kda64_products_tc(const float* dU, const float* dout, const float* states, 
                        const float* U, float* dWt, float* dQg, float* dP, float* dKh, float* dgC, int B, int S,
                        int H, int NC);
 
-// HB_KDA64_TC=1 runs those products on tcgen05; the warp-level (mma.sync)
-// kernels are the default.
+// The products run on tcgen05 (fp32-accurate 3-pass tf32); HB_KDA64_TC=0
+// selects the warp-level (mma.sync) kernel instead.
 static bool kda64_use_tc() {
   static const bool on = [] {
     const char* e = getenv("HB_KDA64_TC");
-    return e && e[0] == '1';
+    return !(e && e[0] == '0');
   }();
   return on;
 }

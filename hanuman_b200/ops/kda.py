@@ -157,9 +157,6 @@ class KdaFrontFn(torch.autograd.Function):
         z = lambda t: torch.zeros_like(f) if t is None else t.float().contiguous()
         dq, dk, dv, dg = z(dq), z(dk), z(dv), z(dg)
         dbeta = torch.zeros(T, H, device=dev) if dbeta is None else dbeta.float().contiguous()
-        # fused backward (empty dconv): the conv-output gradient stays on chip
-        fused = os.environ.get("HB_KDA_PREP_FUSED", "1") != "0"
-        dconv = torch.empty(0 if fused else T * 3 * HK, dtype=torch.float32, device=dev)
         df = torch.empty(T, HK, dtype=torch.bfloat16, device=dev)
         dbraw = torch.empty(T, H, dtype=torch.float32, device=dev)
         d_alog = torch.zeros(H, dtype=torch.float32, device=dev)
@@ -168,7 +165,7 @@ class KdaFrontFn(torch.autograd.Function):
         dcq = torch.zeros(HK, 1, 4, dtype=torch.float32, device=dev)
         dck, dcv = torch.zeros_like(dcq), torch.zeros_like(dcq)
         ext().kda_prep_bwd(big[:, :3 * HK], cq, ck, cv, f, al, dtb, beta, gate_mode, S,
-                           dq, dk, dv, dg, dbeta, dconv, df, dbraw, d_alog, d_dtb,
+                           dq, dk, dv, dg, dbeta, df, dbraw, d_alog, d_dtb,
                            dbig[:, :3 * HK], dcq, dck, dcv)
         p_wq, p_wk, p_wv, p_f0, p_g0, p_wb, p_f1, p_g1 = ctx.params
         # low-rank second stage: d f0 / d g0 straight into their dbig columns
