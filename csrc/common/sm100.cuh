@@ -79,7 +79,10 @@ HB_DEVICE bool mbar_try_wait(uint32_t addr, uint32_t parity) {
 }
 
 // Wait for `parity` on an mbarrier for at most `budget_ns`; false on timeout
-// (the error code is recorded in `status`).
+// (the error code is recorded in `status`).  An error that another kernel
+// recorded earlier does not end the wait: the barriers of this CTA still
+// complete, and a kernel that gave up on them would leave its outputs
+// unwritten for the rest of the step.
 HB_DEVICE bool mbar_wait(uint32_t addr, uint32_t parity, int* status, int code,
                          uint64_t budget_ns) {
   if (mbar_try_wait(addr, parity)) return true;
@@ -91,7 +94,6 @@ HB_DEVICE bool mbar_wait(uint32_t addr, uint32_t parity, int* status, int code,
       set_error(status, code);
       return false;
     }
-    if (status && *((volatile int*)status) != 0) return false;  // someone else failed
   }
 }
 

@@ -137,7 +137,9 @@ __global__ void __launch_bounds__(THREADS, 2)
   for (int c = blockIdx.x; c < chunks && alive; c += gridDim.x, ++it) {
     const uint32_t par = it & 1;
     bool ok = mbar_wait(smem_u32(full), par, p.status, kErrTimeoutProducer, p.budget_ns);
-    if (!ok) mbar_wait(smem_u32(full), par, nullptr, 0, p.budget_ns);  // copies still in flight
+    // after a timeout, wait (bounded) for the copies still in flight; if they
+    // land the chunk is computed all the same
+    if (!ok) ok = mbar_wait(smem_u32(full), par, nullptr, 0, p.budget_ns);
     // ---- hi / lo split in place (elementwise: the swizzle does not matter)
     if (ok) {
       float4* hi = reinterpret_cast<float4*>(smem);
@@ -155,8 +157,10 @@ __global__ void __launch_bounds__(THREADS, 2)
       fence_proxy_async();   // generic-proxy smem writes -> visible to the tensor core
     }
     tc_fence_before();
-    // one decision for the whole CTA: thread 0's view of its loads and the status
-    if (threadIdx.x == 0) *go_flag = (ok && *reinterpret_cast<volatile int*>(p.status) == 0) ? 1 : 0;
+    // one decision for the whole CTA: thread 0's view of its loads (an error
+    // recorded by another kernel does not stop this one: its outputs feed the
+    // rest of the step and must be written)
+    if (threadIdx.x == 0) *go_flag = ok ? 1 : 0;
     __syncthreads();
     const bool go = *go_flag != 0;
     const uint32_t tmem = tmem0 + 64 * par;
@@ -176,7 +180,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     ok = go;
     if (go) {
       ok = mbar_wait(smem_u32(done), par, p.status, kErrTimeoutMma, p.budget_ns);
-      if (!ok) mbar_wait(smem_u32(done), par, nullptr, 0, p.budget_ns);  // MMAs still in flight
+      if (!ok) ok = mbar_wait(smem_u32(done), par, nullptr, 0, p.budget_ns);  // MMAs still in flight
     }
     tc_fence_after();
     if (!ok) alive = false;

@@ -92,18 +92,23 @@ HB_DEVICE void route_token(int t, float (&lg)[8], const float* __restrict__ bias
     }
   }
   ent = warp_sum(ent);
-  // top-k by repeated warp argmax (ties -> lowest expert id, like top_k)
+  // top-k by repeated warp argmax (ties -> lowest expert id, like top_k).  A NaN
+  // score ranks as -inf, and every round picks an expert not yet taken, so the
+  // K ids are always distinct and in [0, N) (they index shared memory and the
+  // dispatch), whatever the logits hold.
   float selsum = 0.f;
   float selv[MAXK];
   int seli[MAXK];
+  unsigned taken = 0;
   for (int kk = 0; kk < K; ++kk) {
     float bv = -INFINITY;
     int bi = 0x7fffffff;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int e = lane + 32 * i;
-      if (i < EPL && e < N && (ef[i] > bv || (ef[i] == bv && e < bi))) {
-        bv = ef[i];
+      const float v = ef[i] != ef[i] ? -INFINITY : ef[i];
+      if (i < EPL && e < N && !(taken >> i & 1u) && (v > bv || (v == bv && e < bi))) {
+        bv = v;
         bi = e;
       }
     }
@@ -116,12 +121,13 @@ HB_DEVICE void route_token(int t, float (&lg)[8], const float* __restrict__ bias
         bi = oi;
       }
     }
+    if (bi >= N) bi = 0;  // unreachable for K <= N; keeps the id in range regardless
     float s_win = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i)
       if (lane + 32 * i == bi) {
         s_win = sc[i];
-        ef[i] = -INFINITY;
+        taken |= 1u << i;
       }
     s_win = warp_sum(s_win);
     seli[kk] = bi;

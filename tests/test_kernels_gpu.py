@@ -343,6 +343,35 @@ def test_router_logits_and_grads_match_fp32(N):
     assert rel(dW, x.float().t() @ dl) < 1e-4
 
 
+@pytest.mark.parametrize("N", [32, 12])
+def test_router_ids_stay_in_range_on_nan_logits(N):
+    """NaN activations (a diverged step) must not produce out-of-range expert
+    ids: those index shared memory and the dispatch.  Every token gets K
+    distinct ids in [0, N), NaN rows included."""
+    from hanuman_b200.ops._ext import ext
+    torch.manual_seed(13)
+    T, D, S, K = 512, 256, 128, 4
+    x = torch.randn(T, D, device=DEV).bfloat16()
+    x[::3] = float("nan")
+    W = torch.randn(D, N, device=DEV) * 0.02
+    bias = torch.zeros(N, device=DEV)
+    lg = torch.empty(T, N, device=DEV)
+    ti = torch.full((T, K), -7, dtype=torch.int32, device=DEV)
+    tw = torch.empty(T, K, device=DEV)
+    sc, sp = torch.zeros(T // S, N, device=DEV), torch.zeros(T // S, N, device=DEV)
+    su = torch.zeros(2, device=DEV)
+    ext().router_fwd(x, W, bias, S, K, False, 2.5, lg, ti, tw, sc, sp, su)
+    torch.cuda.synchronize()
+    tl = ti.long()
+    assert tl.min().item() >= 0 and tl.max().item() < N
+    assert (tl.sort(-1)[0].diff(dim=-1) > 0).all()
+    assert sc.sum().item() == T * K
+    clean = torch.ones(T, dtype=torch.bool, device=DEV)
+    clean[::3] = False
+    want = torch.topk(torch.sigmoid(x[clean].double() @ W.double()), K, dim=-1).indices
+    assert torch.equal(tl[clean].sort(-1)[0], want.sort(-1)[0])
+
+
 def test_add_norm_fwd_bwd():
     from hanuman_b200.ops.norm import add_rms_norm_cuda
     torch.manual_seed(12)
