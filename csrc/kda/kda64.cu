@@ -791,7 +791,7 @@ void kda64_products_tc(const float* dU, const float* dout, const float* states, 
 static bool kda64_use_tc() {
   static const bool on = [] {
     const char* e = getenv("HB_KDA64_TC");
-    return e && e[0] == '1';
+    return !(e && e[0] == '0');
   }();
   return on;
 }
