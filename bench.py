@@ -142,6 +142,19 @@ def count_native_launches(trainer, tokens):
     return native, other
 
 
+def _expert_layout(cfg, trainer, world):
+    """How the MoE expert weights live across ranks in this run."""
+    if world <= 1:
+        return "local"
+    if cfg.mesh_expert_axis > 1:
+        return "expert_parallel"
+    if cfg.expert_weights == "fused_gather":
+        return "fused_gather"
+    if getattr(trainer.engine, "sharded_units", None):
+        return "fsdp_sharded"
+    return "replicated"
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -245,7 +258,7 @@ def main():
                        "per_gpu_batch": B, "micro_batch": cfg.micro_batch,
                        "parallelism": (f"fsdp{world}" if getattr(trainer.engine, "sharded_units", None)
                                        else f"dp{world}") if world > 1 else "single",
-                       "expert_weights": cfg.expert_weights if world > 1 else "local",
+                       "expert_weights": _expert_layout(cfg, trainer, world),
                        "layers": cfg.layers, "expert_parallel": cfg.mesh_expert_axis,
                        "overlap_reduce": bool(cfg.overlap_reduce) if world > 1 else False,
                        "optimizer": cfg.optimizer,
