@@ -613,14 +613,15 @@ void flash_bwd_kv_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::T
 void flash_bwd_q_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor dout, torch::Tensor lse,
                     torch::Tensor delta, torch::Tensor dq, int64_t window);
 
-// Head dim 64 runs on the tcgen05 kernels (flash_tc.cu: forward, and dK / dV
-// of the backward) unless HB_FA_TC=0.
+// Head dims 64 and 128 run on the tcgen05 kernels (flash_tc.cu: forward, dK /
+// dV and dQ of the backward) unless HB_FA_TC=0; head dim 32 and HB_FA_TC=0 on
+// the mma.sync kernels of this file.
 static bool use_fwd_tc(int H) {
   static const bool on = [] {
     const char* e = std::getenv("HB_FA_TC");
     return !(e && std::string(e) == "0");
   }();
-  return on && H == 64;
+  return on && (H == 64 || H == 128);
 }
 
 void flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
@@ -712,8 +713,13 @@ void flash_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor 
       fa::set_smem<128>((const void*)fa::bwd_dq_kernel<128>, smem_q);
       c = true;
     }
-    fa::bwd_dkdv_kernel<128><<<gkv, fa::NT, smem_kv, cur_stream()>>>(p);
-    fa::bwd_dq_kernel<128><<<gq, fa::NT, smem_q, cur_stream()>>>(p);
+    if (use_fwd_tc(128)) {
+      flash_bwd_kv_tc(q, k, v, dout, lse, delta, dk, dv, window);
+      flash_bwd_q_tc(q, k, v, dout, lse, delta, dq, window);
+    } else {
+      fa::bwd_dkdv_kernel<128><<<gkv, fa::NT, smem_kv, cur_stream()>>>(p);
+      fa::bwd_dq_kernel<128><<<gq, fa::NT, smem_q, cur_stream()>>>(p);
+    }
   }
   HB_CUDA_CHECK(cudaGetLastError());
 }

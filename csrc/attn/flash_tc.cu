@@ -1,6 +1,13 @@
 // Causal / sliding-window GQA attention forward on the 5th-generation tensor
-// cores (tcgen05 + TMEM), head dim 64 (model/attention.py:136-224 semantics:
-// query i sees key j iff j <= i and, with a window W > 0, i - j < W).
+// cores (tcgen05 + TMEM), head dims 64 and 128 (model/attention.py:136-224
+// semantics: query i sees key j iff j <= i and, with a window W > 0, i - j < W).
+//
+// Head dim H: every K-major tile (Q, K, V rows of H bf16) is stored as H / 64
+// swizzle atoms of 128-byte rows (one TMA box each); a K step of 16 inside
+// atom a = k / 64 starts at atom a's base + (k % 64) * 2 bytes.  The MN-major
+// operands (V, dO, Q, K as the B of P V, dS K, P^T dO, dS^T Q) are 64-row
+// tiles whose 64-column atoms lie 8 KB apart, the descriptor's leading-byte
+// offset, so the same descriptor covers N = 64 and N = 128.
 //
 // CTA = 128 query rows of one head; key/value tiles of 64.  Warp roles:
 //   warp 0     TMA producer: Q once, then K_j / V_j into a 3-deep ring
@@ -19,8 +26,9 @@
 // rescaled (tcgen05.ld / st, warp-uniform: the whole warp takes that path when
 // any of its rows needs it) only on those rare steps.  Double-buffered
 // barriers (s_full, p_full, pv_done per buffer) keep every mbarrier at most
-// one phase ahead of its waiter.  Two CTAs share an SM (97 KB of shared memory,
-// 256 TMEM columns each).  Every wait is bounded (status word).
+// one phase ahead of its waiter.  Head dim 64: two CTAs share an SM (97 KB of
+// shared memory, 256 TMEM columns each); head dim 128: one CTA (161 KB).
+// Every wait is bounded (status word).
 #include <torch/extension.h>
 
 #include "../common/host.h"
@@ -29,18 +37,32 @@
 namespace hb {
 namespace fatc {
 
-constexpr int H = 64;
 constexpr int BQ = 128;
 constexpr int BK = 64;
 constexpr int THREADS = 320;   // producer, MMA, 8 softmax warps
-constexpr int Q_BYTES = BQ * H * 2;          // 16 KB
-constexpr int K_BYTES = BK * H * 2;          // 8 KB
-constexpr int V_BYTES = BK * H * 2;          // 8 KB
 constexpr int P_BYTES = BQ * BK * 2;         // 16 KB
 constexpr int KV_STAGES = 3;
-constexpr int SMEM = Q_BYTES + KV_STAGES * (K_BYTES + V_BYTES) + 2 * P_BYTES + 1024 + 256 + 6 * BQ * 4;
 constexpr int TMEM_COLS = 256;
-constexpr int S_COL = 0, O_COL = 128;   // S buffers at columns 0 and 64
+constexpr int S_COL = 0, O_COL = 128;   // S buffers at columns 0 and 64; O: H columns
+template <int H>
+struct Fwd {
+  static constexpr int Q_BYTES = BQ * H * 2;   // 16 / 32 KB
+  static constexpr int K_BYTES = BK * H * 2;   // 8 / 16 KB
+  static constexpr int V_BYTES = BK * H * 2;
+  static constexpr int SMEM = Q_BYTES + KV_STAGES * (K_BYTES + V_BYTES) + 2 * P_BYTES + 1024 + 256 + 6 * BQ * 4;
+};
+
+// K-major descriptor of K step kk (16 elements) of a tile of `rows` rows of H
+// bf16 stored as H / 64 swizzle atoms of rows x 128 bytes.
+HB_DEVICE uint64_t kdesc(uint32_t base, int rows, int kk) {
+  return make_smem_desc(base + (kk >> 2) * rows * 128 + (kk & 3) * 32, 16, 1024);
+}
+// TMA of a rows x H tile: one 64-column box per atom.
+template <int H>
+HB_DEVICE void load_tile(uint32_t dst, const CUtensorMap* m, uint32_t bar, int col, int row, int rows) {
+#pragma unroll
+  for (int a = 0; a < H / 64; ++a) tma_load_2d(dst + a * rows * 128, m, bar, col + 64 * a, row);
+}
 
 // 2^x on the special-function unit (PTX ex2.approx, flush-to-zero).
 HB_DEVICE float ex2(float x) {
@@ -64,9 +86,12 @@ HB_DEVICE bool visible(const TcParams& p, int qi, int kj) {
   return kj <= qi && (p.window <= 0 || qi - kj < p.window) && kj < p.S && qi < p.S;
 }
 
-__global__ void __launch_bounds__(THREADS, 2)
+template <int H>
+__global__ void __launch_bounds__(THREADS, H == 64 ? 2 : 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, const TcParams p) {
+  constexpr int Q_BYTES = Fwd<H>::Q_BYTES, K_BYTES = Fwd<H>::K_BYTES, V_BYTES = Fwd<H>::V_BYTES;
+  constexpr int HC = H / 64;   // 32-column chunks per half row of O
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sQ = smem_u32(smem);
@@ -125,7 +150,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     // ------------------------------------------------------------ producer
     if (elect_one()) {
       mbar_expect_tx(smem_u32(q_full), Q_BYTES);
-      tma_load_2d(sQ, &tmQ, smem_u32(q_full), h * H, row0 + q0);
+      load_tile<H>(sQ, &tmQ, smem_u32(q_full), h * H, row0 + q0, BQ);
       for (int j = 0; j < nkt; ++j) {
         const int st = j % KV_STAGES;
         if (!mbar_wait(smem_u32(&kv_empty[st]), ((j / KV_STAGES) & 1) ^ 1, p.status, kErrTimeoutProducer,
@@ -134,8 +159,8 @@ __global__ void __launch_bounds__(THREADS, 2)
         const uint32_t fb = smem_u32(&kv_full[st]);
         mbar_expect_tx(fb, K_BYTES + V_BYTES);
         const int k0 = (jb0 + j) * BK;
-        tma_load_2d(sK0 + st * K_BYTES, &tmK, fb, hk * H, row0 + k0);
-        tma_load_2d(sV0 + st * V_BYTES, &tmV, fb, hk * H, row0 + k0);
+        load_tile<H>(sK0 + st * K_BYTES, &tmK, fb, hk * H, row0 + k0, BK);
+        load_tile<H>(sV0 + st * V_BYTES, &tmV, fb, hk * H, row0 + k0, BK);
       }
     }
   } else if (warp == 1) {
@@ -152,8 +177,8 @@ __global__ void __launch_bounds__(THREADS, 2)
         const uint32_t sk = sK0 + st * K_BYTES;
 #pragma unroll
         for (int kk = 0; kk < H / 16; ++kk)
-          umma_f16(tmem + S_COL + (j & 1) * BK, make_smem_desc(sQ + kk * 32, 16, 1024),
-                   make_smem_desc(sk + kk * 32, 16, 1024), idesc_s, kk != 0 ? 1u : 0u);
+          umma_f16(tmem + S_COL + (j & 1) * BK, kdesc(sQ, BQ, kk), kdesc(sk, BK, kk), idesc_s,
+                   kk != 0 ? 1u : 0u);
         umma_commit(smem_u32(&s_full[j & 1]));
         return true;
       };
@@ -230,12 +255,16 @@ __global__ void __launch_bounds__(THREADS, 2)
                          p.budget_ns);
         ok = __all_sync(0xffffffffu, ok);
         tc_fence_after();
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(trow + O_COL + half * 32, v);
-        tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
-        tmem_st_32x32b_x32(trow + O_COL + half * 32, v);
+        for (int c = 0; c < HC; ++c) {
+          uint32_t v[32];
+          const uint32_t col = O_COL + half * (H / 2) + 32 * c;
+          tmem_ld_32x32b_x32(trow + col, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+          tmem_st_32x32b_x32(trow + col, v);
+        }
         tmem_st_wait();
       }
       // P buffer j % 2 is free once P V_{j-2} is complete
@@ -284,23 +313,28 @@ __global__ void __launch_bounds__(THREADS, 2)
     if (all_ok) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* og = p.out + ((long long)b * p.S + qi) * p.q_row + h * H + half * 32;
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(trow + O_COL + half * 32, v);
-      tmem_ld_wait();
-      if (qi < p.S) {
-        uint4* o4 = reinterpret_cast<uint4*>(og);
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
-          uint4 w;
-          w.x = pack_bf16x2(__uint_as_float(v[q8 * 8 + 0]) * inv, __uint_as_float(v[q8 * 8 + 1]) * inv);
-          w.y = pack_bf16x2(__uint_as_float(v[q8 * 8 + 2]) * inv, __uint_as_float(v[q8 * 8 + 3]) * inv);
-          w.z = pack_bf16x2(__uint_as_float(v[q8 * 8 + 4]) * inv, __uint_as_float(v[q8 * 8 + 5]) * inv);
-          w.w = pack_bf16x2(__uint_as_float(v[q8 * 8 + 6]) * inv, __uint_as_float(v[q8 * 8 + 7]) * inv);
-          o4[q8] = w;
+      for (int c = 0; c < HC; ++c) {
+        const int col = half * (H / 2) + 32 * c;
+        __nv_bfloat16* og = p.out + ((long long)b * p.S + qi) * p.q_row + h * H + col;
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(trow + O_COL + col, v);
+        tmem_ld_wait();
+        if (qi < p.S) {
+          uint4* o4 = reinterpret_cast<uint4*>(og);
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(v[q8 * 8 + 0]) * inv, __uint_as_float(v[q8 * 8 + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(v[q8 * 8 + 2]) * inv, __uint_as_float(v[q8 * 8 + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(v[q8 * 8 + 4]) * inv, __uint_as_float(v[q8 * 8 + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(v[q8 * 8 + 6]) * inv, __uint_as_float(v[q8 * 8 + 7]) * inv);
+            o4[q8] = w;
+          }
         }
-        if (half == 0) p.lse[((long long)b * p.Nq + h) * p.S + qi] = l > 0.f ? m_used + log2f(l) : INFINITY;
       }
+      if (qi < p.S && half == 0)
+        p.lse[((long long)b * p.Nq + h) * p.S + qi] = l > 0.f ? m_used + log2f(l) : INFINITY;
     }
   }
 
@@ -323,12 +357,15 @@ __global__ void __launch_bounds__(THREADS, 2)
 constexpr int KBT = 128;    // keys per CTA
 constexpr int QBT = 64;     // queries per tile
 constexpr int BWD_THREADS = 320;
-constexpr int QT_BYTES = QBT * H * 2;     // 8 KB
-constexpr int KT_BYTES = KBT * H * 2;     // 16 KB
 constexpr int PT_BYTES = KBT * QBT * 2;   // 16 KB
-constexpr int BWD_SMEM = 2 * KT_BYTES + 2 * 2 * QT_BYTES + 2 * PT_BYTES + 2 * 2 * QBT * 4 + 1024 + 256;
-constexpr int BWD_TMEM = 256;
-constexpr int ST_COL = 0, DPT_COL = 64, DV_COL = 128, DK_COL = 192;
+constexpr int ST_COL = 0, DPT_COL = 64, DV_COL = 128;   // dK at DV_COL + H
+template <int H>
+struct BwdKV {
+  static constexpr int QT_BYTES = QBT * H * 2;   // 8 / 16 KB
+  static constexpr int KT_BYTES = KBT * H * 2;   // 16 / 32 KB
+  static constexpr int SMEM = 2 * KT_BYTES + 2 * 2 * QT_BYTES + 2 * PT_BYTES + 2 * 2 * QBT * 4 + 1024 + 256;
+  static constexpr int TMEM = H == 64 ? 256 : 512;
+};
 
 struct BwdParams {
   int B, S, Nq, Nkv, window;
@@ -344,10 +381,14 @@ HB_DEVICE bool visible_b(const BwdParams& p, int qi, int kj) {
   return kj <= qi && (p.window <= 0 || qi - kj < p.window) && kj < p.S && qi < p.S;
 }
 
-__global__ void __launch_bounds__(BWD_THREADS, 2)
+template <int H>
+__global__ void __launch_bounds__(BWD_THREADS, H == 64 ? 2 : 1)
     bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                      const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmD,
                      const BwdParams p) {
+  constexpr int QT_BYTES = BwdKV<H>::QT_BYTES, KT_BYTES = BwdKV<H>::KT_BYTES, BWD_TMEM = BwdKV<H>::TMEM;
+  constexpr int DK_COL = DV_COL + H;
+  constexpr int HC = H / 64;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sK = smem_u32(smem);
@@ -402,8 +443,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 2)
     // ------------------------------------------------------------ producer (whole warp)
     if (lane == 0) {
       mbar_expect_tx(smem_u32(kv_full), 2 * KT_BYTES);
-      tma_load_2d(sK, &tmK, smem_u32(kv_full), hk * H, row0 + k0);
-      tma_load_2d(sV, &tmV, smem_u32(kv_full), hk * H, row0 + k0);
+      load_tile<H>(sK, &tmK, smem_u32(kv_full), hk * H, row0 + k0, KBT);
+      load_tile<H>(sV, &tmV, smem_u32(kv_full), hk * H, row0 + k0, KBT);
     }
     for (int it = 0; it < total; ++it) {
       const int st = it & 1;
@@ -421,8 +462,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 2)
       const uint32_t fb = smem_u32(&qd_full[st]);
       if (lane == 0) {
         mbar_expect_tx(fb, 2 * QT_BYTES);
-        tma_load_2d(sQ0 + st * QT_BYTES, &tmQ, fb, hq * H, row0 + q0);
-        tma_load_2d(sD0 + st * QT_BYTES, &tmD, fb, hq * H, row0 + q0);
+        load_tile<H>(sQ0 + st * QT_BYTES, &tmQ, fb, hq * H, row0 + q0, QBT);
+        load_tile<H>(sD0 + st * QT_BYTES, &tmD, fb, hq * H, row0 + q0, QBT);
       } else {
         mbar_arrive(fb);
       }
@@ -440,10 +481,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 2)
         const uint32_t sq = sQ0 + st * QT_BYTES, sd = sD0 + st * QT_BYTES;
 #pragma unroll
         for (int kk = 0; kk < H / 16; ++kk) {
-          umma_f16(tmem + ST_COL, make_smem_desc(sK + kk * 32, 16, 1024), make_smem_desc(sq + kk * 32, 16, 1024),
-                   idesc_s, kk != 0 ? 1u : 0u);
-          umma_f16(tmem + DPT_COL, make_smem_desc(sV + kk * 32, 16, 1024), make_smem_desc(sd + kk * 32, 16, 1024),
-                   idesc_s, kk != 0 ? 1u : 0u);
+          umma_f16(tmem + ST_COL, kdesc(sK, KBT, kk), kdesc(sq, QBT, kk), idesc_s, kk != 0 ? 1u : 0u);
+          umma_f16(tmem + DPT_COL, kdesc(sV, KBT, kk), kdesc(sd, QBT, kk), idesc_s, kk != 0 ? 1u : 0u);
         }
         umma_commit(smem_u32(s_full));
         return true;
@@ -521,12 +560,15 @@ __global__ void __launch_bounds__(BWD_THREADS, 2)
     if (ok && total > 0) ok = mbar_wait(smem_u32(pv_done), (total - 1) & 1, p.status, kErrTimeoutEpilogue, p.budget_ns);
     if (__all_sync(0xffffffffu, ok)) {
       tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < HC; ++c) {
+      const int col = half * (H / 2) + 32 * c;
       uint32_t vv[32], kv[32];
-      tmem_ld_32x32b_x32(trow + DV_COL + half * 32, vv);
-      tmem_ld_32x32b_x32(trow + DK_COL + half * 32, kv);
+      tmem_ld_32x32b_x32(trow + DV_COL + col, vv);
+      tmem_ld_32x32b_x32(trow + DK_COL + col, kv);
       tmem_ld_wait();
       if (kj < p.S) {
-        const long long o = ((long long)b * p.S + kj) * p.kv_row + hk * H + half * 32;
+        const long long o = ((long long)b * p.S + kj) * p.kv_row + hk * H + col;
         uint4* dv4 = reinterpret_cast<uint4*>(p.dv + o);
         uint4* dk4 = reinterpret_cast<uint4*>(p.dk + o);
         const bool any = total > 0;
@@ -547,6 +589,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 2)
           dk4[q8] = u;
         }
       }
+      }
     }
   }
 
@@ -564,10 +607,14 @@ __global__ void __launch_bounds__(BWD_THREADS, 2)
 // then dQ * scale -> bf16.
 constexpr int DQ_THREADS = 320;
 constexpr int DQ_KB = 64;
-constexpr int DQ_KT = DQ_KB * H * 2;          // 8 KB
-constexpr int DQ_SMEM = 2 * Q_BYTES + 2 * 2 * DQ_KT + BQ * DQ_KB * 2 + 1024 + 256;
 constexpr int DQ_TMEM = 256;
 constexpr int DQ_S = 0, DQ_DP = 64, DQ_ACC = 128;
+template <int H>
+struct BwdQ {
+  static constexpr int Q_BYTES = BQ * H * 2;
+  static constexpr int KT = DQ_KB * H * 2;      // 8 / 16 KB
+  static constexpr int SMEM = 2 * Q_BYTES + 2 * 2 * KT + BQ * DQ_KB * 2 + 1024 + 256;
+};
 
 struct DqParams {
   int B, S, Nq, Nkv, window;
@@ -583,10 +630,13 @@ HB_DEVICE bool visible_q(const DqParams& p, int qi, int kj) {
   return kj <= qi && (p.window <= 0 || qi - kj < p.window) && kj < p.S && qi < p.S;
 }
 
-__global__ void __launch_bounds__(DQ_THREADS, 2)
+template <int H>
+__global__ void __launch_bounds__(DQ_THREADS, H == 64 ? 2 : 1)
     bwd_q_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmD,
                     const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                     const DqParams p) {
+  constexpr int Q_BYTES = BwdQ<H>::Q_BYTES, DQ_KT = BwdQ<H>::KT;
+  constexpr int HC = H / 64;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sQ = smem_u32(smem);
@@ -638,8 +688,8 @@ __global__ void __launch_bounds__(DQ_THREADS, 2)
   if (warp == 0) {
     if (elect_one()) {
       mbar_expect_tx(smem_u32(q_full), 2 * Q_BYTES);
-      tma_load_2d(sQ, &tmQ, smem_u32(q_full), h * H, row0 + q0);
-      tma_load_2d(sD, &tmD, smem_u32(q_full), h * H, row0 + q0);
+      load_tile<H>(sQ, &tmQ, smem_u32(q_full), h * H, row0 + q0, BQ);
+      load_tile<H>(sD, &tmD, smem_u32(q_full), h * H, row0 + q0, BQ);
       for (int j = 0; j < nkt; ++j) {
         const int st = j & 1;
         if (!mbar_wait(smem_u32(&kv_empty[st]), ((j >> 1) & 1) ^ 1, p.status, kErrTimeoutProducer, p.budget_ns))
@@ -647,8 +697,8 @@ __global__ void __launch_bounds__(DQ_THREADS, 2)
         const uint32_t fb = smem_u32(&kv_full[st]);
         mbar_expect_tx(fb, 2 * DQ_KT);
         const int k0 = (jb0 + j) * DQ_KB;
-        tma_load_2d(sK0 + st * DQ_KT, &tmK, fb, hk * H, row0 + k0);
-        tma_load_2d(sV0 + st * DQ_KT, &tmV, fb, hk * H, row0 + k0);
+        load_tile<H>(sK0 + st * DQ_KT, &tmK, fb, hk * H, row0 + k0, DQ_KB);
+        load_tile<H>(sV0 + st * DQ_KT, &tmV, fb, hk * H, row0 + k0, DQ_KB);
       }
     }
   } else if (warp == 1) {
@@ -663,10 +713,8 @@ __global__ void __launch_bounds__(DQ_THREADS, 2)
         const uint32_t sk = sK0 + st * DQ_KT, sv = sV0 + st * DQ_KT;
 #pragma unroll
         for (int kk = 0; kk < H / 16; ++kk) {
-          umma_f16(tmem + DQ_S, make_smem_desc(sQ + kk * 32, 16, 1024), make_smem_desc(sk + kk * 32, 16, 1024),
-                   idesc_s, kk != 0 ? 1u : 0u);
-          umma_f16(tmem + DQ_DP, make_smem_desc(sD + kk * 32, 16, 1024), make_smem_desc(sv + kk * 32, 16, 1024),
-                   idesc_s, kk != 0 ? 1u : 0u);
+          umma_f16(tmem + DQ_S, kdesc(sQ, BQ, kk), kdesc(sk, DQ_KB, kk), idesc_s, kk != 0 ? 1u : 0u);
+          umma_f16(tmem + DQ_DP, kdesc(sD, BQ, kk), kdesc(sv, DQ_KB, kk), idesc_s, kk != 0 ? 1u : 0u);
         }
         umma_commit(smem_u32(s_full));
         return true;
@@ -734,11 +782,14 @@ __global__ void __launch_bounds__(DQ_THREADS, 2)
     if (ok && nkt > 0) ok = mbar_wait(smem_u32(pv_done), (nkt - 1) & 1, p.status, kErrTimeoutEpilogue, p.budget_ns);
     if (__all_sync(0xffffffffu, ok) && nkt > 0) {
       tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < HC; ++c) {
+      const int col = half * (H / 2) + 32 * c;
       uint32_t v[32];
-      tmem_ld_32x32b_x32(trow + DQ_ACC + half * 32, v);
+      tmem_ld_32x32b_x32(trow + DQ_ACC + col, v);
       tmem_ld_wait();
       if (qin) {
-        uint4* o4 = reinterpret_cast<uint4*>(p.dq + ((long long)b * p.S + qi) * p.q_row + h * H + half * 32);
+        uint4* o4 = reinterpret_cast<uint4*>(p.dq + ((long long)b * p.S + qi) * p.q_row + h * H + col);
 #pragma unroll
         for (int q8 = 0; q8 < 4; ++q8) {
           const float* f = reinterpret_cast<const float*>(v) + q8 * 8;
@@ -750,6 +801,7 @@ __global__ void __launch_bounds__(DQ_THREADS, 2)
           o4[q8] = w;
         }
       }
+      }
     }
   }
 
@@ -760,112 +812,135 @@ __global__ void __launch_bounds__(DQ_THREADS, 2)
 
 }  // namespace fatc
 
-// q [B,S,Nq,64], k/v [B,S,Nkv,64] bf16 contiguous; out like q; lse [B,Nq,S] fp32.
-void flash_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
-                  int64_t window) {
+namespace {
+template <int H>
+void fwd_tc_launch(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
+                   int64_t window) {
   const int B = q.size(0), S = q.size(1), Nq = q.size(2), Nkv = k.size(2);
-  HB_CHECK(q.size(3) == fatc::H, "flash_fwd_tc: head dim 64");
-  const c10::cuda::CUDAGuard guard(q.device());
   fatc::TcParams p{};
   p.B = B;
   p.S = S;
   p.Nq = Nq;
   p.Nkv = Nkv;
   p.window = (int)window;
-  p.sl2 = (1.f / std::sqrt((float)fatc::H)) * fatc::LOG2E;
-  p.q_row = (long long)Nq * fatc::H;
+  p.sl2 = (1.f / std::sqrt((float)H)) * fatc::LOG2E;
+  p.q_row = (long long)Nq * H;
   p.out = (__nv_bfloat16*)out.data_ptr();
   p.lse = lse.data_ptr<float>();
   p.status = status_ptr();
   p.budget_ns = wait_budget_ns();
   const uint64_t rows = (uint64_t)B * S;
-  CUtensorMap tq = tmap_bf16_2d(q.data_ptr(), rows, (uint64_t)Nq * fatc::H, (uint64_t)Nq * fatc::H, 64, fatc::BQ);
-  CUtensorMap tk = tmap_bf16_2d(k.data_ptr(), rows, (uint64_t)Nkv * fatc::H, (uint64_t)Nkv * fatc::H, 64, fatc::BK);
-  CUtensorMap tv = tmap_bf16_2d(v.data_ptr(), rows, (uint64_t)Nkv * fatc::H, (uint64_t)Nkv * fatc::H, 64, fatc::BK);
+  CUtensorMap tq = tmap_bf16_2d(q.data_ptr(), rows, (uint64_t)Nq * H, (uint64_t)Nq * H, 64, fatc::BQ);
+  CUtensorMap tk = tmap_bf16_2d(k.data_ptr(), rows, (uint64_t)Nkv * H, (uint64_t)Nkv * H, 64, fatc::BK);
+  CUtensorMap tv = tmap_bf16_2d(v.data_ptr(), rows, (uint64_t)Nkv * H, (uint64_t)Nkv * H, 64, fatc::BK);
   static bool configured = false;
   if (!configured) {
-    HB_CUDA_CHECK(cudaFuncSetAttribute(fatc::fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fatc::SMEM));
+    HB_CUDA_CHECK(cudaFuncSetAttribute(fatc::fwd_tc_kernel<H>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       fatc::Fwd<H>::SMEM));
     configured = true;
   }
   dim3 grid((S + fatc::BQ - 1) / fatc::BQ, Nq, B);
-  fatc::fwd_tc_kernel<<<grid, fatc::THREADS, fatc::SMEM, cur_stream()>>>(tq, tk, tv, p);
+  fatc::fwd_tc_kernel<H><<<grid, fatc::THREADS, fatc::Fwd<H>::SMEM, cur_stream()>>>(tq, tk, tv, p);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
-
-// dK, dV of the attention backward on tcgen05 (head dim 64); lse / delta as
-// produced by the forward and the delta kernel.
-void flash_bwd_kv_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor dout, torch::Tensor lse,
-                     torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, int64_t window) {
+template <int H>
+void bwd_kv_tc_launch(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor dout, torch::Tensor lse,
+                      torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, int64_t window) {
   const int B = q.size(0), S = q.size(1), Nq = q.size(2), Nkv = k.size(2);
-  HB_CHECK(q.size(3) == fatc::H, "flash_bwd_kv_tc: head dim 64");
-  const c10::cuda::CUDAGuard guard(q.device());
   fatc::BwdParams p{};
   p.B = B;
   p.S = S;
   p.Nq = Nq;
   p.Nkv = Nkv;
   p.window = (int)window;
-  p.scale = 1.f / std::sqrt((float)fatc::H);
+  p.scale = 1.f / std::sqrt((float)H);
   p.sl2 = p.scale * fatc::LOG2E;
   p.lse = lse.data_ptr<float>();
   p.delta = delta.data_ptr<float>();
   p.dk = (__nv_bfloat16*)dk.data_ptr();
   p.dv = (__nv_bfloat16*)dv.data_ptr();
-  p.kv_row = (long long)Nkv * fatc::H;
+  p.kv_row = (long long)Nkv * H;
   p.status = status_ptr();
   p.budget_ns = wait_budget_ns();
   const uint64_t rows = (uint64_t)B * S;
-  CUtensorMap tk = tmap_bf16_2d(k.data_ptr(), rows, (uint64_t)Nkv * fatc::H, (uint64_t)Nkv * fatc::H, 64, fatc::KBT);
-  CUtensorMap tv = tmap_bf16_2d(v.data_ptr(), rows, (uint64_t)Nkv * fatc::H, (uint64_t)Nkv * fatc::H, 64, fatc::KBT);
-  CUtensorMap tq = tmap_bf16_2d(q.data_ptr(), rows, (uint64_t)Nq * fatc::H, (uint64_t)Nq * fatc::H, 64, fatc::QBT);
-  CUtensorMap td = tmap_bf16_2d(dout.data_ptr(), rows, (uint64_t)Nq * fatc::H, (uint64_t)Nq * fatc::H, 64, fatc::QBT);
+  CUtensorMap tk = tmap_bf16_2d(k.data_ptr(), rows, (uint64_t)Nkv * H, (uint64_t)Nkv * H, 64, fatc::KBT);
+  CUtensorMap tv = tmap_bf16_2d(v.data_ptr(), rows, (uint64_t)Nkv * H, (uint64_t)Nkv * H, 64, fatc::KBT);
+  CUtensorMap tq = tmap_bf16_2d(q.data_ptr(), rows, (uint64_t)Nq * H, (uint64_t)Nq * H, 64, fatc::QBT);
+  CUtensorMap td = tmap_bf16_2d(dout.data_ptr(), rows, (uint64_t)Nq * H, (uint64_t)Nq * H, 64, fatc::QBT);
   static bool configured = false;
   if (!configured) {
-    HB_CUDA_CHECK(cudaFuncSetAttribute(fatc::bwd_kv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       fatc::BWD_SMEM));
+    HB_CUDA_CHECK(cudaFuncSetAttribute(fatc::bwd_kv_tc_kernel<H>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       fatc::BwdKV<H>::SMEM));
     configured = true;
   }
   dim3 grid((S + fatc::KBT - 1) / fatc::KBT, Nkv, B);
-  fatc::bwd_kv_tc_kernel<<<grid, fatc::BWD_THREADS, fatc::BWD_SMEM, cur_stream()>>>(tk, tv, tq, td, p);
+  fatc::bwd_kv_tc_kernel<H><<<grid, fatc::BWD_THREADS, fatc::BwdKV<H>::SMEM, cur_stream()>>>(tk, tv, tq, td, p);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
-
-// dQ of the attention backward on tcgen05 (head dim 64).
-void flash_bwd_q_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor dout, torch::Tensor lse,
-                    torch::Tensor delta, torch::Tensor dq, int64_t window) {
+template <int H>
+void bwd_q_tc_launch(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor dout, torch::Tensor lse,
+                     torch::Tensor delta, torch::Tensor dq, int64_t window) {
   const int B = q.size(0), S = q.size(1), Nq = q.size(2), Nkv = k.size(2);
-  HB_CHECK(q.size(3) == fatc::H, "flash_bwd_q_tc: head dim 64");
-  const c10::cuda::CUDAGuard guard(q.device());
   fatc::DqParams p{};
   p.B = B;
   p.S = S;
   p.Nq = Nq;
   p.Nkv = Nkv;
   p.window = (int)window;
-  p.scale = 1.f / std::sqrt((float)fatc::H);
+  p.scale = 1.f / std::sqrt((float)H);
   p.sl2 = p.scale * fatc::LOG2E;
   p.lse = lse.data_ptr<float>();
   p.delta = delta.data_ptr<float>();
   p.dq = (__nv_bfloat16*)dq.data_ptr();
-  p.q_row = (long long)Nq * fatc::H;
+  p.q_row = (long long)Nq * H;
   p.status = status_ptr();
   p.budget_ns = wait_budget_ns();
   const uint64_t rows = (uint64_t)B * S;
-  CUtensorMap tq = tmap_bf16_2d(q.data_ptr(), rows, (uint64_t)Nq * fatc::H, (uint64_t)Nq * fatc::H, 64, fatc::BQ);
-  CUtensorMap td = tmap_bf16_2d(dout.data_ptr(), rows, (uint64_t)Nq * fatc::H, (uint64_t)Nq * fatc::H, 64, fatc::BQ);
-  CUtensorMap tk = tmap_bf16_2d(k.data_ptr(), rows, (uint64_t)Nkv * fatc::H, (uint64_t)Nkv * fatc::H, 64, fatc::DQ_KB);
-  CUtensorMap tv = tmap_bf16_2d(v.data_ptr(), rows, (uint64_t)Nkv * fatc::H, (uint64_t)Nkv * fatc::H, 64, fatc::DQ_KB);
+  CUtensorMap tq = tmap_bf16_2d(q.data_ptr(), rows, (uint64_t)Nq * H, (uint64_t)Nq * H, 64, fatc::BQ);
+  CUtensorMap td = tmap_bf16_2d(dout.data_ptr(), rows, (uint64_t)Nq * H, (uint64_t)Nq * H, 64, fatc::BQ);
+  CUtensorMap tk = tmap_bf16_2d(k.data_ptr(), rows, (uint64_t)Nkv * H, (uint64_t)Nkv * H, 64, fatc::DQ_KB);
+  CUtensorMap tv = tmap_bf16_2d(v.data_ptr(), rows, (uint64_t)Nkv * H, (uint64_t)Nkv * H, 64, fatc::DQ_KB);
   static bool configured = false;
   if (!configured) {
-    HB_CUDA_CHECK(cudaFuncSetAttribute(fatc::bwd_q_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       fatc::DQ_SMEM));
+    HB_CUDA_CHECK(cudaFuncSetAttribute(fatc::bwd_q_tc_kernel<H>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       fatc::BwdQ<H>::SMEM));
     configured = true;
   }
   dim3 grid((S + fatc::BQ - 1) / fatc::BQ, Nq, B);
-  fatc::bwd_q_tc_kernel<<<grid, fatc::DQ_THREADS, fatc::DQ_SMEM, cur_stream()>>>(tq, td, tk, tv, p);
+  fatc::bwd_q_tc_kernel<H><<<grid, fatc::DQ_THREADS, fatc::BwdQ<H>::SMEM, cur_stream()>>>(tq, td, tk, tv, p);
   HB_CUDA_CHECK(cudaGetLastError());
+}
+}  // namespace
+
+// q [B,S,Nq,H], k/v [B,S,Nkv,H] bf16 contiguous (H = 64 or 128); out like q;
+// lse [B,Nq,S] fp32.
+void flash_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
+                  int64_t window) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  if (q.size(3) == 64) fwd_tc_launch<64>(q, k, v, out, lse, window);
+  else if (q.size(3) == 128) fwd_tc_launch<128>(q, k, v, out, lse, window);
+  else HB_CHECK(false, "flash_fwd_tc: head dim 64 or 128");
+}
+
+// dK, dV of the attention backward on tcgen05; lse / delta as produced by the
+// forward and the delta kernel.
+void flash_bwd_kv_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor dout, torch::Tensor lse,
+                     torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, int64_t window) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  if (q.size(3) == 64) bwd_kv_tc_launch<64>(q, k, v, dout, lse, delta, dk, dv, window);
+  else if (q.size(3) == 128) bwd_kv_tc_launch<128>(q, k, v, dout, lse, delta, dk, dv, window);
+  else HB_CHECK(false, "flash_bwd_kv_tc: head dim 64 or 128");
+}
+
+// dQ of the attention backward on tcgen05.
+void flash_bwd_q_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor dout, torch::Tensor lse,
+                    torch::Tensor delta, torch::Tensor dq, int64_t window) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  if (q.size(3) == 64) bwd_q_tc_launch<64>(q, k, v, dout, lse, delta, dq, window);
+  else if (q.size(3) == 128) bwd_q_tc_launch<128>(q, k, v, dout, lse, delta, dq, window);
+  else HB_CHECK(false, "flash_bwd_q_tc: head dim 64 or 128");
 }
 
 }  // namespace hb

@@ -225,6 +225,28 @@ def case_flash_bwd():
         2.5 * 4 * B * Nq * H * S * (S + 1) / 2, "flop"
 
 
+def case_flash128_fwd():
+    """Head dim 128 (16 query heads, 4 KV heads, 4 x 4096 tokens)."""
+    q, k, v = _attn_inputs(B=4, H=128)
+    B, S, Nq, H = q.shape
+    out = torch.empty_like(q)
+    lse = torch.empty(B, Nq, S, device="cuda")
+    return (lambda: ext().flash_fwd(q, k, v, out, lse, 0)), 4 * B * Nq * H * S * (S + 1) / 2, "flop"
+
+
+def case_flash128_bwd():
+    q, k, v = _attn_inputs(B=4, H=128)
+    B, S, Nq, H = q.shape
+    out = torch.empty_like(q)
+    lse = torch.empty(B, Nq, S, device="cuda")
+    ext().flash_fwd(q, k, v, out, lse, 0)
+    do = torch.randn_like(q)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    delta = torch.empty(B, Nq, S, device="cuda")
+    return (lambda: ext().flash_bwd(q, k, v, out, do, lse, delta, dq, dk, dv, 0)), \
+        2.5 * 4 * B * Nq * H * S * (S + 1) / 2, "flop"
+
+
 def case_router_fwd():
     T, D, N, K = 32768, 1024, 32, 4
     x = torch.randn(T, D, device="cuda").bfloat16()

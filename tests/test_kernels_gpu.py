@@ -140,7 +140,7 @@ def test_head_ce_full_vocab_against_fp32_head_and_memory():
 @pytest.mark.parametrize("H,window,S,Nq,Nkv", [(64, 0, 256, 4, 2), (64, 0, 200, 4, 4),
                                                (32, 0, 128, 2, 1), (32, 64, 128, 2, 1),
                                                (64, 96, 300, 4, 1), (128, 0, 192, 2, 2),
-                                               (128, 64, 130, 4, 2)])
+                                               (128, 64, 130, 4, 2), (128, 0, 777, 4, 1)])
 def test_flash_attention_fwd_bwd(H, window, S, Nq, Nkv):
     from hanuman_b200.ops.flash import flash_attention
     torch.manual_seed(4)
