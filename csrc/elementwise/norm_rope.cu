@@ -154,8 +154,8 @@ __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfl
     const __nv_bfloat162 u2 = *reinterpret_cast<const __nv_bfloat162*>(gu + r * 2 * F + F + c);
     const float g0 = __bfloat162float(g2.x), g1 = __bfloat162float(g2.y);
     // silu in the compute dtype, then the product (moe.py:23-29 rounds silu(g) to bf16)
-    const float s0 = __bfloat162float(__float2bfloat16_rn(g0 / (1.f + __expf(-g0))));
-    const float s1 = __bfloat162float(__float2bfloat16_rn(g1 / (1.f + __expf(-g1))));
+    const float s0 = __bfloat162float(__float2bfloat16_rn(__fdividef(g0, 1.f + __expf(-g0))));
+    const float s1 = __bfloat162float(__float2bfloat16_rn(__fdividef(g1, 1.f + __expf(-g1))));
     __nv_bfloat162 o = __floats2bfloat162_rn(s0 * __bfloat162float(u2.x), s1 * __bfloat162float(u2.y));
     *reinterpret_cast<__nv_bfloat162*>(h + r * F + c) = o;
   }
@@ -178,7 +178,7 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dh, const __
     const float g = __bfloat162float(gu[r * 2 * F + c]);
     const float u = __bfloat162float(gu[r * 2 * F + F + c]);
     const float d = __bfloat162float(dh[r * F + c]);
-    const float sg = 1.f / (1.f + __expf(-g));
+    const float sg = __fdividef(1.f, 1.f + __expf(-g));
     const float silu = g * sg;
     const float dsilu = sg * (1.f + g * (1.f - sg));
     dgu[r * 2 * F + c] = __float2bfloat16_rn(d * u * dsilu);

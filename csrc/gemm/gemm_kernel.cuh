@@ -257,8 +257,8 @@ HB_DEVICE void swiglu_fwd_store(const GemmArgs& args, int m, int n, bool row_ok,
       pu[e] = pack_bf16x2(u0, u1);
       const float gr0 = __uint_as_float(pg[e] << 16), gr1 = __uint_as_float(pg[e] & 0xffff0000u);
       const float ur0 = __uint_as_float(pu[e] << 16), ur1 = __uint_as_float(pu[e] & 0xffff0000u);
-      const float s0 = __bfloat162float(__float2bfloat16_rn(gr0 / (1.f + __expf(-gr0))));
-      const float s1 = __bfloat162float(__float2bfloat16_rn(gr1 / (1.f + __expf(-gr1))));
+      const float s0 = __bfloat162float(__float2bfloat16_rn(__fdividef(gr0, 1.f + __expf(-gr0))));
+      const float s1 = __bfloat162float(__float2bfloat16_rn(__fdividef(gr1, 1.f + __expf(-gr1))));
       ph[e] = pack_bf16x2(s0 * ur0, s1 * ur1);
     }
     h4[q] = wh;
@@ -559,7 +559,9 @@ __global__ void __launch_bounds__(GATHER ? GEMM_THREADS + GATHER_COPY_THREADS : 
             // dh is rounded to bf16 first, as when it is stored between kernels
             const float d = __bfloat162float(__float2bfloat16_rn(has_k ? __uint_as_float(r[j]) * alpha : 0.f));
             const float g = __bfloat162float(gv[j]), u = __bfloat162float(uv[j]);
-            const float sg = 1.f / (1.f + __expf(-g));
+            // approximate divide (2 ulp; 1 / inf = 0 keeps the limit): the
+            // epilogue is instruction-bound and the results are rounded to bf16
+            const float sg = __fdividef(1.f, 1.f + __expf(-g));
             const float silu = g * sg;
             const float dsilu = sg * (1.f + g * (1.f - sg));
             og[j] = d * u * dsilu;

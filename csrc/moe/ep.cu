@@ -29,12 +29,15 @@ int grid_for(long long work, int per_block) {
   return (int)std::max(1LL, std::min(g, (long long)num_sms() * 16));
 }
 
-// slot -> (global expert, rank within the expert's list); -1 when dropped
+// slot -> (global expert, rank within the expert's list); -1 when dropped.
+// An expert id outside [0, n_exp) (it would pick a peer pointer and a row
+// from outside the tables) drops the slot.
 __device__ __forceinline__ int slot_rank(const int* pos, const int* starts, const int* topi, long long s,
-                                         int cap, int& e) {
+                                         int cap, int n_exp, int& e) {
   e = topi[s];
+  if (e < 0 || e >= n_exp) return -1;
   const int i = pos[s] - starts[e];
-  return i < cap ? i : -1;
+  return i >= 0 && i < cap ? i : -1;
 }
 
 // one warp per slot
@@ -48,7 +51,7 @@ __global__ void scatter_kernel(const __nv_bfloat16* __restrict__ x, const float*
   for (long long s = blockIdx.x * (long long)warps + (threadIdx.x >> 5); s < (long long)T * K;
        s += (long long)gridDim.x * warps) {
     int e;
-    const int i = slot_rank(pos, starts, topi, s, cap, e);
+    const int i = slot_rank(pos, starts, topi, s, cap, E * Nl, e);
     const long long t = s / K;
     if (i < 0) {
       if (backward && lane == 0) dw[s] = 0.f;
@@ -112,7 +115,7 @@ __global__ void return_kernel(const __nv_bfloat16* __restrict__ rows, const int*
 __global__ void combine_kernel(const __nv_bfloat16* __restrict__ ret, const float* __restrict__ w,
                                const int* __restrict__ topi, const int* __restrict__ pos,
                                const int* __restrict__ starts, float* __restrict__ out, int T, int K, int D,
-                               int cap) {
+                               int cap, int n_exp) {
   const long long total = (long long)T * (D / 2);
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
        idx += (long long)gridDim.x * blockDim.x) {
@@ -121,7 +124,7 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ ret, const floa
     float a0 = 0.f, a1 = 0.f;
     for (int k = 0; k < K; ++k) {
       int e;
-      const int i = slot_rank(pos, starts, topi, t * K + k, cap, e);
+      const int i = slot_rank(pos, starts, topi, t * K + k, cap, n_exp, e);
       if (i < 0) continue;
       const float wk = w ? __bfloat162float(__float2bfloat16_rn(w[t * K + k])) : 1.f;
       const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(ret + ((long long)e * cap + i) * D + c);
@@ -177,7 +180,7 @@ void ep_combine(torch::Tensor ret, c10::optional<torch::Tensor> w, torch::Tensor
   combine_kernel<<<grid_for((long long)T * D / 2, 256), 256, 0, cur_stream()>>>(
       (const __nv_bfloat16*)ret.data_ptr(), w.has_value() ? w->data_ptr<float>() : nullptr,
       topi.data_ptr<int>(), pos.data_ptr<int>(), starts.data_ptr<int>(), out.data_ptr<float>(), T, K, D,
-      (int)cap);
+      (int)cap, (int)starts.numel());
   HB_CUDA_CHECK(cudaGetLastError());
 }
 

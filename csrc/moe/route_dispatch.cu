@@ -484,16 +484,32 @@ __global__ void router_dw_kernel(const __nv_bfloat16* __restrict__ x, const floa
 }
 
 // ------------------------------------------------------------------ plan
-__global__ void hist_kernel(const int* __restrict__ topi, long long n, int N, int* __restrict__ counts) {
+// A stable counting sort of the T*K slots by expert, in three kernels:
+//   plan_hist    block b histograms its PLAN_CH slots -> bh[b][e], counts[e]
+//   plan_scan    expert starts (128-aligned segments), GEMM tile prefix
+//   plan_assign  block b: its base per expert (start + the earlier blocks'
+//                counts), then per warp the rank among equal experts
+//                (__match_any_sync), per-warp offsets by a scan over warps;
+//                slot i goes to row base + offset + rank (slot order kept)
+// Expert ids outside [0, N) are skipped and recorded as kErrBounds.
+constexpr int PLAN_CH = 1024;
+
+__global__ void plan_hist_kernel(const int* __restrict__ topi, long long n, int N, int* __restrict__ counts,
+                                 int* __restrict__ bh, int* status) {
   __shared__ int h[MAXN];
   for (int i = threadIdx.x; i < N; i += blockDim.x) h[i] = 0;
   __syncthreads();
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x)
-    atomicAdd(&h[topi[i]], 1);
+  const long long lo = (long long)blockIdx.x * PLAN_CH, hi = min(n, lo + PLAN_CH);
+  for (long long i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    const int e = topi[i];
+    if (e >= 0 && e < N) atomicAdd(&h[e], 1);
+    else set_error(status, kErrBounds);
+  }
   __syncthreads();
-  for (int i = threadIdx.x; i < N; i += blockDim.x)
+  for (int i = threadIdx.x; i < N; i += blockDim.x) {
+    bh[(long long)blockIdx.x * N + i] = h[i];
     if (h[i]) atomicAdd(counts + i, h[i]);
+  }
 }
 
 // single block: starts (128-aligned), tile prefix for the grouped GEMM.
@@ -516,36 +532,37 @@ __global__ void plan_scan_kernel(const int* __restrict__ counts, int N, int alig
   }
 }
 
-// grid = N blocks; block e walks the slots in order and assigns stable rows.
-__global__ void assign_kernel(const int* __restrict__ topi, long long n, const int* __restrict__ starts,
-                              int* __restrict__ pos, int* __restrict__ row_src, int K) {
-  const int e = blockIdx.x;
-  __shared__ int warp_tot[32];
-  __shared__ int base;
-  if (threadIdx.x == 0) base = starts[e];
+// PLAN_CH threads (32 warps) per block, one slot each.
+__global__ void __launch_bounds__(PLAN_CH) plan_assign_kernel(const int* __restrict__ topi, long long n, int N,
+                                                                const int* __restrict__ starts,
+                                                                const int* __restrict__ bh, int* __restrict__ pos,
+                                                                int* __restrict__ row_src) {
+  __shared__ int wcnt[PLAN_CH / 32][MAXN];   // per warp and expert: count, then offset
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < (PLAN_CH / 32) * N; i += blockDim.x) wcnt[i / N][i % N] = 0;
   __syncthreads();
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (long long c0 = 0; c0 < n; c0 += blockDim.x) {
-    const long long i = c0 + threadIdx.x;
-    const bool hit = i < n && topi[i] == e;
-    const unsigned bal = __ballot_sync(0xffffffffu, hit);
-    const int within = __popc(bal & ((1u << lane) - 1));
-    if (lane == 0) warp_tot[w] = __popc(bal);
-    __syncthreads();
-    int before = 0;
-    for (int j = 0; j < w; ++j) before += warp_tot[j];
-    if (hit) {
-      const int r = base + before + within;
-      pos[i] = r;
-      row_src[r] = (int)i;  // slot id = t * K + k
+  const long long i = (long long)blockIdx.x * PLAN_CH + threadIdx.x;
+  int e = i < n ? topi[i] : -1;
+  if (e < 0 || e >= N) e = -1;
+  const unsigned peers = __match_any_sync(0xffffffffu, e);
+  const int rank = __popc(peers & ((1u << lane) - 1));
+  if (e >= 0 && rank == 0) wcnt[w][e] = __popc(peers);
+  __syncthreads();
+  // thread e: base of this block, then the exclusive scan over the warps
+  for (int x = threadIdx.x; x < N; x += blockDim.x) {
+    int base = starts[x];
+    for (int b = 0; b < (int)blockIdx.x; ++b) base += bh[(long long)b * N + x];
+    for (int ww = 0; ww < PLAN_CH / 32; ++ww) {
+      const int c = wcnt[ww][x];
+      wcnt[ww][x] = base;
+      base += c;
     }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int tot = 0;
-      for (int j = 0; j < nw; ++j) tot += warp_tot[j];
-      base += tot;
-    }
-    __syncthreads();
+  }
+  __syncthreads();
+  if (e >= 0) {
+    const int r = wcnt[w][e] + rank;
+    pos[i] = r;
+    row_src[r] = (int)i;  // slot id = t * K + k
   }
 }
 
@@ -773,14 +790,19 @@ void moe_plan(torch::Tensor topi, int64_t N, int64_t tiles_n, torch::Tensor coun
   const long long n = topi.numel();
   const int K = topi.size(-1);
   HB_CHECK(N <= MAXN, "moe_plan: too many experts");
+  (void)K;
   counts.zero_();
-  hist_kernel<<<grid_for(n, 256), 256, 0, cur_stream()>>>(topi.data_ptr<int>(), n, (int)N,
-                                                          counts.data_ptr<int>());
+  if (n == 0) return;
+  const int nblk = (int)((n + PLAN_CH - 1) / PLAN_CH);
+  auto bh = torch::empty({(long long)nblk * N}, topi.options());
+  plan_hist_kernel<<<nblk, 256, 0, cur_stream()>>>(topi.data_ptr<int>(), n, (int)N, counts.data_ptr<int>(),
+                                                   bh.data_ptr<int>(), status_ptr());
   plan_scan_kernel<<<1, 32, 0, cur_stream()>>>(counts.data_ptr<int>(), (int)N, 128, (int)tiles_n,
                                                starts.data_ptr<int>(), tile_prefix.data_ptr<int>(),
                                                padded_counts.data_ptr<int>(), total_rows.data_ptr<int>());
-  assign_kernel<<<(int)N, 1024, 0, cur_stream()>>>(topi.data_ptr<int>(), n, starts.data_ptr<int>(),
-                                                   pos.data_ptr<int>(), row_src.data_ptr<int>(), K);
+  plan_assign_kernel<<<nblk, PLAN_CH, 0, cur_stream()>>>(topi.data_ptr<int>(), n, (int)N, starts.data_ptr<int>(),
+                                                         bh.data_ptr<int>(), pos.data_ptr<int>(),
+                                                         row_src.data_ptr<int>());
   HB_CUDA_CHECK(cudaGetLastError());
 }
 

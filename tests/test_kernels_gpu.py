@@ -372,6 +372,40 @@ def test_router_ids_stay_in_range_on_nan_logits(N):
     assert torch.equal(tl[clean].sort(-1)[0], want.sort(-1)[0])
 
 
+@pytest.mark.parametrize("T,K,N", [(32768, 4, 32), (1000, 8, 64), (37, 2, 5)])
+def test_moe_plan_is_a_stable_counting_sort(T, K, N):
+    """Slots grouped by expert in slot order, each expert's segment starting
+    at a multiple of 128; the same rows as a CPU stable sort."""
+    from hanuman_b200.ops._ext import ext
+    g = torch.Generator().manual_seed(T)
+    topi_c = torch.randint(0, N, (T, K), generator=g, dtype=torch.int32)
+    topi = topi_c.to(DEV)
+    counts = torch.zeros(N, dtype=torch.int32, device=DEV)
+    starts = torch.empty(N, dtype=torch.int32, device=DEV)
+    tp = torch.empty(N + 1, dtype=torch.int32, device=DEV)
+    padded = torch.empty(N, dtype=torch.int32, device=DEV)
+    total = torch.empty(1, dtype=torch.int32, device=DEV)
+    rmax = T * K + 128 * N
+    pos = torch.full((T * K,), -1, dtype=torch.int32, device=DEV)
+    row_src = torch.full((rmax,), -1, dtype=torch.int32, device=DEV)
+    ext().moe_plan(topi, N, 1, counts, starts, tp, padded, total, pos, row_src)
+    torch.cuda.synchronize()
+    flat = topi_c.flatten().long()
+    cnt = torch.bincount(flat, minlength=N)
+    assert torch.equal(counts.cpu().long(), cnt)
+    pc = (cnt + 127) // 128 * 128
+    st = torch.cumsum(pc, 0) - pc
+    assert torch.equal(starts.cpu().long(), st)
+    want_pos = torch.empty(T * K, dtype=torch.long)
+    for e in range(N):
+        idx = (flat == e).nonzero().flatten()          # slot order
+        want_pos[idx] = st[e] + torch.arange(idx.numel())
+    assert torch.equal(pos.cpu().long(), want_pos)
+    rs = row_src.cpu().long()
+    assert torch.equal(rs[want_pos], torch.arange(T * K))
+    assert ext().read_status() == 0
+
+
 def test_add_norm_fwd_bwd():
     from hanuman_b200.ops.norm import add_rms_norm_cuda
     torch.manual_seed(12)
