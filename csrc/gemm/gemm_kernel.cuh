@@ -267,6 +267,111 @@ HB_DEVICE void swiglu_fwd_store(const GemmArgs& args, int m, int n, bool row_ok,
   }
 }
 
+// EPI_SWIGLU_BWD: one thread's 32 columns of the forward's g and u (bf16).
+// They do not depend on the accumulator, so the epilogue loads a tile's first
+// chunk before it waits for the MMAs and each next chunk while it computes the
+// current one; everything stays in registers (constant indices only).
+struct SwigluAux {
+  uint4 g[4], u[4];
+};
+
+HB_DEVICE void swiglu_aux_load(const GemmArgs& args, long long m, bool row_ok, int n, SwigluAux& a) {
+  const int F = args.N;
+  if (!row_ok || n >= F) return;
+  const __nv_bfloat16* gp = reinterpret_cast<const __nv_bfloat16*>(args.aux) + m * args.ldc + n;
+  const __nv_bfloat16* up = gp + F;
+  if (n + 32 <= F && (F % 8) == 0) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      a.g[q] = reinterpret_cast<const uint4*>(gp)[q];
+      a.u[q] = reinterpret_cast<const uint4*>(up)[q];
+    }
+  } else {
+    const int cnt = F - n;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t wg[4], wu[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int j = q * 8 + 2 * e;
+        const uint32_t g0 = j < cnt ? __bfloat16_as_ushort(gp[j]) : 0u;
+        const uint32_t g1 = j + 1 < cnt ? __bfloat16_as_ushort(gp[j + 1]) : 0u;
+        const uint32_t u0 = j < cnt ? __bfloat16_as_ushort(up[j]) : 0u;
+        const uint32_t u1 = j + 1 < cnt ? __bfloat16_as_ushort(up[j + 1]) : 0u;
+        wg[e] = g0 | (g1 << 16);
+        wu[e] = u0 | (u1 << 16);
+      }
+      a.g[q] = make_uint4(wg[0], wg[1], wg[2], wg[3]);
+      a.u[q] = make_uint4(wu[0], wu[1], wu[2], wu[3]);
+    }
+  }
+}
+
+// dgu = [dh u silu'(g) | dh silu(g)] for one 32-column chunk (pad rows: zeros)
+HB_DEVICE void swiglu_bwd_chunk(const GemmArgs& args, char* cbase, long long m, bool row_ok, int n,
+                                bool has_k, float alpha, const uint32_t (&r)[32], const SwigluAux& a) {
+  const int F = args.N;
+  if (n >= F) return;
+  __nv_bfloat16* dg = reinterpret_cast<__nv_bfloat16*>(cbase) + m * args.ldc + n;
+  __nv_bfloat16* du = dg + F;
+  const bool vec = n + 32 <= F && (F % 8) == 0;
+  uint4 og[4], ou[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t gw[4] = {a.g[q].x, a.g[q].y, a.g[q].z, a.g[q].w};
+    const uint32_t uw[4] = {a.u[q].x, a.u[q].y, a.u[q].z, a.u[q].w};
+    uint32_t pg[4], pu[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float vg[2], vu[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int j = q * 8 + 2 * e + h;
+        // dh is rounded to bf16 first, as when it is stored between kernels
+        const float d = __bfloat162float(__float2bfloat16_rn(has_k ? __uint_as_float(r[j]) * alpha : 0.f));
+        const float g = __uint_as_float(h ? (gw[e] & 0xffff0000u) : (gw[e] << 16));
+        const float u = __uint_as_float(h ? (uw[e] & 0xffff0000u) : (uw[e] << 16));
+        // approximate divide (2 ulp; 1 / inf = 0 keeps the limit): the results are rounded to bf16
+        const float sg = __fdividef(1.f, 1.f + __expf(-g));
+        const float silu = g * sg;
+        const float dsilu = sg * (1.f + g * (1.f - sg));
+        vg[h] = row_ok ? d * u * dsilu : 0.f;
+        vu[h] = row_ok ? d * silu : 0.f;
+      }
+      pg[e] = pack_bf16x2(vg[0], vg[1]);
+      pu[e] = pack_bf16x2(vu[0], vu[1]);
+    }
+    og[q] = make_uint4(pg[0], pg[1], pg[2], pg[3]);
+    ou[q] = make_uint4(pu[0], pu[1], pu[2], pu[3]);
+  }
+  if (vec) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      reinterpret_cast<uint4*>(dg)[q] = og[q];
+      reinterpret_cast<uint4*>(du)[q] = ou[q];
+    }
+  } else {
+    const int cnt = F - n;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t gw[4] = {og[q].x, og[q].y, og[q].z, og[q].w};
+      const uint32_t uw[4] = {ou[q].x, ou[q].y, ou[q].z, ou[q].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int j = q * 8 + 2 * e;
+        if (j < cnt) {
+          dg[j] = __ushort_as_bfloat16((unsigned short)(gw[e] & 0xffffu));
+          du[j] = __ushort_as_bfloat16((unsigned short)(uw[e] & 0xffffu));
+        }
+        if (j + 1 < cnt) {
+          dg[j + 1] = __ushort_as_bfloat16((unsigned short)(gw[e] >> 16));
+          du[j + 1] = __ushort_as_bfloat16((unsigned short)(uw[e] >> 16));
+        }
+      }
+    }
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN, int MODE, int EPI, bool GATHER = false>
 __global__ void __launch_bounds__(GATHER ? GEMM_THREADS + GATHER_COPY_THREADS : GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -491,6 +596,9 @@ __global__ void __launch_bounds__(GATHER ? GEMM_THREADS + GATHER_COPY_THREADS : 
     for (int t = blockIdx.x;; t += gridDim.x) {
       TileInfo ti;
       if (!get_tile<MODE, BN>(args, t, ti)) break;
+      SwigluAux aux[2];   // EPI_SWIGLU_BWD: chunk buffers (first one loaded before the wait)
+      if constexpr (EPI == EPI_SWIGLU_BWD)
+        swiglu_aux_load(args, ti.m0 + row_in_tile, ti.m0 + row_in_tile < ti.m_limit, ti.n0 + half * 32, aux[0]);
       if (!mbar_wait(smem_u32(&tfull_bar[acc]), acc_phase, args.status, kErrTimeoutEpilogue,
                      args.budget_ns))
         break;
@@ -513,85 +621,25 @@ __global__ void __launch_bounds__(GATHER ? GEMM_THREADS + GATHER_COPY_THREADS : 
           if (n < F) swiglu_fwd_store(args, m, n, row_ok, has_k, alpha, rg, ru);
         }
       }
+      if constexpr (EPI == EPI_SWIGLU_BWD) {
+        // chunk j = columns (half + 2 j) * 32: TMEM read, next chunk's g | u
+        // loads in flight, then this chunk's arithmetic and stores
+#pragma unroll
+        for (int j = 0; j < BN / 64; ++j) {
+          const int c = half + 2 * j;
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c * 32, r);
+          if (j + 1 < BN / 64) swiglu_aux_load(args, m, row_ok, ti.n0 + (c + 2) * 32, aux[(j + 1) & 1]);
+          tmem_ld_wait();
+          swiglu_bwd_chunk(args, cbase, m, row_ok, ti.n0 + c * 32, has_k, alpha, r, aux[j & 1]);
+        }
+      }
 #pragma unroll 1
-      for (int c = half; c < (EPI == EPI_SWIGLU_FWD ? 0 : BN / 32); c += 2) {
+      for (int c = half; c < (EPI == EPI_SWIGLU_FWD || EPI == EPI_SWIGLU_BWD ? 0 : BN / 32); c += 2) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c * 32, r);
         tmem_ld_wait();
         const int n = ti.n0 + c * 32;
-        if (EPI == EPI_SWIGLU_BWD) {
-          if (n >= args.N) continue;
-          const int F = args.N;
-          __nv_bfloat16* dg = reinterpret_cast<__nv_bfloat16*>(cbase) + (long long)m * args.ldc + n;
-          __nv_bfloat16* du = dg + F;
-          const int cnt = min(32, F - n);
-          const bool vec = cnt == 32 && (F % 8) == 0;
-          if (!row_ok) {   // pad row of the expert segment
-            if (vec) {
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                reinterpret_cast<uint4*>(dg)[q] = make_uint4(0u, 0u, 0u, 0u);
-                reinterpret_cast<uint4*>(du)[q] = make_uint4(0u, 0u, 0u, 0u);
-              }
-            } else {
-              for (int j = 0; j < cnt; ++j) dg[j] = du[j] = __float2bfloat16_rn(0.f);
-            }
-            continue;
-          }
-          const __nv_bfloat16* gp = reinterpret_cast<const __nv_bfloat16*>(args.aux) + (long long)m * args.ldc + n;
-          const __nv_bfloat16* up = gp + F;
-          __nv_bfloat16 gv[32], uv[32];
-          if (vec) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              reinterpret_cast<uint4*>(gv)[q] = reinterpret_cast<const uint4*>(gp)[q];
-              reinterpret_cast<uint4*>(uv)[q] = reinterpret_cast<const uint4*>(up)[q];
-            }
-          } else {
-            for (int j = 0; j < 32; ++j) {
-              gv[j] = j < cnt ? gp[j] : __float2bfloat16_rn(0.f);
-              uv[j] = j < cnt ? up[j] : __float2bfloat16_rn(0.f);
-            }
-          }
-          float og[32], ou[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            // dh is rounded to bf16 first, as when it is stored between kernels
-            const float d = __bfloat162float(__float2bfloat16_rn(has_k ? __uint_as_float(r[j]) * alpha : 0.f));
-            const float g = __bfloat162float(gv[j]), u = __bfloat162float(uv[j]);
-            // approximate divide (2 ulp; 1 / inf = 0 keeps the limit): the
-            // epilogue is instruction-bound and the results are rounded to bf16
-            const float sg = __fdividef(1.f, 1.f + __expf(-g));
-            const float silu = g * sg;
-            const float dsilu = sg * (1.f + g * (1.f - sg));
-            og[j] = d * u * dsilu;
-            ou[j] = d * silu;
-          }
-          if (vec) {
-            uint4* g4 = reinterpret_cast<uint4*>(dg);
-            uint4* u4 = reinterpret_cast<uint4*>(du);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 w, x;
-              w.x = pack_bf16x2(og[q * 8 + 0], og[q * 8 + 1]);
-              w.y = pack_bf16x2(og[q * 8 + 2], og[q * 8 + 3]);
-              w.z = pack_bf16x2(og[q * 8 + 4], og[q * 8 + 5]);
-              w.w = pack_bf16x2(og[q * 8 + 6], og[q * 8 + 7]);
-              x.x = pack_bf16x2(ou[q * 8 + 0], ou[q * 8 + 1]);
-              x.y = pack_bf16x2(ou[q * 8 + 2], ou[q * 8 + 3]);
-              x.z = pack_bf16x2(ou[q * 8 + 4], ou[q * 8 + 5]);
-              x.w = pack_bf16x2(ou[q * 8 + 6], ou[q * 8 + 7]);
-              g4[q] = w;
-              u4[q] = x;
-            }
-          } else {
-            for (int j = 0; j < cnt; ++j) {
-              dg[j] = __float2bfloat16_rn(og[j]);
-              du[j] = __float2bfloat16_rn(ou[j]);
-            }
-          }
-          continue;
-        }
         if (!row_ok || n >= args.N) continue;
         float v[32];
 #pragma unroll
