@@ -590,7 +590,8 @@ HB_DEVICE float2 load2(const float* p) { return *reinterpret_cast<const float2*>
 
 template <typename T_>
 __global__ void scatter_add_rows_kernel(const T_* __restrict__ dxp, const int* __restrict__ pos,
-                                        float* __restrict__ dx, int T, int D, int K) {
+                                        float* __restrict__ dx, __nv_bfloat16* __restrict__ out_b, int T,
+                                        int D, int K) {
   const long long total = (long long)T * (D / 2);
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -603,8 +604,13 @@ __global__ void scatter_add_rows_kernel(const T_* __restrict__ dxp, const int* _
       a0 += v.x;
       a1 += v.y;
     }
-    dx[t * D + c] += a0;
-    dx[t * D + c + 1] += a1;
+    if (out_b) {   // final gradient in bf16: dx + the rows, no fp32 write
+      const float2 base = *reinterpret_cast<const float2*>(dx + t * D + c);
+      *reinterpret_cast<__nv_bfloat162*>(out_b + t * D + c) = __floats2bfloat162_rn(base.x + a0, base.y + a1);
+    } else {
+      dx[t * D + c] += a0;
+      dx[t * D + c + 1] += a1;
+    }
   }
 }
 
@@ -633,8 +639,8 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const int* _
 // one warp per token.  Pad rows of dy are zeroed by zero_pad_rows.
 __global__ void combine_bwd_kernel(const float* __restrict__ dout, const __nv_bfloat16* __restrict__ y,
                                    const int* __restrict__ pos, const float* __restrict__ w,
-                                   __nv_bfloat16* __restrict__ dy, float* __restrict__ dw, int T, int D,
-                                   int K) {
+                                   __nv_bfloat16* __restrict__ dy, float* __restrict__ dw,
+                                   __nv_bfloat16* __restrict__ db, int T, int D, int K) {
   const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
   for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
     for (int k = 0; k < K; ++k) {
@@ -642,7 +648,10 @@ __global__ void combine_bwd_kernel(const float* __restrict__ dout, const __nv_bf
       const float wk = __bfloat162float(__float2bfloat16_rn(w[(long long)t * K + k]));
       float dot = 0.f;
       for (int c = lane * 2; c < D; c += 64) {
-        const float g0 = dout[(long long)t * D + c], g1 = dout[(long long)t * D + c + 1];
+        const float2 gg = *reinterpret_cast<const float2*>(dout + (long long)t * D + c);
+        const float g0 = gg.x, g1 = gg.y;
+        if (db && k == 0)   // bf16 copy of dout for the shared expert's GEMMs
+          *reinterpret_cast<__nv_bfloat162*>(db + (long long)t * D + c) = __floats2bfloat162_rn(g0, g1);
         const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(y + r * D + c);
         dot += g0 * __bfloat162float(v.x) + g1 * __bfloat162float(v.y);
         *reinterpret_cast<__nv_bfloat162*>(dy + r * D + c) = __floats2bfloat162_rn(wk * g0, wk * g1);
@@ -816,14 +825,23 @@ void moe_gather(torch::Tensor x, torch::Tensor row_src, torch::Tensor xp, int64_
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
-void moe_scatter_add(torch::Tensor dxp, torch::Tensor pos, torch::Tensor dx) {
+// dx += rows of dxp gathered by pos; with out_b the sum goes to out_b (bf16)
+// and dx is left as it was.
+void moe_scatter_add(torch::Tensor dxp, torch::Tensor pos, torch::Tensor dx, c10::optional<torch::Tensor> out_b) {
   const int T = pos.size(0), K = pos.size(1), D = dx.size(1);
+  HB_CHECK(D % 2 == 0 && dx.is_contiguous(), "moe_scatter_add: contiguous dx, even D");
+  __nv_bfloat16* ob = nullptr;
+  if (out_b.has_value()) {
+    HB_CHECK(out_b->scalar_type() == at::kBFloat16 && out_b->is_contiguous() && out_b->numel() == dx.numel(),
+             "moe_scatter_add: out_b like dx, bf16");
+    ob = (__nv_bfloat16*)out_b->data_ptr();
+  }
   if (dxp.scalar_type() == at::kFloat)
     scatter_add_rows_kernel<float><<<grid_for((long long)T * D / 2, 256), 256, 0, cur_stream()>>>(
-        dxp.data_ptr<float>(), pos.data_ptr<int>(), dx.data_ptr<float>(), T, D, K);
+        dxp.data_ptr<float>(), pos.data_ptr<int>(), dx.data_ptr<float>(), ob, T, D, K);
   else
     scatter_add_rows_kernel<__nv_bfloat16><<<grid_for((long long)T * D / 2, 256), 256, 0, cur_stream()>>>(
-        (const __nv_bfloat16*)dxp.data_ptr(), pos.data_ptr<int>(), dx.data_ptr<float>(), T, D, K);
+        (const __nv_bfloat16*)dxp.data_ptr(), pos.data_ptr<int>(), dx.data_ptr<float>(), ob, T, D, K);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -835,15 +853,21 @@ void moe_combine(torch::Tensor y, torch::Tensor pos, torch::Tensor w, torch::Ten
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
+// db (optional): a bf16 copy of dout, written on the way
 void moe_combine_bwd(torch::Tensor dout, torch::Tensor y, torch::Tensor pos, torch::Tensor w,
-                     torch::Tensor row_src, torch::Tensor dy, torch::Tensor dw) {
+                     torch::Tensor row_src, torch::Tensor dy, torch::Tensor dw, c10::optional<torch::Tensor> db) {
   const int T = pos.size(0), K = pos.size(1), D = dout.size(1);
+  HB_CHECK(dout.is_contiguous() && D % 2 == 0, "moe_combine_bwd: contiguous dout, even D");
+  if (db.has_value())
+    HB_CHECK(db->scalar_type() == at::kBFloat16 && db->is_contiguous() && db->numel() == dout.numel(),
+             "moe_combine_bwd: db like dout, bf16");
   const long long R = dy.size(0);
   zero_pad_rows_kernel<<<grid_for(R * D / 8, 256), 256, 0, cur_stream()>>>(
       row_src.data_ptr<int>(), (__nv_bfloat16*)dy.data_ptr(), R, D);
   combine_bwd_kernel<<<grid_for(T, 8), 256, 0, cur_stream()>>>(
       dout.data_ptr<float>(), (const __nv_bfloat16*)y.data_ptr(), pos.data_ptr<int>(), w.data_ptr<float>(),
-      (__nv_bfloat16*)dy.data_ptr(), dw.data_ptr<float>(), T, D, K);
+      (__nv_bfloat16*)dy.data_ptr(), dw.data_ptr<float>(),
+      db.has_value() ? (__nv_bfloat16*)db->data_ptr() : nullptr, T, D, K);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 

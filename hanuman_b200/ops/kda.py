@@ -159,11 +159,12 @@ class KdaFrontFn(torch.autograd.Function):
         dbeta = torch.zeros(T, H, device=dev) if dbeta is None else dbeta.float().contiguous()
         df = torch.empty(T, HK, dtype=torch.bfloat16, device=dev)
         dbraw = torch.empty(T, H, dtype=torch.float32, device=dev)
-        d_alog = torch.zeros(H, dtype=torch.float32, device=dev)
-        d_dtb = torch.zeros(HK, dtype=torch.float32, device=dev)
+        # the five small parameter gradients share one zero-filled buffer (one fill launch)
+        small = torch.zeros(HK + H + 3 * HK * 4, dtype=torch.float32, device=dev)
+        d_dtb, d_alog = small[:HK], small[HK:HK + H]
+        dcq, dck, dcv = (small[HK + H + i * HK * 4:HK + H + (i + 1) * HK * 4].view(HK, 1, 4)
+                         for i in range(3))
         dbig = torch.empty(T, W, dtype=torch.bfloat16, device=dev)
-        dcq = torch.zeros(HK, 1, 4, dtype=torch.float32, device=dev)
-        dck, dcv = torch.zeros_like(dcq), torch.zeros_like(dcq)
         ext().kda_prep_bwd(big[:, :3 * HK], cq, ck, cv, f, al, dtb, beta, gate_mode, S,
                            dq, dk, dv, dg, dbeta, df, dbraw, d_alog, d_dtb,
                            dbig[:, :3 * HK], dcq, dck, dcv)
@@ -225,8 +226,8 @@ class KdaOutGateFn(torch.autograd.Function):
         dy = dy.to(torch.bfloat16).contiguous()
         do = torch.empty_like(o)
         dgl = torch.empty_like(gl)
-        dw = torch.zeros_like(wf)
-        dgb = torch.zeros_like(gbf)
+        buf = torch.zeros(wf.numel() + gbf.numel(), dtype=torch.float32, device=o.device)
+        dw, dgb = buf[:wf.numel()].view_as(wf), buf[wf.numel():].view_as(gbf)
         ext().kda_out_gate_bwd(dy, o, gl, wf, gbf, rstd, do, dgl, dw, dgb)
         return do, dgl, dw.to(ctx.dtypes[0]), dgb.to(ctx.dtypes[1])
 

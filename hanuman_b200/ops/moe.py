@@ -136,9 +136,10 @@ class MoEFn(torch.autograd.Function):
         logits = torch.empty(T, N, **f32)
         topi = torch.empty(T, K, **i32)
         topw = torch.empty(T, K, **f32)
-        seq_counts = torch.zeros(B, N, **f32)
-        seq_probs = torch.zeros(B, N, **f32)
-        sums = torch.zeros(2, **f32)
+        stats = torch.zeros(2 * B * N + 2, **f32)   # counts | probs | sums, one fill
+        seq_counts = stats[:B * N].view(B, N)
+        seq_probs = stats[B * N:2 * B * N].view(B, N)
+        sums = stats[2 * B * N:]
         ext().router_fwd(xb, Wr, bias, S, K, softmax, float(mod.scaling), logits, topi, topw,
                          seq_counts, seq_probs, sums)
         # dispatch plan
@@ -226,7 +227,12 @@ class MoEFn(torch.autograd.Function):
         B, S, T, D, N, K, F, Fs, R, softmax = ctx.meta
         dev = xb.device
         dout = dout.float().contiguous()
-        db = dout.to(torch.bfloat16)
+        # combine backward first: it reads dout anyway and writes its bf16 copy
+        # (the shared expert's GEMM operand) on the way
+        db = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+        dy = torch.empty(R, D, dtype=torch.bfloat16, device=dev)
+        dtopw = torch.empty(T, K, dtype=torch.float32, device=dev)
+        ext().moe_combine_bwd(dout, y, pos, topw, row_src, dy, dtopw, db)
         # shared expert
         sg, su, sd = _work(mod.shared_w_gate), _work(mod.shared_w_up), _work(mod.shared_w_down)
         dsgu = torch.empty_like(sgu)
@@ -245,10 +251,6 @@ class MoEFn(torch.autograd.Function):
         ext().gemm(shh, db, main_grad(mod.shared_w_down), True, False, True, 1.0)
         ext().gemm(xb, dsgu[:, :Fs], main_grad(mod.shared_w_gate), True, False, True, 1.0)
         ext().gemm(xb, dsgu[:, Fs:], main_grad(mod.shared_w_up), True, False, True, 1.0)
-        # combine backward
-        dy = torch.empty(R, D, dtype=torch.bfloat16, device=dev)
-        dtopw = torch.empty(T, K, dtype=torch.float32, device=dev)
-        ext().moe_combine_bwd(dout, y, pos, topw, row_src, dy, dtopw)
         wg, wu, wd = ctx.expert_w
         dgu = torch.empty_like(gu)
         if FUSED_SWIGLU_BWD:
@@ -273,7 +275,6 @@ class MoEFn(torch.autograd.Function):
             ext().grouped_gemm_m(dgu[:, F:], wu, dxp, starts, counts, tprefix_dx, True, True)
         ext().grouped_gemm_k(xp, dgu[:, :F], main_grad(mod.expert_w_gate), starts, padded, True)
         ext().grouped_gemm_k(xp, dgu[:, F:], main_grad(mod.expert_w_up), starts, padded, True)
-        ext().moe_scatter_add(dxp, pos, dx)
         # router backward (z-loss, balance loss, combine weights)
         dz = torch.zeros((), device=dev) if dz is None else dz
         dbal = torch.zeros((), device=dev) if dbal is None else dbal
@@ -284,7 +285,10 @@ class MoEFn(torch.autograd.Function):
                          dlogits)
         ext().router_grads(xb, mod.router.detach().float().contiguous(), dlogits, dx,
                            main_grad(mod.router))
-        return dx.to(torch.bfloat16), None, None, None
+        # the routed rows last: their sum with dx goes out in bf16 (no separate cast)
+        dxb = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+        ext().moe_scatter_add(dxp, pos, dx, dxb)
+        return dxb, None, None, None
 
 
 def moe_layer_cuda(mod, h, dtype):

@@ -120,9 +120,10 @@ class MoEEPFn(torch.autograd.Function):
         logits = torch.empty(T, N, **f32)
         topi = torch.empty(T, K, dtype=torch.int32, device=dev)
         topw = torch.empty(T, K, **f32)
-        seq_counts = torch.zeros(B, N, **f32)
-        seq_probs = torch.zeros(B, N, **f32)
-        sums = torch.zeros(2, **f32)
+        stats = torch.zeros(2 * B * N + 2, **f32)   # counts | probs | sums, one fill
+        seq_counts = stats[:B * N].view(B, N)
+        seq_probs = stats[B * N:2 * B * N].view(B, N)
+        sums = stats[2 * B * N:]
         ext().router_fwd(xb, mod.router.detach().float().contiguous(),
                          mod.bias.detach().float().contiguous(), S, K, softmax, float(mod.scaling),
                          logits, topi, topw, seq_counts, seq_probs, sums)

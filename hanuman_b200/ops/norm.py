@@ -65,8 +65,8 @@ class AddNormFn(torch.autograd.Function):
         g = None if g is None else g.reshape(-1, D).float().contiguous()
         dx = torch.empty_like(xn)
         da = torch.empty_like(xn)
-        drs = torch.zeros(1, dtype=torch.float32, device=xn.device)
-        dw = torch.zeros(D, dtype=torch.float32, device=xn.device)
+        buf = torch.zeros(D + 4, dtype=torch.float32, device=xn.device)   # dw | drs, one fill
+        dw, drs = buf[:D], buf[D:D + 1]
         ext().add_norm_bwd(g, dh, xn, a2, rsf, wf, rstd, dx, da, drs, dw)
         return dx.view(shape), da.view(shape), drs.reshape(()).to(rs_dtype), dw.to(w_dtype), None
 
