@@ -62,8 +62,7 @@ void moe_gather(torch::Tensor x, torch::Tensor row_src, torch::Tensor xp, int64_
 void moe_scatter_add(torch::Tensor dxp, torch::Tensor pos, torch::Tensor dx, c10::optional<torch::Tensor> out_b);
 void moe_combine(torch::Tensor y, torch::Tensor pos, torch::Tensor w, torch::Tensor out);
 void moe_combine_bwd(torch::Tensor dout, torch::Tensor y, torch::Tensor pos, torch::Tensor w,
-                     torch::Tensor row_src, torch::Tensor dy, torch::Tensor dw,
-                     c10::optional<torch::Tensor> db);
+                     torch::Tensor row_src, torch::Tensor dy, torch::Tensor dw);
 // attention
 void flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                int64_t window);
@@ -204,8 +203,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_scatter_add", &hb::moe_scatter_add, py::arg("dxp"), py::arg("pos"), py::arg("dx"),
         py::arg("out_b") = py::none());
   m.def("moe_combine", &hb::moe_combine);
-  m.def("moe_combine_bwd", &hb::moe_combine_bwd, py::arg("dout"), py::arg("y"), py::arg("pos"), py::arg("w"),
-        py::arg("row_src"), py::arg("dy"), py::arg("dw"), py::arg("db") = py::none());
+  m.def("moe_combine_bwd", &hb::moe_combine_bwd);
   m.def("flash_fwd", &hb::flash_fwd);
   m.def("flash_bwd", &hb::flash_bwd);
   m.def("kda_chunk_size", &hb::kda_chunk_size);

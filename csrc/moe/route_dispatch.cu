@@ -637,36 +637,21 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const int* _
 
 // dy[pos[t,k], :] = bf16(w[t,k]) * dout[t, :];  dw[t,k] = <dout[t], y[pos[t,k]]>
 // one warp per token.  Pad rows of dy are zeroed by zero_pad_rows.
-// One warp per token; the token's dout row is read once into registers
-// (NPL float2 per lane, D <= 64 NPL), its bf16 copy written once, then every
-// expert slot k gets dy[pos] = bf16(w_k) dout and dw_k = dout . y[pos].
-template <int NPL>
 __global__ void combine_bwd_kernel(const float* __restrict__ dout, const __nv_bfloat16* __restrict__ y,
                                    const int* __restrict__ pos, const float* __restrict__ w,
-                                   __nv_bfloat16* __restrict__ dy, float* __restrict__ dw,
-                                   __nv_bfloat16* __restrict__ db, int T, int D, int K) {
+                                   __nv_bfloat16* __restrict__ dy, float* __restrict__ dw, int T, int D,
+                                   int K) {
   const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
   for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
-    float2 g[NPL];
-#pragma unroll
-    for (int i = 0; i < NPL; ++i) {
-      const int c = lane * 2 + 64 * i;
-      g[i] = c < D ? *reinterpret_cast<const float2*>(dout + (long long)t * D + c) : make_float2(0.f, 0.f);
-      if (db && c < D)   // bf16 copy of dout for the shared expert's GEMMs
-        *reinterpret_cast<__nv_bfloat162*>(db + (long long)t * D + c) = __floats2bfloat162_rn(g[i].x, g[i].y);
-    }
     for (int k = 0; k < K; ++k) {
       const long long r = pos[(long long)t * K + k];
       const float wk = __bfloat162float(__float2bfloat16_rn(w[(long long)t * K + k]));
       float dot = 0.f;
-#pragma unroll
-      for (int i = 0; i < NPL; ++i) {
-        const int c = lane * 2 + 64 * i;
-        if (c < D) {
-          const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(y + r * D + c);
-          dot += g[i].x * __bfloat162float(v.x) + g[i].y * __bfloat162float(v.y);
-          *reinterpret_cast<__nv_bfloat162*>(dy + r * D + c) = __floats2bfloat162_rn(wk * g[i].x, wk * g[i].y);
-        }
+      for (int c = lane * 2; c < D; c += 64) {
+        const float g0 = dout[(long long)t * D + c], g1 = dout[(long long)t * D + c + 1];
+        const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(y + r * D + c);
+        dot += g0 * __bfloat162float(v.x) + g1 * __bfloat162float(v.y);
+        *reinterpret_cast<__nv_bfloat162*>(dy + r * D + c) = __floats2bfloat162_rn(wk * g0, wk * g1);
       }
       dot = warp_sum(dot);
       if (lane == 0) dw[(long long)t * K + k] = dot;
@@ -865,23 +850,15 @@ void moe_combine(torch::Tensor y, torch::Tensor pos, torch::Tensor w, torch::Ten
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
-// db (optional): a bf16 copy of dout, written on the way
 void moe_combine_bwd(torch::Tensor dout, torch::Tensor y, torch::Tensor pos, torch::Tensor w,
-                     torch::Tensor row_src, torch::Tensor dy, torch::Tensor dw, c10::optional<torch::Tensor> db) {
+                     torch::Tensor row_src, torch::Tensor dy, torch::Tensor dw) {
   const int T = pos.size(0), K = pos.size(1), D = dout.size(1);
-  HB_CHECK(dout.is_contiguous() && D % 2 == 0, "moe_combine_bwd: contiguous dout, even D");
-  if (db.has_value())
-    HB_CHECK(db->scalar_type() == at::kBFloat16 && db->is_contiguous() && db->numel() == dout.numel(),
-             "moe_combine_bwd: db like dout, bf16");
   const long long R = dy.size(0);
   zero_pad_rows_kernel<<<grid_for(R * D / 8, 256), 256, 0, cur_stream()>>>(
       row_src.data_ptr<int>(), (__nv_bfloat16*)dy.data_ptr(), R, D);
-  HB_CHECK(D <= 64 * 64, "moe_combine_bwd: D <= 4096");
-  auto kern = D <= 64 * 16 ? combine_bwd_kernel<16> : D <= 64 * 32 ? combine_bwd_kernel<32> : combine_bwd_kernel<64>;
-  kern<<<grid_for(T, 8), 256, 0, cur_stream()>>>(
+  combine_bwd_kernel<<<grid_for(T, 8), 256, 0, cur_stream()>>>(
       dout.data_ptr<float>(), (const __nv_bfloat16*)y.data_ptr(), pos.data_ptr<int>(), w.data_ptr<float>(),
-      (__nv_bfloat16*)dy.data_ptr(), dw.data_ptr<float>(),
-      db.has_value() ? (__nv_bfloat16*)db->data_ptr() : nullptr, T, D, K);
+      (__nv_bfloat16*)dy.data_ptr(), dw.data_ptr<float>(), T, D, K);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -227,12 +227,10 @@ class MoEFn(torch.autograd.Function):
         B, S, T, D, N, K, F, Fs, R, softmax = ctx.meta
         dev = xb.device
         dout = dout.float().contiguous()
-        # combine backward first: it reads dout anyway and writes its bf16 copy
-        # (the shared expert's GEMM operand) on the way
-        db = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+        db = dout.to(torch.bfloat16)
         dy = torch.empty(R, D, dtype=torch.bfloat16, device=dev)
         dtopw = torch.empty(T, K, dtype=torch.float32, device=dev)
-        ext().moe_combine_bwd(dout, y, pos, topw, row_src, dy, dtopw, db)
+        ext().moe_combine_bwd(dout, y, pos, topw, row_src, dy, dtopw)
         # shared expert
         sg, su, sd = _work(mod.shared_w_gate), _work(mod.shared_w_up), _work(mod.shared_w_down)
         dsgu = torch.empty_like(sgu)
