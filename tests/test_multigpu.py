@@ -35,6 +35,19 @@ def _losses_match(la, lb):
         assert abs(a - b) < 3e-3 * abs(a), (la, lb)
 
 
+def _state_bound(name):
+    """Largest difference of one state element that two correct runs of 3 steps
+    can show.  AdamW parameters: the first updates are sign-like, so an element
+    can move by up to 2 lr per step between runs (lr = 3e-4).  The MoE router
+    bias (`ffn.bias`) is not an AdamW parameter: each step moves it by
+    +-bias_update_rate or 0 by the sign of the expert's load against the mean
+    (reference train.py:259), so one token routed differently between the runs
+    flips that sign and the runs can differ by 2 * rate per step (rate = 1e-3)."""
+    if name.endswith("ffn.bias"):
+        return 3 * 2 * 1e-3 + 1e-6
+    return 6 * 3e-4 + 1e-5
+
+
 def _worker(rank, world, port, out_path):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
@@ -90,15 +103,14 @@ def test_p2p_transport_matches_nccl(tmp_path):
     _losses_match(lg, lp)
     for k in sp:
         diff = (sg[k] - sp[k]).abs()
-        assert diff.max().item() <= 6 * 3e-4 + 1e-5, (k, diff.max().item())
+        assert diff.max().item() <= _state_bound(k), (k, diff.max().item())
     (l0, s0), (l1, s1) = res[False], res[True]
     _losses_match(l0, l1)
     # The embedding gradient is summed with atomics, so the two runs differ in the
-    # last bits; AdamW's first steps are sign-like (|update| ~ lr per step), so an
-    # element can move by up to 2 * lr per step between runs (lr = 3e-4, 3 steps).
+    # last bits, and the state may drift by _state_bound per element.
     for k in s0:
         diff = (s0[k] - s1[k]).abs()
-        assert diff.max().item() <= 6 * 3e-4 + 1e-5, (k, diff.max().item())
+        assert diff.max().item() <= _state_bound(k), (k, diff.max().item())
         if diff.numel() > 1000:
             assert diff.mean().item() < 1e-4, (k, diff.mean().item())
 
@@ -154,7 +166,7 @@ def test_expert_parallel_matches_data_parallel(tmp_path):
     for k in s0:
         assert s0[k].shape == s1[k].shape, k
         diff = (s0[k] - s1[k]).abs()
-        assert diff.max().item() <= 6 * 3e-4 + 1e-5, (k, diff.max().item())
+        assert diff.max().item() <= _state_bound(k), (k, diff.max().item())
 
 
 def _replay_worker(rank, world, port, out_path):
