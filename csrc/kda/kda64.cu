@@ -336,19 +336,21 @@ __global__ void __launch_bounds__(256, 4) state_fwd64_kernel(Ptrs p) {
   float* gc = Kh + C * L;     // D
   const int vs = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int v0 = vs * VS;
-  auto fetch_wu = [&](int n) {
+  // Wt of chunk n+1 is fetched as soon as U = Ut - Wt S of chunk n is done,
+  // so that copy overlaps the rest of the step; Ut, gC and Kh after the step.
+  auto fetch_w = [&](int n) { cp_tile<C, D>(Wt, L, p.Wt + chunk_off(p, b, h, n, C * D), D); };
+  auto fetch_uk = [&](int n) {
     const long long co = chunk_off(p, b, h, n, C * D);
-    cp_tile<C, D>(Wt, L, p.Wt + co, D);
     cp_tile<C, VS>(U, LV, p.Ut + co + v0, D);
     cp_tile<1, D>(gc, D, p.gC + chunk_off(p, b, h, n, D), D);
+    cp_tile<C, D>(Kh, L, p.Kh + co, D);
   };
-  auto fetch_k = [&](int n) { cp_tile<C, D>(Kh, L, p.Kh + chunk_off(p, b, h, n, C * D), D); };
   for (int i = threadIdx.x; i < D * VS; i += blockDim.x) {
     const int r = i / VS, c = i % VS;
     S[r * LV + c] = p.init_state ? p.init_state[((long long)b * p.H + h) * D * D + r * D + v0 + c] : 0.f;
   }
-  fetch_wu(0);
-  fetch_k(0);
+  fetch_w(0);
+  fetch_uk(0);
   cp_async_commit();
   for (int n = 0; n < p.NC; ++n) {
     cp_async_wait_all();
@@ -360,6 +362,10 @@ __global__ void __launch_bounds__(256, 4) state_fwd64_kernel(Ptrs p) {
     }
     mm<C, VS, D, false, false>(U, LV, Wt, L, S, LV, -1.f, true);   // U = Ut - Wt S
     __syncthreads();
+    if (n + 1 < p.NC) {
+      fetch_w(n + 1);
+      cp_async_commit();
+    }
     for (int i = threadIdx.x; i < C * VS / 4; i += blockDim.x) {
       const int r = i / (VS / 4), c = (i % (VS / 4)) * 4;
       st4(p.Usv + co + r * D + v0 + c, ld4(U + r * LV + c));
@@ -369,8 +375,7 @@ __global__ void __launch_bounds__(256, 4) state_fwd64_kernel(Ptrs p) {
     mm<D, VS, C, true, false>(S, LV, Kh, L, U, LV, 1.f, true);      // S += Kh^T U
     __syncthreads();
     if (n + 1 < p.NC) {
-      fetch_wu(n + 1);
-      fetch_k(n + 1);
+      fetch_uk(n + 1);
       cp_async_commit();
     }
   }
@@ -445,16 +450,19 @@ __global__ void __launch_bounds__(256, 4) state_bwd64_kernel(Ptrs p) {
   float* gc = Wt + C * L;     // D
   const int vs = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int v0 = vs * VS;
-  auto fetch = [&](int n) {
+  // Kh of chunk n-1 is fetched as soon as dU = dUp + Kh dS of chunk n is
+  // done, so that copy overlaps the rest of the step; the others after it.
+  auto fetch_k = [&](int n) { cp_tile<C, D>(Kh, L, p.Kh + chunk_off(p, b, h, n, C * D), D); };
+  auto fetch_rest = [&](int n) {
     const long long co = chunk_off(p, b, h, n, C * D);
     cp_tile<C, VS>(dU, LV, p.dUp + co + v0, D);
     cp_tile<D, VS>(Sq, LV, p.dSq + chunk_off(p, b, h, n, D * D) + v0, D);
-    cp_tile<C, D>(Kh, L, p.Kh + co, D);
     cp_tile<C, D>(Wt, L, p.Wt + co, D);
     cp_tile<1, D>(gc, D, p.gC + chunk_off(p, b, h, n, D), D);
   };
   for (int i = threadIdx.x; i < D * LV; i += blockDim.x) dS[i] = 0.f;
-  fetch(p.NC - 1);
+  fetch_k(p.NC - 1);
+  fetch_rest(p.NC - 1);
   cp_async_commit();
   for (int n = p.NC - 1; n >= 0; --n) {
     cp_async_wait_all();
@@ -466,6 +474,10 @@ __global__ void __launch_bounds__(256, 4) state_bwd64_kernel(Ptrs p) {
     }
     mm<C, VS, D, false, false>(dU, LV, Kh, L, dS, LV, 1.f, true);   // dU = dUp + Kh dS
     __syncthreads();
+    if (n > 0) {
+      fetch_k(n - 1);
+      cp_async_commit();
+    }
     for (int i = threadIdx.x; i < C * VS / 4; i += blockDim.x) {
       const int r = i / (VS / 4), c = (i % (VS / 4)) * 4;
       st4(p.dU + co + r * D + v0 + c, ld4(dU + r * LV + c));
@@ -478,7 +490,7 @@ __global__ void __launch_bounds__(256, 4) state_bwd64_kernel(Ptrs p) {
     mm<D, VS, C, true, false>(dS, LV, Wt, L, dU, LV, -1.f, true);  // dS -= Wt^T dU
     __syncthreads();
     if (n > 0) {
-      fetch(n - 1);
+      fetch_rest(n - 1);
       cp_async_commit();
     }
   }
