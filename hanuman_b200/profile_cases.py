@@ -6,7 +6,8 @@ Each case builds inputs on the current GPU (a few GB at most; operands larger
 than the 126 MB L2 where the kernel is memory-bound), runs the kernel a few
 times and exits.  With ``--time`` it prints the CUDA-event time of one launch
 and the achieved TFLOP/s or GB/s.  Cases: gemm_fwd, gemm_dw, grouped_fwd,
-grouped_swiglu_fwd, grouped_swiglu_bwd, grouped_cat2, gather_gemm_emulated, kda_layer, kda_fwd, kda_bwd, kda128_fwd, kda128_bwd, flash_fwd, flash_bwd, router_fwd, p2p_rs_emulated.
+grouped_swiglu_fwd, grouped_swiglu_bwd, grouped_cat2, gather_gemm_emulated, kda_layer, kda_fwd, kda_bwd, kda128_fwd, kda128_bwd, flash_fwd, flash_bwd, router_fwd, p2p_rs_emulated,
+ep_dispatch_emulated, flash128_fwd, flash128_bwd.
 """
 from __future__ import annotations
 
@@ -271,6 +272,39 @@ def case_p2p_rs_emulated():
     peers = torch.tensor([a.data_ptr(), a.data_ptr() + n * 4], dtype=torch.int64, device="cuda")
     return (lambda: ext().p2p_reduce_scatter(peers, 2, 0, n // 2, out, 0.5, s)), \
         3 * (n // 2) * 4, "byte"
+
+
+def case_ep_dispatch_emulated():
+    """Expert-parallel dispatch of one rank on one GPU: the token scatter to the
+    experts' owners, the return of the expert rows and the weighted combine, with
+    the 8 "ranks'" receive / return buffers as local buffers (the kernels and
+    their memory traffic without NVLink).  BASELINE config 5 per GPU: 64
+    experts top-8 over 8 ranks, D 2048, capacity factor 1.25; 4096 tokens."""
+    T, K, N, E, D = 4096, 8, 64, 8, 2048
+    Nl = N // E
+    cap = int(math.ceil(T * K / N * 1.25))
+    dev = "cuda"
+    x = torch.randn(T, D, device=dev).bfloat16()
+    topi = torch.rand(T, N, device=dev).topk(K, dim=-1).indices.int().contiguous()
+    topw = torch.rand(T, K, device=dev)
+    i32 = dict(dtype=torch.int32, device=dev)
+    counts, starts, tp = torch.empty(N, **i32), torch.empty(N, **i32), torch.empty(N + 1, **i32)
+    padded, total, pos = torch.empty(N, **i32), torch.empty(1, **i32), torch.empty(T, K, **i32)
+    row_src = torch.full((((T * K + N * 127 + 127) // 128) * 128,), -1, **i32)
+    ext().moe_plan(topi, N, 1, counts, starts, tp, padded, total, pos, row_src)
+    recv = [torch.zeros(Nl * E * cap, D, device=dev, dtype=torch.bfloat16) for _ in range(E)]
+    ret = [torch.zeros(N * cap, D, device=dev, dtype=torch.bfloat16) for _ in range(E)]
+    recv_peers = torch.tensor([t.data_ptr() for t in recv], dtype=torch.int64, device=dev)
+    ret_peers = torch.tensor([t.data_ptr() for t in ret], dtype=torch.int64, device=dev)
+    # rank 0's own tokens stand in for every source rank's block
+    cnt = torch.clamp(counts[:Nl], max=cap).repeat_interleave(E).int().contiguous()
+    out = torch.zeros(T, D, device=dev)
+
+    def run():
+        ext().ep_scatter(x, None, None, None, None, topi, pos, starts, recv_peers, 0, E, Nl, cap, False)
+        ext().ep_return(recv[0], cnt, ret_peers, 0, E, Nl, cap)
+        ext().ep_combine(ret[0], topw, topi, pos, starts, out, cap)
+    return run, 3 * T * K * D * 2 + 2 * T * D * 4, "byte"
 
 
 CASES = {k[5:]: v for k, v in globals().items() if k.startswith("case_")}
