@@ -111,28 +111,50 @@ __global__ void return_kernel(const __nv_bfloat16* __restrict__ rows, const int*
   }
 }
 
-// out[t] += sum_k (w? bf16(w_tk) : 1) * ret[e][i]   over kept slots
+// out[t] += sum_k (w? bf16(w_tk) : 1) * ret[e][i]   over kept slots.
+// One warp per token: lanes 0..K-1 resolve the token's K (expert, row) pairs
+// once, the pairs are broadcast into registers, then each lane streams two
+// columns at a time (K <= MK).
+constexpr int EP_MAXK = 16;
+template <int MK>
 __global__ void combine_kernel(const __nv_bfloat16* __restrict__ ret, const float* __restrict__ w,
                                const int* __restrict__ topi, const int* __restrict__ pos,
                                const int* __restrict__ starts, float* __restrict__ out, int T, int K, int D,
                                int cap, int n_exp) {
-  const long long total = (long long)T * (D / 2);
-  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
-       idx += (long long)gridDim.x * blockDim.x) {
-    const long long t = idx / (D / 2);
-    const int c = (idx % (D / 2)) * 2;
-    float a0 = 0.f, a1 = 0.f;
-    for (int k = 0; k < K; ++k) {
+  const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+  for (long long t = blockIdx.x * (long long)warps + (threadIdx.x >> 5); t < T;
+       t += (long long)gridDim.x * warps) {
+    int my_row = -1;
+    float my_w = 0.f;
+    if (lane < K) {
       int e;
-      const int i = slot_rank(pos, starts, topi, t * K + k, cap, n_exp, e);
-      if (i < 0) continue;
-      const float wk = w ? __bfloat162float(__float2bfloat16_rn(w[t * K + k])) : 1.f;
-      const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(ret + ((long long)e * cap + i) * D + c);
-      a0 += wk * __bfloat162float(v.x);
-      a1 += wk * __bfloat162float(v.y);
+      const int i = slot_rank(pos, starts, topi, t * K + lane, cap, n_exp, e);
+      if (i >= 0) {
+        my_row = e * cap + i;
+        my_w = w ? __bfloat162float(__float2bfloat16_rn(w[t * K + lane])) : 1.f;
+      }
     }
-    out[t * D + c] += a0;
-    out[t * D + c + 1] += a1;
+    int rows[MK];
+    float wk[MK];
+#pragma unroll
+    for (int k = 0; k < MK; ++k) {
+      rows[k] = __shfl_sync(0xffffffffu, my_row, k);
+      wk[k] = __shfl_sync(0xffffffffu, my_w, k);
+    }
+    for (int c = lane * 2; c < D; c += 64) {
+      float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+      for (int k = 0; k < MK; ++k) {
+        if (k < K && rows[k] >= 0) {
+          const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(ret + (long long)rows[k] * D + c);
+          a0 += wk[k] * __bfloat162float(v.x);
+          a1 += wk[k] * __bfloat162float(v.y);
+        }
+      }
+      float2* o = reinterpret_cast<float2*>(out + t * D + c);
+      const float2 prev = *o;
+      *o = make_float2(prev.x + a0, prev.y + a1);
+    }
   }
 }
 
@@ -177,7 +199,10 @@ void ep_return(torch::Tensor rows, torch::Tensor cnt, torch::Tensor peers, int64
 void ep_combine(torch::Tensor ret, c10::optional<torch::Tensor> w, torch::Tensor topi, torch::Tensor pos,
                 torch::Tensor starts, torch::Tensor out, int64_t cap) {
   const int T = topi.size(0), K = topi.size(1), D = out.size(1);
-  combine_kernel<<<grid_for((long long)T * D / 2, 256), 256, 0, cur_stream()>>>(
+  HB_CHECK(K <= EP_MAXK && D % 2 == 0 && out.is_contiguous(), "ep_combine: K <= 16, even D, contiguous out");
+  HB_CHECK((long long)starts.numel() * cap < (1LL << 31), "ep_combine: row index range");
+  auto kern = K <= 8 ? combine_kernel<8> : combine_kernel<EP_MAXK>;
+  kern<<<grid_for(T, 8), 256, 0, cur_stream()>>>(
       (const __nv_bfloat16*)ret.data_ptr(), w.has_value() ? w->data_ptr<float>() : nullptr,
       topi.data_ptr<int>(), pos.data_ptr<int>(), starts.data_ptr<int>(), out.data_ptr<float>(), T, K, D,
       (int)cap, (int)starts.numel());

@@ -406,6 +406,35 @@ def test_moe_plan_is_a_stable_counting_sort(T, K, N):
     assert ext().read_status() == 0
 
 
+@pytest.mark.parametrize("K,cap", [(4, 40), (8, 1000), (12, 30)])
+def test_ep_combine_matches_torch(K, cap):
+    """Expert-parallel combine: out[t] += sum over kept slots of bf16(w) *
+    ret[e * cap + rank]; slots ranked at or past the capacity are dropped."""
+    from hanuman_b200.ops._ext import ext
+    torch.manual_seed(K)
+    T, N, D = 300, 16, 256
+    i32 = dict(dtype=torch.int32, device=DEV)
+    topi = torch.rand(T, N, device=DEV).topk(K, dim=-1).indices.int().contiguous()
+    counts, starts, tp = torch.empty(N, **i32), torch.empty(N, **i32), torch.empty(N + 1, **i32)
+    padded, total, pos = torch.empty(N, **i32), torch.empty(1, **i32), torch.empty(T, K, **i32)
+    row_src = torch.full((T * K + 128 * N,), -1, **i32)
+    ext().moe_plan(topi, N, 1, counts, starts, tp, padded, total, pos, row_src)
+    ret = torch.randn(N * cap, D, device=DEV).bfloat16()
+    w = torch.rand(T, K, device=DEV)
+    out = torch.randn(T, D, device=DEV)
+    want = out.clone().double()
+    rank = (pos - starts[topi.long()]).long()
+    kept = rank < cap
+    wb = w.bfloat16().double()
+    for k in range(K):
+        rows = (topi[:, k].long() * cap + rank[:, k].clamp(max=cap - 1))
+        want += torch.where(kept[:, k:k + 1], wb[:, k:k + 1] * ret[rows].double(), 0.0)
+    ext().ep_combine(ret, w, topi, pos, starts, out, cap)
+    torch.cuda.synchronize()
+    assert (out.double() - want).abs().max().item() < 1e-4
+    assert ext().read_status() == 0
+
+
 def test_add_norm_fwd_bwd():
     from hanuman_b200.ops.norm import add_rms_norm_cuda
     torch.manual_seed(12)
