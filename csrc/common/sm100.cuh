@@ -31,6 +31,15 @@ HB_DEVICE void set_error(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }
 
+// Bounds check of a data-dependent index (a label, a row position, a slot id):
+// false, with kErrBounds recorded, when v is outside [0, n); the caller skips
+// the access.
+HB_DEVICE bool index_ok(long long v, long long n, int* status) {
+  if (v >= 0 && v < n) return true;
+  set_error(status, kErrBounds);
+  return false;
+}
+
 HB_DEVICE uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

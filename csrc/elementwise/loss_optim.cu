@@ -52,7 +52,8 @@ __device__ __forceinline__ float block_reduce_max(float v, float* sh) {
 // loss_sum: scalar fp32 accumulated; dlogits: [T, V] bf16 = (p - onehot) * scale * valid.
 __global__ void ce_fwd_bwd_kernel(const float* __restrict__ logits, const long long* __restrict__ tgt,
                                   const float* __restrict__ valid, float* __restrict__ loss_sum,
-                                  __nv_bfloat16* __restrict__ dlogits, int T, int V, float scale) {
+                                  __nv_bfloat16* __restrict__ dlogits, int T, int V, float scale,
+                                  int* status) {
   __shared__ float sh[32];
   for (int row = blockIdx.x; row < T; row += gridDim.x) {
     const float* z = logits + (long long)row * V;
@@ -69,9 +70,13 @@ __global__ void ce_fwd_bwd_kernel(const float* __restrict__ logits, const long l
     }
     s = block_reduce_sum(s, sh);
     const float lse = m + __logf(s);
-    const long long t = tgt[row];
-    const float vw = valid ? valid[row] : 1.f;
-    if (threadIdx.x == 0) atomicAdd(loss_sum, (lse - z[t]) * vw);
+    long long t = tgt[row];
+    float vw = valid ? valid[row] : 1.f;
+    if (!index_ok(t, V, status)) {   // a label outside the vocabulary: row skipped
+      t = -4;
+      vw = 0.f;
+    }
+    if (threadIdx.x == 0 && t >= 0) atomicAdd(loss_sum, (lse - z[t]) * vw);
     const float inv = 1.f / s;
     const float g = scale * vw;
     __nv_bfloat16* d = dlogits + (long long)row * V;
@@ -162,7 +167,7 @@ void ce_fwd_bwd(torch::Tensor logits, torch::Tensor tgt, c10::optional<torch::Te
   const int grid = std::min(T, num_sms() * 4);
   ce_fwd_bwd_kernel<<<grid, 512, 0, cur_stream()>>>(
       logits.data_ptr<float>(), reinterpret_cast<long long*>(tgt.data_ptr<int64_t>()), vp, loss_sum.data_ptr<float>(),
-      (__nv_bfloat16*)dlogits.data_ptr(), T, V, (float)scale);
+      (__nv_bfloat16*)dlogits.data_ptr(), T, V, (float)scale, status_ptr());
   HB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -566,9 +566,12 @@ __global__ void __launch_bounds__(PLAN_CH) plan_assign_kernel(const int* __restr
   }
 }
 
-// xp[r, :] = x[row_src[r] / K, :] or 0 for pad rows (row_src = -1).
+// xp[r, :] = x[row_src[r] / K, :] or 0 for pad rows (row_src = -1).  The
+// index-consuming kernels below check every data-dependent row index
+// (index_ok: out of range -> skipped, kErrBounds in the status word).
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ row_src,
-                                   __nv_bfloat16* __restrict__ xp, long long R, int D, int K) {
+                                   __nv_bfloat16* __restrict__ xp, long long R, int D, int K,
+                                   long long n_tok, int* status) {
   const int vec = D / 8;  // uint4 of 8 bf16
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < R * vec;
        i += (long long)gridDim.x * blockDim.x) {
@@ -576,7 +579,8 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, const in
     const int c = i % vec;
     const int src = row_src[r];
     uint4 v = make_uint4(0, 0, 0, 0);
-    if (src >= 0) v = reinterpret_cast<const uint4*>(x + (long long)(src / K) * D)[c];
+    if (src >= 0 && index_ok(src / K, n_tok, status))
+      v = reinterpret_cast<const uint4*>(x + (long long)(src / K) * D)[c];
     reinterpret_cast<uint4*>(xp + r * D)[c] = v;
   }
 }
@@ -591,7 +595,7 @@ HB_DEVICE float2 load2(const float* p) { return *reinterpret_cast<const float2*>
 template <typename T_>
 __global__ void scatter_add_rows_kernel(const T_* __restrict__ dxp, const int* __restrict__ pos,
                                         float* __restrict__ dx, __nv_bfloat16* __restrict__ out_b, int T,
-                                        int D, int K) {
+                                        int D, int K, long long R, int* status) {
   const long long total = (long long)T * (D / 2);
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -600,6 +604,7 @@ __global__ void scatter_add_rows_kernel(const T_* __restrict__ dxp, const int* _
     float a0 = 0.f, a1 = 0.f;
     for (int k = 0; k < K; ++k) {
       const long long r = pos[t * K + k];
+      if (!index_ok(r, R, status)) continue;
       const float2 v = load2(dxp + r * D + c);
       a0 += v.x;
       a1 += v.y;
@@ -616,7 +621,8 @@ __global__ void scatter_add_rows_kernel(const T_* __restrict__ dxp, const int* _
 
 // out[t, :] += sum_k bf16(w[t,k]) * y[pos[t,k], :]
 __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const int* __restrict__ pos,
-                               const float* __restrict__ w, float* __restrict__ out, int T, int D, int K) {
+                               const float* __restrict__ w, float* __restrict__ out, int T, int D, int K,
+                               long long R, int* status) {
   const long long total = (long long)T * (D / 2);
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -625,6 +631,7 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const int* _
     float a0 = 0.f, a1 = 0.f;
     for (int k = 0; k < K; ++k) {
       const long long r = pos[t * K + k];
+      if (!index_ok(r, R, status)) continue;
       const float wk = __bfloat162float(__float2bfloat16_rn(w[t * K + k]));
       const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(y + r * D + c);
       a0 += wk * __bfloat162float(v.x);
@@ -640,11 +647,15 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const int* _
 __global__ void combine_bwd_kernel(const float* __restrict__ dout, const __nv_bfloat16* __restrict__ y,
                                    const int* __restrict__ pos, const float* __restrict__ w,
                                    __nv_bfloat16* __restrict__ dy, float* __restrict__ dw, int T, int D,
-                                   int K) {
+                                   int K, long long R, int* status) {
   const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
   for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
     for (int k = 0; k < K; ++k) {
       const long long r = pos[(long long)t * K + k];
+      if (!index_ok(r, R, status)) {   // warp-uniform: r is the same for every lane
+        if (lane == 0) dw[(long long)t * K + k] = 0.f;
+        continue;
+      }
       const float wk = __bfloat162float(__float2bfloat16_rn(w[(long long)t * K + k]));
       float dot = 0.f;
       for (int c = lane * 2; c < D; c += 64) {
@@ -818,7 +829,7 @@ void moe_gather(torch::Tensor x, torch::Tensor row_src, torch::Tensor xp, int64_
   HB_CHECK(D % 8 == 0, "moe_gather: D % 8");
   gather_rows_kernel<<<grid_for(R * D / 8, 256), 256, 0, cur_stream()>>>(
       (const __nv_bfloat16*)x.data_ptr(), row_src.data_ptr<int>(), (__nv_bfloat16*)xp.data_ptr(), R,
-      D, (int)K);
+      D, (int)K, (long long)x.size(0), status_ptr());
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -835,10 +846,12 @@ void moe_scatter_add(torch::Tensor dxp, torch::Tensor pos, torch::Tensor dx, c10
   }
   if (dxp.scalar_type() == at::kFloat)
     scatter_add_rows_kernel<float><<<grid_for((long long)T * D / 2, 256), 256, 0, cur_stream()>>>(
-        dxp.data_ptr<float>(), pos.data_ptr<int>(), dx.data_ptr<float>(), ob, T, D, K);
+        dxp.data_ptr<float>(), pos.data_ptr<int>(), dx.data_ptr<float>(), ob, T, D, K, (long long)dxp.size(0),
+        status_ptr());
   else
     scatter_add_rows_kernel<__nv_bfloat16><<<grid_for((long long)T * D / 2, 256), 256, 0, cur_stream()>>>(
-        (const __nv_bfloat16*)dxp.data_ptr(), pos.data_ptr<int>(), dx.data_ptr<float>(), ob, T, D, K);
+        (const __nv_bfloat16*)dxp.data_ptr(), pos.data_ptr<int>(), dx.data_ptr<float>(), ob, T, D, K,
+        (long long)dxp.size(0), status_ptr());
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -846,7 +859,7 @@ void moe_combine(torch::Tensor y, torch::Tensor pos, torch::Tensor w, torch::Ten
   const int T = pos.size(0), K = pos.size(1), D = out.size(1);
   combine_kernel<<<grid_for((long long)T * D / 2, 256), 256, 0, cur_stream()>>>(
       (const __nv_bfloat16*)y.data_ptr(), pos.data_ptr<int>(), w.data_ptr<float>(), out.data_ptr<float>(),
-      T, D, K);
+      T, D, K, (long long)y.size(0), status_ptr());
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -858,7 +871,7 @@ void moe_combine_bwd(torch::Tensor dout, torch::Tensor y, torch::Tensor pos, tor
       row_src.data_ptr<int>(), (__nv_bfloat16*)dy.data_ptr(), R, D);
   combine_bwd_kernel<<<grid_for(T, 8), 256, 0, cur_stream()>>>(
       dout.data_ptr<float>(), (const __nv_bfloat16*)y.data_ptr(), pos.data_ptr<int>(), w.data_ptr<float>(),
-      (__nv_bfloat16*)dy.data_ptr(), dw.data_ptr<float>(), T, D, K);
+      (__nv_bfloat16*)dy.data_ptr(), dw.data_ptr<float>(), T, D, K, R, status_ptr());
   HB_CUDA_CHECK(cudaGetLastError());
 }
 

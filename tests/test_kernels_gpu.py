@@ -435,6 +435,42 @@ def test_ep_combine_matches_torch(K, cap):
     assert ext().read_status() == 0
 
 
+def test_out_of_range_indices_are_skipped_and_reported():
+    """A label outside the vocabulary and a MoE row position outside the row
+    buffer are skipped (no read or write outside the tensors) and recorded as
+    kErrBounds (5) in the device status word; the in-range entries are
+    computed as usual."""
+    from hanuman_b200.ops._ext import ext
+    e = ext()
+    e.clear_status()
+    torch.manual_seed(21)
+    T, V = 6, 64
+    logits = torch.randn(T, V, device=DEV)
+    tgt = torch.tensor([3, V, 10, -1, 63, 0], dtype=torch.int64, device=DEV)
+    loss = torch.zeros(1, device=DEV)
+    dl = torch.full((T, V), 7.0, device=DEV).bfloat16()
+    e.ce_fwd_bwd(logits, tgt, None, loss, dl, 1.0)
+    torch.cuda.synchronize()
+    assert e.read_status() == 5
+    ok = torch.tensor([1, 0, 1, 0, 1, 1], dtype=torch.bool, device=DEV)
+    lse = torch.logsumexp(logits, -1)
+    want = (lse - logits.gather(1, tgt.clamp(0, V - 1)[:, None])[:, 0])[ok].sum()
+    assert abs(loss.item() - want.item()) < 1e-4 * abs(want.item()) + 1e-4
+    assert (dl[~ok].float() == 0).all()
+    e.clear_status()
+    R, D, K = 16, 8, 2
+    dxp = torch.randn(R, D, device=DEV)
+    pos = torch.tensor([[0, 5], [R, 3], [7, 15]], dtype=torch.int32, device=DEV)
+    dx = torch.zeros(3, D, device=DEV)
+    e.moe_scatter_add(dxp, pos, dx)
+    torch.cuda.synchronize()
+    assert e.read_status() == 5
+    want = torch.stack([dxp[0] + dxp[5], dxp[3], dxp[7] + dxp[15]])
+    assert torch.allclose(dx, want, atol=1e-6)
+    e.clear_status()
+    assert e.read_status() == 0
+
+
 def test_add_norm_fwd_bwd():
     from hanuman_b200.ops.norm import add_rms_norm_cuda
     torch.manual_seed(12)
