@@ -255,3 +255,16 @@ def test_expert_parallel_construction_slices_the_full_models_experts():
             assert na == nb
             if "expert_w" not in na:
                 assert torch.equal(pa, pb), na
+
+
+@pytest.mark.parametrize("name", sorted(PRESETS))
+def test_flop_breakdown_sums_to_the_step_flops(name):
+    """The per-component split (breakdown.py of the reference) adds up to the
+    model FLOPs of the step accounting for every preset."""
+    from hanuman_b200.breakdown import analytical_breakdown
+    c = get_config(name)
+    parts = analytical_breakdown(c)
+    model, hw = flops.step_flops(c)
+    assert all(v >= 0 for v in parts.values())
+    assert abs(sum(parts.values()) - model) <= 1e-9 * model
+    assert hw >= model
