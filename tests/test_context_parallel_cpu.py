@@ -1,0 +1,72 @@
+"""KDA context parallelism on CPU ranks (gloo): a sequence split across ranks,
+the recurrent state handed along the chain, must give the single-process
+output and gradients of the whole sequence."""
+import os
+import socket
+
+import torch
+import torch.multiprocessing as mp
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _inputs(B=2, S=96, H=2, K=16, V=16):
+    g = torch.Generator().manual_seed(5)
+    q = torch.randn(B, S, H, K, generator=g, dtype=torch.float64)
+    k = torch.nn.functional.normalize(torch.randn(B, S, H, K, generator=g, dtype=torch.float64), dim=-1)
+    v = torch.randn(B, S, H, V, generator=g, dtype=torch.float64)
+    gate = -torch.rand(B, S, H, K, generator=g, dtype=torch.float64) * 0.5
+    beta = torch.rand(B, S, H, generator=g, dtype=torch.float64)
+    w = torch.randn(B, S, H, V, generator=g, dtype=torch.float64)   # loss weights
+    return q, k, v, gate, beta, w
+
+
+def _worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch.distributed as dist
+    from hanuman_b200.parallel.context import kda_context_parallel
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        q, k, v, gate, beta, w = _inputs()
+        S = q.shape[1]
+        seg = slice(rank * S // world, (rank + 1) * S // world)
+        xs = [t[:, seg].clone().requires_grad_() for t in (q, k, v, gate, beta)]
+        o = kda_context_parallel(*xs, chunk=16)
+        (o * w[:, seg]).sum().backward()
+        torch.save((o.detach(), [x.grad for x in xs]), os.path.join(out_dir, f"r{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(tmp_path, world):
+    ctx = mp.get_context("spawn")
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, str(tmp_path))) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0
+    return [torch.load(tmp_path / f"r{r}.pt") for r in range(world)]
+
+
+def test_kda_context_parallel_matches_one_process(tmp_path):
+    from hanuman_b200.ops import reference as ref
+    q, k, v, gate, beta, w = _inputs()
+    xs = [t.clone().requires_grad_() for t in (q, k, v, gate, beta)]
+    o, _ = ref.kda_chunked(*xs, chunk=16)
+    (o * w).sum().backward()
+    for world in (2, 3):
+        res = _run(tmp_path, world)
+        S = q.shape[1]
+        for r, (o_r, grads_r) in enumerate(res):
+            seg = slice(r * S // world, (r + 1) * S // world)
+            assert torch.allclose(o_r, o[:, seg].detach(), atol=1e-10), (world, r)
+            for name, gr, x in zip("q k v g beta".split(), grads_r, xs):
+                assert torch.allclose(gr, x.grad[:, seg], atol=1e-9), (world, r, name)
