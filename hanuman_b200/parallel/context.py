@@ -1,4 +1,5 @@
-"""Context parallelism for the KDA delta rule: state passing along the sequence.
+"""Context parallelism for the token mixers: KDA state passing along the
+sequence, and attention over all-gathered keys and values.
 
 The reference has no sequence or context parallelism (attention keeps heads
 and sequence whole per device, model/attention.py:217-224); its long-context
@@ -20,6 +21,12 @@ them overlap but needs the K x K transition M of every segment.  This is the
 PyTorch chunked form (ops/reference.py:kda_chunked), so it runs on CPU (gloo)
 and on GPU tensors (NCCL) alike; the sm_100a KDA kernels do not take a
 gradient for the initial state, so they are not used here.
+
+Attention (``attention_context_parallel``): every rank gathers the keys and
+values of all segments (a differentiable all-gather: the backward sums the
+key / value gradients of every rank's queries into the owner) and attends its
+own queries at their global positions, causal and with the sliding window,
+over the keys up to the end of its segment.
 """
 from __future__ import annotations
 
@@ -95,3 +102,46 @@ def kda_context_parallel(q, k, v, g, beta, scale: Optional[float] = None, chunk:
     if rank < world - 1:
         o = o + _SendState.apply(s_out, rank + 1, group).to(o.dtype)
     return o
+
+
+class _GatherSeq(torch.autograd.Function):
+    """All-gather along dim 1 (the sequence); the backward sums every rank's
+    gradient of the gathered tensor and keeps this rank's slice (reduce-scatter
+    on NCCL, all-reduce and slice on backends without it)."""
+
+    @staticmethod
+    def forward(ctx, x, group):
+        world = dist.get_world_size(group)
+        parts = [torch.empty_like(x) for _ in range(world)]
+        dist.all_gather(parts, x.contiguous(), group=group)
+        ctx.group, ctx.rank, ctx.world, ctx.n = group, dist.get_rank(group), world, x.shape[1]
+        return torch.cat(parts, dim=1)
+
+    @staticmethod
+    def backward(ctx, grad):
+        grad = grad.contiguous()
+        if dist.get_backend(ctx.group) == dist.Backend.NCCL:
+            parts = [p.contiguous() for p in grad.split(ctx.n, dim=1)]
+            out = torch.empty_like(parts[ctx.rank])
+            dist.reduce_scatter(out, parts, group=ctx.group)
+            return out, None
+        dist.all_reduce(grad, group=ctx.group)
+        return grad[:, ctx.rank * ctx.n:(ctx.rank + 1) * ctx.n].contiguous(), None
+
+
+def attention_context_parallel(q, k, v, window: int = 0, scale: Optional[float] = None, group=None):
+    """Causal GQA attention over a sequence split across the ranks of ``group``.
+
+    Each rank passes its segment: q ``[B, S_r, Nq, H]``, k / v ``[B, S_r, Nkv,
+    H]`` (rank r holds tokens r*S_r .. (r+1)*S_r - 1, equal S_r on every rank).
+    Returns this rank's output ``[B, S_r, Nq, H]``; query i of rank r sits at
+    global position r*S_r + i and sees the keys at or before it (within the
+    window when ``window > 0``), whichever rank holds them."""
+    rank = dist.get_rank(group)
+    n, H = q.shape[1], k.shape[-1]
+    # keys and values in ONE gather: the backward is then one collective too
+    # (two would run in whatever order autograd reaches them on each rank)
+    kv_all = _GatherSeq.apply(torch.cat([k, v], dim=-1), group)
+    k_all, v_all = kv_all[..., :H], kv_all[..., H:]
+    end = (rank + 1) * n          # causal: no key past this segment's last query
+    return ref.causal_attention(q, k_all[:, :end], v_all[:, :end], window, scale, q_offset=rank * n)

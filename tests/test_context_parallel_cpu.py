@@ -1,6 +1,7 @@
-"""KDA context parallelism on CPU ranks (gloo): a sequence split across ranks,
-the recurrent state handed along the chain, must give the single-process
-output and gradients of the whole sequence."""
+"""Context parallelism on CPU ranks (gloo): a sequence split across ranks
+(KDA: the recurrent state handed along the chain; attention: keys and values
+all-gathered) must give the single-process output and gradients of the whole
+sequence."""
 import os
 import socket
 
@@ -70,3 +71,55 @@ def test_kda_context_parallel_matches_one_process(tmp_path):
             assert torch.allclose(o_r, o[:, seg].detach(), atol=1e-10), (world, r)
             for name, gr, x in zip("q k v g beta".split(), grads_r, xs):
                 assert torch.allclose(gr, x.grad[:, seg], atol=1e-9), (world, r, name)
+
+
+def _attn_worker(rank, world, port, out_dir, window):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch.distributed as dist
+    from hanuman_b200.parallel.context import attention_context_parallel
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        q, k, v, w = _attn_inputs()
+        S = q.shape[1]
+        seg = slice(rank * S // world, (rank + 1) * S // world)
+        xs = [t[:, seg].clone().requires_grad_() for t in (q, k, v)]
+        o = attention_context_parallel(*xs, window=window)
+        (o * w[:, seg]).sum().backward()
+        torch.save((o.detach(), [x.grad for x in xs]), os.path.join(out_dir, f"a{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def _attn_inputs(B=2, S=60, Nq=4, Nkv=2, H=8):
+    g = torch.Generator().manual_seed(6)
+    q, k, v = (torch.randn(B, S, n, H, generator=g, dtype=torch.float64) for n in (Nq, Nkv, Nkv))
+    w = torch.randn(B, S, Nq, H, generator=g, dtype=torch.float64)
+    return q, k, v, w
+
+
+def test_attention_context_parallel_matches_one_process(tmp_path):
+    from hanuman_b200.ops import reference as ref
+    q, k, v, w = _attn_inputs()
+    S = q.shape[1]
+    for window in (0, 17):
+        xs = [t.clone().requires_grad_() for t in (q, k, v)]
+        o = ref.causal_attention(*xs, window=window)
+        (o * w).sum().backward()
+        for world in (2, 3):
+            ctx = mp.get_context("spawn")
+            port = _port()
+            procs = [ctx.Process(target=_attn_worker, args=(r, world, port, str(tmp_path), window))
+                     for r in range(world)]
+            for p in procs:
+                p.start()
+            for p in procs:
+                p.join(timeout=300)
+                assert p.exitcode == 0
+            for r in range(world):
+                o_r, grads_r = torch.load(tmp_path / f"a{r}.pt")
+                seg = slice(r * S // world, (r + 1) * S // world)
+                # the attention math runs in fp32 (softmax included), and the key /
+                # value gradients of the ranks' queries are summed in another order
+                assert torch.allclose(o_r, o[:, seg].detach(), atol=1e-6), (window, world, r)
+                for name, gr, x in zip("q k v".split(), grads_r, xs):
+                    assert torch.allclose(gr, x.grad[:, seg], atol=1e-5), (window, world, r, name)
