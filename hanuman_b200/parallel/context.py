@@ -145,3 +145,79 @@ def attention_context_parallel(q, k, v, window: int = 0, scale: Optional[float] 
     k_all, v_all = kv_all[..., :H], kv_all[..., H:]
     end = (rank + 1) * n          # causal: no key past this segment's last query
     return ref.causal_attention(q, k_all[:, :end], v_all[:, :end], window, scale, q_offset=rank * n)
+
+
+class _Halo(torch.autograd.Function):
+    """Prepends the last ``n`` rows (dim 1) of the previous rank's ``x`` (zeros
+    on rank 0) and hands this rank's last ``n`` rows to the next rank; the
+    backward returns the halo's gradient to its owner and adds the gradient
+    the next rank sends for this rank's last rows.  One exchange per call, so
+    callers concatenate what they need (e.g. the q | k | v projections)."""
+
+    @staticmethod
+    def forward(ctx, x, n, group):
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        glob = (lambda r: dist.get_global_rank(group, r)) if group is not None else (lambda r: r)
+        halo = torch.zeros(x.shape[0], n, *x.shape[2:], dtype=x.dtype, device=x.device)
+        reqs = []
+        if rank > 0:
+            reqs.append(dist.irecv(halo, src=glob(rank - 1), group=group))
+        if rank < world - 1:
+            reqs.append(dist.isend(x[:, -n:].contiguous(), dst=glob(rank + 1), group=group))
+        for r in reqs:
+            r.wait()
+        ctx.n, ctx.group, ctx.rank, ctx.world, ctx.glob = n, group, rank, world, glob
+        return torch.cat([halo, x], dim=1)
+
+    @staticmethod
+    def backward(ctx, grad):
+        n = ctx.n
+        gx = grad[:, n:].contiguous()
+        tail = torch.zeros_like(gx[:, -n:])
+        reqs = []
+        if ctx.rank < ctx.world - 1:
+            reqs.append(dist.irecv(tail, src=ctx.glob(ctx.rank + 1), group=ctx.group))
+        if ctx.rank > 0:
+            reqs.append(dist.isend(grad[:, :n].contiguous(), dst=ctx.glob(ctx.rank - 1), group=ctx.group))
+        for r in reqs:
+            r.wait()
+        if ctx.rank < ctx.world - 1:
+            gx[:, -n:] += tail
+        return gx, None, None
+
+
+def kda_layer_context_parallel(mod, h, dtype, group=None):
+    """A KDA layer (models/layers.py:KDA, its CPU math) over a sequence split
+    across the ranks of ``group``: the 4-tap conv reads the previous rank's
+    last 3 projected rows (one halo exchange for q | k | v), the delta rule
+    passes its state along the chain; everything else is per token.  Each
+    rank passes its segment ``h [B, S_r, D]`` and gets its output; parameter
+    gradients are this rank's share (sum them over the ranks)."""
+    import math
+    import torch.nn.functional as F
+    B, S, D = h.shape
+    H, K = mod.n_heads, mod.head_dim
+    V = K
+    xf = h.reshape(B * S, D).float()
+    proj = torch.cat([(xf @ mod.wq.float()).to(dtype), (xf @ mod.wk.float()).to(dtype),
+                      (xf @ mod.wv.float()).to(dtype)], dim=-1).view(B, S, -1)
+    taps = mod.q_conv.weight.shape[-1]
+    full = _Halo.apply(proj, taps - 1, group)
+    HK = H * K
+    convs = []
+    for i, conv in enumerate((mod.q_conv, mod.k_conv, mod.v_conv)):
+        c = ref.short_conv(full[..., i * HK:(i + 1) * HK], conv.weight)[:, taps - 1:]
+        convs.append(F.silu(c.float()))
+    q, k, v = (c.view(B, S, H, K) for c in convs)
+    q = ref.l2_norm(q, 1e-6)
+    k = ref.l2_norm(k, 1e-6)
+    f = ((xf @ mod.f_proj0.float()) @ mod.f_proj1.float()).view(B, S, H, K)
+    g = ref.kda_gate(f, mod.a_log, mod.dt_bias, mod.gate)
+    beta = torch.sigmoid(xf @ mod.wb.float()).view(B, S, H)
+    o = kda_context_parallel(q, k, v, g, beta, 1.0 / math.sqrt(K), mod.chunk, group).float()
+    var = (o * o).mean(-1, keepdim=True)
+    o = o * torch.rsqrt(var + 1e-5) * mod.o_norm
+    gate = torch.sigmoid((xf @ mod.g_proj0.float()) @ mod.g_proj1.float()
+                         + mod.g_proj1_bias).view(B, S, H, V)
+    o = (o * gate).reshape(B * S, H * V)
+    return (o @ mod.wo.float()).view(B, S, D)

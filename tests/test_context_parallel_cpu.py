@@ -123,3 +123,59 @@ def test_attention_context_parallel_matches_one_process(tmp_path):
                 assert torch.allclose(o_r, o[:, seg].detach(), atol=1e-6), (window, world, r)
                 for name, gr, x in zip("q k v".split(), grads_r, xs):
                     assert torch.allclose(gr, x.grad[:, seg], atol=1e-5), (window, world, r, name)
+
+
+def _layer_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch.distributed as dist
+    from hanuman_b200.models.layers import KDA
+    from hanuman_b200.parallel.context import kda_layer_context_parallel
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        m = KDA(32, 2, 16, torch.Generator().manual_seed(8), chunk=16)
+        h, w = _layer_inputs()
+        S = h.shape[1]
+        seg = slice(rank * S // world, (rank + 1) * S // world)
+        hs = h[:, seg].clone().requires_grad_()
+        y = kda_layer_context_parallel(m, hs, torch.float32)
+        (y * w[:, seg]).sum().backward()
+        grads = {n: p.grad.clone() for n, p in m.named_parameters()}
+        for t in grads.values():
+            dist.all_reduce(t)
+        torch.save((y.detach(), hs.grad, grads), os.path.join(out_dir, f"l{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def _layer_inputs(B=2, S=64, D=32):
+    g = torch.Generator().manual_seed(9)
+    return torch.randn(B, S, D, generator=g), torch.randn(B, S, D, generator=g)
+
+
+def test_kda_layer_context_parallel_matches_one_process(tmp_path):
+    """The whole KDA layer (conv halo + state passing) on 2 and 3 ranks gives
+    the single-process output, input gradient and summed parameter gradients."""
+    from hanuman_b200.models.layers import KDA
+    m = KDA(32, 2, 16, torch.Generator().manual_seed(8), chunk=16)
+    h, w = _layer_inputs()
+    hr = h.clone().requires_grad_()
+    y = m(hr, torch.float32)
+    (y * w).sum().backward()
+    S = h.shape[1]
+    for world in (2, 3):
+        ctx = mp.get_context("spawn")
+        port = _port()
+        procs = [ctx.Process(target=_layer_worker, args=(r, world, port, str(tmp_path)))
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=300)
+            assert p.exitcode == 0
+        for r in range(world):
+            y_r, gh_r, grads = torch.load(tmp_path / f"l{r}.pt")
+            seg = slice(r * S // world, (r + 1) * S // world)
+            assert torch.allclose(y_r, y[:, seg].detach(), atol=2e-5, rtol=1e-4), (world, r)
+            assert torch.allclose(gh_r, hr.grad[:, seg], atol=2e-5, rtol=1e-4), (world, r)
+            for n, p in m.named_parameters():
+                assert torch.allclose(grads[n], p.grad, atol=2e-4, rtol=1e-3), (world, r, n)
