@@ -221,3 +221,101 @@ def kda_layer_context_parallel(mod, h, dtype, group=None):
                          + mod.g_proj1_bias).view(B, S, H, V)
     o = (o * gate).reshape(B * S, H * V)
     return (o @ mod.wo.float()).view(B, S, D)
+
+
+def _attention_layer_cp(mod, h, cos, sin, dtype, pos0, group):
+    """models/layers.py:Attention (CPU math) for this rank's segment: RoPE at
+    the global positions, attention over the all-gathered keys / values."""
+    from .. import ops
+    B, S, D = h.shape
+    H = mod.head_dim
+    x2 = h.reshape(B * S, D)
+    q = ops.linear(x2, mod.wq, compute_dtype=dtype).view(B, S, mod.n_q, H)
+    k = ops.linear(x2, mod.wk, compute_dtype=dtype).view(B, S, mod.n_kv, H)
+    v = ops.linear(x2, mod.wv, compute_dtype=dtype).view(B, S, mod.n_kv, H)
+    positions = torch.arange(pos0, pos0 + S, device=h.device)
+    q, k = ops.apply_rope(q, k, cos.to(dtype), sin.to(dtype), positions)
+    o = attention_context_parallel(q, k, v, mod.window, None, group).reshape(B * S, mod.n_q * H)
+    return ops.linear(o, mod.wo, out_dtype=torch.float32, compute_dtype=dtype).view(B, S, D)
+
+
+def _moe_cp(mod, h, dtype, world, group):
+    """models/layers.py:MoE (CPU math) for this rank's segment; the router
+    statistics of the aux losses (ops/reference.py:router_aux) are sums over
+    the whole sequence, so they are summed over the ranks (differentiable:
+    the backward sums every rank's gradient of the global statistics)."""
+    import torch.distributed.nn.functional as dnn
+    B, S, D = h.shape
+    N, K = mod.n_experts, mod.n_active
+    x = h.reshape(B * S, D)
+    logits = x.float() @ mod.router.float()
+    scores, idx, w = ref.route(logits, mod.bias, K, mod.router_type, mod.scaling)
+    routed = ref.moe_dispatch_dense(x.to(dtype), idx, w.to(dtype), mod.expert_w_gate.to(dtype),
+                                    mod.expert_w_up.to(dtype), mod.expert_w_down.to(dtype))
+    out = routed + mod.shared_ffn(x, dtype)
+    lse = torch.logsumexp(logits, dim=-1)
+    counts = torch.zeros(B, N, dtype=torch.float32, device=h.device)
+    counts.scatter_add_(1, idx.reshape(B, S * K), torch.ones(B, S * K, device=h.device))
+    sc = scores.reshape(B, S, N)
+    probs = sc / (sc.sum(-1, keepdim=True) + 1e-9)
+    stats = torch.cat([(lse ** 2).sum().reshape(1), probs.sum(1).reshape(-1),
+                       (-(probs * torch.log(probs + 1e-9)).sum(-1)).sum().reshape(1)])
+    stats = dnn.all_reduce(stats, group=group)
+    dist.all_reduce(counts, group=group)
+    s_tot = S * world
+    aux = {"router_z_loss": stats[0] / (B * s_tot),
+           "balance_loss": (N * (counts / (s_tot * K) * stats[1:1 + B * N].view(B, N) / s_tot)
+                            .sum(-1)).mean(),
+           "mean_entropy": stats[-1] / (B * s_tot),
+           "expert_counts": counts.sum(0)}
+    return out.view(B, S, D), aux
+
+
+def transformer_loss_context_parallel(model, tokens, next_first, group=None):
+    """This rank's share of the training loss of ``models/transformer.py:
+    Transformer.loss`` (CPU math) for a batch whose sequences are split across
+    the ranks of ``group`` in equal contiguous segments.
+
+    ``tokens [B, S_r]`` is this rank's segment; ``next_first [B]`` the first
+    token of the next rank's segment (the target of this segment's last
+    position; unused on the last rank).  The shares of all ranks sum to the
+    single-process loss: CE summed over this rank's positions / all positions,
+    plus the router z and balance losses (computed from statistics summed over
+    the ranks) / world.  The parameter gradients of the shares sum (over the
+    ranks) to the single-process gradients."""
+    from ..models.transformer import merge_aux
+    from .. import ops
+    cfg = model.cfg
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    B, S = tokens.shape
+    dtype = model.dtype
+    x = model.embed(tokens)
+    aux_list = []
+    for blk in model.blocks:
+        h = blk.norm1(x, dtype)
+        if blk.attention_type == "kda":
+            a = kda_layer_context_parallel(blk.attn, h, dtype, group)
+        else:
+            a = _attention_layer_cp(blk.attn, h, model.rope_cos, model.rope_sin, dtype, rank * S, group)
+        x = x + blk.residual_scale.float() * a
+        h = blk.norm2(x, dtype)
+        if blk.use_moe:
+            f, aux = _moe_cp(blk.ffn, h, dtype, world, group)
+            aux_list.append(aux)
+        else:
+            f = blk.ffn(h, dtype)
+        x = x + blk.residual_scale.float() * f
+    hN = model.norm_f(x, dtype)
+    if rank < world - 1:
+        tgt = torch.cat([tokens[:, 1:], next_first[:, None]], dim=1)
+        hs = hN
+    else:
+        tgt = tokens[:, 1:]
+        hs = hN[:, :-1]
+    n_local = hs.shape[0] * hs.shape[1]
+    n_all = B * (S * world - 1)
+    ce = ops.head_cross_entropy(hs.reshape(n_local, -1), model.wte, tgt.reshape(-1),
+                                compute_dtype=dtype) * (n_local / n_all)
+    aux = merge_aux(aux_list, cfg.n_experts, model.n_moe, x.device)
+    return ce + (cfg.z_loss_weight * aux["router_z_loss"]
+                 + cfg.balance_loss_weight * aux["balance_loss"]) / world

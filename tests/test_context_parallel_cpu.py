@@ -179,3 +179,72 @@ def test_kda_layer_context_parallel_matches_one_process(tmp_path):
             assert torch.allclose(gh_r, hr.grad[:, seg], atol=2e-5, rtol=1e-4), (world, r)
             for n, p in m.named_parameters():
                 assert torch.allclose(grads[n], p.grad, atol=2e-4, rtol=1e-3), (world, r, n)
+
+
+def _model_cfg():
+    from hanuman_b200.config import get_config
+    c = get_config("tiny_hybrid")
+    c.seq_len = 48
+    c.batch_size = 2
+    c.vocab_size = 512
+    c.d_model = 64
+    c.n_experts = 4
+    c.d_ff = 64
+    c.kda_heads = 2
+    c.kda_head_dim = 16
+    c.kda_chunk_size = 16
+    c.n_q_heads, c.n_kv_heads, c.head_dim = 2, 1, 16
+    return c
+
+
+def _model_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch.distributed as dist
+    from hanuman_b200.models.transformer import Transformer
+    from hanuman_b200.parallel.context import transformer_loss_context_parallel
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        c = _model_cfg()
+        m = Transformer(c, seed=1)
+        toks = torch.randint(0, c.vocab_size, (c.batch_size, c.seq_len), generator=torch.Generator().manual_seed(2))
+        S = c.seq_len // world
+        seg = toks[:, rank * S:(rank + 1) * S]
+        nxt = toks[:, (rank + 1) * S] if rank < world - 1 else toks[:, -1]
+        loss = transformer_loss_context_parallel(m, seg, nxt)
+        loss.backward()
+        total = loss.detach().clone()
+        dist.all_reduce(total)
+        grads = {n: p.grad.clone() for n, p in m.named_parameters() if p.grad is not None}
+        for t in grads.values():
+            dist.all_reduce(t)
+        torch.save((total, grads), os.path.join(out_dir, f"m{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_transformer_loss_context_parallel_matches_one_process(tmp_path):
+    """The hybrid model (3 KDA layers + 1 attention layer, MoE blocks) with
+    its sequences split across 2 and 3 ranks: the ranks' loss shares sum to
+    the single-process loss and their summed parameter gradients match."""
+    from hanuman_b200.models.transformer import Transformer
+    c = _model_cfg()
+    m = Transformer(c, seed=1)
+    toks = torch.randint(0, c.vocab_size, (c.batch_size, c.seq_len), generator=torch.Generator().manual_seed(2))
+    loss, _ = m.loss(toks)
+    loss.backward()
+    for world in (2, 3):
+        ctx = mp.get_context("spawn")
+        port = _port()
+        procs = [ctx.Process(target=_model_worker, args=(r, world, port, str(tmp_path)))
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=300)
+            assert p.exitcode == 0
+        total, grads = torch.load(tmp_path / "m0.pt")
+        assert abs(total.item() - loss.item()) < 1e-4 * abs(loss.item()), (world, total, loss)
+        for n, p in m.named_parameters():
+            if p.grad is None:
+                continue
+            assert torch.allclose(grads[n], p.grad, atol=2e-5, rtol=2e-3), (world, n)
